@@ -1,0 +1,323 @@
+// Raw-pointer C ABI of the attention engine (include/gtb_attn.h): argument checks, kernel choice,
+// scratch from the stream-ordered allocator, error state.
+//
+// Error messages keep the wording of the reference's checks in gt_flash_attention
+// (csrc/gt_ops_nn.cpp:2425-2454) where the same condition is tested, so callers that match on
+// them (tests/test_pooling_and_attention.py:381,386 look for "cannot be broadcast") keep working.
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <mutex>
+#include <string>
+
+#include "gtb_common.cuh"
+#include "q8_0_internal.h"
+#include "sdpa_args.h"
+
+namespace gtb {
+
+namespace {
+thread_local std::string g_err;
+std::mutex g_status_mtx;
+int* g_status[64] = {};
+}  // namespace
+
+void set_error(const std::string& msg) { g_err = msg; }
+
+void set_errorf(const char* fmt, ...) {
+    char buf[1024];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_err = buf;
+}
+
+const char* last_error() { return g_err.c_str(); }
+void clear_error() { g_err.clear(); }
+
+bool cuda_failed(cudaError_t e, const char* what) {
+    if (e == cudaSuccess) return false;
+    set_errorf("%s: CUDA error %d (%s)", what, (int)e, cudaGetErrorString(e));
+    return true;
+}
+
+int* device_status_word(int device) {
+    if (device < 0 || device >= 64) return nullptr;
+    std::lock_guard<std::mutex> lk(g_status_mtx);
+    if (!g_status[device]) {
+        int* p = nullptr;
+        if (cudaMalloc(&p, sizeof(int)) != cudaSuccess) return nullptr;
+        cudaMemset(p, 0, sizeof(int));
+        g_status[device] = p;
+    }
+    return g_status[device];
+}
+
+namespace {
+
+std::string shape_str(const int64_t* s, int n) {
+    std::string r = "[";
+    for (int i = 0; i < n; ++i) r += (i ? ", " : "") + std::to_string(s[i]);
+    return r + "]";
+}
+
+// Every pointer handed to a kernel must be device (or managed) memory of the current device.
+bool check_device_ptr(const void* p, const char* ctx, const char* name) {
+    if (!p) {
+        set_errorf("%s: %s is NULL", ctx, name);
+        return false;
+    }
+    cudaPointerAttributes attr;
+    if (cudaPointerGetAttributes(&attr, p) != cudaSuccess) {
+        cudaGetLastError();
+        set_errorf("%s: %s is not CUDA memory (this engine has no CPU path)", ctx, name);
+        return false;
+    }
+    if (attr.type != cudaMemoryTypeDevice && attr.type != cudaMemoryTypeManaged) {
+        set_errorf("%s: %s is not CUDA device memory (this engine has no CPU path)", ctx, name);
+        return false;
+    }
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (attr.type == cudaMemoryTypeDevice && attr.device != dev) {
+        set_errorf("%s: %s lives on cuda:%d but the current device is cuda:%d", ctx, name, attr.device, dev);
+        return false;
+    }
+    return true;
+}
+
+int64_t numel4(const gtb_tensor4& t) { return t.shape[0] * t.shape[1] * t.shape[2] * t.shape[3]; }
+
+// Shapes, dtypes and mask of an attention call (gt_ops_nn.cpp:2425-2454).
+bool check_attn(const char* ctx, const gtb_tensor4* q, const gtb_tensor4* k, const gtb_tensor4* v,
+                const gtb_tensor4* mask, AttnShape& sh) {
+    if (!q || !k || !v) {
+        set_errorf("%s expects 4D q, k, v tensors (B, H, L, D)", ctx);
+        return false;
+    }
+    sh.B = q->shape[0]; sh.H = q->shape[1]; sh.L = q->shape[2]; sh.D = q->shape[3];
+    sh.Hkv = k->shape[1]; sh.S = k->shape[2]; sh.Dv = v->shape[3];
+    for (int i = 0; i < 4; ++i) {
+        if (q->shape[i] < 0 || k->shape[i] < 0 || v->shape[i] < 0) {
+            set_errorf("%s: negative size", ctx);
+            return false;
+        }
+    }
+    if (sh.Hkv <= 0 || sh.H % sh.Hkv != 0) {
+        set_errorf("%s: num_heads must be divisible by num_kv_heads", ctx);
+        return false;
+    }
+    if (k->shape[0] != sh.B || v->shape[0] != sh.B || v->shape[1] != sh.Hkv || v->shape[2] != sh.S ||
+        k->shape[3] != sh.D) {
+        set_errorf("%s: q (B, H, L, D), k (B, H_kv, S, D) and v (B, H_kv, S, Dv) do not fit together", ctx);
+        return false;
+    }
+    if (!is_float_dtype(q->dtype) || k->dtype != q->dtype || v->dtype != q->dtype) {
+        set_errorf("%s: q, k and v must share one floating dtype (f32, f16, bf16 or f64)", ctx);
+        return false;
+    }
+    if (mask) {
+        const int64_t want[4] = {sh.B, sh.H, sh.L, sh.S};
+        bool fits = true;
+        for (int i = 0; i < 4; ++i) fits = fits && (mask->shape[i] == 1 || mask->shape[i] == want[i]);
+        if (!fits) {
+            set_errorf("%s: attn_mask of shape %s cannot be broadcast to the attention weights %s", ctx,
+                       shape_str(mask->shape, 4).c_str(), shape_str(want, 4).c_str());
+            return false;
+        }
+        if (mask->dtype != BOOL && !is_float_dtype(mask->dtype)) {
+            set_errorf("%s: attn_mask must be bool or floating point", ctx);
+            return false;
+        }
+    }
+    return true;
+}
+
+gtb_tensor4 broadcast_mask(const gtb_tensor4& m) {
+    gtb_tensor4 r = m;
+    for (int i = 0; i < 4; ++i)
+        if (r.shape[i] == 1) r.stride[i] = 0;
+    return r;
+}
+
+bool same_shape(const gtb_tensor4& a, const int64_t* s) {
+    for (int i = 0; i < 4; ++i)
+        if (a.shape[i] != s[i]) return false;
+    return true;
+}
+
+float resolve_scale(float scale, int64_t D) { return scale <= 0.0f ? 1.0f / std::sqrt((float)D) : scale; }
+
+int env_int(const char* name, int dflt) {
+    const char* e = getenv(name);
+    return e ? atoi(e) : dflt;
+}
+
+}  // namespace
+}  // namespace gtb
+
+using namespace gtb;
+
+extern "C" {
+
+GTB_API const char* gtb_last_error(void) { return gtb::last_error(); }
+GTB_API void gtb_clear_error(void) { gtb::clear_error(); }
+
+GTB_API const char* gtb_version(void) { return "gguf_train_b200 attention engine 0.1 (sm_100a)"; }
+
+GTB_API int gtb_device_status(void) {
+    int dev = 0;
+    if (cuda_failed(cudaGetDevice(&dev), "gtb_device_status")) return -1;
+    if (cuda_failed(cudaDeviceSynchronize(), "gtb_device_status: synchronize")) return -1;
+    int* w = device_status_word(dev);
+    if (!w) return 0;
+    int v = 0;
+    if (cuda_failed(cudaMemcpy(&v, w, sizeof(int), cudaMemcpyDeviceToHost), "gtb_device_status: read")) return -1;
+    if (v) cudaMemset(w, 0, sizeof(int));
+    return v;
+}
+
+GTB_API int gtb_sdpa_fwd(const gtb_tensor4* q, const gtb_tensor4* k, const gtb_tensor4* v, const gtb_tensor4* mask,
+                         float scale, int is_causal, gtb_tensor4* out, void* lse, void* stream) {
+    const char* ctx = "flash_attention";
+    FwdArgs a;
+    if (!check_attn(ctx, q, k, v, mask, a.sh)) return -1;
+    if (!out) {
+        set_errorf("%s: out is NULL", ctx);
+        return -1;
+    }
+    const int64_t osh[4] = {a.sh.B, a.sh.H, a.sh.L, a.sh.Dv};
+    if (!same_shape(*out, osh) || out->dtype != q->dtype) {
+        set_errorf("%s: out must be %s in q's dtype", ctx, shape_str(osh, 4).c_str());
+        return -1;
+    }
+    if (numel4(*out) == 0) return 0;
+    if (!check_device_ptr(q->data, ctx, "q") || !check_device_ptr(out->data, ctx, "out")) return -1;
+    if (a.sh.S > 0 && (!check_device_ptr(k->data, ctx, "k") || !check_device_ptr(v->data, ctx, "v"))) return -1;
+    if (mask && !check_device_ptr(mask->data, ctx, "attn_mask")) return -1;
+    if (lse && !check_device_ptr(lse, ctx, "lse")) return -1;
+    a.q = *q; a.k = *k; a.v = *v; a.o = *out;
+    a.has_mask = mask != nullptr;
+    if (mask) a.mask = broadcast_mask(*mask);
+    a.scale = resolve_scale(scale, a.sh.D);
+    a.causal = is_causal ? 1 : 0;
+    a.lse = lse;
+    cudaStream_t st = (cudaStream_t)stream;
+    // GTB_FWD_SIMT=1 forces the SIMT kernel (used to cross-check the two kernels)
+    static const int force_simt = env_int("GTB_FWD_SIMT", 0);
+    if (!force_simt && fwd_sm100_supported(a)) return launch_fwd_sm100(a, st);
+    return launch_fwd_simt(a, st);
+}
+
+GTB_API int gtb_sdpa_bwd(const gtb_tensor4* dout, const gtb_tensor4* q, const gtb_tensor4* k, const gtb_tensor4* v,
+                         const gtb_tensor4* mask, const gtb_tensor4* out, const void* lse, float scale, int is_causal,
+                         gtb_tensor4* dq, gtb_tensor4* dk, gtb_tensor4* dv, void* stream) {
+    const char* ctx = "flash_attention_backward";
+    BwdArgs a;
+    if (!check_attn(ctx, q, k, v, mask, a.sh)) return -1;
+    if (!dout || !out || !lse || !dq || !dk || !dv) {
+        set_errorf("%s: dout, out, lse, dq, dk and dv are required", ctx);
+        return -1;
+    }
+    const int64_t osh[4] = {a.sh.B, a.sh.H, a.sh.L, a.sh.Dv};
+    if (!same_shape(*dout, osh) || !same_shape(*out, osh) || dout->dtype != q->dtype || out->dtype != q->dtype) {
+        set_errorf("%s: dout and out must be %s in q's dtype", ctx, shape_str(osh, 4).c_str());
+        return -1;
+    }
+    if (!same_shape(*dq, q->shape) || !same_shape(*dk, k->shape) || !same_shape(*dv, v->shape) ||
+        dq->dtype != q->dtype || dk->dtype != q->dtype || dv->dtype != q->dtype) {
+        set_errorf("%s: dq, dk, dv must match q, k, v in shape and dtype", ctx);
+        return -1;
+    }
+    if (numel4(*q) == 0 && numel4(*k) == 0) return 0;
+    const gtb_tensor4* all[] = {dout, q, k, v, out, dq, dk, dv};
+    const char* names[] = {"dout", "q", "k", "v", "out", "dq", "dk", "dv"};
+    for (int i = 0; i < 8; ++i)
+        if (numel4(*all[i]) > 0 && !check_device_ptr(all[i]->data, ctx, names[i])) return -1;
+    if (mask && !check_device_ptr(mask->data, ctx, "attn_mask")) return -1;
+    if (a.sh.L > 0 && !check_device_ptr(lse, ctx, "lse")) return -1;
+    a.q = *q; a.k = *k; a.v = *v; a.o = *out; a.dout = *dout; a.dq = *dq; a.dk = *dk; a.dv = *dv;
+    a.has_mask = mask != nullptr;
+    if (mask) a.mask = broadcast_mask(*mask);
+    a.scale = resolve_scale(scale, a.sh.D);
+    a.causal = is_causal ? 1 : 0;
+    a.lse = lse;
+    cudaStream_t st = (cudaStream_t)stream;
+    const size_t bytes = bwd_simt_scratch_bytes(a);
+    void* scratch = nullptr;
+    if (bytes && cuda_failed(cudaMallocAsync(&scratch, bytes, st), "flash_attention_backward: scratch allocation"))
+        return -1;
+    a.scratch = scratch;
+    const int rc = launch_bwd_simt(a, st);
+    if (scratch) cudaFreeAsync(scratch, st);
+    return rc;
+}
+
+GTB_API int gtb_q8_0_quantize(const void* x, int x_dtype, int64_t n_rows, int64_t row_len, void* out, void* stream) {
+    if (n_rows < 0 || row_len < 0) {
+        set_error("quantize: negative size");
+        return -1;
+    }
+    const int64_t n = n_rows * row_len;
+    if (n % 32 != 0) {
+        set_error("Tensor size must be a multiple of ggml quantization block size");
+        return -1;
+    }
+    if (n == 0) return 0;
+    if (!check_device_ptr(x, "quantize", "input") || !check_device_ptr(out, "quantize", "output")) return -1;
+    return launch_q8_0_quantize(x, x_dtype, n / 32, out, (cudaStream_t)stream);
+}
+
+GTB_API int gtb_q8_0_dequantize(const void* blocks, int64_t n_rows, int64_t row_len, void* out, int out_dtype,
+                                void* stream) {
+    const int64_t n = n_rows * row_len;
+    if (n_rows < 0 || row_len < 0 || n % 32 != 0) {
+        set_error("dequantize: the value count must be a non-negative multiple of 32");
+        return -1;
+    }
+    if (n == 0) return 0;
+    if (!check_device_ptr(blocks, "dequantize", "input") || !check_device_ptr(out, "dequantize", "output")) return -1;
+    return launch_q8_0_dequantize(blocks, n / 32, out, out_dtype, (cudaStream_t)stream);
+}
+
+GTB_API int gtb_decode_q8_0(const void* q, int q_dtype, const void* k_q8, const void* v_q8, const int32_t* seq_lens,
+                            int64_t B, int64_t H, int64_t Hkv, int64_t Smax, int64_t D, float scale, void* out,
+                            void* stream) {
+    const char* ctx = "flash_decode_q8_0";
+    if (B < 0 || H < 0 || Hkv <= 0 || Smax < 0 || D <= 0) {
+        set_errorf("%s: bad sizes", ctx);
+        return -1;
+    }
+    if (H % Hkv != 0) {
+        set_errorf("%s: num_heads must be divisible by num_kv_heads", ctx);
+        return -1;
+    }
+    if (D % 32 != 0) {
+        set_errorf("%s: the head size must be a multiple of the Q8_0 block (32)", ctx);
+        return -1;
+    }
+    if (q_dtype != F16 && q_dtype != BF16 && q_dtype != F32) {
+        set_errorf("%s: q must be f16, bf16 or f32", ctx);
+        return -1;
+    }
+    if (B == 0 || H == 0) return 0;
+    if (!check_device_ptr(q, ctx, "q") || !check_device_ptr(out, ctx, "out") ||
+        !check_device_ptr(seq_lens, ctx, "seq_lens"))
+        return -1;
+    if (Smax > 0 && (!check_device_ptr(k_q8, ctx, "k") || !check_device_ptr(v_q8, ctx, "v"))) return -1;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    DecodeArgs a{q, q_dtype, k_q8, v_q8, seq_lens, B, H, Hkv, Smax, D, resolve_scale(scale, D), out,
+                 device_status_word(dev)};
+    cudaStream_t st = (cudaStream_t)stream;
+    const size_t bytes = decode_scratch_bytes(B, H, Hkv, Smax, D);
+    void* scratch = nullptr;
+    if (bytes && cuda_failed(cudaMallocAsync(&scratch, bytes, st), "flash_decode_q8_0: scratch allocation")) return -1;
+    const int rc = launch_decode_q8_0(a, (float*)scratch, st);
+    if (scratch) cudaFreeAsync(scratch, st);
+    return rc;
+}
+
+}  // extern "C"

@@ -1,0 +1,28 @@
+// Launchers of the Q8_0 kernels (quantise, dequantise, split-KV decode).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace gtb {
+
+struct DecodeArgs {
+    const void* q;
+    int q_dtype;
+    const void* k;
+    const void* v;
+    const int32_t* lens;
+    int64_t B, H, Hkv, Smax, D;
+    float scale;  // resolved (> 0)
+    void* out;
+    int* status;  // device status word for bounded waits
+};
+
+int launch_q8_0_quantize(const void* x, int x_dtype, int64_t nblocks, void* out, cudaStream_t st);
+int launch_q8_0_dequantize(const void* blocks, int64_t nblocks, void* out, int out_dtype, cudaStream_t st);
+int64_t decode_num_chunks(int64_t Smax);
+size_t decode_scratch_bytes(int64_t B, int64_t H, int64_t Hkv, int64_t Smax, int64_t D);
+int launch_decode_q8_0(const DecodeArgs& a, float* scratch, cudaStream_t st);
+
+}  // namespace gtb

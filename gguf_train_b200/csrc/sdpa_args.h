@@ -1,0 +1,45 @@
+// Validated argument bundles passed from the C-ABI layer to the kernel launchers.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/gtb_attn.h"
+
+namespace gtb {
+
+struct AttnShape {
+    int64_t B, H, Hkv, L, S, D, Dv;
+};
+
+struct FwdArgs {
+    AttnShape sh;
+    gtb_tensor4 q, k, v, o;
+    bool has_mask;
+    gtb_tensor4 mask;  // broadcast dims carry stride 0
+    float scale;       // already resolved (> 0)
+    int causal;
+    void* lse;         // nullable, (B,H,L) contiguous; double for f64 inputs, else float
+};
+
+struct BwdArgs {
+    AttnShape sh;
+    gtb_tensor4 q, k, v, o, dout, dq, dk, dv;
+    bool has_mask;
+    gtb_tensor4 mask;
+    float scale;
+    int causal;
+    const void* lse;   // (B,H,L) contiguous, from the forward (double for f64 inputs)
+    void* scratch;     // B*H*L accumulators (float or double) for rowsum(dout * out)
+};
+
+// SIMT kernels: any float dtype, any D/Dv <= 256, masks, any strides.
+int launch_fwd_simt(const FwdArgs& a, cudaStream_t st);
+int launch_bwd_simt(const BwdArgs& a, cudaStream_t st);
+size_t bwd_simt_scratch_bytes(const BwdArgs& a);
+
+// tcgen05/TMA forward: bf16/f16, D == Dv in {64,128}, unit inner stride, no mask.
+bool fwd_sm100_supported(const FwdArgs& a);
+int launch_fwd_sm100(const FwdArgs& a, cudaStream_t st);
+
+}  // namespace gtb

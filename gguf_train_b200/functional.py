@@ -1,0 +1,270 @@
+"""Attention functions of the engine: the gguf_train surface over the sm_100a kernels.
+
+`scaled_dot_product_attention` and `FlashAttentionFn` keep the names, arguments, defaults, mask
+rules and error messages of the reference (gguf_train/nn/functional.py:724-767,
+gguf_train/_functions.py:1922-1965). Tensors are torch CUDA tensors; torch provides storage,
+streams and autograd bookkeeping, while the forward and backward run in this package's native
+library through its C ABI. A CPU tensor is an error: the engine has no CPU path.
+
+Differences from the reference, by design:
+* FlashAttentionFn saves the output and the per-row log-sum-exp and runs a fused backward
+  instead of recomputing the probabilities with separate matmul/softmax ops. For a row in which
+  every key is masked, the forward gives 0 (as the reference) and the backward gives zero
+  gradients; the reference's op-by-op backward would instead differentiate a softmax over
+  -1e9 scores there.
+* The dropout path (dropout_p > 0) is the reference's composite of basic ops, run in torch.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import math
+
+import torch
+
+from . import _C
+
+_DTYPE_CODE = {
+    torch.float32: _C.GT_F32,
+    torch.float16: _C.GT_F16,
+    torch.bfloat16: _C.GT_BF16,
+    torch.float64: _C.GT_F64,
+    torch.bool: _C.GT_BOOL,
+}
+
+
+def _code(t: torch.Tensor) -> int:
+    try:
+        return _DTYPE_CODE[t.dtype]
+    except KeyError:
+        raise RuntimeError(f"flash_attention: unsupported dtype {t.dtype}") from None
+
+
+def _t4(t: torch.Tensor, shape=None, stride=None) -> _C.Tensor4:
+    r = _C.Tensor4()
+    r.data = t.data_ptr() if t.numel() else 0
+    shp = tuple(t.shape) if shape is None else tuple(shape)
+    std = tuple(t.stride()) if stride is None else tuple(stride)
+    for i in range(4):
+        r.shape[i] = int(shp[i])
+        r.stride[i] = int(std[i])
+    r.dtype = _code(t)
+    return r
+
+
+def _stream(dev: torch.device) -> int:
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+def _require_cuda(name: str, *ts) -> None:
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError(
+                f"{name}: this engine runs CUDA tensors only (got a {t.device} tensor); move it with .cuda()"
+            )
+
+
+def _native_mask(mask: torch.Tensor, B: int, H: int, L: int, S: int) -> _C.Tensor4:
+    """The native layer's mask rule (gt_ops_nn.cpp:2437-2454): a 2-D (L|1, S|1) or 4-D
+    (B|1, H|1, L|1, S|1) mask; size-1 dimensions broadcast."""
+    want = (B, H, L, S)
+    fits = mask.ndim in (2, 4) and all(m == 1 or m == w for m, w in zip(mask.shape, want[4 - mask.ndim:]))
+    if not fits:
+        raise RuntimeError(
+            f"flash_attention: attn_mask of shape {list(mask.shape)} cannot be broadcast to the attention weights "
+            f"{list(want)}"
+        )
+    shape = (1,) * (4 - mask.ndim) + tuple(mask.shape)
+    stride = (0,) * (4 - mask.ndim) + tuple(mask.stride())
+    stride = tuple(0 if s == 1 else st for s, st in zip(shape, stride))
+    return _t4(mask, shape, stride)
+
+
+def sdpa_forward(q, k, v, mask=None, scale: float | None = None, is_causal: bool = False, need_lse: bool = True):
+    """One call of the native forward: returns (out, lse). lse is (B, H, L), float64 for float64
+    inputs and float32 otherwise, or None."""
+    _require_cuda("flash_attention", q, k, v, mask)
+    if q.ndim != 4 or k.ndim != 4 or v.ndim != 4:
+        raise RuntimeError("flash_attention expects 4D q, k, v tensors (B, H, L, D)")
+    B, H, L, D = q.shape
+    S, Dv = k.shape[2], v.shape[3]
+    sc = (1.0 / math.sqrt(D)) if scale is None else float(scale)
+    out = torch.empty((B, H, L, Dv), dtype=q.dtype, device=q.device)
+    lse_dt = torch.float64 if q.dtype == torch.float64 else torch.float32
+    lse = torch.empty((B, H, L), dtype=lse_dt, device=q.device) if need_lse else None
+    mt = _native_mask(mask, B, H, L, S) if mask is not None else None
+    tq, tk, tv, to = _t4(q), _t4(k), _t4(v), _t4(out)
+    rc = _C.lib.gtb_sdpa_fwd(ctypes.byref(tq), ctypes.byref(tk), ctypes.byref(tv),
+                             ctypes.byref(mt) if mt is not None else None, sc, 1 if is_causal else 0,
+                             ctypes.byref(to), lse.data_ptr() if lse is not None and lse.numel() else None,
+                             _stream(q.device))
+    _C.check_rc(rc, "flash_attention")
+    return out, lse
+
+
+def sdpa_backward(grad_out, q, k, v, mask, out, lse, scale: float, is_causal: bool):
+    """One call of the native backward: returns (dq, dk, dv)."""
+    B, H, L, D = q.shape
+    S = k.shape[2]
+    dq = torch.empty_like(q, memory_format=torch.contiguous_format)
+    dk = torch.empty_like(k, memory_format=torch.contiguous_format)
+    dv = torch.empty_like(v, memory_format=torch.contiguous_format)
+    if grad_out.dtype != q.dtype:
+        grad_out = grad_out.to(q.dtype)
+    mt = _native_mask(mask, B, H, L, S) if mask is not None else None
+    tg, tq, tk, tv, to = _t4(grad_out), _t4(q), _t4(k), _t4(v), _t4(out)
+    tdq, tdk, tdv = _t4(dq), _t4(dk), _t4(dv)
+    rc = _C.lib.gtb_sdpa_bwd(ctypes.byref(tg), ctypes.byref(tq), ctypes.byref(tk), ctypes.byref(tv),
+                             ctypes.byref(mt) if mt is not None else None, ctypes.byref(to),
+                             lse.data_ptr() if lse.numel() else None, float(scale), 1 if is_causal else 0,
+                             ctypes.byref(tdq), ctypes.byref(tdk), ctypes.byref(tdv), _stream(q.device))
+    _C.check_rc(rc, "flash_attention_backward")
+    return dq, dk, dv
+
+
+class FlashAttentionFn(torch.autograd.Function):
+    """The autograd Function behind scaled_dot_product_attention (reference _functions.py:1922).
+
+    apply(q, k, v, mask, scale, is_causal): q (B,H,L,D), k (B,Hkv,S,D), v (B,Hkv,S,Dv), mask None,
+    (L,S) or 4-D, bool (True = may attend) or float (added); scale None -> 1/sqrt(D)."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, mask, scale, is_causal):
+        ctx.scale = float(scale) if scale is not None else (1.0 / math.sqrt(q.shape[-1]))
+        ctx.is_causal = bool(is_causal)
+        out, lse = sdpa_forward(q, k, v, mask, ctx.scale, ctx.is_causal, need_lse=True)
+        ctx.save_for_backward(q, k, v, mask, out, lse)
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        if grad_out is None:
+            return (None,) * 6
+        q, k, v, mask, out, lse = ctx.saved_tensors
+        dq, dk, dv = sdpa_backward(grad_out, q, k, v, mask, out, lse, ctx.scale, ctx.is_causal)
+        return dq, dk, dv, None, None, None
+
+
+def _autocast_lower(*ts):
+    """Inside torch.autocast, floating arguments are cast to the autocast dtype, as the reference's
+    _autocast_op(_AUTOCAST_LOWER) does for SDPA (gguf_train/_tensor.py:261-282)."""
+    if not torch.is_autocast_enabled("cuda"):
+        return ts, False
+    dt = torch.get_autocast_dtype("cuda")
+    return tuple(t.to(dt) if (t is not None and t.is_floating_point()) else t for t in ts), True
+
+
+def scaled_dot_product_attention(
+    query: torch.Tensor,
+    key: torch.Tensor,
+    value: torch.Tensor,
+    attn_mask: torch.Tensor | None = None,
+    dropout_p: float = 0.0,
+    is_causal: bool = False,
+    scale: float | None = None,
+    enable_gqa: bool = False,
+) -> torch.Tensor:
+    """torch.nn.functional.scaled_dot_product_attention, as gguf_train defines it
+    (nn/functional.py:724-767): a bool mask marks keys that MAY be attended, a float mask is added,
+    masks broadcast from the right against (B, H, L, S), GQA applies whenever H % Hkv == 0
+    (`enable_gqa` is accepted and ignored), causal masking is top-left aligned."""
+    (enable_gqa,)
+    (query, key, value, attn_mask), cast = _autocast_lower(query, key, value, attn_mask)
+    if cast:
+        with torch.autocast("cuda", enabled=False):
+            return scaled_dot_product_attention(query, key, value, attn_mask, dropout_p, is_causal, scale)
+    sc = (1.0 / math.sqrt(query.shape[-1])) if scale is None else float(scale)
+    if attn_mask is not None:
+        if query.ndim == 4 and key.ndim == 4:
+            want = (query.shape[0], query.shape[1], query.shape[2], key.shape[2])
+            if attn_mask.ndim > 4 or any(m != 1 and m != w for m, w in zip(reversed(attn_mask.shape), reversed(want))):
+                raise RuntimeError(
+                    f"scaled_dot_product_attention: attn_mask of shape {list(attn_mask.shape)} cannot be broadcast "
+                    f"to the attention weights {list(want)}"
+                )
+            if attn_mask.ndim != 4:
+                attn_mask = attn_mask.reshape((1,) * (4 - attn_mask.ndim) + tuple(attn_mask.shape))
+    if dropout_p == 0.0:
+        return FlashAttentionFn.apply(query, key, value, attn_mask, sc, is_causal)
+    return _sdpa_dropout(query, key, value, attn_mask, dropout_p, is_causal, sc)
+
+
+def _sdpa_dropout(query, key, value, attn_mask, dropout_p, is_causal, sc):
+    """The reference's dropout path (nn/functional.py:750-767): a composite of basic ops with -1e9
+    masking, run in torch (the engine has no fused dropout kernel)."""
+    B, H, L, D = query.shape
+    H_kv = key.shape[1]
+    k_u = key if H == H_kv else key.repeat_interleave(H // H_kv, dim=1)
+    v_u = value if H == H_kv else value.repeat_interleave(H // H_kv, dim=1)
+    scores = query.matmul(k_u.transpose(-2, -1)) * sc
+    if is_causal:
+        S = key.shape[-2]
+        cm = torch.ones((L, S), dtype=query.dtype, device=query.device).triu(diagonal=1) * (-1e9)
+        scores = scores + cm
+    if attn_mask is not None:
+        if attn_mask.dtype == torch.bool:
+            scores = scores.masked_fill(~attn_mask, -1e9)
+        else:
+            scores = scores + attn_mask
+    probs = torch.softmax(scores, dim=-1)
+    probs = torch.nn.functional.dropout(probs, p=dropout_p, training=True)
+    return probs.matmul(v_u)
+
+
+# ------------------------------------------------------------------ Q8_0 KV cache
+
+def quantize_q8_0(x: torch.Tensor) -> torch.Tensor:
+    """GGUF Q8_0 blocks of a CUDA tensor (rows along the last dim), as uint8 of shape
+    (..., last/32*34). Bit-exact with ggml's reference quantiser (gt_quantize, reference
+    csrc/gt_ops_extra.cpp:2002)."""
+    _require_cuda("quantize", x)
+    if x.shape[-1] % 32:
+        raise RuntimeError("Tensor size must be a multiple of ggml quantization block size")
+    x = x.contiguous()
+    out = torch.empty(tuple(x.shape[:-1]) + (x.shape[-1] // 32 * 34,), dtype=torch.uint8, device=x.device)
+    row = x.shape[-1]
+    rc = _C.lib.gtb_q8_0_quantize(x.data_ptr() if x.numel() else None, _code(x), x.numel() // max(row, 1), row,
+                                  out.data_ptr() if out.numel() else None, _stream(x.device))
+    _C.check_rc(rc, "quantize")
+    return out
+
+
+def dequantize_q8_0(blocks: torch.Tensor, dtype=torch.float32) -> torch.Tensor:
+    """Inverse of quantize_q8_0: x = q * d, in `dtype`."""
+    _require_cuda("dequantize", blocks)
+    if blocks.shape[-1] % 34:
+        raise RuntimeError("dequantize: the last dimension must hold whole 34-byte Q8_0 blocks")
+    row = blocks.shape[-1] // 34 * 32
+    out = torch.empty(tuple(blocks.shape[:-1]) + (row,), dtype=dtype, device=blocks.device)
+    blocks = blocks.contiguous()
+    rc = _C.lib.gtb_q8_0_dequantize(blocks.data_ptr() if blocks.numel() else None, out.numel() // max(row, 1), row,
+                                    out.data_ptr() if out.numel() else None, _DTYPE_CODE[dtype], _stream(out.device))
+    _C.check_rc(rc, "dequantize")
+    return out
+
+
+def decode_q8_0(q: torch.Tensor, k_q8: torch.Tensor, v_q8: torch.Tensor, seq_lens: torch.Tensor,
+                scale: float | None = None) -> torch.Tensor:
+    """One decode step: q (B, H, 1, D) against Q8_0 caches k_q8, v_q8 of shape (B, Hkv, Smax, D/32*34)
+    (uint8, from quantize_q8_0), sequence b attending its first seq_lens[b] rows. Returns (B, H, 1, D)
+    in q's dtype. Equivalent to dequantising the caches and calling scaled_dot_product_attention."""
+    _require_cuda("flash_decode_q8_0", q, k_q8, v_q8, seq_lens)
+    B, H, Lq, D = q.shape
+    if Lq != 1:
+        raise RuntimeError("flash_decode_q8_0: q must be (B, H, 1, D)")
+    if k_q8.ndim != 4 or k_q8.shape != v_q8.shape or k_q8.shape[0] != B or k_q8.shape[3] != D // 32 * 34:
+        raise RuntimeError("flash_decode_q8_0: k and v caches must be (B, Hkv, Smax, D/32*34) uint8 Q8_0 rows")
+    if seq_lens.dtype != torch.int32 or seq_lens.shape != (B,):
+        raise RuntimeError("flash_decode_q8_0: seq_lens must be an int32 (B) tensor")
+    Hkv, Smax = k_q8.shape[1], k_q8.shape[2]
+    q = q.contiguous()
+    k_q8 = k_q8.contiguous()
+    v_q8 = v_q8.contiguous()
+    seq_lens = seq_lens.contiguous()
+    out = torch.empty_like(q)
+    sc = 0.0 if scale is None else float(scale)
+    rc = _C.lib.gtb_decode_q8_0(q.data_ptr(), _code(q), k_q8.data_ptr() if k_q8.numel() else None,
+                                v_q8.data_ptr() if v_q8.numel() else None, seq_lens.data_ptr(), B, H, Hkv, Smax, D,
+                                sc, out.data_ptr(), _stream(q.device))
+    _C.check_rc(rc, "flash_decode_q8_0")
+    return out

@@ -1,0 +1,102 @@
+/* B200 (sm_100a) scaled-dot-product-attention engine: raw-pointer C ABI.
+ *
+ * Every entry point takes device pointers, sizes and element strides, and a CUDA stream
+ * (cudaStream_t passed as void*; NULL = the legacy default stream). No entry point takes a
+ * framework type. All return 0 on success and -1 on failure with a thread-local message in
+ * gtb_last_error(), the convention of the reference's gt_last_error (csrc/gt_core.cpp:7-23).
+ * Tensors must live on the current CUDA device. There is no CPU path: host pointers are an error.
+ *
+ * The reference-shaped handle ABI (gt_tensor *, gguf_train.h) is declared in gguf_train_attn.h and
+ * is implemented on top of these functions.
+ */
+#ifndef GTB_ATTN_H
+#define GTB_ATTN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GTB_API __attribute__((visibility("default")))
+
+/* A strided 4-D view of device memory. data points at element [0,0,0,0]; strides count elements
+ * (a stride of 0 broadcasts a size-1 dimension). dtype is a gt_dtype code (gguf_train.h:22-36):
+ * 0 = f32, 1 = f16, 2 = bf16, 3 = f64, 9 = bool (masks only). */
+typedef struct gtb_tensor4 {
+    void *data;
+    int64_t shape[4];
+    int64_t stride[4];
+    int32_t dtype;
+} gtb_tensor4;
+
+/* Attention forward.
+ * Replaces the body of gt_flash_attention (reference csrc/gt_ops_nn.cpp:2423-2525, declared
+ * csrc/gguf_train.h:311) for CUDA tensors.
+ *   q (B,H,L,D), k (B,Hkv,S,D), v (B,Hkv,S,Dv); H % Hkv == 0 (query head h reads kv head
+ *   h / (H/Hkv)); out (B,H,L,Dv) in q's dtype.
+ *   mask: NULL or (B|1,H|1,L|1,S|1), bool (0 = may not attend) or float (added to the scores).
+ *   scale <= 0 means 1/sqrt(D). is_causal masks s > l (top-left aligned).
+ *   lse: NULL or a (B,H,L) contiguous buffer that receives the natural-log sum of exp(scores)
+ *   per row (-inf for a row with no allowed key, whose output is 0): float64 for f64 inputs,
+ *   float32 otherwise.
+ * Kernel choice: bf16/f16 with D == Dv in {64,128}, unit inner stride and no mask runs the
+ * tcgen05/TMA kernel; everything else runs the SIMT kernel (f32/f64 accumulate as the input). */
+GTB_API int gtb_sdpa_fwd(const gtb_tensor4 *q, const gtb_tensor4 *k, const gtb_tensor4 *v,
+                         const gtb_tensor4 *mask, float scale, int is_causal,
+                         gtb_tensor4 *out, void *lse, void *stream);
+
+/* Attention backward: dq, dk, dv from dout, the forward inputs, the forward output and its lse.
+ * Replaces FlashAttentionFn.backward (reference gguf_train/_functions.py:1934-1965), which
+ * recomputes the probabilities with a chain of separate ops. dk/dv are summed over the query
+ * heads of each kv head, as that function does (:1958-1962). Scratch (rowsum(dout*out) per row)
+ * is taken from the stream-ordered allocator. */
+GTB_API int gtb_sdpa_bwd(const gtb_tensor4 *dout, const gtb_tensor4 *q, const gtb_tensor4 *k,
+                         const gtb_tensor4 *v, const gtb_tensor4 *mask, const gtb_tensor4 *out,
+                         const void *lse, float scale, int is_causal,
+                         gtb_tensor4 *dq, gtb_tensor4 *dk, gtb_tensor4 *dv, void *stream);
+
+/* Q8_0 quantisation of n_rows rows of row_len values (row_len % 32 == 0) into GGUF Q8_0 blocks
+ * (fp16 scale + 32 int8, 34 bytes per 32 values), bit-exact with ggml's reference quantiser.
+ * Replaces gt_quantize(t, GT_Q_BASE + 8) (reference csrc/gt_ops_extra.cpp:2002, which goes
+ * through a host float buffer in gt_tensor_to_dtype, csrc/gt_core.cpp:792-840).
+ * x: contiguous f32/f16/bf16 (x_dtype); out: n_rows * row_len / 32 * 34 bytes. */
+GTB_API int gtb_q8_0_quantize(const void *x, int x_dtype, int64_t n_rows, int64_t row_len,
+                              void *out, void *stream);
+
+/* Q8_0 -> f32/f16/bf16 (out_dtype), x = q * d. Replaces gt_dequantize (csrc/gt_ops_extra.cpp:2006). */
+GTB_API int gtb_q8_0_dequantize(const void *blocks, int64_t n_rows, int64_t row_len,
+                                void *out, int out_dtype, void *stream);
+
+/* One decode step against a Q8_0 KV cache.
+ * Replaces the reference's route for this step: k.dequantize(), v.dequantize(), then
+ * F.scaled_dot_product_attention(q, k, v) with q (B,H,1,D) (gguf_train/_tensor.py:1188-1196,
+ * csrc/gt_ops_nn.cpp:2423-2525), which has no fused path.
+ *   q: (B,H,D) contiguous, q_dtype f16/bf16/f32; k_q8, v_q8: (B,Hkv,Smax,D) as rows of D/32
+ *   Q8_0 blocks; seq_lens: int32 (B), sequence b attends its first seq_lens[b] rows (clamped to
+ *   [0, Smax]); out: (B,H,D) in q_dtype. D % 32 == 0 and D <= 256.
+ * Split-KV: each (b, kv head) is cut into chunks of up to GTB_DECODE_CHUNK rows that run in
+ * parallel; a second kernel merges the partial results. The partials live in scratch taken from
+ * the stream-ordered allocator. */
+#define GTB_DECODE_CHUNK 512
+GTB_API int gtb_decode_q8_0(const void *q, int q_dtype, const void *k_q8, const void *v_q8,
+                            const int32_t *seq_lens, int64_t B, int64_t H, int64_t Hkv, int64_t Smax,
+                            int64_t D, float scale, void *out, void *stream);
+
+/* Thread-local message of the last failure ("" if none). */
+GTB_API const char *gtb_last_error(void);
+GTB_API void gtb_clear_error(void);
+
+/* Synchronises the current device and returns (then clears) its kernel status word: 0 = fine,
+ * otherwise a code that a kernel wrote when one of its bounded waits ran out. */
+GTB_API int gtb_device_status(void);
+
+/* Build-time facts: number of sm_100a kernels compiled in, and a version string. */
+GTB_API const char *gtb_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GTB_ATTN_H */

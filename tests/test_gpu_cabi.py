@@ -1,0 +1,87 @@
+"""The reference-shaped handle ABI (include/gguf_train_attn.h) driven through ctypes exactly as the
+reference's gguf_train/_C.py binds gt_flash_attention (:471-472), on CUDA tensors."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+from tests._util import assert_close, seeded
+
+pytestmark = pytest.mark.gpu
+
+
+def _h(x, dtype):
+    from gguf_train_b200 import _C
+    from gguf_train_b200.handles import Handle
+
+    if dtype == "bf16":
+        return Handle.from_numpy(O.to_bits(x, O.BF16), _C.GT_BF16)
+    return Handle.from_numpy(x.astype(np.float32))
+
+
+def _back(h, dtype):
+    a = h.to_numpy()
+    return O.from_bits(a, O.BF16) if dtype == "bf16" else a.astype(np.float64)
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_handle_forward_backward(dtype):
+    from gguf_train_b200 import handles as H
+
+    O.manual_seed(21)
+    B, Hq, Hkv, L, D = 1, 4, 2, 150, 128
+    s = 0.5 if dtype == "bf16" else 1.0
+    q, k, v = seeded((B, Hq, L, D), dtype, s), seeded((B, Hkv, L, D), dtype, s), seeded((B, Hkv, L, D), dtype, s)
+    g = seeded((B, Hq, L, D), dtype)
+    hq, hk, hv, hg = _h(q, dtype), _h(k, dtype), _h(v, dtype), _h(g, dtype)
+    tol = (2e-2, 1e-2) if dtype == "bf16" else (1e-4, 1e-4)
+    out = H.flash_attention(hq, hk, hv, None, 0.0, True)
+    assert_close(_back(out, dtype), O.sdpa_fwd(q, k, v, is_causal=True), *tol, "gt_flash_attention")
+    out2, lse = H.flash_attention_fwd_lse(hq, hk, hv, None, 0.0, True)
+    assert lse.shape == (B, Hq, L)
+    dq, dk, dv = H.flash_attention_backward(hg, hq, hk, hv, None, out2, lse, 0.0, True)
+    wq, wk, wv = O.sdpa_bwd(q, k, v, g, is_causal=True)
+    for name, got, want in (("dq", dq, wq), ("dk", dk, wk), ("dv", dv, wv)):
+        assert_close(_back(got, dtype), want, *(tol if dtype == "bf16" else (1e-3, 1e-3)), name)
+
+
+def test_handle_errors_match_the_reference():
+    from gguf_train_b200 import _C
+    from gguf_train_b200 import handles as H
+
+    q = H.Handle.from_numpy(np.zeros((2, 3, 4, 6), np.float32))
+    k = H.Handle.from_numpy(np.zeros((2, 3, 5, 6), np.float32))
+    for shape in ((2, 3), (5, 1, 1, 1), (4, 6)):
+        m = H.Handle.from_numpy(np.ones(shape, np.bool_))
+        with pytest.raises(RuntimeError, match="cannot be broadcast"):
+            H.flash_attention(q, k, k, m)
+    k2 = H.Handle.from_numpy(np.zeros((2, 2, 5, 6), np.float32))
+    with pytest.raises(RuntimeError, match="num_heads must be divisible by num_kv_heads"):
+        H.flash_attention(q, k2, k2)
+    qc = H.Handle.from_numpy(np.zeros((2, 3, 4, 6), np.float32), device=_C.GT_DEV_CPU)
+    with pytest.raises(RuntimeError, match="CUDA tensors only"):
+        H.flash_attention(qc, qc, qc)
+
+
+def test_handle_quantize_and_decode():
+    from gguf_train_b200 import _C
+    from gguf_train_b200 import handles as H
+
+    O.manual_seed(22)
+    B, Hq, Hkv, S, D = 2, 8, 2, 600, 128
+    kf = O.randn(B, Hkv, S, D).astype(np.float32)
+    vf = O.randn(B, Hkv, S, D).astype(np.float32)
+    hk = H.quantize(H.Handle.from_numpy(kf))
+    hv = H.quantize(H.Handle.from_numpy(vf))
+    assert hk.dtype == _C.GT_Q8_0 and hk.shape == (B, Hkv, S, D)
+    assert np.array_equal(hk.to_numpy(), O.q8_0_quantize(kf))
+    back = H.dequantize(hk, _C.GT_F32).to_numpy()
+    assert np.array_equal(back, O.q8_0_dequantize(O.q8_0_quantize(kf), kf.shape))
+    q = seeded((B, Hq, 1, D), "f16")
+    hq = H.Handle.from_numpy(q.astype(np.float16))
+    lens = np.array([600, 257], np.int32)
+    out = H.flash_decode_q8_0(hq, hk, hv, H.Handle.from_numpy(lens))
+    want = O.decode_q8_0(q, O.q8_0_quantize(kf), O.q8_0_quantize(vf), lens, Hkv, S)
+    assert_close(out.to_numpy().astype(np.float64), want, 2e-2, 1e-2, "gt_flash_decode_q8_0")

@@ -1,0 +1,92 @@
+"""GPU parity of the Q8_0 codec (bit-exact) and of the Q8_0-cache decode step against the oracle."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+from tests._util import assert_close, seeded, to_dev
+
+pytestmark = pytest.mark.gpu
+
+
+def test_quantize_is_bit_exact_with_ggml():
+    import torch
+
+    import gguf_train_b200 as gtb
+    from gguf_train_b200 import _C
+
+    O.manual_seed(3)
+    x = (O.randn(64, 256) * 3.0).astype(np.float32)
+    x[0, :32] = 0.0                       # an all-zero block: d = 0, id = 0
+    x[1, :32] = np.linspace(-1, 1, 32)    # exact halves after scaling
+    x[2, 5] = 1e-30                       # subnormal-range scale
+    x[3, :32] = 65504.0 * 127             # scale above the fp16 range -> inf
+    want = O.q8_0_quantize(x)
+    got = gtb.quantize_q8_0(torch.tensor(x).cuda())
+    assert _C.device_status() == 0
+    assert np.array_equal(got.cpu().numpy().reshape(-1), want)
+    # bf16 / f16 inputs quantise their (exactly representable) values the same way
+    xb = O.round_to(x.astype(np.float64), O.BF16).astype(np.float32)
+    gotb = gtb.quantize_q8_0(torch.tensor(xb).cuda().to(torch.bfloat16))
+    assert np.array_equal(gotb.cpu().numpy().reshape(-1), O.q8_0_quantize(xb))
+
+
+def test_dequantize_round_trip():
+    import torch
+
+    import gguf_train_b200 as gtb
+
+    O.manual_seed(4)
+    x = O.randn(8, 128).astype(np.float32)
+    blocks = O.q8_0_quantize(x)
+    dev = torch.tensor(blocks.reshape(8, 136)).cuda()
+    got = gtb.dequantize_q8_0(dev, torch.float32).cpu().numpy()
+    assert np.array_equal(got, O.q8_0_dequantize(blocks, (8, 128)))
+    cos = float((got * x).sum() / np.sqrt((got * got).sum() * (x * x).sum()))
+    assert cos > 0.999  # the reference's own check is cosine > 0.85 (test_gguf_and_llama.py:66-79)
+
+
+def _decode_case(B, H, Hkv, Smax, D, lens, qdtype="f16", seed=5):
+    import torch
+
+    import gguf_train_b200 as gtb
+    from gguf_train_b200 import _C
+
+    O.manual_seed(seed)
+    q = seeded((B, H, 1, D), qdtype)
+    kf = O.randn(B, Hkv, Smax, D).astype(np.float32)
+    vf = O.randn(B, Hkv, Smax, D).astype(np.float32)
+    kq = O.q8_0_quantize(kf)
+    vq = O.q8_0_quantize(vf)
+    want = O.decode_q8_0(q, kq, vq, np.asarray(lens, np.int32), Hkv, Smax)
+    row = D // 32 * 34
+    tk = torch.tensor(kq.reshape(B, Hkv, Smax, row)).cuda()
+    tv = torch.tensor(vq.reshape(B, Hkv, Smax, row)).cuda()
+    got = gtb.decode_q8_0(to_dev(q, qdtype), tk, tv, torch.tensor(lens, dtype=torch.int32).cuda())
+    assert _C.device_status() == 0
+    assert_close(got, want, 2e-2, 1e-2, f"decode B={B} H={H} Hkv={Hkv} Smax={Smax} D={D} lens={lens}")
+    return got
+
+
+@pytest.mark.parametrize("B,H,Hkv,Smax,D,lens", [
+    (3, 8, 2, 300, 128, [1, 150, 300]),        # one chunk per sequence
+    (2, 32, 8, 2500, 128, [2500, 1029]),       # several chunks: split-KV + combine
+    (2, 4, 4, 64, 64, [64, 33]),               # D = 64, group of 1
+    (1, 6, 2, 100, 128, [77]),                 # group of 3
+    (2, 8, 1, 200, 256, [200, 5]),             # D = 256, group of 8 (split in two)
+    (2, 4, 2, 301, 128, [301, 300]),           # odd Smax: word-wise staging instead of bulk copies
+])
+def test_decode_matches_oracle(B, H, Hkv, Smax, D, lens):
+    _decode_case(B, H, Hkv, Smax, D, lens)
+
+
+def test_decode_bf16_and_f32_queries():
+    _decode_case(2, 8, 2, 700, 128, [700, 513], qdtype="bf16")
+    _decode_case(2, 8, 2, 700, 128, [1, 699], qdtype="f32")
+
+
+def test_decode_empty_sequence_gives_zero():
+    got = _decode_case(2, 4, 2, 1100, 128, [0, 1100])
+    assert float(got[0].abs().max()) == 0.0

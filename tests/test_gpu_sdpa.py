@@ -1,0 +1,210 @@
+"""GPU parity of the attention forward and backward against the CPU oracle.
+
+The oracle restates gt_flash_attention (reference csrc/gt_ops_nn.cpp:2423-2525) and
+FlashAttentionFn.backward (gguf_train/_functions.py:1934-1965) in float64. Tolerances: the
+north-star's 1e-3 for fp32 (these kernels reach ~1e-6), 2e-2 abs / 1e-2 rel for bf16/fp16,
+1e-10 for f64. Inputs come from the reference's generator (mt19937_64 + normal, seed fixed).
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+from tests._util import assert_close, seeded, to_dev
+
+pytestmark = pytest.mark.gpu
+
+TOL = {"f32": (1e-4, 1e-4), "f64": (1e-10, 1e-10), "bf16": (2e-2, 1e-2), "f16": (2e-2, 1e-2)}
+
+
+def _mask(kind, B, H, L, S, seed):
+    """bool: (B,1,L,S), True = may attend, key 0 always allowed; float: (1,1,L,S) additive with
+    -inf at ~10% of positions, key 0 finite."""
+    if kind is None:
+        return None, None
+    O.manual_seed(seed)
+    if kind == "bool":
+        m = O.rand(B, 1, L, S) < 0.7
+        m[..., 0] = True
+        return m.astype(np.float64), True
+    m = O.randn(1, 1, L, S) * 0.5
+    drop = O.rand(1, 1, L, S) < 0.1
+    drop[..., 0] = False
+    m[drop] = -np.inf
+    return m, False
+
+
+def _mask_dev(m, is_bool, dtype):
+    import torch
+
+    if m is None:
+        return None
+    if is_bool:
+        return torch.tensor(m != 0).cuda()
+    return to_dev(m, dtype)
+
+
+FWD_CASES = [
+    # dtype, B, H, Hkv, L, S, D, Dv, causal, mask
+    ("f32", 2, 4, 4, 128, 128, 64, 64, True, None),      # config 1 shape
+    ("f32", 2, 3, 3, 4, 5, 6, 6, False, "bool"),        # reference test shape (test_pooling_and_attention.py:349)
+    ("f32", 2, 3, 3, 4, 5, 6, 6, False, "float"),
+    ("f64", 1, 2, 2, 4, 4, 8, 8, True, None),           # gradcheck shape (test_autograd.py:136)
+    ("bf16", 1, 4, 2, 300, 300, 128, 128, True, None),  # tcgen05 path, ragged last tile, GQA
+    ("bf16", 2, 4, 1, 200, 333, 128, 128, False, None), # tcgen05 path, L != S
+    ("bf16", 1, 2, 2, 257, 130, 128, 128, True, None),  # causal with L > S (top-left)
+    ("bf16", 1, 2, 2, 100, 700, 128, 128, True, None),  # causal with L < S
+    ("f16", 1, 4, 4, 256, 256, 64, 64, True, None),     # tcgen05 path, D = 64, fp16
+    ("f16", 2, 2, 1, 64, 1000, 64, 64, False, None),
+    ("bf16", 1, 4, 2, 128, 128, 128, 128, False, "float"),  # mask -> SIMT
+    ("bf16", 1, 2, 2, 64, 64, 96, 96, True, None),      # D = 96 -> SIMT
+    ("f32", 1, 2, 2, 1, 1, 8, 8, True, None),
+    ("f32", 1, 2, 2, 3, 0, 8, 8, False, None),          # no keys: output 0
+    ("bf16", 1, 1, 1, 1, 1, 128, 128, True, None),
+]
+
+
+@pytest.mark.parametrize("dtype,B,H,Hkv,L,S,D,Dv,causal,mask", FWD_CASES)
+def test_forward_matches_oracle(dtype, B, H, Hkv, L, S, D, Dv, causal, mask):
+    import gguf_train_b200 as gtb
+    from gguf_train_b200 import _C
+
+    O.manual_seed(1000 + L + S + D)
+    sc = 0.5 if dtype in ("bf16", "f16") else 1.0
+    q = seeded((B, H, L, D), dtype, sc)
+    k = seeded((B, Hkv, S, D), dtype, sc)
+    v = seeded((B, Hkv, S, Dv), dtype, sc)
+    m, mb = _mask(mask, B, H, L, S, 7)
+    if m is not None and not mb:
+        m = O.round_to(m, {"f32": O.F32, "f64": O.F64, "bf16": O.BF16, "f16": O.F16}[dtype])
+    want = O.sdpa_fwd(q, k, v, m, mb, scale=0.0, is_causal=causal)
+    got = gtb.scaled_dot_product_attention(to_dev(q, dtype), to_dev(k, dtype), to_dev(v, dtype),
+                                           attn_mask=_mask_dev(m, mb, dtype), is_causal=causal)
+    assert _C.device_status() == 0
+    atol, rtol = TOL[dtype]
+    assert_close(got, want, atol, rtol, f"forward {dtype} {(B, H, Hkv, L, S, D)} causal={causal} mask={mask}")
+
+
+BWD_CASES = [
+    ("f32", 2, 4, 4, 128, 128, 64, 64, True, None),     # config 1: fwd+bwd, tol 1e-3 required
+    ("f32", 2, 3, 3, 4, 5, 6, 6, False, "bool"),
+    ("f32", 1, 4, 2, 33, 47, 16, 24, False, "float"),
+    ("f64", 1, 2, 2, 4, 4, 8, 8, True, None),
+    ("bf16", 1, 4, 2, 200, 200, 128, 128, True, None),
+    ("f16", 1, 2, 2, 130, 70, 64, 64, False, None),
+]
+
+
+@pytest.mark.parametrize("dtype,B,H,Hkv,L,S,D,Dv,causal,mask", BWD_CASES)
+def test_backward_matches_oracle(dtype, B, H, Hkv, L, S, D, Dv, causal, mask):
+    import gguf_train_b200 as gtb
+    from gguf_train_b200 import _C
+
+    O.manual_seed(2000 + L + S + D)
+    sc = 0.5 if dtype in ("bf16", "f16") else 1.0
+    q = seeded((B, H, L, D), dtype, sc)
+    k = seeded((B, Hkv, S, D), dtype, sc)
+    v = seeded((B, Hkv, S, Dv), dtype, sc)
+    g = seeded((B, H, L, Dv), dtype)
+    m, mb = _mask(mask, B, H, L, S, 9)
+    dq, dk, dv = O.sdpa_bwd(q, k, v, g, m, mb, is_causal=causal)
+    tq, tk, tv = (to_dev(x, dtype, True) for x in (q, k, v))
+    out = gtb.scaled_dot_product_attention(tq, tk, tv, attn_mask=_mask_dev(m, mb, dtype), is_causal=causal)
+    out.backward(to_dev(g, dtype))
+    assert _C.device_status() == 0
+    atol, rtol = TOL[dtype]
+    if dtype == "f32":
+        atol, rtol = 1e-3, 1e-3
+    label = f"{dtype} {(B, H, Hkv, L, S, D, Dv)} causal={causal} mask={mask}"
+    assert_close(tq.grad, dq, atol, rtol, "dq " + label)
+    assert_close(tk.grad, dk, atol, rtol, "dk " + label)
+    assert_close(tv.grad, dv, atol, rtol, "dv " + label)
+
+
+def test_strided_views_give_the_same_result():
+    """SDPA on strided views equals SDPA on fresh tensors (reference
+    tests/test_views_and_fast_paths.py:334-336): the (B, L, H, D) -> (B, H, L, D) transpose of MHA."""
+    import torch
+
+    import gguf_train_b200 as gtb
+
+    O.manual_seed(5)
+    B, L, H, D = 2, 160, 4, 128
+    base = to_dev(seeded((B, L, 3, H, D), "bf16", 0.5), "bf16")
+    q, k, v = (base[:, :, i].transpose(1, 2) for i in range(3))
+    got = gtb.scaled_dot_product_attention(q, k, v, is_causal=True)
+    want = gtb.scaled_dot_product_attention(q.contiguous(), k.contiguous(), v.contiguous(), is_causal=True)
+    assert torch.equal(got, want)
+
+
+def test_mask_shape_errors():
+    """tests/test_pooling_and_attention.py:375-386: bad masks raise 'cannot be broadcast', both via F
+    and via FlashAttentionFn.apply directly."""
+    import torch
+
+    import gguf_train_b200 as gtb
+
+    q = torch.randn(2, 3, 4, 6, device="cuda")
+    k = torch.randn(2, 3, 5, 6, device="cuda")
+    v = torch.randn(2, 3, 5, 6, device="cuda")
+    for shape in ((2, 3), (4, 6), (7, 4, 5), (2, 3, 4, 5, 1)):
+        with pytest.raises(RuntimeError, match="cannot be broadcast"):
+            gtb.scaled_dot_product_attention(q, k, v, attn_mask=torch.ones(*shape, dtype=torch.bool, device="cuda"))
+    for shape in ((2, 3), (5,), (2, 4, 5)):
+        with pytest.raises(RuntimeError, match="cannot be broadcast"):
+            gtb.FlashAttentionFn.apply(q, k, v, torch.ones(*shape, dtype=torch.bool, device="cuda"), 0.4, False)
+    with pytest.raises(RuntimeError, match="num_heads must be divisible by num_kv_heads"):
+        gtb.scaled_dot_product_attention(q, k[:, :2], v[:, :2])
+    with pytest.raises(RuntimeError, match="CUDA tensors only"):
+        gtb.scaled_dot_product_attention(q.cpu(), k.cpu(), v.cpu())
+
+
+def test_masks_broadcast_from_the_right():
+    """tests/test_pooling_and_attention.py:364-373: every right-aligned broadcast of a bool mask
+    and its -1e9 additive twin give the composite's answer."""
+    import torch
+
+    import gguf_train_b200 as gtb
+
+    O.manual_seed(6)
+    q, k, v = seeded((2, 3, 4, 6)), seeded((2, 3, 5, 6)), seeded((2, 3, 5, 6))
+    base = O.rand(2, 3, 4, 5) < 0.6
+    base[..., 0] = True
+    tq, tk, tv = to_dev(q, "f32"), to_dev(k, "f32"), to_dev(v, "f32")
+    for mask in (base, base[:, :1], base[:1], base[0], base[0, 0], base[0, 0, :1], base[..., :1, :]):
+        m4 = mask.reshape((1,) * (4 - mask.ndim) + mask.shape)
+        want = O.sdpa_fwd(q, k, v, np.broadcast_to(m4, (2, 3, 4, 5)).astype(np.float64), True)
+        got = gtb.scaled_dot_product_attention(tq, tk, tv, attn_mask=torch.tensor(mask).cuda())
+        assert_close(got, want, 1e-5, 1e-5, f"bool mask {mask.shape}")
+        additive = torch.zeros(mask.shape).masked_fill(~torch.tensor(mask), -1e9).cuda()
+        got = gtb.scaled_dot_product_attention(tq, tk, tv, attn_mask=additive)
+        assert_close(got, want, 1e-5, 1e-5, f"additive mask {mask.shape}")
+
+
+def test_fully_masked_row_gives_zero_output():
+    """A row with no allowed key outputs 0 (gt_ops_nn.cpp:2509: inv = 0 when the sum is 0)."""
+    import torch
+
+    import gguf_train_b200 as gtb
+
+    q = torch.randn(1, 2, 4, 8, device="cuda")
+    k = torch.randn(1, 2, 6, 8, device="cuda")
+    v = torch.randn(1, 2, 6, 8, device="cuda")
+    mask = torch.ones(4, 6, dtype=torch.bool, device="cuda")
+    mask[2] = False
+    out = gtb.scaled_dot_product_attention(q, k, v, attn_mask=mask)
+    assert torch.all(out[:, :, 2] == 0)
+    assert torch.all(out[:, :, 1].abs().sum(-1) > 0)
+
+
+def test_gradcheck_float64_causal():
+    """tests/test_autograd.py:136-140: finite-difference gradcheck of causal SDPA in float64."""
+    import torch
+
+    import gguf_train_b200 as gtb
+
+    O.manual_seed(11)
+    q, k, v = (to_dev(seeded((1, 2, 4, 8), "f64"), "f64", True) for _ in range(3))
+    assert torch.autograd.gradcheck(lambda a, b, c: gtb.scaled_dot_product_attention(a, b, c, is_causal=True), (q, k, v))
