@@ -1,0 +1,330 @@
+"""Benchmark of the B200 attention engine: causal GQA prefill.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+Workload (one "step"): one causal GQA attention forward over a batch of B=8 sequences,
+Hq=32, Hkv=8, L=S=4096, D=128, bf16, inputs N(0,1)*0.5 (seeded, generated on the device),
+scale 1/sqrt(128). Work per step: 4*B*Hq*(L(L+1)/2)*D = 1.0998e12 FLOP.
+
+Multi-GPU: one process per GPU (torchrun); batch x kv-head units are independent, so each rank
+runs its own full batch with no collective on the data path (weak scaling: per-GPU work fixed).
+The process group is used only for barriers and the max-over-ranks of the timed region.
+
+Reported on one JSON line by rank 0:
+  value        whole-job TFLOP/s with inputs resident in HBM (CUDA events on the launching
+               stream, K steps between barriers + synchronize, max over ranks);
+  e2e          the same through the public API (gguf_train_b200.scaled_dot_product_attention)
+               with the inputs copied from pinned host memory and the output copied back inside
+               every timed step;
+  roofline     the tcgen05 forward kernel against the measured bf16 dense peak;
+  cpu_baseline the reference's CPU forward (restated loop, float64, OpenMP on every host
+               core) on a bounded sample of the same workload, rank 0 at N=1 only;
+  clocks       SM clocks and throttle reasons sampled through NVML during the timed region.
+`--impl reference` times that CPU forward alone (rank 0; other ranks exit at once).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import re
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+METRIC = "SDPA TFLOP/s (fwd, fwd+bwd) & decode KV GB/s, % of B200 peak, 1/2/4/8 GPUs"
+CFG = dict(B=8, H=32, Hkv=8, L=4096, D=128)
+WORKLOAD = "config 3: causal GQA prefill forward, bf16, B=8 Hq=32 Hkv=8 L=S=4096 D=128"
+FALLBACK_PEAKS = {"bf16_tflops": 1590.0, "hbm_gbs": 6650.0}
+
+
+def fwd_flops(B, H, L, D, causal=True):
+    pairs = L * (L + 1) / 2 if causal else L * L
+    return 4.0 * B * H * pairs * D
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return {"bf16_tflops": float(p["bf16_tflops"]), "hbm_gbs": float(p["hbm_gbs"]), "source": "measured"}
+    except Exception:
+        return dict(FALLBACK_PEAKS, source="fallback")
+
+
+def profile_traffic(name: str):
+    """DRAM bytes per launch recorded in the committed ncu summary profiles/<name>.md
+    (a line 'traffic_bytes_per_launch: N'), or None."""
+    path = os.path.join(ROOT, "profiles", name + ".md")
+    try:
+        with open(path) as f:
+            m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", f.read())
+        return float(m.group(1)) if m else None
+    except OSError:
+        return None
+
+
+# ------------------------------------------------------------------ CPU baseline (reference arm)
+
+def cpu_sample(reps: int = 1, rows: int = 256):
+    """The reference's CPU forward (gt_flash_attention's loop in float64 with OpenMP over heads,
+    restated in oracle/) on a bounded sample of the workload: one unit per host thread, a unit
+    being the last `rows` query rows of one (batch, head) against all their keys (causal).
+    Returns (TFLOP/s, threads, description)."""
+    import numpy as np
+
+    from oracle import oracle as O
+
+    threads = O.num_threads()
+    L, D, H = CFG["L"], CFG["D"], threads
+    rng = np.random.default_rng(0)
+    q = rng.standard_normal((1, H, rows, D)) * 0.5
+    k = rng.standard_normal((1, 1, L, D)) * 0.5
+    v = rng.standard_normal((1, 1, L, D)) * 0.5
+    out = np.zeros((1, H, rows, D))
+    off = L - rows
+    flops = 4.0 * H * D * sum(l + 1 for l in range(off, L))
+    O.sdpa_fwd_reforder(q[:, :1, :8], k, v, 1.0 / math.sqrt(D), True, threads, off + rows - 8)  # warm the pages
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        O.sdpa_fwd_reforder(q, k, v, 1.0 / math.sqrt(D), True, threads, off, out)
+    dt = (time.perf_counter() - t0) / reps
+    desc = (f"{threads} units per step, each the last {rows} query rows of one (batch, head) of the workload "
+            f"against all their keys (L=4096, D=128, causal), float64, one unit per OpenMP thread")
+    return flops / dt / 1e12, threads, desc
+
+
+def run_reference(args, rank: int) -> None:
+    if rank != 0:
+        return
+    vals, times = [], []
+    for i in range(args.warmup + args.steps):
+        t0 = time.perf_counter()
+        v, threads, desc = cpu_sample(1)
+        if i >= args.warmup:
+            vals.append(v)
+            times.append((time.perf_counter() - t0) * 1e3)
+    value = statistics.mean(vals)
+    cfg = {"workload": WORKLOAD, "global_batch": CFG["B"] * args.gpus, "seq_len": CFG["L"],
+           "parallelism": f"replicas x{args.gpus}", "kernel": "reference CPU loop (restated, not ggml)"}
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": statistics.mean(times), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic (seeded normal)",
+        "config": cfg,
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": "port", "sample": desc},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------ clocks
+
+class ClockSampler:
+    """Samples SM clock and clock-event (throttle) reasons of one GPU through NVML (read-only)."""
+
+    REASONS = {
+        0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+        0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+        0x100: "display_clock_setting",
+    }
+
+    def __init__(self, index: int):
+        self.samples, self.reasons, self._stop = [], 0, threading.Event()
+        self.max_mhz = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self._nv = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self.samples.append(self._nv.nvmlDeviceGetClockInfo(self._h, self._nv.NVML_CLOCK_SM))
+                self.reasons |= self._nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+            except Exception:
+                pass
+            time.sleep(0.01)
+
+    def __enter__(self):
+        if self._nv:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *exc):
+        if self._nv:
+            self._stop.set()
+            self._t.join()
+
+    def summary(self):
+        if not self._nv or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["nvml unavailable"]}
+        names = [n for bit, n in self.REASONS.items() if self.reasons & bit and n != "gpu_idle"]
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz, "reasons": names,
+                "samples": len(self.samples)}
+
+
+# ------------------------------------------------------------------ GPU arm
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--e2e-steps", type=int, default=None)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    import gguf_train_b200 as gtb
+    from gguf_train_b200 import _C
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    B, H, Hkv, L, D = CFG["B"], CFG["H"], CFG["Hkv"], CFG["L"], CFG["D"]
+    g = torch.Generator(device=dev)
+    g.manual_seed(1234 + rank)
+    q = (torch.randn((B, H, L, D), generator=g, device=dev) * 0.5).to(torch.bfloat16)
+    k = (torch.randn((B, Hkv, L, D), generator=g, device=dev) * 0.5).to(torch.bfloat16)
+    v = (torch.randn((B, Hkv, L, D), generator=g, device=dev) * 0.5).to(torch.bfloat16)
+    scale = 1.0 / math.sqrt(D)
+    flops = fwd_flops(B, H, L, D)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        out, _ = gtb.functional.sdpa_forward(q, k, v, None, scale, True, need_lse=False)
+        return out
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize(dev)
+    assert _C.device_status() == 0, "a kernel reported a wait timeout during warm-up"
+
+    # ---- kernel-resident timing: K launches, one event pair per launch
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    sampler = ClockSampler(torch.cuda.current_device())
+    barrier()
+    torch.cuda.synchronize(dev)
+    with sampler:
+        t_all0 = torch.cuda.Event(enable_timing=True)
+        t_all1 = torch.cuda.Event(enable_timing=True)
+        t_all0.record(stream)
+        for i in range(args.steps):
+            starts[i].record(stream)
+            step()
+            ends[i].record(stream)
+        t_all1.record(stream)
+        torch.cuda.synchronize(dev)
+    barrier()
+    total_ms = max_over_ranks(t_all0.elapsed_time(t_all1))
+    launch_ms = statistics.mean(s.elapsed_time(e) for s, e in zip(starts, ends))
+    launch_ms = max_over_ranks(launch_ms)
+    status = _C.device_status()
+    ms_per_step = total_ms / args.steps
+    value = flops * world / (ms_per_step * 1e-3) / 1e12
+
+    # ---- end to end through the public API with host buffers
+    e2e_steps = args.e2e_steps or max(3, min(args.steps, 10))
+    qh = q.cpu().pin_memory()
+    kh = k.cpu().pin_memory()
+    vh = v.cpu().pin_memory()
+    oh = torch.empty((B, H, L, D), dtype=torch.bfloat16).pin_memory()
+    qd, kd, vd = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+
+    def e2e_step():
+        qd.copy_(qh, non_blocking=True)
+        kd.copy_(kh, non_blocking=True)
+        vd.copy_(vh, non_blocking=True)
+        out = gtb.scaled_dot_product_attention(qd, kd, vd, is_causal=True, scale=scale)
+        oh.copy_(out, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    barrier()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1)) / e2e_steps
+    h2d = qh.numel() * 2 + kh.numel() * 2 + vh.numel() * 2
+    d2h = oh.numel() * 2
+    status |= _C.device_status()
+
+    peaks = load_peaks()
+    achieved = flops / (launch_ms * 1e-3) / 1e12
+    traffic = profile_traffic("fwd_sm100_config3")
+    line = {
+        "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+        "warmup": max(args.warmup, 3), "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic: seeded N(0,1)*0.5 generated on the device (the configuration's shapes and distribution)",
+        "config": {"workload": WORKLOAD, "global_batch": B * world, "seq_len": L, "heads": H, "kv_heads": Hkv,
+                   "head_dim": D, "parallelism": f"batch x kv-head units, {world} replica(s), no collective",
+                   "l2": "inputs larger than L2 (q+k+v = 402 MB per GPU)", "kernel": "fwd_sm100 (tcgen05/TMA)"},
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                     "frac": achieved / peaks["bf16_tflops"],
+                     "traffic": traffic, "peak_source": peaks["source"] + " bf16 dense (burst)",
+                     "flops_per_launch": flops, "launch_ms": launch_ms},
+        "e2e": {"value": flops * world / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "api": "gguf_train_b200.scaled_dot_product_attention, pinned host buffers"},
+        "gpu_launches": args.steps,
+        "clocks": sampler.summary(),
+        "status": status,
+    }
+    if world == 1 and rank == 0 and not args.no_cpu_baseline:
+        cv, threads, desc = cpu_sample(2)
+        line["cpu_baseline"] = {"value": cv, "unit": "TFLOP/s", "cores": threads, "kind": "port", "sample": desc}
+    if world > 1:
+        barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -10,7 +10,9 @@
 //   warps 2..5  softmax, one query row per thread (TMEM lane = row): read S_j from TMEM, mask,
 //               online softmax in the log2 domain with lazy rescaling (O and the running sum are
 //               rescaled only when the row maximum grows by more than 2^8), write P_j (bf16/f16)
-//               back to TMEM or to shared memory, and at the end normalise O and store it.
+//               back into the TMEM columns of S_j (the A operand of the PV MMA), and at the end
+//               normalise O and store it. A fixed share of the exponentials is computed with a
+//               polynomial on the FMA pipe instead of the MUFU unit (exp2_poly).
 // TMEM: S0 = columns [0,128), S1 = [128,256), O = [256, 256+D); 512 columns allocated.
 //
 // Semantics are those of gt_flash_attention (reference csrc/gt_ops_nn.cpp:2423-2525): causal is
@@ -43,22 +45,39 @@ constexpr uint32_t TMEM_COLS = 512;
 constexpr uint32_t S_COL0 = 0;
 constexpr uint32_t O_COL = 256;
 
-template <int D, bool P_TMEM>
+template <int D>
 struct Cfg {
     static constexpr int ATOMS = D / 64;                  // 128-byte swizzle atoms along D
     static constexpr int TILE = BM * D * 2;               // bytes of a 128-row Q, K or V tile
     static constexpr int ATOM_BYTES = BM * 128;           // 16 KB: one 64-column slab of a tile
     static constexpr int KS = 2;                          // K stages
     static constexpr int VS = 2;                          // V stages
-    static constexpr int P_TILE = BM * BN * 2;            // P tile in shared memory (if used)
     static constexpr int OFF_Q = 0;
     static constexpr int OFF_K = OFF_Q + TILE;
     static constexpr int OFF_V = OFF_K + KS * TILE;
-    static constexpr int OFF_P = OFF_V + VS * TILE;
-    static constexpr int OFF_BAR = OFF_P + (P_TMEM ? 0 : 2 * P_TILE);
+    static constexpr int OFF_BAR = OFF_V + VS * TILE;
     static constexpr int NBAR = 1 + 2 * KS + 2 * VS + 2 + 2 + 3;
     static constexpr int SMEM = OFF_BAR + NBAR * 8 + 16 + 1024;  // + TMEM slot, + alignment slack
 };
+
+// 2^x on the FMA/ALU pipes, to take part of the softmax's exponentials off the MUFU unit.
+// Range reduction x = n + f with n = round(x) (adding 1.5 * 2^23 rounds to an integer held in
+// the low mantissa bits) and f in [-1/2, 1/2]; 2^f from a cubic fitted for this kernel (minimax in
+// relative error on [-1/2, 1/2], max error 7.5e-5, far below the 2^-9 of the bf16 P it feeds);
+// 2^n is added to the exponent field. x is clamped below at -126 so the exponent cannot wrap.
+__device__ __forceinline__ float exp2_poly(float x) {
+    constexpr float C0 = 0.9999280571937561f, C1 = 0.6932609677314758f;
+    constexpr float C2 = 0.2426111400127411f, C3 = 0.0551716573536396f;
+    constexpr float SHIFT = 12582912.0f;  // 1.5 * 2^23
+    x = fmaxf(x, -126.0f);
+    const float t = x + SHIFT;
+    const int n = __float_as_int(t) - 0x4B400000;
+    const float f = x - (t - SHIFT);
+    float q = fmaf(C3, f, C2);
+    q = fmaf(q, f, C1);
+    q = fmaf(q, f, C0);
+    return __int_as_float(__float_as_int(q) + (n << 23));
+}
 
 // two floats -> one 32-bit word of two 16-bit values (lo in the low half), round to nearest even
 template <bool BF16>
@@ -87,11 +106,12 @@ struct Params {
     int* status;
 };
 
-template <int D, bool BF16, bool P_TMEM>
+// EMU: how many of every 8 exponentials of a row are computed by exp2_poly instead of MUFU.
+template <int D, bool BF16, int EMU>
 __global__ void __launch_bounds__(NTHREADS, 1)
 fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                  const __grid_constant__ CUtensorMap tmV, const Params p) {
-    using C = Cfg<D, P_TMEM>;
+    using C = Cfg<D>;
     using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
     extern __shared__ unsigned char smem_raw[];
     unsigned char* smem = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -209,13 +229,8 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
                 for (int kk = 0; kk < BN / 16; ++kk) {
                     const uint64_t bdesc = desc_sw128(v_addr + kk * 2048, C::ATOM_BYTES, 1024);
                     const uint32_t acc = (j > 0 || kk > 0) ? 1u : 0u;
-                    if constexpr (P_TMEM) {
-                        mma_ts(tmem + O_COL, tmem + S_COL0 + (uint32_t)(j & 1) * BN + kk * 8, bdesc, IDESC_PV, acc);
-                    } else {
-                        const uint32_t p_addr = smem_u32(smem + C::OFF_P + (j & 1) * C::P_TILE);
-                        const uint32_t off = (uint32_t)((kk / 4) * C::ATOM_BYTES + (kk % 4) * 32);
-                        mma_ss(tmem + O_COL, desc_sw128(p_addr + off, 16, 1024), bdesc, IDESC_PV, acc);
-                    }
+                    // A = P_j, 16-bit, packed two per TMEM column in the columns of S_j
+                    mma_ts(tmem + O_COL, tmem + S_COL0 + (uint32_t)(j & 1) * BN + kk * 8, bdesc, IDESC_PV, acc);
                 }
                 mma_commit(o_full);
                 mma_commit(&v_empty[vs]);
@@ -257,9 +272,14 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
                 for (int i = 0; i < BN; ++i)
                     if (kv0 + i > lim) x[i] = -INFINITY;
             }
-            float mx = x[0];
+            // row max: eight independent partial maxima, then a tree (no 128-long dependency chain)
+            float pm[8];
 #pragma unroll
-            for (int i = 1; i < BN; ++i) mx = fmaxf(mx, x[i]);
+            for (int u = 0; u < 8; ++u) pm[u] = x[u];
+#pragma unroll
+            for (int i = 8; i < BN; ++i) pm[i & 7] = fmaxf(pm[i & 7], x[i]);
+            const float mx = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])),
+                                   fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7])));
             const float m_new = fmaxf(m_used, mx * p.scale_log2);
             const bool rescale = m_new > m_used + 8.0f;  // false while the row has no finite score
             if (__any_sync(0xffffffffu, rescale && j > 0)) {
@@ -286,31 +306,21 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
             }
             const float neg_m = (m_used == -INFINITY) ? 0.0f : -m_used;
             uint32_t pk[BN / 2];
-            float rs = 0.0f;
+            float ps[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
             for (int i = 0; i < BN; i += 2) {
-                const float p0 = ex2(fmaf(x[i], p.scale_log2, neg_m));
-                const float p1 = ex2(fmaf(x[i + 1], p.scale_log2, neg_m));
-                rs += p0 + p1;
+                const float a0 = fmaf(x[i], p.scale_log2, neg_m);
+                const float a1 = fmaf(x[i + 1], p.scale_log2, neg_m);
+                const float p0 = (i & 7) < EMU ? exp2_poly(a0) : ex2(a0);
+                const float p1 = ((i + 1) & 7) < EMU ? exp2_poly(a1) : ex2(a1);
+                ps[i & 7] += p0;
+                ps[(i + 1) & 7] += p1;
                 pk[i / 2] = pack2<BF16>(p0, p1);
             }
-            lsum += rs;
-            if constexpr (P_TMEM) {
-                tmem_st32(s_tmem, pk);
-                tmem_st32(s_tmem + 32, pk + 32);
-                tmem_st_wait();
-            } else {
-                // row r of a K-major 128-byte-swizzled tile: 16-byte chunk c of a 128-byte row lands
-                // at chunk c ^ (r % 8); 64 columns per 16 KB slab
-                unsigned char* pbase = smem + C::OFF_P + (j & 1) * C::P_TILE;
-#pragma unroll
-                for (int c = 0; c < BN / 8; ++c) {
-                    const int slab = c / 8, cc = c % 8;
-                    uint4 v = make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
-                    *(uint4*)(pbase + slab * C::ATOM_BYTES + r * 128 + ((cc ^ (r & 7)) * 16)) = v;
-                }
-                fence_proxy_async_smem();
-            }
+            lsum += ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
+            tmem_st32(s_tmem, pk);
+            tmem_st32(s_tmem + 32, pk + 32);
+            tmem_st_wait();
             tc_fence_before();
             mbar_arrive(&p_full[j & 1]);
         }
@@ -407,10 +417,10 @@ bool make_map(CUtensorMap* tm, const gtb_tensor4& t, int64_t d_extent, bool bf16
 
 bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
 
-template <int D, bool BF16, bool P_TMEM>
+template <int D, bool BF16, int EMU>
 int run(const FwdArgs& a, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, cudaStream_t st) {
-    using C = Cfg<D, P_TMEM>;
-    auto kern = fwd_sm100_kernel<D, BF16, P_TMEM>;
+    using C = Cfg<D>;
+    auto kern = fwd_sm100_kernel<D, BF16, EMU>;
     static bool attr_set = false;  // benign race: setting the same attribute twice is harmless
     if (!attr_set) {
         if (cuda_failed(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM),
@@ -435,14 +445,24 @@ int run(const FwdArgs& a, const CUtensorMap& mq, const CUtensorMap& mk, const CU
     return cuda_failed(cudaGetLastError(), "flash_attention (sm100) launch") ? -1 : 0;
 }
 
-// P staged in TMEM (aliasing S) by default; GTB_FWD_P_SMEM=1 stages it in shared memory instead.
-bool p_in_tmem() {
+// Exponentials emulated per 8 (GTB_FWD_EMU overrides the default for tuning: 0, 2 or 3).
+int emu_setting() {
     static int v = -1;
     if (v < 0) {
-        const char* e = getenv("GTB_FWD_P_SMEM");
-        v = (e && atoi(e) == 1) ? 0 : 1;
+        const char* e = getenv("GTB_FWD_EMU");
+        v = e ? atoi(e) : 2;
+        if (v != 0 && v != 2 && v != 3) v = 2;
     }
-    return v == 1;
+    return v;
+}
+
+template <int D, bool BF16>
+int run_emu(const FwdArgs& a, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, cudaStream_t st) {
+    switch (emu_setting()) {
+        case 0: return run<D, BF16, 0>(a, mq, mk, mv, st);
+        case 3: return run<D, BF16, 3>(a, mq, mk, mv, st);
+        default: return run<D, BF16, 2>(a, mq, mk, mv, st);
+    }
 }
 
 }  // namespace
@@ -470,13 +490,8 @@ int launch_fwd_sm100(const FwdArgs& a, cudaStream_t st) {
     CUtensorMap mq, mk, mv;
     if (!make_map(&mq, a.q, a.sh.D, bf16) || !make_map(&mk, a.k, a.sh.D, bf16) || !make_map(&mv, a.v, a.sh.Dv, bf16))
         return -1;
-    const bool pt = p_in_tmem();
-    if (a.sh.D == 128) {
-        if (bf16) return pt ? run<128, true, true>(a, mq, mk, mv, st) : run<128, true, false>(a, mq, mk, mv, st);
-        return pt ? run<128, false, true>(a, mq, mk, mv, st) : run<128, false, false>(a, mq, mk, mv, st);
-    }
-    if (bf16) return pt ? run<64, true, true>(a, mq, mk, mv, st) : run<64, true, false>(a, mq, mk, mv, st);
-    return pt ? run<64, false, true>(a, mq, mk, mv, st) : run<64, false, false>(a, mq, mk, mv, st);
+    if (a.sh.D == 128) return bf16 ? run_emu<128, true>(a, mq, mk, mv, st) : run_emu<128, false>(a, mq, mk, mv, st);
+    return bf16 ? run_emu<64, true>(a, mq, mk, mv, st) : run_emu<64, false>(a, mq, mk, mv, st);
 }
 
 }  // namespace gtb

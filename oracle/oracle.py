@@ -36,7 +36,7 @@ def lib() -> ctypes.CDLL:
         L.orc_to_bits.argtypes = [P, i64, i32, P]
         L.orc_from_bits.argtypes = [P, i64, i32, P]
         L.orc_sdpa_fwd.argtypes = [P, P, P, i64, i64, i64, i64, i64, i64, i64, P, i32, P, i32, f32, i32, P, i32]
-        L.orc_sdpa_fwd_reforder.argtypes = [P, P, P, i64, i64, i64, i64, i64, i64, i64, f32, i32, P, i32]
+        L.orc_sdpa_fwd_reforder.argtypes = [P, P, P, i64, i64, i64, i64, i64, i64, i64, f32, i32, i64, P, i32]
         L.orc_sdpa_bwd.argtypes = [P, P, P, P, i64, i64, i64, i64, i64, i64, i64, P, i32, P, i32, f64, i32, P, P, P, i32]
         L.orc_q8_0_quantize.argtypes = [P, i64, P]
         L.orc_q8_0_dequantize.argtypes = [P, i64, P]
@@ -136,14 +136,17 @@ def sdpa_fwd(q, k, v, mask=None, mask_is_bool=False, scale: float = 0.0, is_caus
     return out
 
 
-def sdpa_fwd_reforder(q, k, v, scale: float = 0.0, is_causal: bool = False, nthreads: int = 0) -> np.ndarray:
-    """The same forward with the reference's literal loop order (the timed CPU baseline)."""
+def sdpa_fwd_reforder(q, k, v, scale: float = 0.0, is_causal: bool = False, nthreads: int = 0,
+                      q_offset: int = 0, out: np.ndarray | None = None) -> np.ndarray:
+    """The same forward with the reference's literal loop order (the timed CPU baseline).
+    q holds query rows q_offset.. of the sequence (causal masking uses absolute rows)."""
     q, k, v = _c64(q), _c64(k), _c64(v)
     B, H, L, D = q.shape
     _, Hkv, S, Dv = v.shape
-    out = np.zeros((B, H, L, Dv), dtype=np.float64)
+    if out is None:
+        out = np.zeros((B, H, L, Dv), dtype=np.float64)
     lib().orc_sdpa_fwd_reforder(_p(q), _p(k), _p(v), B, H, Hkv, L, S, D, Dv, float(scale),
-                                int(bool(is_causal)), _p(out), int(nthreads))
+                                int(bool(is_causal)), int(q_offset), _p(out), int(nthreads))
     return out
 
 

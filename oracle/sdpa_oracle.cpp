@@ -257,10 +257,12 @@ int orc_sdpa_fwd(const double* q, const double* k, const double* v,
 
 // Same as orc_sdpa_fwd but with the reference's literal loop order and V access pattern
 // (dv outer, s inner, V read with stride Dv: gt_ops_nn.cpp:2511-2519). Used only as the timed
-// CPU baseline so that its memory behaviour matches the reference's loop.
+// CPU baseline so that its memory behaviour matches the reference's loop. q holds query rows
+// q_offset .. q_offset+L-1 of a longer sequence (causal masking uses the absolute row index), so a
+// bounded slice of a large workload can be timed with its exact amount of work.
 int orc_sdpa_fwd_reforder(const double* q, const double* k, const double* v,
                           int64_t B, int64_t H, int64_t Hkv, int64_t L, int64_t S, int64_t D, int64_t Dv,
-                          float scale, int is_causal, double* out, int nthreads) {
+                          float scale, int is_causal, int64_t q_offset, double* out, int nthreads) {
     if (Hkv <= 0 || H % Hkv != 0) return -1;
     const int64_t group = H / Hkv;
     if (scale <= 0.0f) scale = 1.0f / std::sqrt((float)D);
@@ -274,7 +276,7 @@ int orc_sdpa_fwd_reforder(const double* q, const double* k, const double* v,
             for (int64_t l = 0; l < L; ++l) {
                 double mx = ninf;
                 for (int64_t s = 0; s < S; ++s) {
-                    if (is_causal && s > l) { sc[s] = ninf; continue; }
+                    if (is_causal && s > l + q_offset) { sc[s] = ninf; continue; }
                     double dot = 0.0;
                     const int64_t qo = ((b * H + h) * L + l) * D;
                     const int64_t ko = ((b * Hkv + hk) * S + s) * D;
