@@ -79,7 +79,7 @@ GTB_API int gtb_q8_0_dequantize(const void *blocks, int64_t n_rows, int64_t row_
  * Split-KV: each (b, kv head) is cut into chunks of up to GTB_DECODE_CHUNK rows that run in
  * parallel; a second kernel merges the partial results. The partials live in scratch taken from
  * the stream-ordered allocator. */
-#define GTB_DECODE_CHUNK 512
+#define GTB_DECODE_CHUNK 1024
 GTB_API int gtb_decode_q8_0(const void *q, int q_dtype, const void *k_q8, const void *v_q8,
                             const int32_t *seq_lens, int64_t B, int64_t H, int64_t Hkv, int64_t Smax,
                             int64_t D, float scale, void *out, void *stream);

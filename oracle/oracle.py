@@ -42,6 +42,7 @@ def lib() -> ctypes.CDLL:
         L.orc_q8_0_dequantize.argtypes = [P, i64, P]
         L.orc_decode_q8_0.argtypes = [P, P, P, P, i64, i64, i64, i64, i64, f32, P, i32]
         L.orc_num_threads.restype = i32
+        L.orc_engine_raw.argtypes = [ctypes.c_uint64, i64, P]
         _lib = L
     return _lib
 
@@ -65,6 +66,13 @@ def randn(*shape, mean: float = 0.0, std: float = 1.0) -> np.ndarray:
     """torch.randn -> gt_fill_normal (gt_core.cpp:1199-1215): float64 draws, row-major."""
     out = np.empty(shape, dtype=np.float64)
     lib().orc_fill_normal(_p(out), out.size, float(mean), float(std))
+    return out
+
+
+def engine_raw(seed: int, n: int) -> np.ndarray:
+    """The first n raw outputs of std::mt19937_64 seeded with `seed` (the reference's engine)."""
+    out = np.empty(n, dtype=np.uint64)
+    lib().orc_engine_raw(int(seed), int(n), _p(out))
     return out
 
 

@@ -137,6 +137,14 @@ int orc_fill_normal(double* out, int64_t n, double mean, double stdv) {
     return 0;
 }
 
+// Raw 64-bit outputs of the engine after seeding (for the C++ standard's known-answer check of
+// mt19937_64: the 10000th output of a default-seeded engine is 9981545732273789042).
+void orc_engine_raw(uint64_t seed, int64_t n, uint64_t* out) {
+    std::lock_guard<std::mutex> lk(g_rng_mtx);
+    std::mt19937_64 e(seed);
+    for (int64_t i = 0; i < n; ++i) out[i] = e();
+}
+
 // gt_fill_uniform, gt_core.cpp:1182-1197
 int orc_fill_uniform(double* out, int64_t n, double lo, double hi) {
     std::lock_guard<std::mutex> lk(g_rng_mtx);

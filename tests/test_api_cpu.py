@@ -1,0 +1,77 @@
+"""The Python surface (F.scaled_dot_product_attention, FlashAttentionFn, MultiheadAttention) on
+CPU: argument checks and error messages that fire before any kernel, as the reference's tests
+exercise them (tests/test_pooling_and_attention.py:303-319, :375-386)."""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+
+def test_sdpa_mask_shape_errors_before_any_device_work():
+    import gguf_train_b200 as gtb
+
+    q, k, v = torch.randn(2, 3, 4, 6), torch.randn(2, 3, 5, 6), torch.randn(2, 3, 5, 6)
+    for shape in ((2, 3), (4, 6), (7, 4, 5), (2, 3, 4, 5, 1)):
+        with pytest.raises(RuntimeError, match="cannot be broadcast"):
+            gtb.scaled_dot_product_attention(q, k, v, attn_mask=torch.ones(*shape, dtype=torch.bool))
+
+
+def test_sdpa_refuses_cpu_tensors():
+    import gguf_train_b200 as gtb
+
+    q = torch.randn(1, 2, 4, 8)
+    with pytest.raises(RuntimeError, match="CUDA tensors only"):
+        gtb.scaled_dot_product_attention(q, q, q)
+    with pytest.raises(RuntimeError, match="CUDA tensors only"):
+        gtb.FlashAttentionFn.apply(q, q, q, None, 0.4, False)
+
+
+def test_mha_argument_checks():
+    import gguf_train_b200 as gtb
+
+    m = gtb.MultiheadAttention(8, 2, batch_first=True).eval()
+    x = torch.randn(3, 4, 8)
+    cases = {
+        "2D attn_mask": dict(attn_mask=torch.zeros(4, 5)),
+        "3D attn_mask": dict(attn_mask=torch.zeros(3, 4, 4)),
+        "4D attn_mask": dict(attn_mask=torch.zeros(3, 2, 4, 4)),
+        "key_padding_mask": dict(key_padding_mask=torch.zeros(3, 5, dtype=torch.bool)),
+        "integer mask": dict(attn_mask=torch.zeros(4, 4, dtype=torch.int64)),
+    }
+    for name, kwargs in cases.items():
+        with pytest.raises(RuntimeError, match="MultiheadAttention"):
+            m(x, x, x, **kwargs)
+    with pytest.raises(RuntimeError):
+        m(x[0], x, x)
+
+
+def test_mha_parameters_follow_the_reference():
+    import gguf_train_b200 as gtb
+
+    m = gtb.MultiheadAttention(512, 8, batch_first=True)
+    assert tuple(m.in_proj_weight.shape) == (1536, 512)
+    assert float(m.in_proj_bias.detach().abs().max()) == 0.0
+    bound = (6.0 / (512 + 1536)) ** 0.5  # Xavier-uniform over the (3E, E) matrix (init.py:105-109)
+    assert float(m.in_proj_weight.detach().abs().max()) <= bound
+    assert m.head_dim == 64
+
+
+def test_mha_need_weights_path_runs_on_cpu():
+    """need_weights=True materialises the weights with matmul + softmax, as the reference does
+    (transformer.py:153-166), so it needs no attention kernel."""
+    import gguf_train_b200 as gtb
+
+    torch.manual_seed(0)
+    m = gtb.MultiheadAttention(8, 2, batch_first=True).eval()
+    x = torch.randn(2, 4, 8)
+    out, w = m(x, x, x)
+    assert out.shape == (2, 4, 8) and w.shape == (2, 4, 4)
+    assert torch.allclose(w.sum(-1), torch.ones(2, 4))
+
+
+def test_q8_0_python_checks():
+    import gguf_train_b200 as gtb
+
+    with pytest.raises(RuntimeError, match="CUDA tensors only"):
+        gtb.quantize_q8_0(torch.zeros(4, 64))
