@@ -84,6 +84,21 @@ GTB_API int gtb_decode_q8_0(const void *q, int q_dtype, const void *k_q8, const 
                             const int32_t *seq_lens, int64_t B, int64_t H, int64_t Hkv, int64_t Smax,
                             int64_t D, float scale, void *out, void *stream);
 
+/* The same decode step as gtb_decode_q8_0, for callers that cannot let the library allocate device
+ * memory: a serving runtime whose own allocator owns the GPU, or a loop that must never reach
+ * cudaMalloc/cudaFree (they synchronise the device) or grow a memory pool mid-run. It allocates
+ * nothing: the split-KV partial results go to a fixed device array of
+ * GTB_DECODE_NOALLOC_SCRATCH_BYTES that every GPU loading this library holds until the process
+ * exits. Calls needing more scratch than that, B*Hkv*ceil(Smax/GTB_DECODE_CHUNK)*(H/Hkv)*(D+2)*4
+ * bytes, are rejected with an error (config 5a, B=64 Hkv=8 H=32 D=128 Smax=32768, needs 34.1 MB).
+ * The first call on a device sets up the array's device address (call it once before any stream
+ * capture). Calls share the array: calls whose kernels overlap on the GPU race.
+ * No counterpart in the reference: it is an addition of this engine. */
+#define GTB_DECODE_NOALLOC_SCRATCH_BYTES (40u << 20)
+GTB_API int gtb_decode_q8_0_noalloc(const void *q, int q_dtype, const void *k_q8, const void *v_q8,
+                                    const int32_t *seq_lens, int64_t B, int64_t H, int64_t Hkv,
+                                    int64_t Smax, int64_t D, float scale, void *out, void *stream);
+
 /* Thread-local message of the last failure ("" if none). */
 GTB_API const char *gtb_last_error(void);
 GTB_API void gtb_clear_error(void);
