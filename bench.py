@@ -178,6 +178,68 @@ class ClockSampler:
                 "samples": len(self.samples)}
 
 
+# ------------------------------------------------------------------ decode workload (config 5a)
+
+DEC = dict(B=64, H=32, Hkv=8, D=128, Smax=32768, Lmin=1024)
+
+
+def run_decode(args, rank: int, world: int, local: int) -> None:
+    """Config 5a: one decode step of B=64 sequences (Hq=32, Hkv=8, D=128) against Q8_0 K/V caches
+    with lengths uniform in [1024, 32768]; q fp16. Metric: cache bytes read per second (HBM-bound)."""
+    import torch
+
+    import gguf_train_b200 as gtb
+    from gguf_train_b200 import _C
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    B, H, Hkv, D, Smax = DEC["B"], DEC["H"], DEC["Hkv"], DEC["D"], DEC["Smax"]
+    g = torch.Generator(device=dev)
+    g.manual_seed(77 + rank)
+    lens = torch.randint(DEC["Lmin"], Smax + 1, (B,), generator=g, device=dev).to(torch.int32)
+    row = D // 32 * 34
+    kq = torch.empty((B, Hkv, Smax, row), dtype=torch.uint8, device=dev)
+    vq = torch.empty_like(kq)
+    for b in range(B):  # N(0,1) values quantised to Q8_0 by the engine's own quantiser
+        kq[b] = gtb.quantize_q8_0(torch.randn((Hkv, Smax, D), generator=g, device=dev))
+        vq[b] = gtb.quantize_q8_0(torch.randn((Hkv, Smax, D), generator=g, device=dev))
+    q = torch.randn((B, H, 1, D), generator=g, device=dev).to(torch.float16)
+    tokens = int(lens.sum().item())
+    nbytes = tokens * Hkv * 2 * row + q.numel() * 2 * 2
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)  # > L2: every step reads from HBM
+    for _ in range(max(args.warmup, 3)):
+        gtb.decode_q8_0(q, kq, vq, lens)
+    torch.cuda.synchronize(dev)
+    stream = torch.cuda.current_stream(dev)
+    times = []
+    sampler = ClockSampler(torch.cuda.current_device())
+    with sampler:
+        for _ in range(args.steps):
+            flush.zero_()
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record(stream)
+            gtb.decode_q8_0(q, kq, vq, lens)
+            e.record(stream)
+            torch.cuda.synchronize(dev)
+            times.append(s.elapsed_time(e))
+    ms = statistics.mean(times)
+    peaks = load_peaks()
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    line = {
+        "metric": METRIC, "value": gbs * world, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": max(args.warmup, 3), "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "q8_0 K/V, f16 q", "data": "synthetic: N(0,1) K/V quantised to Q8_0",
+        "config": {"workload": "config 5a: Q8_0-KV decode, B=64 Hq=32 Hkv=8 D=128, L_b ~ U[1024, 32768]",
+                   "tokens": tokens, "bytes_per_step": nbytes, "l2": "256 MB flush before every step"},
+        "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": gbs / peaks["hbm_gbs"], "traffic": profile_traffic("decode_q8_0_config5a"),
+                     "peak_source": peaks["source"] + " HBM copy"},
+        "gpu_launches": 2 * args.steps, "clocks": sampler.summary(), "status": _C.device_status(),
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
 # ------------------------------------------------------------------ GPU arm
 
 def main() -> None:
@@ -188,6 +250,8 @@ def main() -> None:
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", default="prefill", choices=["prefill", "decode"],
+                    help="prefill: config 3 (the default line); decode: config 5a, Q8_0 KV cache")
     args = ap.parse_args()
 
     rank = int(os.environ.get("RANK", "0"))
@@ -195,6 +259,9 @@ def main() -> None:
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         run_reference(args, rank)
+        return
+    if args.workload == "decode":
+        run_decode(args, rank, world, local)
         return
 
     import torch

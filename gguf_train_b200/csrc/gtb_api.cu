@@ -150,6 +150,23 @@ bool same_shape(const gtb_tensor4& a, const int64_t* s) {
 
 float resolve_scale(float scale, int64_t D) { return scale <= 0.0f ? 1.0f / std::sqrt((float)D) : scale; }
 
+// The scratch of the backward and of the split-KV decode comes from the device's stream-ordered
+// pool. By default that pool hands unused memory back to the driver at every synchronisation, so a
+// call after a synchronize would map its scratch afresh (milliseconds for tens of MB) while the GPU
+// idles; keeping the memory in the pool makes repeated calls allocation-free after the first.
+void keep_pool_memory(int dev) {
+    static std::once_flag once[64];
+    if (dev < 0 || dev >= 64) return;
+    std::call_once(once[dev], [dev] {
+        cudaMemPool_t pool;
+        if (cudaDeviceGetDefaultMemPool(&pool, dev) == cudaSuccess) {
+            uint64_t keep = UINT64_MAX;
+            cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep);
+        }
+        cudaGetLastError();
+    });
+}
+
 int env_int(const char* name, int dflt) {
     const char* e = getenv(name);
     return e ? atoi(e) : dflt;
@@ -246,6 +263,9 @@ GTB_API int gtb_sdpa_bwd(const gtb_tensor4* dout, const gtb_tensor4* q, const gt
     a.lse = lse;
     cudaStream_t st = (cudaStream_t)stream;
     const size_t bytes = bwd_simt_scratch_bytes(a);
+    int dev = 0;
+    cudaGetDevice(&dev);
+    keep_pool_memory(dev);
     void* scratch = nullptr;
     if (bytes && cuda_failed(cudaMallocAsync(&scratch, bytes, st), "flash_attention_backward: scratch allocation"))
         return -1;
@@ -313,6 +333,7 @@ GTB_API int gtb_decode_q8_0(const void* q, int q_dtype, const void* k_q8, const 
                  device_status_word(dev)};
     cudaStream_t st = (cudaStream_t)stream;
     const size_t bytes = decode_scratch_bytes(B, H, Hkv, Smax, D);
+    keep_pool_memory(dev);
     void* scratch = nullptr;
     if (bytes && cuda_failed(cudaMallocAsync(&scratch, bytes, st), "flash_decode_q8_0: scratch allocation")) return -1;
     const int rc = launch_decode_q8_0(a, (float*)scratch, st);

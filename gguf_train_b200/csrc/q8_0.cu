@@ -128,11 +128,15 @@ __device__ inline float read_half_block(const uint8_t* base, uint32_t o, int hal
     uint32_t ww[5];
 #pragma unroll
     for (int i = 0; i < 5; ++i) ww[i] = w[i];
+    // int8 -> float without the (slow) integer-to-float conversion unit: flip the sign bit so the
+    // byte reads as u = s + 128, place it in the low mantissa byte of a float with exponent 2^23
+    // (value 2^23 + u), and subtract 2^23 + 128. Exact for every int8.
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-        const uint32_t x = __funnelshift_r(ww[i], ww[i + 1], sh);
+        const uint32_t x = __funnelshift_r(ww[i], ww[i + 1], sh) ^ 0x80808080u;
 #pragma unroll
-        for (int b = 0; b < 4; ++b) q[4 * i + b] = (float)(int)(int8_t)((x >> (8 * b)) & 0xff);
+        for (int b = 0; b < 4; ++b)
+            q[4 * i + b] = __int_as_float((int)__byte_perm(x, 0x4B000000u, 0x7440u | (uint32_t)b)) - 8388736.0f;
     }
     return __half2float(__ushort_as_half(dbits));
 }
@@ -403,6 +407,11 @@ int run_decode_gh(DecP p, cudaStream_t st) {
     if (cuda_failed(cudaFuncSetAttribute(decode_q8_0_kernel<D, GH>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                     "cudaFuncSetAttribute(decode)"))
         return -1;
+    // all of the unified L1/shared storage as shared memory: more resident CTAs, more bytes in flight
+    if (cuda_failed(cudaFuncSetAttribute(decode_q8_0_kernel<D, GH>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                         (int)cudaSharedmemCarveoutMaxShared),
+                    "cudaFuncSetAttribute(decode carveout)"))
+        return -1;
     p.nhg = p.G / GH;
     dim3 grid((unsigned)p.nchunks, (unsigned)(p.Hkv * p.nhg), (unsigned)p.B);
     decode_q8_0_kernel<D, GH><<<grid, DEC_WARPS * 32, smem, st>>>(p);
@@ -415,13 +424,28 @@ int run_decode_gh(DecP p, cudaStream_t st) {
     return 0;
 }
 
+// Query heads per CTA: the largest of 4, 3, 2, 1 dividing the group (GTB_DECODE_GH caps it, for tuning:
+// fewer heads per CTA means fewer registers and more resident CTAs, but K/V are dequantised once
+// per head group).
+int max_gh() {
+    static int v = -1;
+    if (v < 0) {
+        const char* e = getenv("GTB_DECODE_GH");
+        v = e ? atoi(e) : 4;
+        if (v < 1 || v > 4) v = 4;
+    }
+    return v;
+}
+
 template <int D>
 int run_decode(DecP p, cudaStream_t st) {
-    if (p.G % 4 == 0) return run_decode_gh<D, 4>(p, st);
-    if (p.G % 3 == 0) return run_decode_gh<D, 3>(p, st);
-    if (p.G % 2 == 0) return run_decode_gh<D, 2>(p, st);
+    const int cap = max_gh();
+    if (cap >= 4 && p.G % 4 == 0) return run_decode_gh<D, 4>(p, st);
+    if (cap >= 3 && p.G % 3 == 0) return run_decode_gh<D, 3>(p, st);
+    if (cap >= 2 && p.G % 2 == 0) return run_decode_gh<D, 2>(p, st);
     return run_decode_gh<D, 1>(p, st);
 }
+
 
 }  // namespace
 
