@@ -1,23 +1,31 @@
 // Flash-style attention forward for sm_100a: tcgen05 tensor cores, TMEM accumulators, TMA tiles.
 //
-// One CTA computes one 128-row query tile of one (batch, query head). Six warps, specialised:
-//   warp 0      TMA producer: the Q tile once, then K and V tiles of 128 keys into a ring of
-//               shared-memory stages (128-byte swizzled, the layout tcgen05 descriptors read);
-//   warp 1      MMA issuer (one thread) and TMEM owner:
-//                 S_j = Q K_j^T         (M=128, N=128, K=D; A, B from shared memory, K-major)
-//                 O  += P_j V_j         (M=128, N=D,  K=128; A = P, B = V read MN-major)
-//               S is double-buffered in TMEM so S_{j+2} is computed while the softmax works on S_j;
-//   warps 2..5  softmax, one query row per thread (TMEM lane = row): read S_j from TMEM, mask,
-//               online softmax in the log2 domain with lazy rescaling (O and the running sum are
-//               rescaled only when the row maximum grows by more than 2^8), write P_j (bf16/f16)
-//               back into the TMEM columns of S_j (the A operand of the PV MMA), and at the end
-//               normalise O and store it. A fixed share of the exponentials is computed with a
-//               polynomial on the FMA pipe instead of the MUFU unit (exp2_poly).
-// TMEM: S0 = columns [0,128), S1 = [128,256), O = [256, 256+D); 512 columns allocated.
+// One CTA computes two 128-row query tiles (rows 256c .. 256c+255) of one (batch, query head) that
+// share every K/V tile it loads. Twelve warps, specialised:
+//   warp 0       TMA producer: both Q tiles once, then K and V tiles of 128 keys into a ring of
+//                shared-memory stages (128-byte swizzled, the layout the tcgen05 descriptors read);
+//   warp 1       TMEM owner (512 columns) and MMA issuer (one thread), ping-ponging the two tiles:
+//                  S_t = Q_t K_j^T        (M=128, N=128, K=D; both operands K-major in shared memory)
+//                  O_t += P_t V_j         (M=128, N=D, K=128; P_t from TMEM, V read MN-major)
+//                in the order  PV_0(j), S_0(j+1), PV_1(j), S_1(j+1), ...  so that while one softmax
+//                warpgroup works on its S the tensor core runs the other tile's MMAs;
+//   warps 2-3    idle;
+//   warps 4-7    softmax + epilogue of tile 0, warps 8-11 of tile 1: one query row per thread (TMEM
+//                lane = row). Two passes over S in TMEM (row maximum, then exponentials) so a row never
+//                has to sit in registers whole; online softmax in the log2 domain with lazy rescaling
+//                (O and the running sum are rescaled only when the maximum grows by more than 2^8);
+//                P (bf16/f16) is written into the upper half of the tile's S columns, where the PV MMA
+//                reads it as its A operand.
+// TMEM columns: S_0 [0,128), S_1 [128,256), O_0 [256,256+D), O_1 [384,384+D).
 //
 // Semantics are those of gt_flash_attention (reference csrc/gt_ops_nn.cpp:2423-2525): causal is
 // top-left aligned (key s masked for query l when s > l), GQA maps query head h to kv head
 // h / (H/Hkv), rows are normalised by the sum of exp over allowed keys. Accumulation is f32.
+//
+// tcgen05 MMAs issued by one thread complete in issue order, and tcgen05.commit arrives once all
+// earlier MMAs of the thread are done. Two consequences the schedule relies on: S_t(j+1) may reuse
+// the TMEM columns PV_t(j) reads P_t(j) from, and when S_t(j+1) is reported complete, PV_t(j) is
+// complete too, so the softmax may rescale O_t without waiting on anything else.
 //
 // Every wait on an mbarrier is bounded (about a second); on timeout the kernel records a status
 // code, skips its remaining work, drains its own in-flight copies and MMAs with bounded waits,
@@ -38,12 +46,10 @@ namespace {
 
 using namespace sm100;
 
-constexpr int BM = 128;
-constexpr int BN = 128;
-constexpr int NTHREADS = 192;
+constexpr int BM = 128;          // rows per query tile
+constexpr int BN = 128;          // keys per K/V tile
+constexpr int NTHREADS = 384;
 constexpr uint32_t TMEM_COLS = 512;
-constexpr uint32_t S_COL0 = 0;
-constexpr uint32_t O_COL = 256;
 
 template <int D>
 struct Cfg {
@@ -52,13 +58,17 @@ struct Cfg {
     static constexpr int ATOM_BYTES = BM * 128;           // 16 KB: one 64-column slab of a tile
     static constexpr int KS = 2;                          // K stages
     static constexpr int VS = 2;                          // V stages
-    static constexpr int OFF_Q = 0;
-    static constexpr int OFF_K = OFF_Q + TILE;
+    static constexpr int OFF_Q = 0;                       // Q_0, Q_1
+    static constexpr int OFF_K = 2 * TILE;
     static constexpr int OFF_V = OFF_K + KS * TILE;
     static constexpr int OFF_BAR = OFF_V + VS * TILE;
-    static constexpr int NBAR = 1 + 2 * KS + 2 * VS + 2 + 2 + 3;
-    static constexpr int SMEM = OFF_BAR + NBAR * 8 + 16 + 1024;  // + TMEM slot, + alignment slack
+    static constexpr int NBAR = 1 + 2 * KS + 2 * VS + 2 + 2 + 2 + 1;
+    static constexpr int SMEM = OFF_BAR + NBAR * 8 + 16 + 1024;  // + TMEM slot and flag, + alignment slack
 };
+
+__device__ __forceinline__ uint32_t s_col(int t) { return (uint32_t)t * 128u; }
+__device__ __forceinline__ uint32_t o_col(int t) { return 256u + (uint32_t)t * 128u; }
+constexpr uint32_t P_OFF = 64;  // P_t lives in S_t's columns [64, 128)
 
 // 2^x on the FMA/ALU pipes, to take part of the softmax's exponentials off the MUFU unit.
 // Range reduction x = n + f with n = round(x) (adding 1.5 * 2^23 rounds to an integer held in
@@ -97,7 +107,7 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* s
 struct Params {
     int64_t H, Hkv, L, S;
     int group;
-    int n_qtiles;
+    int n_pairs;  // CTAs along the query dimension (two 128-row tiles each)
     float scale_log2;
     int causal;
     void* o;
@@ -106,7 +116,22 @@ struct Params {
     int* status;
 };
 
-// EMU: how many of every 8 exponentials of a row are computed by exp2_poly instead of MUFU.
+// keys a row of tile t may see: [0, n_kv*BN) minus causal / ragged masking
+__device__ __forceinline__ int tile_blocks(int row0, const Params& p, int n_kv) {
+    if (row0 >= p.L) return 0;
+    if (!p.causal) return n_kv;
+    const int last = (int)min((int64_t)row0 + BM - 1, p.L - 1);
+    return min(n_kv, last / BN + 1);
+}
+
+// Scores of one 32-column chunk, masked: column s (absolute key index kv0 + i) is excluded when
+// s >= S or, for causal attention, s > row.
+__device__ __forceinline__ void mask_chunk(float* x, int kv0, int lim) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+        if (kv0 + i > lim) x[i] = -INFINITY;
+}
+
 template <int D, bool BF16, int EMU>
 __global__ void __launch_bounds__(NTHREADS, 1)
 fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -121,30 +146,27 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
     uint64_t* k_empty = k_full + C::KS;
     uint64_t* v_full = k_empty + C::KS;
     uint64_t* v_empty = v_full + C::VS;
-    uint64_t* s_full = v_empty + C::VS;      // [2]
-    uint64_t* p_full = s_full + 2;           // [2]
-    uint64_t* o_full = p_full + 2;           // one phase per PV block
-    uint64_t* o_final = o_full + 1;          // single phase: all MMAs done
-    uint64_t* drain = o_final + 1;           // error path only
+    uint64_t* s_full = v_empty + C::VS;      // [2] per tile: S_t(j) computed
+    uint64_t* p_full = s_full + 2;           // [2] per tile: P_t(j) written (128 arrivals)
+    uint64_t* o_final = p_full + 2;          // [2] per tile: every MMA of the tile done
+    uint64_t* drain = o_final + 2;           // error path only
     uint32_t* tmem_slot = (uint32_t*)(bars + C::NBAR);
     int* abort_flag = (int*)(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int tile = p.causal ? (p.n_qtiles - 1 - (int)blockIdx.x) : (int)blockIdx.x;  // heavy tiles first
+    const int pair = p.causal ? (p.n_pairs - 1 - (int)blockIdx.x) : (int)blockIdx.x;  // heavy pairs first
     const int h = blockIdx.y, b = blockIdx.z;
     const int hk = h / p.group;
-    const int row0 = tile * BM;
     const int n_kv = (int)((p.S + BN - 1) / BN);
-    const int row_last = (int)min((int64_t)row0 + BM - 1, p.L - 1);
-    const int nblk = p.causal ? min(n_kv, row_last / BN + 1) : n_kv;
+    const int row0[2] = {pair * 2 * BM, pair * 2 * BM + BM};
+    const int nblk[2] = {tile_blocks(row0[0], p, n_kv), tile_blocks(row0[1], p, n_kv)};
+    const int n = max(nblk[0], nblk[1]);  // nblk[0] >= 1: the CTA exists because row0[0] < L
 
     if (threadIdx.x == 0) {
         mbar_init(q_full, 1);
         for (int i = 0; i < C::KS; ++i) { mbar_init(&k_full[i], 1); mbar_init(&k_empty[i], 1); }
         for (int i = 0; i < C::VS; ++i) { mbar_init(&v_full[i], 1); mbar_init(&v_empty[i], 1); }
-        for (int i = 0; i < 2; ++i) { mbar_init(&s_full[i], 1); mbar_init(&p_full[i], 128); }
-        mbar_init(o_full, 1);
-        mbar_init(o_final, 1);
+        for (int t = 0; t < 2; ++t) { mbar_init(&s_full[t], 1); mbar_init(&p_full[t], 128); mbar_init(&o_final[t], 1); }
         mbar_init(drain, 1);
         *abort_flag = 0;
         fence_mbar_init();
@@ -163,10 +185,12 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
             prefetch_tmap(&tmV);
             int last_k = -1, last_v = -1;
             bool ok = true;
-            mbar_expect_tx(q_full, C::TILE);
-            for (int a = 0; a < C::ATOMS; ++a)
-                tma_load_4d(smem + C::OFF_Q + a * C::ATOM_BYTES, &tmQ, a * 64, row0, h, b, q_full);
-            for (int j = 0; j < nblk && ok; ++j) {
+            const int nq = nblk[1] > 0 ? 2 : 1;
+            mbar_expect_tx(q_full, nq * C::TILE);
+            for (int t = 0; t < nq; ++t)
+                for (int a = 0; a < C::ATOMS; ++a)
+                    tma_load_4d(smem + C::OFF_Q + t * C::TILE + a * C::ATOM_BYTES, &tmQ, a * 64, row0[t], h, b, q_full);
+            for (int j = 0; j < n && ok; ++j) {
                 const int ks = j % C::KS;
                 if (j >= C::KS) ok = mbar_wait(&k_empty[ks], ((j / C::KS) - 1) & 1, p.status, 11);
                 if (!ok || *(volatile int*)abort_flag) break;
@@ -197,98 +221,102 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
         if (lane == 0) {
             constexpr uint32_t IDESC_S = idesc_f16(BM, BN, BF16, false);
             constexpr uint32_t IDESC_PV = idesc_f16(BM, D, BF16, true);
-            const uint32_t q_addr = smem_u32(smem + C::OFF_Q);
             bool ok = mbar_wait(q_full, 0, p.status, 21);
-            auto issue_s = [&](int j) -> bool {
+            auto issue_s = [&](int t, int j) -> bool {
                 const int ks = j % C::KS;
                 if (!mbar_wait(&k_full[ks], (j / C::KS) & 1, p.status, 22)) return false;
                 tc_fence_after();
+                const uint32_t q_addr = smem_u32(smem + C::OFF_Q + t * C::TILE);
                 const uint32_t k_addr = smem_u32(smem + C::OFF_K + ks * C::TILE);
-                const uint32_t d_tmem = tmem + S_COL0 + (uint32_t)(j & 1) * BN;
 #pragma unroll
                 for (int kk = 0; kk < D / 16; ++kk) {
                     const uint32_t off = (uint32_t)((kk / 4) * C::ATOM_BYTES + (kk % 4) * 32);
-                    mma_ss(d_tmem, desc_sw128(q_addr + off, 16, 1024), desc_sw128(k_addr + off, 16, 1024), IDESC_S,
-                           kk > 0 ? 1u : 0u);
+                    mma_ss(tmem + s_col(t), desc_sw128(q_addr + off, 16, 1024), desc_sw128(k_addr + off, 16, 1024),
+                           IDESC_S, kk > 0 ? 1u : 0u);
                 }
-                mma_commit(&s_full[j & 1]);
-                mma_commit(&k_empty[ks]);
+                mma_commit(&s_full[t]);
                 return true;
             };
-            if (ok) ok = issue_s(0);
-            if (ok && nblk > 1) ok = issue_s(1);
-            for (int j = 0; j < nblk && ok; ++j) {
-                ok = mbar_wait(&p_full[j & 1], (j >> 1) & 1, p.status, 23);
-                if (!ok || *(volatile int*)abort_flag) break;
+            auto issue_pv = [&](int t, int j) -> bool {
+                if (!mbar_wait(&p_full[t], j & 1, p.status, 23)) return false;
                 const int vs = j % C::VS;
-                ok = mbar_wait(&v_full[vs], (j / C::VS) & 1, p.status, 24);
-                if (!ok || *(volatile int*)abort_flag) break;
+                if (!mbar_wait(&v_full[vs], (j / C::VS) & 1, p.status, 24)) return false;
                 tc_fence_after();
                 const uint32_t v_addr = smem_u32(smem + C::OFF_V + vs * C::TILE);
 #pragma unroll
                 for (int kk = 0; kk < BN / 16; ++kk) {
                     const uint64_t bdesc = desc_sw128(v_addr + kk * 2048, C::ATOM_BYTES, 1024);
-                    const uint32_t acc = (j > 0 || kk > 0) ? 1u : 0u;
-                    // A = P_j, 16-bit, packed two per TMEM column in the columns of S_j
-                    mma_ts(tmem + O_COL, tmem + S_COL0 + (uint32_t)(j & 1) * BN + kk * 8, bdesc, IDESC_PV, acc);
+                    // A = P_t(j): 16-bit values packed two per TMEM column, 8 columns per K step
+                    mma_ts(tmem + o_col(t), tmem + s_col(t) + P_OFF + kk * 8, bdesc, IDESC_PV,
+                           (j > 0 || kk > 0) ? 1u : 0u);
                 }
-                mma_commit(o_full);
-                mma_commit(&v_empty[vs]);
-                if (j + 2 < nblk) ok = issue_s(j + 2);
+                return true;
+            };
+            for (int t = 0; t < 2 && ok; ++t)
+                if (nblk[t] > 0) ok = issue_s(t, 0);
+            if (ok) mma_commit(&k_empty[0]);
+            for (int j = 0; j < n && ok; ++j) {
+                for (int t = 0; t < 2 && ok; ++t) {
+                    if (j >= nblk[t]) continue;
+                    ok = issue_pv(t, j);
+                    if (ok && j + 1 < nblk[t]) ok = issue_s(t, j + 1);
+                    if (ok && j + 1 == nblk[t]) mma_commit(&o_final[t]);
+                }
+                if (!ok || *(volatile int*)abort_flag) break;
+                mma_commit(&v_empty[j % C::VS]);
+                if (j + 1 < n) mma_commit(&k_empty[(j + 1) % C::KS]);
             }
             if (!ok) *(volatile int*)abort_flag = 1;
-            if (ok && !*(volatile int*)abort_flag) {
-                mma_commit(o_final);
-            } else {
+            if (*(volatile int*)abort_flag) {
                 mma_commit(drain);  // wait (bounded) for every MMA we issued before TMEM is freed
                 mbar_wait(drain, 0, nullptr, 0);
             }
         }
-    } else {
-        // ------------------------------------------------------------ softmax + epilogue
+    } else if (warp >= 4) {
+        // ------------------------------------------------------------ softmax + epilogue of tile t
+        const int t = (warp - 4) >> 2;
         const int quad = warp & 3;                    // TMEM lanes this warp may access
         const int r = quad * 32 + lane;               // row of the tile
-        const int grow = row0 + r;                    // query index
+        const int grow = row0[t] + r;                 // query index
         const uint32_t lane_addr = (uint32_t)(quad * 32) << 16;
+        const uint32_t s_tmem = tmem + lane_addr + s_col(t);
+        const uint32_t o_tmem = tmem + lane_addr + o_col(t);
+        const int lim_s = (int)min(p.S, (int64_t)INT32_MAX) - 1;
+        const int lim = p.causal ? min(lim_s, grow) : lim_s;  // last key this row may see
         float m_used = -INFINITY, lsum = 0.0f;
         bool ok = true;
-        for (int j = 0; j < nblk; ++j) {
-            ok = warp_wait(&s_full[j & 1], (j >> 1) & 1, p.status, 31);
+        for (int j = 0; j < nblk[t]; ++j) {
+            ok = warp_wait(&s_full[t], j & 1, p.status, 31);
             if (!ok || __any_sync(0xffffffffu, *(volatile int*)abort_flag)) break;
             tc_fence_after();
-            const uint32_t s_tmem = tmem + lane_addr + S_COL0 + (uint32_t)(j & 1) * BN;
-            uint32_t xr[BN];
-#pragma unroll
-            for (int c = 0; c < BN / 32; ++c) tmem_ld32(s_tmem + c * 32, &xr[c * 32]);
-            tmem_ld_wait();
-            float x[BN];
-#pragma unroll
-            for (int i = 0; i < BN; ++i) x[i] = __uint_as_float(xr[i]);
             const int kv0 = j * BN;
-            const bool need_mask = (kv0 + BN > p.S) || (p.causal && kv0 + BN - 1 > row0);
-            if (need_mask) {
-                const int lim = p.causal ? min((int)min(p.S, (int64_t)INT32_MAX) - 1, grow) : (int)p.S - 1;
-#pragma unroll
-                for (int i = 0; i < BN; ++i)
-                    if (kv0 + i > lim) x[i] = -INFINITY;
-            }
-            // row max: eight independent partial maxima, then a tree (no 128-long dependency chain)
+            const bool need_mask = (kv0 + BN > p.S) || (p.causal && kv0 + BN - 1 > row0[t]);
+            // pass 1: row maximum, 64 columns at a time; columns 64..127 stay in registers for pass 2
+            uint32_t ra[32], rb[32];
+            float* xa = (float*)ra;
+            float* xb = (float*)rb;
             float pm[8];
+            tmem_ld32(s_tmem + 0, ra);
+            tmem_ld32(s_tmem + 32, rb);
+            tmem_ld_wait();
+            if (need_mask) { mask_chunk(xa, kv0, lim); mask_chunk(xb, kv0 + 32, lim); }
 #pragma unroll
-            for (int u = 0; u < 8; ++u) pm[u] = x[u];
+            for (int u = 0; u < 8; ++u) pm[u] = fmaxf(xa[u], xb[u]);
 #pragma unroll
-            for (int i = 8; i < BN; ++i) pm[i & 7] = fmaxf(pm[i & 7], x[i]);
+            for (int i = 8; i < 32; ++i) pm[i & 7] = fmaxf(pm[i & 7], fmaxf(xa[i], xb[i]));
+            tmem_ld32(s_tmem + 64, ra);
+            tmem_ld32(s_tmem + 96, rb);
+            tmem_ld_wait();
+            if (need_mask) { mask_chunk(xa, kv0 + 64, lim); mask_chunk(xb, kv0 + 96, lim); }
+#pragma unroll
+            for (int i = 0; i < 32; ++i) pm[i & 7] = fmaxf(pm[i & 7], fmaxf(xa[i], xb[i]));
             const float mx = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])),
                                    fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7])));
             const float m_new = fmaxf(m_used, mx * p.scale_log2);
             const bool rescale = m_new > m_used + 8.0f;  // false while the row has no finite score
             if (__any_sync(0xffffffffu, rescale && j > 0)) {
-                // PV_{j-1} must be complete before O is read; PV_{j-2} is known complete here
-                ok = warp_wait(o_full, (j - 1) & 1, p.status, 32);
-                if (!ok) break;
-                tc_fence_after();
+                // PV_t(j-1) is complete: it was issued before S_t(j), whose completion we just saw
                 const float alpha = rescale ? ex2(m_used - m_new) : 1.0f;
-                const uint32_t o_tmem = tmem + lane_addr + O_COL;
 #pragma unroll
                 for (int c = 0; c < D / 32; ++c) {
                     uint32_t ov[32];
@@ -298,39 +326,48 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
                     for (int i = 0; i < 32; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
                     tmem_st32(o_tmem + c * 32, ov);
                 }
-                tmem_st_wait();
             }
             if (rescale) {
                 lsum *= ex2(m_used - m_new);
                 m_used = m_new;
             }
             const float neg_m = (m_used == -INFINITY) ? 0.0f : -m_used;
-            uint32_t pk[BN / 2];
-            float ps[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+            float ps[4] = {0.f, 0.f, 0.f, 0.f};
+            // pass 2: exponentials, 32 columns at a time, P into S's columns [64, 128)
+            auto emit = [&](const float* x, int c) {
+                uint32_t pk[16];
 #pragma unroll
-            for (int i = 0; i < BN; i += 2) {
-                const float a0 = fmaf(x[i], p.scale_log2, neg_m);
-                const float a1 = fmaf(x[i + 1], p.scale_log2, neg_m);
-                const float p0 = (i & 7) < EMU ? exp2_poly(a0) : ex2(a0);
-                const float p1 = ((i + 1) & 7) < EMU ? exp2_poly(a1) : ex2(a1);
-                ps[i & 7] += p0;
-                ps[(i + 1) & 7] += p1;
-                pk[i / 2] = pack2<BF16>(p0, p1);
-            }
-            lsum += ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
-            tmem_st32(s_tmem, pk);
-            tmem_st32(s_tmem + 32, pk + 32);
+                for (int i = 0; i < 32; i += 2) {
+                    const float a0 = fmaf(x[i], p.scale_log2, neg_m);
+                    const float a1 = fmaf(x[i + 1], p.scale_log2, neg_m);
+                    const float p0 = (i & 7) < EMU ? exp2_poly(a0) : ex2(a0);
+                    const float p1 = ((i + 1) & 7) < EMU ? exp2_poly(a1) : ex2(a1);
+                    ps[(i >> 1) & 3] += p0 + p1;
+                    pk[i / 2] = pack2<BF16>(p0, p1);
+                }
+                tmem_st16(s_tmem + P_OFF + c * 16, pk);
+            };
+            // P chunk c (keys 32c..32c+31) goes to columns 64+16c. Chunks 2, 3 come from the registers
+            // first (their P lands on columns already read), then columns 0..63 are read again.
+            emit(xa, 2);
+            emit(xb, 3);
+            tmem_ld32(s_tmem + 0, ra);
+            tmem_ld32(s_tmem + 32, rb);
+            tmem_ld_wait();
+            if (need_mask) { mask_chunk(xa, kv0, lim); mask_chunk(xb, kv0 + 32, lim); }
+            emit(xa, 0);
+            emit(xb, 1);
+            lsum += (ps[0] + ps[1]) + (ps[2] + ps[3]);
             tmem_st_wait();
             tc_fence_before();
-            mbar_arrive(&p_full[j & 1]);
+            mbar_arrive(&p_full[t]);
         }
         if (!ok) *(volatile int*)abort_flag = 1;
-        if (ok && !*(volatile int*)abort_flag) {
-            ok = warp_wait(o_final, 0, p.status, 33);
+        if (nblk[t] > 0 && ok && !*(volatile int*)abort_flag) {
+            ok = warp_wait(&o_final[t], 0, p.status, 33);
             if (ok) {
                 tc_fence_after();
                 const float inv = lsum > 0.0f ? 1.0f / lsum : 0.0f;
-                const uint32_t o_tmem = tmem + lane_addr + O_COL;
                 T* orow = (T*)p.o + (int64_t)b * p.os0 + (int64_t)h * p.os1 + (int64_t)grow * p.os2;
 #pragma unroll
                 for (int c = 0; c < D / 32; ++c) {
@@ -431,7 +468,7 @@ int run(const FwdArgs& a, const CUtensorMap& mq, const CUtensorMap& mk, const CU
     Params p;
     p.H = a.sh.H; p.Hkv = a.sh.Hkv; p.L = a.sh.L; p.S = a.sh.S;
     p.group = (int)(a.sh.H / a.sh.Hkv);
-    p.n_qtiles = (int)((a.sh.L + BM - 1) / BM);
+    p.n_pairs = (int)((a.sh.L + 2 * BM - 1) / (2 * BM));
     p.scale_log2 = a.scale * 1.4426950408889634f;
     p.causal = a.causal;
     p.o = a.o.data;
@@ -440,13 +477,12 @@ int run(const FwdArgs& a, const CUtensorMap& mq, const CUtensorMap& mk, const CU
     int dev = 0;
     cudaGetDevice(&dev);
     p.status = device_status_word(dev);
-    dim3 grid((unsigned)p.n_qtiles, (unsigned)a.sh.H, (unsigned)a.sh.B);
+    dim3 grid((unsigned)p.n_pairs, (unsigned)a.sh.H, (unsigned)a.sh.B);
     kern<<<grid, NTHREADS, C::SMEM, st>>>(mq, mk, mv, p);
     return cuda_failed(cudaGetLastError(), "flash_attention (sm100) launch") ? -1 : 0;
 }
 
-// Exponentials emulated per 8. Default 0: this kernel's softmax is latency-bound, not MUFU-bound
-// (measured 855 / 794 / 754 TFLOP/s for 0 / 2 / 3 on config 3). GTB_FWD_EMU=2|3 selects the others.
+// Exponentials computed by exp2_poly per 8 (GTB_FWD_EMU=0|2|3, default 0).
 int emu_setting() {
     static int v = -1;
     if (v < 0) {
@@ -481,7 +517,7 @@ bool fwd_sm100_supported(const FwdArgs& a) {
             (a.v.shape[i] > 1 && a.v.stride[i] % 8 != 0))
             return false;
     }
-    if (a.sh.L >= (1ll << 31) || a.sh.S >= (1ll << 31) || a.sh.H > 65535 || a.sh.B > 65535) return false;
+    if (a.sh.L >= (1ll << 30) || a.sh.S >= (1ll << 30) || a.sh.H > 65535 || a.sh.B > 65535) return false;
     if (a.sh.L < 1 || a.sh.S < 1) return false;
     return encode_fn() != nullptr;
 }
