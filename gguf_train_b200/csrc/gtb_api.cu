@@ -262,7 +262,10 @@ GTB_API int gtb_sdpa_bwd(const gtb_tensor4* dout, const gtb_tensor4* q, const gt
     a.causal = is_causal ? 1 : 0;
     a.lse = lse;
     cudaStream_t st = (cudaStream_t)stream;
-    const size_t bytes = bwd_simt_scratch_bytes(a);
+    // GTB_BWD_SIMT=1 forces the SIMT kernels (used to cross-check the two implementations)
+    static const int force_simt = env_int("GTB_BWD_SIMT", 0);
+    const bool fast = !force_simt && bwd_sm100_supported(a);
+    const size_t bytes = fast ? bwd_sm100_scratch_bytes(a) : bwd_simt_scratch_bytes(a);
     int dev = 0;
     cudaGetDevice(&dev);
     keep_pool_memory(dev);
@@ -270,7 +273,7 @@ GTB_API int gtb_sdpa_bwd(const gtb_tensor4* dout, const gtb_tensor4* q, const gt
     if (bytes && cuda_failed(cudaMallocAsync(&scratch, bytes, st), "flash_attention_backward: scratch allocation"))
         return -1;
     a.scratch = scratch;
-    const int rc = launch_bwd_simt(a, st);
+    const int rc = fast ? launch_bwd_sm100(a, st) : launch_bwd_simt(a, st);
     if (scratch) cudaFreeAsync(scratch, st);
     return rc;
 }

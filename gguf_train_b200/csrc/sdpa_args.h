@@ -1,6 +1,8 @@
 // Validated argument bundles passed from the C-ABI layer to the kernel launchers.
 #pragma once
 
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -38,8 +40,19 @@ int launch_fwd_simt(const FwdArgs& a, cudaStream_t st);
 int launch_bwd_simt(const BwdArgs& a, cudaStream_t st);
 size_t bwd_simt_scratch_bytes(const BwdArgs& a);
 
+// TMA: the driver's tensor-map encoder (nullptr if unavailable) and a 4-D (d, row, head, batch) map of
+// a 16-bit tensor with a 64 x box_rows box and 128-byte swizzle.
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn();
+bool make_tma_map_4d(CUtensorMap* tm, const gtb_tensor4& t, int64_t d_extent, bool bf16, int box_rows);
+
 // tcgen05/TMA forward: bf16/f16, D == Dv in {64,128}, unit inner stride, no mask.
 bool fwd_sm100_supported(const FwdArgs& a);
 int launch_fwd_sm100(const FwdArgs& a, cudaStream_t st);
+
+// tcgen05/TMA backward (dK/dV kernel + dQ kernel): same conditions as the forward, plus dq/dk/dv
+// with unit inner stride and 16-byte aligned rows; scratch = bwd_sm100_scratch_bytes().
+bool bwd_sm100_supported(const BwdArgs& a);
+size_t bwd_sm100_scratch_bytes(const BwdArgs& a);
+int launch_bwd_sm100(const BwdArgs& a, cudaStream_t st);
 
 }  // namespace gtb

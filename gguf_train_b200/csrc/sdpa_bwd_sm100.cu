@@ -1,0 +1,628 @@
+// Attention backward for sm_100a: tcgen05 tensor cores, TMEM accumulators, TMA tiles.
+//
+// The reference's backward (FlashAttentionFn.backward, gguf_train/_functions.py:1934-1965) recomputes
+// the probabilities with separate matmul / softmax / elementwise ops and materialises several
+// (B, H, L, S) tensors. Here it is three kernels that never hold more than 128x128 tiles:
+//
+//   preprocess  per query row: delta = sum(dO * O), lse2 = lse * log2(e) (+inf for rows that are
+//               padding or had no allowed key, so their probabilities come out 0); both stored in
+//               (B, H, Lpad) buffers, Lpad = L rounded up to 128, so tiles load with bulk copies.
+//   dK/dV       one CTA per 128-key block of one (batch, kv head); it loops over the 128-row query
+//               tiles of every query head of the kv head's group, so dK and dV are complete when the
+//               CTA ends (no cross-CTA reduction). Per query tile, in TMEM (lane = key):
+//                 S^T = K Q^T, dP^T = V dO^T                      (M=128 keys, N=128 queries, K=D)
+//                 P^T = exp2(S^T * scale*log2e - lse2), dS^T = P^T * (dP^T - delta)
+//                 dV += P^T dO, dK += dS^T Q                       (M=128, N=D, K=128; A from TMEM)
+//   dQ          one CTA per 128-row query tile; it loops over the key blocks the tile attends:
+//                 S = Q K^T, dP = dO V^T, dS = P * (dP - delta), dQ += dS K  (A from TMEM)
+// TMEM columns: dK/dV kernel: dV [0,D), dK [128,128+D), S^T [256,384), dP^T [384,512);
+//               dQ kernel: S [0,128), dP [128,256), dQ [256,256+D).
+// P^T / dS^T / dS (bf16 or f16, packed two per column) are written back over the S / dP columns
+// they were computed from: chunk c (32 columns) lands in columns 16c..16c+15, which were read before.
+//
+// Warps (both main kernels): 0 = TMA producer, 1 = TMEM owner and MMA issuer (one thread), 2-5 =
+// compute, one key (dK/dV) or query (dQ) row per thread. Causal masking is top-left (key s masked for
+// query l when s > l), as in gt_flash_attention (csrc/gt_ops_nn.cpp:2476). Every wait is bounded as in
+// the forward kernel: a timeout records a status code, drains, frees TMEM and returns.
+
+#include <cmath>
+
+#include "gtb_common.cuh"
+#include "sdpa_args.h"
+#include "sm100_ptx.cuh"
+
+namespace gtb {
+namespace {
+
+using namespace sm100;
+
+constexpr int BT = 128;        // rows of a query tile and of a key block
+constexpr int NTHREADS = 192;  // 6 warps
+constexpr uint32_t TMEM_COLS = 512;
+constexpr float LOG2E = 1.4426950408889634f;
+
+template <int D>
+struct BCfg {
+    static constexpr int ATOMS = D / 64;      // 64-column (128-byte) slabs along D
+    static constexpr int TILE = BT * D * 2;   // one 128-row tile of Q, K, V or dO
+    static constexpr int SLAB = BT * 128;     // one slab of a tile
+};
+
+template <bool BF16>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+    uint32_t r;
+    if constexpr (BF16) asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+    else asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+    return r;
+}
+
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* status, int code) {
+    const bool ok = mbar_wait(bar, parity, status, code);
+    return __all_sync(0xffffffffu, ok);
+}
+
+// K-major operand descriptor: k-step kk (16 elements) of a 128-row tile made of 64-column slabs
+__device__ __forceinline__ uint64_t kmajor(uint32_t base, int kk, int slab_bytes) {
+    return desc_sw128(base + (uint32_t)((kk / 4) * slab_bytes + (kk % 4) * 32), 16, 1024);
+}
+// MN-major operand descriptor: k-step kk = rows 16kk..16kk+15 of a tile (rows are the K dimension)
+__device__ __forceinline__ uint64_t mnmajor(uint32_t base, int kk, int slab_bytes) {
+    return desc_sw128(base + (uint32_t)(kk * 2048), (uint32_t)slab_bytes, 1024);
+}
+
+// store 32 accumulator columns (f32 in registers) of one row as 16-bit values, times `mul`
+template <bool BF16>
+__device__ __forceinline__ void store_row32(void* dst, const uint32_t* v, float mul) {
+    uint32_t w[16];
+#pragma unroll
+    for (int i = 0; i < 32; i += 2) w[i / 2] = pack2<BF16>(__uint_as_float(v[i]) * mul, __uint_as_float(v[i + 1]) * mul);
+    uint4* d = (uint4*)dst;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) d[q] = make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+}
+
+// ------------------------------------------------------------------ preprocess
+
+struct PreP {
+    const void* o;
+    const void* g;            // dO
+    int64_t os0, os1, os2;    // strides of O (b, h, l); d stride 1
+    int64_t gs0, gs1, gs2;    // strides of dO
+    const float* lse;         // (B, H, L)
+    float* lse2;              // (B, H, Lpad)
+    float* delta;             // (B, H, Lpad)
+    int64_t B, H, L, Lpad, D;
+};
+
+template <typename T>
+__global__ void __launch_bounds__(128) bwd_pre_kernel(PreP p) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t row = (int64_t)blockIdx.x * 4 + warp;  // over B*H*Lpad
+    if (row >= p.B * p.H * p.Lpad) return;
+    const int64_t l = row % p.Lpad, bh = row / p.Lpad, h = bh % p.H, b = bh / p.H;
+    float acc = 0.0f;
+    if (l < p.L) {
+        const T* o = (const T*)p.o + b * p.os0 + h * p.os1 + l * p.os2;
+        const T* g = (const T*)p.g + b * p.gs0 + h * p.gs1 + l * p.gs2;
+        for (int64_t d = lane; d < p.D; d += 32) acc += (float)Elem<T>::load(o + d) * (float)Elem<T>::load(g + d);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+    if (lane == 0) {
+        float l2 = INFINITY;  // padding rows and rows without an allowed key: probabilities 0
+        if (l < p.L) {
+            const float lse = p.lse[bh * p.L + l];
+            if (lse != -INFINITY) l2 = lse * LOG2E;
+        }
+        p.lse2[row] = l2;
+        p.delta[row] = acc;
+    }
+}
+
+// ------------------------------------------------------------------ dK / dV
+
+struct KvP {
+    int64_t H, Hkv, L, S, Lpad;
+    int group, n_qt, n_kvt;
+    float scale_log2, scale;
+    int causal;
+    void* dk;
+    int64_t ks0, ks1, ks2;
+    void* dv;
+    int64_t vs0, vs1, vs2;
+    const float* lse2;
+    const float* delta;
+    int* status;
+};
+
+template <int D, bool BF16>
+__global__ void __launch_bounds__(NTHREADS, 1)
+bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmG, const KvP p) {
+    using C = BCfg<D>;
+    using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+    constexpr int OFF_K = 0, OFF_V = C::TILE, OFF_ST = 2 * C::TILE;
+    constexpr int ST_BYTES = 2 * C::TILE + 1024;  // Q, dO, lse2[128], delta[128]
+    constexpr int OFF_BAR = OFF_ST + 2 * ST_BYTES;
+    extern __shared__ unsigned char smem_raw[];
+    unsigned char* smem = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint64_t* bars = (uint64_t*)(smem + OFF_BAR);
+    uint64_t* kv_full = bars;
+    uint64_t* st_full = bars + 1;     // [2]
+    uint64_t* st_empty = bars + 3;    // [2]
+    uint64_t* s_full = bars + 5;      // S^T, dP^T of the current tile computed
+    uint64_t* p_full = bars + 6;      // P^T, dS^T written (128 arrivals)
+    uint64_t* acc_final = bars + 7;   // every MMA done
+    uint64_t* drain = bars + 8;
+    uint32_t* tmem_slot = (uint32_t*)(bars + 9);
+    int* abort_flag = (int*)(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int jt = blockIdx.x, hk = blockIdx.y, b = blockIdx.z;
+    const int key0 = jt * BT;
+    // query tiles that see this key block: rows l >= key0 when causal (top-left)
+    const int i_start = p.causal ? min(p.n_qt, key0 / BT) : 0;
+    const int nq = p.n_qt - i_start;
+    const int nit = p.group * nq;
+
+    if (threadIdx.x == 0) {
+        mbar_init(kv_full, 1);
+        for (int i = 0; i < 2; ++i) { mbar_init(&st_full[i], 1); mbar_init(&st_empty[i], 1); }
+        mbar_init(s_full, 1);
+        mbar_init(p_full, 128);
+        mbar_init(acc_final, 1);
+        mbar_init(drain, 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) tmem_alloc(tmem_slot, TMEM_COLS);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0 && nit > 0) {
+            prefetch_tmap(&tmQ);
+            prefetch_tmap(&tmG);
+            mbar_expect_tx(kv_full, 2 * C::TILE);
+            for (int a = 0; a < C::ATOMS; ++a) {
+                tma_load_4d(smem + OFF_K + a * C::SLAB, &tmK, a * 64, key0, hk, b, kv_full);
+                tma_load_4d(smem + OFF_V + a * C::SLAB, &tmV, a * 64, key0, hk, b, kv_full);
+            }
+            int last = -1;
+            bool ok = true;
+            for (int it = 0; it < nit && ok; ++it) {
+                const int st = it & 1;
+                if (it >= 2) ok = mbar_wait(&st_empty[st], ((it >> 1) - 1) & 1, p.status, 41);
+                if (!ok || *(volatile int*)abort_flag) break;
+                const int g = it / nq, i = i_start + it % nq;
+                const int h = hk * p.group + g;
+                unsigned char* sb = smem + OFF_ST + st * ST_BYTES;
+                mbar_expect_tx(&st_full[st], ST_BYTES);
+                for (int a = 0; a < C::ATOMS; ++a) {
+                    tma_load_4d(sb + a * C::SLAB, &tmQ, a * 64, i * BT, h, b, &st_full[st]);
+                    tma_load_4d(sb + C::TILE + a * C::SLAB, &tmG, a * 64, i * BT, h, b, &st_full[st]);
+                }
+                const int64_t r0 = ((int64_t)b * p.H + h) * p.Lpad + (int64_t)i * BT;
+                bulk_load(sb + 2 * C::TILE, p.lse2 + r0, 512, &st_full[st]);
+                bulk_load(sb + 2 * C::TILE + 512, p.delta + r0, 512, &st_full[st]);
+                last = it;
+            }
+            if (!ok) *(volatile int*)abort_flag = 1;
+            if (*(volatile int*)abort_flag) {
+                mbar_wait(kv_full, 0, nullptr, 0);
+                for (int it = max(0, last - 1); it <= last; ++it) mbar_wait(&st_full[it & 1], (it >> 1) & 1, nullptr, 0);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && nit > 0) {
+            constexpr uint32_t IDESC_S = idesc_f16(BT, BT, BF16, false);
+            constexpr uint32_t IDESC_ACC = idesc_f16(BT, D, BF16, true);
+            const uint32_t k_addr = smem_u32(smem + OFF_K), v_addr = smem_u32(smem + OFF_V);
+            bool ok = mbar_wait(kv_full, 0, p.status, 42);
+            for (int it = 0; it < nit && ok; ++it) {
+                const int st = it & 1;
+                ok = mbar_wait(&st_full[st], (it >> 1) & 1, p.status, 43);
+                if (!ok || *(volatile int*)abort_flag) break;
+                tc_fence_after();
+                const uint32_t q_addr = smem_u32(smem + OFF_ST + st * ST_BYTES);
+                const uint32_t g_addr = q_addr + C::TILE;
+#pragma unroll
+                for (int kk = 0; kk < D / 16; ++kk)
+                    mma_ss(tmem + 256, kmajor(k_addr, kk, C::SLAB), kmajor(q_addr, kk, C::SLAB), IDESC_S, kk > 0);
+#pragma unroll
+                for (int kk = 0; kk < D / 16; ++kk)
+                    mma_ss(tmem + 384, kmajor(v_addr, kk, C::SLAB), kmajor(g_addr, kk, C::SLAB), IDESC_S, kk > 0);
+                mma_commit(s_full);
+                ok = mbar_wait(p_full, it & 1, p.status, 44);
+                if (!ok) break;
+                tc_fence_after();
+#pragma unroll
+                for (int kk = 0; kk < BT / 16; ++kk) {
+                    const uint32_t acc = (it > 0 || kk > 0) ? 1u : 0u;
+                    mma_ts(tmem + 0, tmem + 256 + kk * 8, mnmajor(g_addr, kk, C::SLAB), IDESC_ACC, acc);   // dV
+                    mma_ts(tmem + 128, tmem + 384 + kk * 8, mnmajor(q_addr, kk, C::SLAB), IDESC_ACC, acc); // dK
+                }
+                mma_commit(&st_empty[st]);
+            }
+            if (!ok) *(volatile int*)abort_flag = 1;
+            if (ok && !*(volatile int*)abort_flag) {
+                mma_commit(acc_final);
+            } else {
+                mma_commit(drain);
+                mbar_wait(drain, 0, nullptr, 0);
+            }
+        }
+    } else {
+        const int quad = warp & 3;
+        const int r = quad * 32 + lane;
+        const int key = key0 + r;
+        const uint32_t lane_addr = (uint32_t)(quad * 32) << 16;
+        bool ok = true;
+        for (int it = 0; it < nit; ++it) {
+            const int st = it & 1;
+            const int q0 = (i_start + it % nq) * BT;
+            ok = warp_wait(&st_full[st], (it >> 1) & 1, p.status, 45);  // lse2 / delta of this tile
+            if (ok) ok = warp_wait(s_full, it & 1, p.status, 46);
+            if (!ok || __any_sync(0xffffffffu, *(volatile int*)abort_flag)) break;
+            tc_fence_after();
+            const float* lse_s = (const float*)(smem + OFF_ST + st * ST_BYTES + 2 * C::TILE);
+            const float* dl_s = lse_s + 128;
+            const bool need_mask = p.causal && (q0 < key0 + BT - 1);
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                uint32_t ra[32], rb[32], pk[16], dk[16];
+                tmem_ld32(tmem + lane_addr + 256 + c * 32, ra);
+                tmem_ld32(tmem + lane_addr + 384 + c * 32, rb);
+                tmem_ld_wait();
+#pragma unroll
+                for (int i = 0; i < 32; i += 2) {
+                    float pv[2], dsv[2];
+#pragma unroll
+                    for (int u = 0; u < 2; ++u) {
+                        const int qc = c * 32 + i + u;
+                        float pr = ex2(fmaf(__uint_as_float(ra[i + u]), p.scale_log2, -lse_s[qc]));
+                        if (need_mask && key > q0 + qc) pr = 0.0f;
+                        pv[u] = pr;
+                        dsv[u] = pr * (__uint_as_float(rb[i + u]) - dl_s[qc]);
+                    }
+                    pk[i / 2] = pack2<BF16>(pv[0], pv[1]);
+                    dk[i / 2] = pack2<BF16>(dsv[0], dsv[1]);
+                }
+                tmem_st16(tmem + lane_addr + 256 + c * 16, pk);
+                tmem_st16(tmem + lane_addr + 384 + c * 16, dk);
+            }
+            tmem_st_wait();
+            tc_fence_before();
+            mbar_arrive(p_full);
+        }
+        if (!ok) *(volatile int*)abort_flag = 1;
+        if (nit > 0 && ok && !*(volatile int*)abort_flag) {
+            ok = warp_wait(acc_final, 0, p.status, 47);
+            if (ok) {
+                tc_fence_after();
+                T* dvrow = (T*)p.dv + (int64_t)b * p.vs0 + (int64_t)hk * p.vs1 + (int64_t)key * p.vs2;
+                T* dkrow = (T*)p.dk + (int64_t)b * p.ks0 + (int64_t)hk * p.ks1 + (int64_t)key * p.ks2;
+#pragma unroll
+                for (int c = 0; c < D / 32; ++c) {
+                    uint32_t v[32];
+                    tmem_ld32(tmem + lane_addr + c * 32, v);
+                    tmem_ld_wait();
+                    if (key < p.S) store_row32<BF16>(dvrow + c * 32, v, 1.0f);
+                    tmem_ld32(tmem + lane_addr + 128 + c * 32, v);
+                    tmem_ld_wait();
+                    if (key < p.S) store_row32<BF16>(dkrow + c * 32, v, p.scale);
+                }
+            } else {
+                *(volatile int*)abort_flag = 1;
+            }
+        } else if (nit == 0 && key < p.S) {
+            // no query sees this key block: its gradients are zero
+            T* dvrow = (T*)p.dv + (int64_t)b * p.vs0 + (int64_t)hk * p.vs1 + (int64_t)key * p.vs2;
+            T* dkrow = (T*)p.dk + (int64_t)b * p.ks0 + (int64_t)hk * p.ks1 + (int64_t)key * p.ks2;
+            for (int d = 0; d < D; d += 8) {
+                *(uint4*)(dvrow + d) = make_uint4(0, 0, 0, 0);
+                *(uint4*)(dkrow + d) = make_uint4(0, 0, 0, 0);
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, TMEM_COLS);
+    }
+}
+
+// ------------------------------------------------------------------ dQ
+
+struct DqP {
+    int64_t H, Hkv, L, S, Lpad;
+    int group, n_qt, n_kvt;
+    float scale_log2, scale;
+    int causal;
+    void* dq;
+    int64_t s0, s1, s2;
+    const float* lse2;
+    const float* delta;
+    int* status;
+};
+
+template <int D, bool BF16>
+__global__ void __launch_bounds__(NTHREADS, 1)
+bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+              const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmG, const DqP p) {
+    using C = BCfg<D>;
+    using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+    constexpr int OFF_Q = 0, OFF_G = C::TILE, OFF_K = 2 * C::TILE, OFF_V = 4 * C::TILE, OFF_BAR = 6 * C::TILE;
+    extern __shared__ unsigned char smem_raw[];
+    unsigned char* smem = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint64_t* bars = (uint64_t*)(smem + OFF_BAR);
+    uint64_t* qg_full = bars;
+    uint64_t* k_full = bars + 1;    // [2]
+    uint64_t* k_empty = bars + 3;   // [2]
+    uint64_t* v_full = bars + 5;    // [2]
+    uint64_t* v_empty = bars + 7;   // [2]
+    uint64_t* s_full = bars + 9;    // S and dP computed
+    uint64_t* ds_full = bars + 10;  // dS written (128 arrivals)
+    uint64_t* dq_final = bars + 11;
+    uint64_t* drain = bars + 12;
+    uint32_t* tmem_slot = (uint32_t*)(bars + 13);
+    int* abort_flag = (int*)(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int tile = p.causal ? (p.n_qt - 1 - (int)blockIdx.x) : (int)blockIdx.x;  // heavy tiles first
+    const int h = blockIdx.y, b = blockIdx.z;
+    const int hk = h / p.group;
+    const int row0 = tile * BT;
+    const int last_row = (int)min((int64_t)row0 + BT - 1, p.L - 1);
+    const int nblk = p.causal ? min(p.n_kvt, last_row / BT + 1) : p.n_kvt;
+
+    if (threadIdx.x == 0) {
+        mbar_init(qg_full, 1);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&k_full[i], 1); mbar_init(&k_empty[i], 1);
+            mbar_init(&v_full[i], 1); mbar_init(&v_empty[i], 1);
+        }
+        mbar_init(s_full, 1);
+        mbar_init(ds_full, 128);
+        mbar_init(dq_final, 1);
+        mbar_init(drain, 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) tmem_alloc(tmem_slot, TMEM_COLS);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            prefetch_tmap(&tmK);
+            prefetch_tmap(&tmV);
+            int last_k = -1, last_v = -1;
+            bool ok = true;
+            mbar_expect_tx(qg_full, 2 * C::TILE);
+            for (int a = 0; a < C::ATOMS; ++a) {
+                tma_load_4d(smem + OFF_Q + a * C::SLAB, &tmQ, a * 64, row0, h, b, qg_full);
+                tma_load_4d(smem + OFF_G + a * C::SLAB, &tmG, a * 64, row0, h, b, qg_full);
+            }
+            for (int j = 0; j < nblk && ok; ++j) {
+                const int s = j & 1;
+                if (j >= 2) ok = mbar_wait(&k_empty[s], ((j >> 1) - 1) & 1, p.status, 51);
+                if (!ok || *(volatile int*)abort_flag) break;
+                mbar_expect_tx(&k_full[s], C::TILE);
+                for (int a = 0; a < C::ATOMS; ++a)
+                    tma_load_4d(smem + OFF_K + s * C::TILE + a * C::SLAB, &tmK, a * 64, j * BT, hk, b, &k_full[s]);
+                last_k = j;
+                if (j >= 2) ok = mbar_wait(&v_empty[s], ((j >> 1) - 1) & 1, p.status, 52);
+                if (!ok || *(volatile int*)abort_flag) break;
+                mbar_expect_tx(&v_full[s], C::TILE);
+                for (int a = 0; a < C::ATOMS; ++a)
+                    tma_load_4d(smem + OFF_V + s * C::TILE + a * C::SLAB, &tmV, a * 64, j * BT, hk, b, &v_full[s]);
+                last_v = j;
+            }
+            if (!ok) *(volatile int*)abort_flag = 1;
+            if (*(volatile int*)abort_flag) {
+                mbar_wait(qg_full, 0, nullptr, 0);
+                for (int j = max(0, last_k - 1); j <= last_k; ++j) mbar_wait(&k_full[j & 1], (j >> 1) & 1, nullptr, 0);
+                for (int j = max(0, last_v - 1); j <= last_v; ++j) mbar_wait(&v_full[j & 1], (j >> 1) & 1, nullptr, 0);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t IDESC_S = idesc_f16(BT, BT, BF16, false);
+            constexpr uint32_t IDESC_DQ = idesc_f16(BT, D, BF16, true);
+            const uint32_t q_addr = smem_u32(smem + OFF_Q), g_addr = smem_u32(smem + OFF_G);
+            bool ok = mbar_wait(qg_full, 0, p.status, 53);
+            for (int j = 0; j < nblk && ok; ++j) {
+                const int s = j & 1;
+                const uint32_t k_addr = smem_u32(smem + OFF_K + s * C::TILE);
+                const uint32_t v_addr = smem_u32(smem + OFF_V + s * C::TILE);
+                ok = mbar_wait(&k_full[s], (j >> 1) & 1, p.status, 54);
+                if (!ok || *(volatile int*)abort_flag) break;
+                tc_fence_after();
+#pragma unroll
+                for (int kk = 0; kk < D / 16; ++kk)
+                    mma_ss(tmem + 0, kmajor(q_addr, kk, C::SLAB), kmajor(k_addr, kk, C::SLAB), IDESC_S, kk > 0);
+                ok = mbar_wait(&v_full[s], (j >> 1) & 1, p.status, 55);
+                if (!ok) break;
+                tc_fence_after();
+#pragma unroll
+                for (int kk = 0; kk < D / 16; ++kk)
+                    mma_ss(tmem + 128, kmajor(g_addr, kk, C::SLAB), kmajor(v_addr, kk, C::SLAB), IDESC_S, kk > 0);
+                mma_commit(s_full);
+                mma_commit(&v_empty[s]);
+                ok = mbar_wait(ds_full, j & 1, p.status, 56);
+                if (!ok) break;
+                tc_fence_after();
+#pragma unroll
+                for (int kk = 0; kk < BT / 16; ++kk)
+                    mma_ts(tmem + 256, tmem + 0 + kk * 8, mnmajor(k_addr, kk, C::SLAB), IDESC_DQ, (j > 0 || kk > 0) ? 1u : 0u);
+                mma_commit(&k_empty[s]);
+            }
+            if (!ok) *(volatile int*)abort_flag = 1;
+            if (ok && !*(volatile int*)abort_flag) {
+                mma_commit(dq_final);
+            } else {
+                mma_commit(drain);
+                mbar_wait(drain, 0, nullptr, 0);
+            }
+        }
+    } else {
+        const int quad = warp & 3;
+        const int r = quad * 32 + lane;
+        const int row = row0 + r;
+        const uint32_t lane_addr = (uint32_t)(quad * 32) << 16;
+        const int64_t prow = ((int64_t)b * p.H + h) * p.Lpad + row;  // row < Lpad
+        const float lse2 = p.lse2[prow];
+        const float dl = p.delta[prow];
+        const int lim_s = (int)min(p.S, (int64_t)INT32_MAX) - 1;
+        const int lim = p.causal ? min(lim_s, row) : lim_s;  // last key this row may see
+        bool ok = true;
+        for (int j = 0; j < nblk; ++j) {
+            ok = warp_wait(s_full, j & 1, p.status, 57);
+            if (!ok || __any_sync(0xffffffffu, *(volatile int*)abort_flag)) break;
+            tc_fence_after();
+            const int kv0 = j * BT;
+            const bool need_mask = (kv0 + BT > p.S) || (p.causal && kv0 + BT - 1 > row0);
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                uint32_t ra[32], rb[32], pk[16];
+                tmem_ld32(tmem + lane_addr + c * 32, ra);
+                tmem_ld32(tmem + lane_addr + 128 + c * 32, rb);
+                tmem_ld_wait();
+#pragma unroll
+                for (int i = 0; i < 32; i += 2) {
+                    float dsv[2];
+#pragma unroll
+                    for (int u = 0; u < 2; ++u) {
+                        float pr = ex2(fmaf(__uint_as_float(ra[i + u]), p.scale_log2, -lse2));
+                        if (need_mask && kv0 + c * 32 + i + u > lim) pr = 0.0f;
+                        dsv[u] = pr * (__uint_as_float(rb[i + u]) - dl);
+                    }
+                    pk[i / 2] = pack2<BF16>(dsv[0], dsv[1]);
+                }
+                tmem_st16(tmem + lane_addr + c * 16, pk);
+            }
+            tmem_st_wait();
+            tc_fence_before();
+            mbar_arrive(ds_full);
+        }
+        if (!ok) *(volatile int*)abort_flag = 1;
+        if (ok && !*(volatile int*)abort_flag) {
+            ok = warp_wait(dq_final, 0, p.status, 58);
+            if (ok) {
+                tc_fence_after();
+                T* qrow = (T*)p.dq + (int64_t)b * p.s0 + (int64_t)h * p.s1 + (int64_t)row * p.s2;
+#pragma unroll
+                for (int c = 0; c < D / 32; ++c) {
+                    uint32_t v[32];
+                    tmem_ld32(tmem + lane_addr + 256 + c * 32, v);
+                    tmem_ld_wait();
+                    if (row < p.L) store_row32<BF16>(qrow + c * 32, v, p.scale);
+                }
+            } else {
+                *(volatile int*)abort_flag = 1;
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, TMEM_COLS);
+    }
+}
+
+// ------------------------------------------------------------------ host side
+
+bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
+
+bool fast_view(const gtb_tensor4& t, int dtype) {
+    if (t.dtype != dtype || t.stride[3] != 1 || !aligned16(t.data)) return false;
+    for (int i = 0; i < 3; ++i)
+        if (t.shape[i] > 1 && t.stride[i] % 8 != 0) return false;
+    return true;
+}
+
+int64_t lpad_of(int64_t L) { return (L + BT - 1) / BT * BT; }
+
+template <int D, bool BF16>
+int run_bwd(const BwdArgs& a, cudaStream_t st) {
+    using C = BCfg<D>;
+    const int64_t B = a.sh.B, H = a.sh.H, L = a.sh.L, S = a.sh.S, Lpad = lpad_of(L);
+    float* lse2 = (float*)a.scratch;
+    float* delta = lse2 + B * H * Lpad;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    int* status = device_status_word(dev);
+
+    PreP pp{a.o.data, a.dout.data, a.o.stride[0], a.o.stride[1], a.o.stride[2], a.dout.stride[0], a.dout.stride[1],
+            a.dout.stride[2], (const float*)a.lse, lse2, delta, B, H, L, Lpad, a.sh.Dv};
+    const int64_t rows = B * H * Lpad;
+    using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+    bwd_pre_kernel<T><<<(unsigned)((rows + 3) / 4), 128, 0, st>>>(pp);
+    if (cuda_failed(cudaGetLastError(), "flash_attention_backward: preprocess launch")) return -1;
+
+    CUtensorMap mq, mk, mv, mg;
+    if (!make_tma_map_4d(&mq, a.q, D, BF16, BT) || !make_tma_map_4d(&mk, a.k, D, BF16, BT) ||
+        !make_tma_map_4d(&mv, a.v, D, BF16, BT) || !make_tma_map_4d(&mg, a.dout, D, BF16, BT))
+        return -1;
+    const int n_qt = (int)((L + BT - 1) / BT), n_kvt = (int)((S + BT - 1) / BT);
+    const int group = (int)(H / a.sh.Hkv);
+    const float scale_log2 = a.scale * LOG2E;
+
+    static bool attr_set = false;
+    constexpr int SMEM_KV = 2 * C::TILE + 2 * (2 * C::TILE + 1024) + 16 * 8 + 1024;
+    constexpr int SMEM_DQ = 6 * C::TILE + 16 * 8 + 1024;
+    if (!attr_set) {
+        if (cuda_failed(cudaFuncSetAttribute(bwd_dkdv_kernel<D, BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             SMEM_KV), "cudaFuncSetAttribute(bwd dkdv)") ||
+            cuda_failed(cudaFuncSetAttribute(bwd_dq_kernel<D, BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             SMEM_DQ), "cudaFuncSetAttribute(bwd dq)"))
+            return -1;
+        attr_set = true;
+    }
+    KvP kp{H, a.sh.Hkv, L, S, Lpad, group, n_qt, n_kvt, scale_log2, a.scale, a.causal,
+           a.dk.data, a.dk.stride[0], a.dk.stride[1], a.dk.stride[2],
+           a.dv.data, a.dv.stride[0], a.dv.stride[1], a.dv.stride[2], lse2, delta, status};
+    bwd_dkdv_kernel<D, BF16><<<dim3((unsigned)n_kvt, (unsigned)a.sh.Hkv, (unsigned)B), NTHREADS, SMEM_KV, st>>>(
+        mq, mk, mv, mg, kp);
+    if (cuda_failed(cudaGetLastError(), "flash_attention_backward: dK/dV launch")) return -1;
+    DqP dp{H, a.sh.Hkv, L, S, Lpad, group, n_qt, n_kvt, scale_log2, a.scale, a.causal,
+           a.dq.data, a.dq.stride[0], a.dq.stride[1], a.dq.stride[2], lse2, delta, status};
+    bwd_dq_kernel<D, BF16><<<dim3((unsigned)n_qt, (unsigned)H, (unsigned)B), NTHREADS, SMEM_DQ, st>>>(mq, mk, mv, mg, dp);
+    return cuda_failed(cudaGetLastError(), "flash_attention_backward: dQ launch") ? -1 : 0;
+}
+
+}  // namespace
+
+bool bwd_sm100_supported(const BwdArgs& a) {
+    if (a.has_mask) return false;
+    const int dt = a.q.dtype;
+    if (dt != BF16 && dt != F16) return false;
+    if (a.sh.D != a.sh.Dv || (a.sh.D != 64 && a.sh.D != 128)) return false;
+    const gtb_tensor4* ts[] = {&a.q, &a.k, &a.v, &a.o, &a.dout, &a.dq, &a.dk, &a.dv};
+    for (const gtb_tensor4* t : ts)
+        if (!fast_view(*t, dt)) return false;
+    if (a.sh.L < 1 || a.sh.S < 1 || a.sh.L >= (1ll << 30) || a.sh.S >= (1ll << 30)) return false;
+    if (a.sh.H > 65535 || a.sh.B > 65535 || a.sh.Hkv > 65535) return false;
+    return encode_fn() != nullptr;
+}
+
+size_t bwd_sm100_scratch_bytes(const BwdArgs& a) {
+    return 2 * sizeof(float) * (size_t)(a.sh.B * a.sh.H * lpad_of(a.sh.L));
+}
+
+int launch_bwd_sm100(const BwdArgs& a, cudaStream_t st) {
+    const bool bf16 = a.q.dtype == BF16;
+    if (a.sh.D == 128) return bf16 ? run_bwd<128, true>(a, st) : run_bwd<128, false>(a, st);
+    return bf16 ? run_bwd<64, true>(a, st) : run_bwd<64, false>(a, st);
+}
+
+}  // namespace gtb

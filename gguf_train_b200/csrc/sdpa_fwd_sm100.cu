@@ -401,6 +401,8 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
     }
 }
 
+}  // namespace
+
 // ------------------------------------------------------------------ host side
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -416,8 +418,8 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     return fn;
 }
 
-// 4-D map over (d, row, head, batch) with a 64 x 128 box and 128-byte swizzle
-bool make_map(CUtensorMap* tm, const gtb_tensor4& t, int64_t d_extent, bool bf16) {
+// 4-D map over (d, row, head, batch) with a 64 x box_rows box and 128-byte swizzle
+bool make_tma_map_4d(CUtensorMap* tm, const gtb_tensor4& t, int64_t d_extent, bool bf16, int box_rows) {
     auto enc = encode_fn();
     if (!enc) {
         set_error("flash_attention: cuTensorMapEncodeTiled is unavailable");
@@ -440,7 +442,7 @@ bool make_map(CUtensorMap* tm, const gtb_tensor4& t, int64_t d_extent, bool bf16
         }
         strides[i] = (cuuint64_t)bytes;
     }
-    cuuint32_t box[4] = {64, (cuuint32_t)BM, 1, 1};
+    cuuint32_t box[4] = {64, (cuuint32_t)box_rows, 1, 1};
     cuuint32_t estr[4] = {1, 1, 1, 1};
     CUresult r = enc(tm, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, t.data, dims,
                      strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -451,6 +453,8 @@ bool make_map(CUtensorMap* tm, const gtb_tensor4& t, int64_t d_extent, bool bf16
     }
     return true;
 }
+
+namespace {
 
 bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
 
@@ -525,7 +529,8 @@ bool fwd_sm100_supported(const FwdArgs& a) {
 int launch_fwd_sm100(const FwdArgs& a, cudaStream_t st) {
     const bool bf16 = a.q.dtype == BF16;
     CUtensorMap mq, mk, mv;
-    if (!make_map(&mq, a.q, a.sh.D, bf16) || !make_map(&mk, a.k, a.sh.D, bf16) || !make_map(&mv, a.v, a.sh.Dv, bf16))
+    if (!make_tma_map_4d(&mq, a.q, a.sh.D, bf16, BM) || !make_tma_map_4d(&mk, a.k, a.sh.D, bf16, BN) ||
+        !make_tma_map_4d(&mv, a.v, a.sh.Dv, bf16, BN))
         return -1;
     if (a.sh.D == 128) return bf16 ? run_emu<128, true>(a, mq, mk, mv, st) : run_emu<128, false>(a, mq, mk, mv, st);
     return bf16 ? run_emu<64, true>(a, mq, mk, mv, st) : run_emu<64, false>(a, mq, mk, mv, st);

@@ -97,6 +97,11 @@ BWD_CASES = [
     ("f64", 1, 2, 2, 4, 4, 8, 8, True, None),
     ("bf16", 1, 4, 2, 200, 200, 128, 128, True, None),
     ("f16", 1, 2, 2, 130, 70, 64, 64, False, None),
+    ("bf16", 1, 4, 1, 384, 384, 128, 128, True, None),   # tcgen05 backward: GQA group of 4, 3 tiles
+    ("bf16", 1, 2, 2, 300, 170, 128, 128, True, None),   # causal with L > S
+    ("bf16", 1, 2, 1, 150, 400, 128, 128, True, None),   # causal with L < S (key blocks no query sees)
+    ("bf16", 2, 2, 2, 256, 256, 64, 64, True, None),     # D = 64
+    ("f16", 1, 2, 2, 129, 129, 128, 128, False, None),
 ]
 
 
@@ -211,3 +216,30 @@ def test_gradcheck_float64_causal():
     O.manual_seed(11)
     q, k, v = (to_dev(seeded((1, 2, 4, 8), "f64"), "f64", True) for _ in range(3))
     assert torch.autograd.gradcheck(lambda a, b, c: gtb.scaled_dot_product_attention(a, b, c, is_causal=True), (q, k, v))
+
+
+def test_backward_sampled_group_at_larger_size():
+    """Causal GQA backward at L = S = 1024 (B=2, H=8, Hkv=2): the whole batch on the GPU, one
+    (batch, kv head) group checked against the oracle (groups are independent)."""
+    import torch
+
+    import gguf_train_b200 as gtb
+    from gguf_train_b200 import _C
+
+    O.manual_seed(77)
+    B, H, Hkv, L, D = 2, 8, 2, 1024, 128
+    q = seeded((B, H, L, D), "bf16", 0.5)
+    k = seeded((B, Hkv, L, D), "bf16", 0.5)
+    v = seeded((B, Hkv, L, D), "bf16", 0.5)
+    g = seeded((B, H, L, D), "bf16")
+    tq, tk, tv = (to_dev(x, "bf16", True) for x in (q, k, v))
+    out = gtb.scaled_dot_product_attention(tq, tk, tv, is_causal=True)
+    out.backward(to_dev(g, "bf16"))
+    assert _C.device_status() == 0
+    b, hk, G = 1, 1, H // Hkv
+    hs = slice(hk * G, (hk + 1) * G)
+    dq, dk, dv = O.sdpa_bwd(q[b:b + 1, hs], k[b:b + 1, hk:hk + 1], v[b:b + 1, hk:hk + 1], g[b:b + 1, hs], is_causal=True)
+    assert_close(tq.grad[b:b + 1, hs], dq, 2e-2, 1e-2, "dq sampled group")
+    assert_close(tk.grad[b:b + 1, hk:hk + 1], dk, 2e-2, 1e-2, "dk sampled group")
+    assert_close(tv.grad[b:b + 1, hk:hk + 1], dv, 2e-2, 1e-2, "dv sampled group")
+    del torch
