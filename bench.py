@@ -42,7 +42,7 @@ if ROOT not in sys.path:
 METRIC = "SDPA TFLOP/s (fwd, fwd+bwd) & decode KV GB/s, % of B200 peak, 1/2/4/8 GPUs"
 CFG = dict(B=8, H=32, Hkv=8, L=4096, D=128)
 WORKLOAD = "config 3: causal GQA prefill forward, bf16, B=8 Hq=32 Hkv=8 L=S=4096 D=128"
-FALLBACK_PEAKS = {"bf16_tflops": 1590.0, "hbm_gbs": 6650.0}
+FALLBACK_PEAKS = {"bf16_tflops": 1590.0, "hbm_gbs": 6650.0, "bf16_tflops_sustained": 1400.0}
 
 
 def fwd_flops(B, H, L, D, causal=True):
@@ -55,18 +55,20 @@ def load_peaks():
     try:
         with open(path) as f:
             p = json.load(f)
-        return {"bf16_tflops": float(p["bf16_tflops"]), "hbm_gbs": float(p["hbm_gbs"]), "source": "measured"}
+        return {"bf16_tflops": float(p["bf16_tflops"]), "hbm_gbs": float(p["hbm_gbs"]),
+                "bf16_tflops_sustained": float(p.get("bf16_tflops_sustained", p["bf16_tflops"])), "source": "measured"}
     except Exception:
         return dict(FALLBACK_PEAKS, source="fallback")
 
 
-def profile_traffic(name: str):
+def profile_traffic(name: str, kernel: str = ""):
     """DRAM bytes per launch recorded in the committed ncu summary profiles/<name>.md
-    (a line 'traffic_bytes_per_launch: N'), or None."""
+    (a line 'traffic_bytes_per_launch: N', or 'traffic_bytes_per_launch (kernel): N'), or None."""
     path = os.path.join(ROOT, "profiles", name + ".md")
+    tag = r"\s*\(" + re.escape(kernel) + r"\)" if kernel else ""
     try:
         with open(path) as f:
-            m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", f.read())
+            m = re.search(r"traffic_bytes_per_launch" + tag + r":\s*([0-9.eE+]+)", f.read())
         return float(m.group(1)) if m else None
     except OSError:
         return None
@@ -183,7 +185,7 @@ class ClockSampler:
 DEC = dict(B=64, H=32, Hkv=8, D=128, Smax=32768, Lmin=1024)
 
 
-def run_decode(args, rank: int, world: int, local: int) -> None:
+def run_decode(args, rank: int, world: int, dev, max_over_ranks=lambda x: x) -> dict:
     """Config 5a: one decode step of B=64 sequences (Hq=32, Hkv=8, D=128) against Q8_0 K/V caches
     with lengths uniform in [1024, 32768]; q fp16. Metric: cache bytes read per second (HBM-bound)."""
     import torch
@@ -191,8 +193,6 @@ def run_decode(args, rank: int, world: int, local: int) -> None:
     import gguf_train_b200 as gtb
     from gguf_train_b200 import _C
 
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
     B, H, Hkv, D, Smax = DEC["B"], DEC["H"], DEC["Hkv"], DEC["D"], DEC["Smax"]
     g = torch.Generator(device=dev)
     g.manual_seed(77 + rank)
@@ -222,7 +222,7 @@ def run_decode(args, rank: int, world: int, local: int) -> None:
             e.record(stream)
             torch.cuda.synchronize(dev)
             times.append(s.elapsed_time(e))
-    ms = statistics.mean(times)
+    ms = max_over_ranks(statistics.mean(times))
     peaks = load_peaks()
     gbs = nbytes / (ms * 1e-3) / 1e9
     line = {
@@ -236,8 +236,68 @@ def run_decode(args, rank: int, world: int, local: int) -> None:
                      "peak_source": peaks["source"] + " HBM copy"},
         "gpu_launches": 2 * args.steps, "clocks": sampler.summary(), "status": _C.device_status(),
     }
-    if rank == 0:
-        print(json.dumps(line), flush=True)
+    del kq, vq, flush
+    torch.cuda.empty_cache()
+    return line
+
+
+# ------------------------------------------------------------------ training workload (config 4)
+
+TRAIN = dict(B=4, H=32, Hkv=8, L=8192, D=128)
+
+
+def run_train(args, rank: int, world: int, dev, max_over_ranks=lambda x: x) -> dict:
+    """Config 4: causal GQA attention forward + backward, bf16, B=4 Hq=32 Hkv=8 L=S=8192 D=128,
+    q/k/v N(0,1)*0.5 and upstream gradient N(0,1). Work per step: forward 4*B*Hq*L(L+1)/2*D FLOP and
+    backward twice that (the 4-GEMM convention; the kernels recompute S and dP, which is not credited)."""
+    import torch
+
+    from gguf_train_b200 import _C
+    from gguf_train_b200 import functional as Fn
+
+    B, H, Hkv, L, D = TRAIN["B"], TRAIN["H"], TRAIN["Hkv"], TRAIN["L"], TRAIN["D"]
+    g = torch.Generator(device=dev)
+    g.manual_seed(4321 + rank)
+    q = (torch.randn((B, H, L, D), generator=g, device=dev) * 0.5).to(torch.bfloat16)
+    k = (torch.randn((B, Hkv, L, D), generator=g, device=dev) * 0.5).to(torch.bfloat16)
+    v = (torch.randn((B, Hkv, L, D), generator=g, device=dev) * 0.5).to(torch.bfloat16)
+    gd = torch.randn((B, H, L, D), generator=g, device=dev).to(torch.bfloat16)
+    scale = 1.0 / math.sqrt(D)
+    fwd = fwd_flops(B, H, L, D)
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(max(args.warmup, 3)):
+        out, lse = Fn.sdpa_forward(q, k, v, None, scale, True)
+        Fn.sdpa_backward(gd, q, k, v, None, out, lse, scale, True)
+    torch.cuda.synchronize(dev)
+    steps = max(3, min(args.steps, 20))
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(steps)]
+    for i in range(steps):
+        ev[i][0].record(stream)
+        out, lse = Fn.sdpa_forward(q, k, v, None, scale, True)
+        ev[i][1].record(stream)
+        Fn.sdpa_backward(gd, q, k, v, None, out, lse, scale, True)
+        ev[i][2].record(stream)
+    torch.cuda.synchronize(dev)
+    f_ms = max_over_ranks(statistics.mean(e[0].elapsed_time(e[1]) for e in ev))
+    b_ms = max_over_ranks(statistics.mean(e[1].elapsed_time(e[2]) for e in ev))
+    peaks = load_peaks()
+    tf = 3 * fwd / ((f_ms + b_ms) * 1e-3) / 1e12
+    line = {
+        "workload": "config 4: causal GQA forward+backward, bf16, B=4 Hq=32 Hkv=8 L=S=8192 D=128",
+        "value": tf * world, "unit": "TFLOP/s", "ms_per_step": f_ms + b_ms, "fwd_ms": f_ms, "bwd_ms": b_ms,
+        "flops_per_step": 3 * fwd,
+        "roofline": {"bound": "tensor", "achieved": tf, "peak": peaks["bf16_tflops_sustained"], "unit": "TFLOP/s",
+                     "frac": tf / peaks["bf16_tflops_sustained"],
+                     "peak_source": peaks["source"] + " bf16 dense (sustained)",
+                     "backward_tflops": 2 * fwd / (b_ms * 1e-3) / 1e12, "forward_tflops": fwd / (f_ms * 1e-3) / 1e12},
+        "launches_per_step": "forward 1, backward 3 (preprocess, dK/dV, dQ)",
+        "gpu_launches": 4 * steps, "status": _C.device_status(),
+    }
+    line["roofline"]["traffic_bwd_dkdv"] = profile_traffic("bwd_sm100_config4", "dkdv")
+    line["roofline"]["traffic_bwd_dq"] = profile_traffic("bwd_sm100_config4", "dq")
+    del q, k, v, gd, out, lse
+    torch.cuda.empty_cache()
+    return line
 
 
 # ------------------------------------------------------------------ GPU arm
@@ -250,8 +310,10 @@ def main() -> None:
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="prefill", choices=["prefill", "decode"],
-                    help="prefill: config 3 (the default line); decode: config 5a, Q8_0 KV cache")
+    ap.add_argument("--workload", default="prefill", choices=["prefill", "decode", "train"],
+                    help="prefill: config 3 (the default line); train: config 4 fwd+bwd; decode: config 5a")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="default line without the fwd+bwd (config 4) and decode (config 5a) measurements")
     args = ap.parse_args()
 
     rank = int(os.environ.get("RANK", "0"))
@@ -259,9 +321,6 @@ def main() -> None:
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         run_reference(args, rank)
-        return
-    if args.workload == "decode":
-        run_decode(args, rank, world, local)
         return
 
     import torch
@@ -287,6 +346,22 @@ def main() -> None:
         t = torch.tensor([x], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
+
+    if args.workload in ("decode", "train"):
+        barrier()
+        runner = run_decode if args.workload == "decode" else run_train
+        res = runner(args, rank, world, dev, max_over_ranks)
+        if args.workload == "train":
+            res = dict(metric=METRIC, n_gpus=world, steps=max(3, min(args.steps, 20)), warmup=max(args.warmup, 3),
+                       higher_is_better=True, scaling="weak", vs_baseline=None, dtype="bf16",
+                       data="synthetic: seeded normal inputs generated on the device",
+                       config={"workload": res.pop("workload")}, **res)
+        if world > 1:
+            barrier()
+            dist.destroy_process_group()
+        if rank == 0:
+            print(json.dumps(res), flush=True)
+        return
 
     B, H, Hkv, L, D = CFG["B"], CFG["H"], CFG["Hkv"], CFG["L"], CFG["D"]
     g = torch.Generator(device=dev)
@@ -383,6 +458,13 @@ def main() -> None:
         "clocks": sampler.summary(),
         "status": status,
     }
+    if not args.no_extra:
+        del q, k, v, qh, kh, vh, oh, qd, kd, vd
+        torch.cuda.empty_cache()
+        barrier()
+        line["extra"] = {"fwd_bwd": run_train(args, rank, world, dev, max_over_ranks)}
+        barrier()
+        line["extra"]["decode_q8_0"] = run_decode(args, rank, world, dev, max_over_ranks)
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
         cv, threads, desc = cpu_sample(2)
         line["cpu_baseline"] = {"value": cv, "unit": "TFLOP/s", "cores": threads, "kind": "port", "sample": desc}
