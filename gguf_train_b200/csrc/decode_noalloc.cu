@@ -12,7 +12,8 @@
 // address with cudaGetSymbolAddress; a host-side use of the array's name would not be a device
 // address. That first call should come before any stream capture. Calls share the array: two calls
 // whose kernels overlap on the GPU (other streams, other threads) race on it. Nothing in it has to
-// start at zero: every partial record the combine step reads is written earlier in the same call.
+// start at zero: the work area (item counter and per-sequence item prefix) and every partial record
+// the combine step reads are written earlier in the same call.
 
 #include <cmath>
 #include <mutex>
@@ -101,7 +102,8 @@ extern "C" GTB_API int gtb_decode_q8_0_noalloc(const void* q, int q_dtype, const
     const size_t need = decode_scratch_bytes(B, H, Hkv, Smax, D);
     if (need > (size_t)GTB_DECODE_NOALLOC_SCRATCH_BYTES) {
         set_errorf("%s: this call needs %zu bytes of scratch, more than the fixed %zu bytes this entry point has "
-                   "(B * Hkv * ceil(Smax / %d) * (H / Hkv) * (D + 2) * 4); use gtb_decode_q8_0",
+                   "(B * Hkv * ceil(Smax / %d) * (H / Hkv) * (D + 2) * 4, plus 4 * (B + 2) rounded up to 256); "
+                   "use gtb_decode_q8_0",
                    ctx, need, (size_t)GTB_DECODE_NOALLOC_SCRATCH_BYTES, GTB_DECODE_CHUNK);
         return -1;
     }

@@ -338,8 +338,8 @@ GTB_API int gtb_decode_q8_0(const void* q, int q_dtype, const void* k_q8, const 
     const size_t bytes = decode_scratch_bytes(B, H, Hkv, Smax, D);
     keep_pool_memory(dev);
     void* scratch = nullptr;
-    if (bytes && cuda_failed(cudaMallocAsync(&scratch, bytes, st), "flash_decode_q8_0: scratch allocation")) return -1;
-    const int rc = launch_decode_q8_0(a, (float*)scratch, st);
+    if (cuda_failed(cudaMallocAsync(&scratch, bytes, st), "flash_decode_q8_0: scratch allocation")) return -1;
+    const int rc = launch_decode_q8_0(a, scratch, st);
     if (scratch) cudaFreeAsync(scratch, st);
     return rc;
 }

@@ -478,16 +478,20 @@ int64_t decode_num_chunks(int64_t Smax) {
     return Smax <= 0 ? 1 : (Smax + GTB_DECODE_CHUNK - 1) / GTB_DECODE_CHUNK;
 }
 
-size_t decode_scratch_bytes(int64_t B, int64_t H, int64_t Hkv, int64_t Smax, int64_t D) {
-    const int64_t nch = decode_num_chunks(Smax);
-    if (nch <= 1) return 0;
-    return (size_t)B * Hkv * nch * (H / Hkv) * (D + 2) * sizeof(float);
+size_t decode_work_bytes(int64_t B) {
+    return (size_t)((B + 2) * sizeof(int) + 255) / 256 * 256;
 }
 
-int launch_decode_q8_0(const DecodeArgs& a, float* scratch, cudaStream_t st) {
+size_t decode_scratch_bytes(int64_t B, int64_t H, int64_t Hkv, int64_t Smax, int64_t D) {
+    const int64_t nch = decode_num_chunks(Smax);
+    const size_t part = nch <= 1 ? 0 : (size_t)B * Hkv * nch * (H / Hkv) * (D + 2) * sizeof(float);
+    return decode_work_bytes(B) + part;
+}
+
+int launch_decode_q8_0(const DecodeArgs& a, void* scratch, cudaStream_t st) {
     DecP p;
     p.q = a.q; p.q_dtype = a.q_dtype; p.k = (const uint8_t*)a.k; p.v = (const uint8_t*)a.v;
-    p.lens = a.lens; p.out = a.out; p.part = scratch;
+    p.lens = a.lens; p.out = a.out;
     p.B = a.B; p.H = a.H; p.Hkv = a.Hkv; p.Smax = a.Smax; p.D = a.D; p.G = a.H / a.Hkv;
     p.nchunks = decode_num_chunks(a.Smax);
     p.chunk = GTB_DECODE_CHUNK;
@@ -499,9 +503,19 @@ int launch_decode_q8_0(const DecodeArgs& a, float* scratch, cudaStream_t st) {
     p.bulk = ((uintptr_t)a.k % 16 == 0) && ((uintptr_t)a.v % 16 == 0) && (a.Smax % p.rows_align == 0);
     p.status = a.status;
     p.nhg = 1;
-    if (p.nchunks > 1 && scratch == nullptr) {
+    if (scratch == nullptr) {
         set_error("decode_q8_0: scratch buffer missing");
         return -1;
+    }
+    p.part = (float*)((char*)scratch + decode_work_bytes(a.B));
+    if (decode_sm100_supported(a)) {
+        if (launch_decode_sm100(a, (int*)scratch, p.part, p.nchunks, st) != 0) return -1;
+        if (p.nchunks > 1) {
+            dim3 g2((unsigned)p.H, (unsigned)p.B);
+            decode_combine_kernel<<<g2, (unsigned)p.D, 0, st>>>(p);
+            if (cuda_failed(cudaGetLastError(), "decode_q8_0 combine launch")) return -1;
+        }
+        return 0;
     }
     switch (a.D) {
         case 64: return run_decode<64>(p, st);

@@ -22,7 +22,15 @@ struct DecodeArgs {
 int launch_q8_0_quantize(const void* x, int x_dtype, int64_t nblocks, void* out, cudaStream_t st);
 int launch_q8_0_dequantize(const void* blocks, int64_t nblocks, void* out, int out_dtype, cudaStream_t st);
 int64_t decode_num_chunks(int64_t Smax);
+// Scratch of one decode call: a work area of decode_work_bytes(B) (the tensor-core kernel's item
+// counter and per-sequence item prefix), then the split-KV partials [B][Hkv][nchunks][G][D + 2] f32.
+size_t decode_work_bytes(int64_t B);
 size_t decode_scratch_bytes(int64_t B, int64_t H, int64_t Hkv, int64_t Smax, int64_t D);
-int launch_decode_q8_0(const DecodeArgs& a, float* scratch, cudaStream_t st);
+int launch_decode_q8_0(const DecodeArgs& a, void* scratch, cudaStream_t st);
+
+// tcgen05 decode (decode_sm100.cu): D = 128, f16 q, H/Hkv in {1, 2, 4, 8}, even Smax, 16-byte
+// aligned q/k/v. Launches the plan kernel and the persistent kernel; partials as above.
+bool decode_sm100_supported(const DecodeArgs& a);
+int launch_decode_sm100(const DecodeArgs& a, int* work, float* part, int64_t nchunks, cudaStream_t st);
 
 }  // namespace gtb

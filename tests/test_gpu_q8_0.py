@@ -48,7 +48,7 @@ def test_dequantize_round_trip():
     assert cos > 0.999  # the reference's own check is cosine > 0.85 (test_gguf_and_llama.py:66-79)
 
 
-def _decode_case(B, H, Hkv, Smax, D, lens, qdtype="f16", seed=5):
+def _decode_case(B, H, Hkv, Smax, D, lens, qdtype="f16", seed=5, kscale=1.0, vscale=1.0):
     import torch
 
     import gguf_train_b200 as gtb
@@ -56,8 +56,8 @@ def _decode_case(B, H, Hkv, Smax, D, lens, qdtype="f16", seed=5):
 
     O.manual_seed(seed)
     q = seeded((B, H, 1, D), qdtype)
-    kf = O.randn(B, Hkv, Smax, D).astype(np.float32)
-    vf = O.randn(B, Hkv, Smax, D).astype(np.float32)
+    kf = (O.randn(B, Hkv, Smax, D) * kscale).astype(np.float32)
+    vf = (O.randn(B, Hkv, Smax, D) * vscale).astype(np.float32)
     kq = O.q8_0_quantize(kf)
     vq = O.q8_0_quantize(vf)
     want = O.decode_q8_0(q, kq, vq, np.asarray(lens, np.int32), Hkv, Smax)
@@ -66,7 +66,9 @@ def _decode_case(B, H, Hkv, Smax, D, lens, qdtype="f16", seed=5):
     tv = torch.tensor(vq.reshape(B, Hkv, Smax, row)).cuda()
     got = gtb.decode_q8_0(to_dev(q, qdtype), tk, tv, torch.tensor(lens, dtype=torch.int32).cuda())
     assert _C.device_status() == 0
-    assert_close(got, want, 2e-2, 1e-2, f"decode B={B} H={H} Hkv={Hkv} Smax={Smax} D={D} lens={lens}")
+    # outputs are compared in units of the V scale, so that the absolute tolerance keeps its meaning
+    assert_close(got.double() / vscale, want / vscale, 2e-2, 1e-2,
+                 f"decode B={B} H={H} Hkv={Hkv} Smax={Smax} D={D} lens={lens}")
     return got
 
 
@@ -80,6 +82,32 @@ def _decode_case(B, H, Hkv, Smax, D, lens, qdtype="f16", seed=5):
 ])
 def test_decode_matches_oracle(B, H, Hkv, Smax, D, lens):
     _decode_case(B, H, Hkv, Smax, D, lens)
+
+
+# D = 128 with an f16 query, H/Hkv in {1, 2, 4, 8} and an even Smax run on the tensor-core kernel
+# (persistent CTAs, 128-row tiles, chunks of 1024 rows): tile and chunk edges, group sizes, and
+# rows past the end of a sequence inside a tile.
+@pytest.mark.parametrize("B,H,Hkv,Smax,D,lens", [
+    (4, 8, 8, 2050, 128, [1, 127, 128, 129]),           # group of 1, ragged first tiles
+    (4, 16, 2, 2050, 128, [1023, 1024, 1025, 2050]),    # group of 8, chunk edges
+    (3, 32, 8, 4096, 128, [4096, 2049, 640]),           # the config-5a group (4), several chunks
+    (2, 4, 2, 256, 128, [256, 255]),                    # one chunk: normalised directly
+])
+def test_decode_tensor_core_path(B, H, Hkv, Smax, D, lens):
+    _decode_case(B, H, Hkv, Smax, D, lens)
+
+
+def test_decode_many_sequences():
+    # more sequences than the plan kernel's 1024 threads: each thread scans a segment of lengths
+    rng = np.random.default_rng(11)
+    lens = rng.integers(0, 9, size=1100).tolist()
+    _decode_case(1100, 4, 2, 8, 128, lens)
+
+
+def test_decode_cache_scales():
+    # tiny V scales (block scales near the f16 subnormal range) and large K scales (a peaked softmax)
+    _decode_case(2, 8, 2, 600, 128, [600, 311], vscale=1e-5, kscale=30.0)
+    _decode_case(2, 8, 2, 600, 128, [599, 1], vscale=300.0)
 
 
 def test_decode_bf16_and_f32_queries():
