@@ -194,6 +194,8 @@ def run_decode(args, rank: int, world: int, dev, max_over_ranks=lambda x: x) -> 
     from gguf_train_b200 import _C
 
     B, H, Hkv, D, Smax = DEC["B"], DEC["H"], DEC["Hkv"], DEC["D"], DEC["Smax"]
+    if getattr(args, "decode_batch", None):
+        B = args.decode_batch  # smaller case of the same kernel (profiling); the workload line says so
     g = torch.Generator(device=dev)
     g.manual_seed(77 + rank)
     lens = torch.randint(DEC["Lmin"], Smax + 1, (B,), generator=g, device=dev).to(torch.int32)
@@ -229,7 +231,7 @@ def run_decode(args, rank: int, world: int, dev, max_over_ranks=lambda x: x) -> 
         "metric": METRIC, "value": gbs * world, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": max(args.warmup, 3), "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "q8_0 K/V, f16 q", "data": "synthetic: N(0,1) K/V quantised to Q8_0",
-        "config": {"workload": "config 5a: Q8_0-KV decode, B=64 Hq=32 Hkv=8 D=128, L_b ~ U[1024, 32768]",
+        "config": {"workload": f"config 5a: Q8_0-KV decode, B={B} Hq=32 Hkv=8 D=128, L_b ~ U[1024, 32768]",
                    "tokens": tokens, "bytes_per_step": nbytes, "l2": "256 MB flush before every step"},
         "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": gbs / peaks["hbm_gbs"], "traffic": profile_traffic("decode_q8_0_config5a"),
@@ -311,6 +313,8 @@ def main() -> None:
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--decode-batch", type=int, default=None,
+                    help="sequences of the decode workload (default: config 5a's 64; smaller for profiling)")
     ap.add_argument("--workload", default="prefill", choices=["prefill", "decode", "train"],
                     help="prefill: config 3 (the default line); train: config 4 fwd+bwd; decode: config 5a")
     ap.add_argument("--no-extra", action="store_true",

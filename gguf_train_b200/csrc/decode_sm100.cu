@@ -30,9 +30,10 @@
 // largest |dV| of the tile at 2^14, away from f16 subnormals for small-scale caches (p <= 1).
 //
 // Phase rule: a parity wait cannot tell phase n from phase n+2, so no barrier may complete twice
-// while one of its waiters is still behind. K of tile i+1 depends only on the softmax of tile i-1,
-// so the K-ready barrier is double-buffered by tile parity; every other barrier's next phase needs
-// its waiters to have passed (the V tile needs PV, PV needs the softmax, S needs the K tile...).
+// while one of its waiters is still behind. The K tile of i+1 depends only on the softmax of tile
+// i-1, so the K-ready barrier is double-buffered by tile parity; the V tile is double-buffered
+// (V(i) waits for PV(i-2)), and so are its barriers; every other barrier's next phase needs its
+// waiters to have passed (PV needs the softmax, S needs the K tile, ...).
 //
 // Every mbarrier wait is bounded (about a second); on timeout the kernel records a status code,
 // stops, drains its own copies and MMAs with bounded waits, frees TMEM and returns.
@@ -75,26 +76,26 @@ struct DC {
     static constexpr int PSLAB = NP * 128;
     static constexpr int PBUF = 2 * PSLAB;
     static constexpr int OFF_K = 0;
-    static constexpr int OFF_V = DEQB;
-    static constexpr int OFF_Q = 2 * DEQB;       // [2] by item parity
+    static constexpr int OFF_V = DEQB;           // [2] by tile parity
+    static constexpr int OFF_Q = 3 * DEQB;       // [2] by item parity
     static constexpr int OFF_P = OFF_Q + 2 * QBUF;  // [2] by tile parity
     static constexpr int OFF_RAW = OFF_P + 2 * PBUF;
     // tail: scales, reductions, metadata, barriers
     static constexpr int T_DK = 0;                    // uint2 [2][TILE]
-    static constexpr int T_DV = T_DK + 2 * TILE * 8;  // uint2 [TILE]
-    static constexpr int T_DVW = T_DV + TILE * 8;     // float [4]
-    static constexpr int T_RED = T_DVW + 16;          // float [2][4][G]
+    static constexpr int T_DV = T_DK + 2 * TILE * 8;  // uint2 [2][TILE]
+    static constexpr int T_DVW = T_DV + 2 * TILE * 8; // float [2][4]
+    static constexpr int T_RED = T_DVW + 32;          // float [2][4][G]
     static constexpr int T_REDL = T_RED + 2 * 4 * G * 4;  // float [2][4][G]
     static constexpr int T_META = ((T_REDL + 2 * 4 * G * 4) + 31) / 32 * 32;  // TileMeta [2]
     static constexpr int T_SMETA = T_META + 2 * 32;                        // TileMeta [R]
-    static constexpr int TAIL_FIXED = T_SMETA + 4 * 32 + 8 * (2 * 4 + 18) + 16;
+    static constexpr int TAIL_FIXED = T_SMETA + 4 * 32 + 8 * (2 * 4 + 20) + 16;
     static constexpr int TAIL = (TAIL_FIXED + 127) / 128 * 128;
     static constexpr int R0 = (SMEM_LIMIT - 1024 - OFF_RAW - TAIL) / (2 * RAWB);
     static constexpr int R = R0 > 4 ? 4 : R0;  // raw stages
     static_assert(R >= 2, "decode_sm100: not enough shared memory for two stages");
     static constexpr int OFF_TAIL = OFF_RAW + R * 2 * RAWB;
     static constexpr int T_BAR = T_SMETA + R * 32;
-    static constexpr int NBAR = 2 * R + 18;
+    static constexpr int NBAR = 2 * R + 20;
     static constexpr int T_SLOT = T_BAR + NBAR * 8;
     static constexpr int SMEM = OFF_TAIL + TAIL + 1024;
     static_assert(T_SLOT + 8 <= TAIL, "decode_sm100 tail layout");
@@ -252,9 +253,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_sm100_kernel(const DecSmPa
     uint64_t* empty = full + R;         // [R] raw stage consumed (256 dequantiser threads)
     uint64_t* k_full = empty + R;       // [2] by tile parity: K tile dequantised (128)
     uint64_t* k_empty = k_full + 2;     // S MMAs done with the K tile (commit)
-    uint64_t* v_full = k_empty + 1;     // V tile dequantised (128)
-    uint64_t* v_empty = v_full + 1;     // PV MMAs done with the V tile (commit)
-    uint64_t* s_full = v_empty + 1;     // [2] S computed (commit)
+    uint64_t* v_full = k_empty + 1;     // [2] by tile parity: V tile dequantised (128)
+    uint64_t* v_empty = v_full + 2;     // [2] PV MMAs done with the V tile (commit)
+    uint64_t* s_full = v_empty + 2;     // [2] S computed (commit)
     uint64_t* p_full = s_full + 2;      // [2] P~ written, S read (128)
     uint64_t* o_full = p_full + 2;      // [2] O~ computed (commit)
     uint64_t* o_empty = o_full + 2;     // [2] O~ read (128)
@@ -269,7 +270,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_sm100_kernel(const DecSmPa
     if (threadIdx.x == 0) {
         for (int s = 0; s < R; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 256); }
         mbar_init(&k_full[0], 128); mbar_init(&k_full[1], 128); mbar_init(k_empty, 1);
-        mbar_init(v_full, 128); mbar_init(v_empty, 1);
+        for (int j = 0; j < 2; ++j) { mbar_init(&v_full[j], 128); mbar_init(&v_empty[j], 1); }
         for (int j = 0; j < 2; ++j) {
             mbar_init(&s_full[j], 1); mbar_init(&p_full[j], 128);
             mbar_init(&o_full[j], 1); mbar_init(&o_empty[j], 128);
@@ -381,32 +382,49 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_sm100_kernel(const DecSmPa
             auto issue_pv = [&](int i) {
                 const int par = i & 1;
                 const uint32_t pb = pa + (uint32_t)(par * C::PBUF);
+                const uint32_t vb = va + (uint32_t)(par * DEQB);
 #pragma unroll
                 for (int kk = 0; kk < TILE / 16; ++kk) {
-                    const uint64_t ad = desc_sw128(va + kk * 2048, SLAB, 1024);  // MN-major: rows of the tile along K
+                    const uint64_t ad = desc_sw128(vb + kk * 2048, SLAB, 1024);  // MN-major: rows of the tile along K
                     const uint64_t bd = desc_sw128(pb + (kk >> 2) * C::PSLAB + (kk & 3) * 32, 16, 1024);
                     mma_ss(tmem + 2 * C::S_COLS + par * C::NP, ad, bd, IDESC_PV, kk > 0 ? 1u : 0u);
                 }
                 mma_commit(&o_full[par]);
-                mma_commit(v_empty);
+                mma_commit(&v_empty[par]);
             };
-            bool ok = mbar_wait(&k_full[0], 0, p.status, 61);
-            if (ok && !(meta[0].flags & F_END)) {
-                tc_fence_after();
-                issue_s(0);
-                for (int i = 0;; ++i) {
-                    ok = mbar_wait(&k_full[(i + 1) & 1], ((i + 1) >> 1) & 1, p.status, 62);
-                    if (!ok) break;
-                    const bool end_next = (meta[(i + 1) & 1].flags & F_END) != 0;
-                    tc_fence_after();
-                    if (!end_next) issue_s(i + 1);
-                    ok = mbar_wait(&p_full[i & 1], (i >> 1) & 1, p.status, 63) && mbar_wait(v_full, i & 1, p.status, 64) &&
-                         (i < 2 || mbar_wait(&o_empty[i & 1], ((i - 2) >> 1) & 1, p.status, 65));
-                    if (!ok) break;
-                    tc_fence_after();
-                    issue_pv(i);
-                    if (end_next || *(volatile int*)abort_flag) break;
+            // Issue S(ns) as soon as its K tile is ready and PV(np) as soon as its P~ and V tile are,
+            // in order within each kind. S(ns) reuses the S columns of tile ns-2, free once PV(ns-2)
+            // was issued (which waited for the softmax of ns-2). No progress for ~2^31 cycles -> error.
+            bool ok = true;
+            int ns = 0, np = 0, end_tile = 0x7fffffff;
+            long long t_last = clock64();
+            while (np < end_tile) {
+                bool progressed = false;
+                if (ns < end_tile && ns <= np + 1 && mbar_test(&k_full[ns & 1], (ns >> 1) & 1)) {
+                    if (meta[ns & 1].flags & F_END) {
+                        end_tile = ns;
+                    } else {
+                        tc_fence_after();
+                        issue_s(ns);
+                        ++ns;
+                    }
+                    progressed = true;
                 }
+                if (np < ns && mbar_test(&p_full[np & 1], (np >> 1) & 1) && mbar_test(&v_full[np & 1], (np >> 1) & 1) &&
+                    (np < 2 || mbar_test(&o_empty[np & 1], ((np - 2) >> 1) & 1))) {
+                    tc_fence_after();
+                    issue_pv(np);
+                    ++np;
+                    progressed = true;
+                }
+                if (progressed) {
+                    t_last = clock64();
+                } else if (clock64() - t_last > (1ll << 31)) {
+                    if (p.status) atomicCAS(p.status, 0, 61);
+                    ok = false;
+                    break;
+                }
+                if (*(volatile int*)abort_flag) break;
             }
             if (!ok) *(volatile int*)abort_flag = 1;
             if (*(volatile int*)abort_flag) {
@@ -451,18 +469,18 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_sm100_kernel(const DecSmPa
                 mbar_arrive(&empty[s]);
             } else {
                 if (m.flags & F_END) break;
-                if (i >= 1) ok = warp_wait(v_empty, (i - 1) & 1, p.status, 82);
+                if (i >= 2) ok = warp_wait(&v_empty[par], ((i - 2) >> 1) & 1, p.status, 82);
                 if (!ok) break;
-                const uint2 sc = dequant_row(raw + s * 2 * RAWB + RAWB + r * ROWB, deq, r);
-                dvs[r] = sc;
+                const uint2 sc = dequant_row(raw + s * 2 * RAWB + RAWB + r * ROWB, deq + par * DEQB, r);
+                dvs[par * TILE + r] = sc;
                 float mx = 0.0f;
                 if (r < m.nrows)
                     mx = fmaxf(fmaxf(fabsf(half_lo(sc.x)), fabsf(half_hi(sc.x))), fmaxf(fabsf(half_lo(sc.y)), fabsf(half_hi(sc.y))));
                 mx = warp_max(mx);
-                if (lane == 0) dvw[warp - 10] = mx;
+                if (lane == 0) dvw[par * 4 + warp - 10] = mx;
                 __syncwarp();
                 fence_proxy_async_smem();
-                mbar_arrive(v_full);
+                mbar_arrive(&v_full[par]);
                 mbar_arrive(&empty[s]);
             }
         }
@@ -531,9 +549,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_sm100_kernel(const DecSmPa
                     l_run[h] = fmaf(l_run[h], alpha[h], pr[h]);
                     m_run[h] = m_new;
                 }
-                ok = warp_wait(v_full, i & 1, p.status, 53);
+                ok = warp_wait(&v_full[par], (i >> 1) & 1, p.status, 53);
                 if (!ok) break;
-                const float dvmax = fmaxf(fmaxf(dvw[0], dvw[1]), fmaxf(dvw[2], dvw[3]));
+                const float* dw = dvw + par * 4;
+                const float dvmax = fmaxf(fmaxf(dw[0], dw[1]), fmaxf(dw[2], dw[3]));
                 float f = 1.0f;
                 invf = 1.0f;
                 if (dvmax > 0.0f) {  // dvmax * f in [2^14, 2^15)
@@ -541,7 +560,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_sm100_kernel(const DecSmPa
                     f = __uint_as_float((uint32_t)(127 + 14 - e) << 23);
                     invf = __uint_as_float((uint32_t)(127 - 14 + e) << 23);
                 }
-                const uint2 dv2 = dvs[u];
+                const uint2 dv2 = dvs[par * TILE + u];
                 const float dv[4] = {half_lo(dv2.x) * f, half_hi(dv2.x) * f, half_lo(dv2.y) * f, half_hi(dv2.y) * f};
                 unsigned char* pb = pbuf + par * C::PBUF + (u >> 6) * C::PSLAB + (u & 7) * 2;
                 const int chunk16 = (u & 63) >> 3;
@@ -643,8 +662,7 @@ int run_decode_sm100(const DecodeArgs& a, int* work, float* part, int64_t nchunk
     if (cuda_failed(cudaFuncSetAttribute(decode_sm100_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM),
                     "cudaFuncSetAttribute(decode_sm100)"))
         return -1;
-    decode_plan_kernel<<<1, 1024, 0, st>>>(a.lens, a.B, a.Smax, a.Hkv, GTB_DECODE_CHUNK, work);
-    if (cuda_failed(cudaGetLastError(), "decode plan launch")) return -1;
+    if (launch_decode_plan(a, work, st) != 0) return -1;
     DecSmParams p;
     p.q = (const __half*)a.q;
     p.k = (const uint8_t*)a.k;
@@ -667,6 +685,11 @@ int run_decode_sm100(const DecodeArgs& a, int* work, float* part, int64_t nchunk
 }
 
 }  // namespace
+
+int launch_decode_plan(const DecodeArgs& a, int* work, cudaStream_t st) {
+    decode_plan_kernel<<<1, 1024, 0, st>>>(a.lens, a.B, a.Smax, a.Hkv, GTB_DECODE_CHUNK, work);
+    return cuda_failed(cudaGetLastError(), "decode plan launch") ? -1 : 0;
+}
 
 bool decode_sm100_supported(const DecodeArgs& a) {
     static const int force_simt = [] {

@@ -508,8 +508,11 @@ int launch_decode_q8_0(const DecodeArgs& a, void* scratch, cudaStream_t st) {
         return -1;
     }
     p.part = (float*)((char*)scratch + decode_work_bytes(a.B));
-    if (decode_sm100_supported(a)) {
-        if (launch_decode_sm100(a, (int*)scratch, p.part, p.nchunks, st) != 0) return -1;
+    const bool mma = decode_mma_supported(a);
+    if (mma || decode_sm100_supported(a)) {
+        const int rc = mma ? launch_decode_mma(a, (int*)scratch, p.part, p.nchunks, st)
+                           : launch_decode_sm100(a, (int*)scratch, p.part, p.nchunks, st);
+        if (rc != 0) return -1;
         if (p.nchunks > 1) {
             dim3 g2((unsigned)p.H, (unsigned)p.B);
             decode_combine_kernel<<<g2, (unsigned)p.D, 0, st>>>(p);

@@ -32,5 +32,12 @@ int launch_decode_q8_0(const DecodeArgs& a, void* scratch, cudaStream_t st);
 // aligned q/k/v. Launches the plan kernel and the persistent kernel; partials as above.
 bool decode_sm100_supported(const DecodeArgs& a);
 int launch_decode_sm100(const DecodeArgs& a, int* work, float* part, int64_t nchunks, cudaStream_t st);
+// Plan kernel of both persistent decode kernels: per-sequence item prefix and a zeroed item counter.
+int launch_decode_plan(const DecodeArgs& a, int* work, cudaStream_t st);
+
+// Warp-MMA decode (decode_mma.cu): D = 128, f16 q, H/Hkv in {1, 2, 4}, even Smax, 16-byte aligned
+// q/k/v. Same work area and partials as the tcgen05 kernel.
+bool decode_mma_supported(const DecodeArgs& a);
+int launch_decode_mma(const DecodeArgs& a, int* work, float* part, int64_t nchunks, cudaStream_t st);
 
 }  // namespace gtb

@@ -44,6 +44,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t addr, uint32_t parity) {
     return done != 0;
 }
 
+// non-blocking: has the phase of `parity` completed?
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+
 // Wait for the phase of `parity` to complete, for at most ~2^31 SM cycles (about a second).
 // On timeout: records `code` in the device status word (the first code since the word was last
 // cleared is kept) and returns false. Never traps or hangs.
