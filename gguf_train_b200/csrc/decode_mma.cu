@@ -142,7 +142,8 @@ __device__ __forceinline__ uint32_t i8x2_to_f16x2(uint32_t x) {
 
 // Half of a cached row (Q8_0 blocks 2*hb and 2*hb+1: 68 bytes starting at row + 68*hb) -> 64 f16
 // integers at row r of a 16-row tile of 256-byte rows whose 16-byte chunks are XOR-swizzled by
-// (r & 7); returns the two scales.
+// (r >> 1) & 7 (ldmatrix reads the even and the odd rows as separate 8-row matrices); returns the
+// two scales.
 __device__ __forceinline__ float2 dequant_half_row(const unsigned char* row, int hb, uint32_t out_row, int r) {
     uint32_t w[17];
     const uint32_t* src = (const uint32_t*)(row + 68 * hb);  // 4-byte aligned (136 and 68 are multiples of 4)
@@ -168,7 +169,7 @@ __device__ __forceinline__ float2 dequant_half_row(const unsigned char* row, int
                 asm("sub.f16x2 %0, %1, %2;" : "=r"(h[2 * k + 1]) : "r"(__byte_perm(u, 0x64u, 0x4342u)), "r"(0x64806480u));
             }
             const int chunk = 4 * (2 * hb + j) + cc;
-            const uint32_t addr = out_row + (uint32_t)((chunk ^ (r & 7)) << 4);
+            const uint32_t addr = out_row + (uint32_t)((chunk ^ ((r >> 1) & 7)) << 4);
             asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(h[0]), "r"(h[1]), "r"(h[2]),
                          "r"(h[3])
                          : "memory");
@@ -364,7 +365,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_mma_kernel(const DecMmaPar
             // V rows of the slice -> f16 (two lanes per row), and the largest |dV| of the valid rows
             float dvm = 0.0f;
             {
-                const int r = lane >> 1, hb = lane & 1;
+                // a quarter-warp stores 8 different swizzle phases: lanes 0-7 even rows, 8-15 odd rows
+                const int r = 2 * (lane & 7) + ((lane >> 3) & 1), hb = lane >> 4;
                 const float2 sv = dequant_half_row(st + RAWB + (rb + r) * ROWB, hb, vst + r * 256, r);
                 if (rb + r < m.nrows) dvm = fmaxf(fabsf(sv.x), fabsf(sv.y));
             }
@@ -382,17 +384,20 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_mma_kernel(const DecMmaPar
                 const int off = 34 * (ks >> 1) + 2 + 16 * (ks & 1) + 2 * c;  // byte of quant (16ks + 2c) in a row
 #pragma unroll
                 for (int nt = 0; nt < 2; ++nt) {
-                    const unsigned char* kr = st + (rb + 8 * nt + g) * ROWB + off;
+                    // column tile nt holds the slice's rows 2n + nt (row order inside an MMA is free; rows
+                    // 2 apart start 4 banks apart, so the 8 rows' 2-byte reads never share a bank)
+                    const unsigned char* kr = st + (rb + 2 * g + nt) * ROWB + off;
                     mma16816(sacc[nt][ks & 1], qa, i8x2_to_f16x2(lds_u16(kr)), i8x2_to_f16x2(lds_u16(kr + 8)));
                 }
             }
 #pragma unroll
             for (int off = 16; off > 0; off >>= 1) dvm = fmaxf(dvm, __shfl_xor_sync(0xffffffffu, dvm, off));
-            // scores of this thread's head hh at slice rows t = 2c, 2c+1, 8+2c, 9+2c
+            // scores of this thread's head hh; value k = 2 nt + e is column 2c + e of tile nt: slice row
+            // t = 2 (2c + e) + nt = 4c + 2e + nt
             float sc4[4], dv0[4], dv1[4];
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
-                const int t = 8 * (k >> 1) + 2 * c + (k & 1);
+                const int t = 4 * c + 2 * (k & 1) + (k >> 1);
                 const unsigned char* kr = st + (rb + t) * ROWB;
                 const unsigned char* vr = kr + RAWB;
                 const float s0 = sacc[k >> 1][0][k & 1] + sacc[k >> 1][1][k & 1];
@@ -425,7 +430,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_mma_kernel(const DecMmaPar
             float mx = -INFINITY;
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
-                const int t = 8 * (k >> 1) + 2 * c + (k & 1);
+                const int t = 4 * c + 2 * (k & 1) + (k >> 1);
                 sc4[k] = (v0 && rb + t < m.nrows) ? sc4[k] * p.scale_log2 : -INFINITY;
                 mx = fmaxf(mx, sc4[k]);
             }
@@ -466,7 +471,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_mma_kernel(const DecMmaPar
                 pr[k] = ex2(sc4[k] + neg);
                 l_run += pr[k];
             }
-            // P~ rows g, g+8 at slice rows 2c, 2c+1 | 2c+8, 2c+9: B fragments of the two column tiles
+            // P~ rows g, g+8 as B fragments of PV. PV's reduction index k maps to slice row
+            // 2 (k mod 8) + k / 8: k = 2c, 2c+1 are rows 4c, 4c+2 (tile 0), k = 2c+8, 2c+9 rows 4c+1, 4c+3
             uint32_t pa[4];
             {
                 const float fv = f == 0.0f ? 1.0f : f;
@@ -474,7 +480,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_mma_kernel(const DecMmaPar
 #pragma unroll
                 for (int k = 0; k < 4; ++k) {
                     // rows past the end of the sequence hold stale bytes: select, never multiply by 0
-                    const bool tv = rb + 8 * (k >> 1) + 2 * c + (k & 1) < m.nrows;
+                    const bool tv = rb + 4 * c + 2 * (k & 1) + (k >> 1) < m.nrows;
                     w0[k] = (v0 && tv) ? pr[k] * dv0[k] * fv : 0.0f;
                     w1[k] = (v1 && tv) ? pr[k] * dv1[k] * fv : 0.0f;
                 }
@@ -487,12 +493,13 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_mma_kernel(const DecMmaPar
             // O^T[d, r] += Vx^T[d, t] P~^T[t, r]: one MMA per 16 head dims, with the column tile of
             // the operand rows of the dims' Q8_0 block
             {
-                const int lr = (lane & 7) + ((lane >> 4) << 3);  // V row (slice token) this lane addresses
+                // matrices: k 0-7 / 8-15 (slice rows 2i / 2i+1) x head dims 16mt.. / 16mt+8..
+                const int lr = 2 * (lane & 7) + (lane >> 4);  // V row (slice row) this lane addresses
                 const int lc = (lane >> 3) & 1;
 #pragma unroll
                 for (int mt = 0; mt < 8; ++mt) {
                     uint32_t a[4];
-                    ldsm_x4_t(vst + lr * 256 + (((2 * mt + lc) ^ (lr & 7)) << 4), a[0], a[1], a[2], a[3]);
+                    ldsm_x4_t(vst + lr * 256 + (((2 * mt + lc) ^ ((lr >> 1) & 7)) << 4), a[0], a[1], a[2], a[3]);
                     const int ntile = ((mt >> 1) * G) >> 3;
                     mma16816(ot[mt], a, ntile ? pa[1] : pa[0], ntile ? pa[3] : pa[2]);
                 }
