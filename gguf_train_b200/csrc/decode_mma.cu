@@ -25,10 +25,11 @@
 // own Q8_0 block.
 //
 // Work: items (sequence b, kv head hk, chunk of GTB_DECODE_CHUNK rows) from the compacted list of the
-// plan kernel (decode_sm100.cu), claimed through an atomic counter by a producer warp. The 8 consumer
-// warps form two groups of 4 with their own items and their own 2-stage ring, so that the groups'
-// phases interleave; the producer streams 128-row tiles of raw K/V rows (and the item's q rows) into
-// both rings with cp.async.bulk. Warp wi of a group owns rows [32 wi, 32 wi + 32) of its tiles, as two
+// plan kernel (decode_sm100.cu), claimed through an atomic counter. The 8 consumer warps form two
+// groups of 4 with their own items, their own 2-stage ring and their own producer warp, so that the
+// groups' phases interleave; a producer streams 128-row tiles of raw K/V rows (and the item's q rows)
+// into its ring with cp.async.bulk (issuing a tile's copies takes the issuing thread ~1000 cycles, so
+// one producer per ring keeps a ring from waiting behind the other's issue). Warp wi of a group owns rows [32 wi, 32 wi + 32) of its tiles, as two
 // 16-row slices: K fragments come straight from the raw rows (two int8 -> f16x2 per load), V rows are
 // dequantised into a private f16 slice and read back transposed with ldmatrix. No barrier spans warps
 // inside an item; at its end the group's 4 partial (max, sum, out) are merged through shared memory.
@@ -48,16 +49,24 @@ namespace {
 
 using namespace sm100;
 
-constexpr int TILE = 128;           // cached rows per tile
+#ifndef GTB_DECODE_GROUPS
+#define GTB_DECODE_GROUPS 2
+#endif
+#ifndef GTB_DECODE_SLICES
+#define GTB_DECODE_SLICES 2
+#endif
 constexpr int HD = 128;             // head size
 constexpr int NBLK = HD / 32;       // Q8_0 blocks per row
 constexpr int ROWB = NBLK * 34;     // bytes per cached row
+constexpr int NGRP = GTB_DECODE_GROUPS;  // consumer groups, each with its own items and stage ring
+constexpr int GW = 4;               // warps per group
+constexpr int SPW = GTB_DECODE_SLICES;   // 16-row slices per warp and tile
+constexpr int TILE = GW * 16 * SPW; // cached rows per tile: warp wi owns rows [16 SPW wi, 16 SPW (wi + 1))
 constexpr int RAWB = TILE * ROWB;   // raw bytes of a K (or V) tile
-constexpr int NGRP = 2;             // consumer groups, each with its own items and stage ring
-constexpr int GW = 4;               // warps per group: warp wi owns rows [32 wi, 32 wi + 32) of a tile
 constexpr int NCW = NGRP * GW;
 constexpr int RS = 2;               // stages per group ring
-constexpr int NTHREADS = (NCW + 1) * 32;
+constexpr int NTHREADS = (NCW + NGRP) * 32;  // + one producer warp per group
+static_assert(GTB_DECODE_CHUNK % TILE == 0, "tiles must divide a chunk");
 constexpr int SMEM_LIMIT = 232448;
 
 enum : int { F_FIRST = 1, F_LAST = 2, F_END = 4 };
@@ -90,6 +99,7 @@ struct DecMmaParams {
     __half* out;
     float* part;  // [B][Hkv][nchunks][G][HD + 2] when nchunks > 1
     int* work;    // [0] item counter, [1 .. B+1] prefix of items per sequence (plan kernel)
+    const int2* items;  // item list (b, hk << 16 | chunk), written by the plan kernel
     int64_t B, H, Hkv, Smax;
     int nchunks, chunk;
     float scale_log2;
@@ -202,81 +212,48 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_mma_kernel(const DecMmaPar
     }
     __syncthreads();
 
-    if (warp == NCW) {
-        // ------------------------------------------------------------ producer
-        // Claims items for the two groups as they need them and fills each group's ring in turn,
-        // never blocking on one ring while the other has room; no progress for ~2^31 cycles -> error.
+    if (warp >= NCW) {
+        // ------------------------------------------------------------ producer of group warp - NCW
         if (lane == 0) {
-            const int* prefix = p.work + 1;
-            const int total = prefix[p.B];
-            struct Cur {
-                int b, hk, chunk, nt, t, seq;
-                int64_t c0, c1;
-                bool live;
-            } cur[NGRP];
-            int n[NGRP], seqs[NGRP];
-            bool done[NGRP];
-            for (int gp = 0; gp < NGRP; ++gp) { cur[gp].live = false; n[gp] = 0; seqs[gp] = 0; done[gp] = false; }
-            bool no_more = false, ok = true;
-            long long t_last = clock64();
-            while (!(done[0] && done[1])) {
-                bool progressed = false;
-#pragma unroll
-                for (int gp = 0; gp < NGRP; ++gp) {
-                    if (done[gp]) continue;
-                    const int s = n[gp] % RS;
-                    if (n[gp] >= RS && !mbar_test(&empty[gp * RS + s], ((n[gp] / RS) - 1) & 1)) continue;
-                    if (!cur[gp].live && !no_more) {
-                        const int item = atomicAdd(p.work, 1);
-                        if (item >= total) {
-                            no_more = true;
-                        } else {
-                            int lo = 0, hi = (int)p.B - 1;  // last sequence whose first item is <= item
-                            while (lo < hi) {
-                                const int mid = (lo + hi + 1) >> 1;
-                                if (prefix[mid] <= item) lo = mid; else hi = mid - 1;
-                            }
-                            Cur& c = cur[gp];
-                            c.b = lo;
-                            const int nch = (prefix[lo + 1] - prefix[lo]) / (int)p.Hkv;
-                            const int rem = item - prefix[lo];
-                            c.hk = rem / nch;
-                            c.chunk = rem % nch;
-                            int64_t len = p.lens[lo];
-                            len = len < 0 ? 0 : (len > p.Smax ? p.Smax : len);
-                            c.c0 = (int64_t)c.chunk * p.chunk;
-                            c.c1 = min(len, c.c0 + p.chunk);
-                            c.nt = c.c1 > c.c0 ? (int)((c.c1 - c.c0 + TILE - 1) / TILE) : 1;
-                            c.t = 0;
-                            c.seq = seqs[gp]++;
-                            c.live = true;
-                        }
-                    }
+            const int gp = warp - NCW;
+            const int total = p.work[1 + p.B];
+            // claims run two deep: the counter for item k+2 and the list entry of item k+1 are fetched
+            // while item k's tiles are issued, so neither latency stalls the ring
+            int n1 = atomicAdd(p.work, 1);
+            int n2 = atomicAdd(p.work, 1);
+            int2 d1 = n1 < total ? p.items[n1] : make_int2(0, 0);
+            int n = 0, seq = 0;
+            bool ok = true;
+            while (ok && n1 < total) {  // claims only grow: once n1 is past the end, so is n2
+                const int b = d1.x, hk = d1.y >> 16, chunk = d1.y & 0xFFFF;
+                n1 = n2;
+                d1 = n1 < total ? p.items[n1] : make_int2(0, 0);
+                n2 = atomicAdd(p.work, 1);
+                int64_t len = p.lens[b];
+                len = len < 0 ? 0 : (len > p.Smax ? p.Smax : len);
+                const int64_t c0 = (int64_t)chunk * p.chunk;
+                const int64_t c1 = min(len, c0 + p.chunk);
+                const int nt = c1 > c0 ? (int)((c1 - c0 + TILE - 1) / TILE) : 1;
+                const int64_t slab = ((int64_t)b * p.Hkv + hk) * p.Smax;
+                const __half* qs = p.q + ((int64_t)b * p.H + (int64_t)hk * G) * HD;
+                for (int t = 0; t < nt; ++t) {
+                    const int s = n % RS;
+                    if (n >= RS) ok = mbar_wait(&empty[gp * RS + s], ((n / RS) - 1) & 1, p.status, 41);
+                    if (!ok || *(volatile int*)abort_flag) { ok = false; break; }
+                    const int64_t r0 = c0 + (int64_t)t * TILE;
+                    const int nrows = (int)max((int64_t)0, min((int64_t)TILE, c1 - r0));
                     TileMeta& m = smeta[gp * RS + s];
-                    uint64_t* fb = &full[gp * RS + s];
-                    if (!cur[gp].live) {
-                        m.flags = F_END;
-                        mbar_arrive(fb);
-                        done[gp] = true;
-                        ++n[gp];
-                        progressed = true;
-                        continue;
-                    }
-                    Cur& c = cur[gp];
-                    const int64_t r0 = c.c0 + (int64_t)c.t * TILE;
-                    const int nrows = (int)max((int64_t)0, min((int64_t)TILE, c.c1 - r0));
-                    m.b = c.b; m.hk = c.hk; m.chunk = c.chunk; m.nrows = nrows; m.seq = c.seq;
-                    m.flags = (c.t == 0 ? F_FIRST : 0) | (c.t == c.nt - 1 ? F_LAST : 0);
+                    m.b = b; m.hk = hk; m.chunk = chunk; m.nrows = nrows; m.seq = seq;
+                    m.flags = (t == 0 ? F_FIRST : 0) | (t == nt - 1 ? F_LAST : 0);
                     // whole row pairs: 2 * 136 bytes is a multiple of 16, and Smax is even on this path
                     const uint32_t bytes = (uint32_t)(((nrows + 1) & ~1) * ROWB);
-                    const uint32_t qbytes = c.t == 0 ? (uint32_t)C::QB : 0u;
+                    const uint32_t qbytes = t == 0 ? (uint32_t)C::QB : 0u;
                     unsigned char* kd = smem + C::OFF_RAW + (gp * RS + s) * C::STAGE;
                     unsigned char* vd = kd + RAWB;
                     unsigned char* qd = kd + 2 * RAWB;
-                    const int64_t slab = ((int64_t)c.b * p.Hkv + c.hk) * p.Smax;
                     const uint8_t* ks = p.k + (slab + r0) * ROWB;
                     const uint8_t* vs = p.v + (slab + r0) * ROWB;
-                    const __half* qs = p.q + ((int64_t)c.b * p.H + (int64_t)c.hk * G) * HD;
+                    uint64_t* fb = &full[gp * RS + s];
                     const bool aligned = ((((uintptr_t)ks | (uintptr_t)vs | (uintptr_t)qs | (uintptr_t)smem_u32(kd) |
                                             (uintptr_t)smem_u32(vd) | (uintptr_t)smem_u32(qd) | bytes) & 15) == 0);
                     if (!aligned && p.status) atomicCAS(p.status, 0, 2);  // never issue a misaligned copy
@@ -291,24 +268,22 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_mma_kernel(const DecMmaPar
                         }
                         if (qbytes) bulk_load(qd, qs, qbytes, fb);
                     }
-                    if (++c.t == c.nt) c.live = false;
-                    ++n[gp];
-                    progressed = true;
+                    ++n;
                 }
-                if (progressed) {
-                    t_last = clock64();
-                } else if (clock64() - t_last > (1ll << 31)) {
-                    if (p.status) atomicCAS(p.status, 0, 41);
-                    ok = false;
-                    break;
+                ++seq;
+            }
+            if (ok && !*(volatile int*)abort_flag) {
+                const int s = n % RS;
+                if (n >= RS) ok = mbar_wait(&empty[gp * RS + s], ((n / RS) - 1) & 1, p.status, 43);
+                if (ok) {
+                    smeta[gp * RS + s].flags = F_END;
+                    mbar_arrive(&full[gp * RS + s]);
+                    ++n;
                 }
-                if (*(volatile int*)abort_flag) break;
             }
             if (!ok) *(volatile int*)abort_flag = 1;
             if (*(volatile int*)abort_flag) {
-                for (int gp = 0; gp < NGRP; ++gp)
-                    for (int j = max(0, n[gp] - RS); j < n[gp]; ++j)
-                        mbar_wait(&full[gp * RS + j % RS], (j / RS) & 1, nullptr, 0);
+                for (int j = max(0, n - RS); j < n; ++j) mbar_wait(&full[gp * RS + j % RS], (j / RS) & 1, nullptr, 0);
             }
         }
         return;
@@ -360,8 +335,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_mma_kernel(const DecMmaPar
         }
 
 #pragma unroll 1
-        for (int sl = 0; sl < 2; ++sl) {
-            const int rb = 32 * wi + 16 * sl;  // first tile row of this 16-row slice
+        for (int sl = 0; sl < SPW; ++sl) {
+            const int rb = 16 * (SPW * wi + sl);  // first tile row of this 16-row slice
             // V rows of the slice -> f16 (two lanes per row), and the largest |dV| of the valid rows
             float dvm = 0.0f;
             {
@@ -599,6 +574,7 @@ int run_decode_mma(const DecodeArgs& a, int* work, float* part, int64_t nchunks,
     p.out = (__half*)a.out;
     p.part = part;
     p.work = work;
+    p.items = (const int2*)(work + decode_list_offset(a.B));
     p.B = a.B; p.H = a.H; p.Hkv = a.Hkv; p.Smax = a.Smax;
     p.nchunks = (int)nchunks;
     p.chunk = GTB_DECODE_CHUNK;
@@ -622,7 +598,8 @@ bool decode_mma_supported(const DecodeArgs& a) {
     const int64_t G = a.Hkv > 0 ? a.H / a.Hkv : 0;
     return !force_off && a.D == HD && a.q_dtype == F16 && (G == 1 || G == 2 || G == 4) && a.Smax > 0 &&
            a.Smax % 2 == 0 && ((uintptr_t)a.q % 16 == 0) && ((uintptr_t)a.k % 16 == 0) && ((uintptr_t)a.v % 16 == 0) &&
-           a.B * a.Hkv * decode_num_chunks(a.Smax) < (int64_t)INT32_MAX && a.B < INT32_MAX;
+           a.B * a.Hkv * decode_num_chunks(a.Smax) < (int64_t)INT32_MAX && a.B < INT32_MAX && a.Hkv < 32768 &&
+           decode_num_chunks(a.Smax) < 65536;
 }
 
 int launch_decode_mma(const DecodeArgs& a, int* work, float* part, int64_t nchunks, cudaStream_t st) {

@@ -102,7 +102,7 @@ extern "C" GTB_API int gtb_decode_q8_0_noalloc(const void* q, int q_dtype, const
     const size_t need = decode_scratch_bytes(B, H, Hkv, Smax, D);
     if (need > (size_t)GTB_DECODE_NOALLOC_SCRATCH_BYTES) {
         set_errorf("%s: this call needs %zu bytes of scratch, more than the fixed %zu bytes this entry point has "
-                   "(B * Hkv * ceil(Smax / %d) * (H / Hkv) * (D + 2) * 4, plus 4 * (B + 2) rounded up to 256); "
+                   "(B * Hkv * ceil(Smax / %d) * ((H / Hkv) * (D + 2) * 4 + 8), plus 4 * (B + 3), rounded up to 256); "
                    "use gtb_decode_q8_0",
                    ctx, need, (size_t)GTB_DECODE_NOALLOC_SCRATCH_BYTES, GTB_DECODE_CHUNK);
         return -1;

@@ -194,8 +194,10 @@ __device__ __forceinline__ int seq_items(const int32_t* lens, int64_t b, int64_t
     return (int)(Hkv * nch);
 }
 
-// One block: work[1 + b] = items of sequences < b, work[1 + B] = all items, work[0] = 0 (the counter).
-__global__ void decode_plan_kernel(const int32_t* lens, int64_t B, int64_t Smax, int64_t Hkv, int chunk, int* work) {
+// One block: work[1 + b] = items of sequences < b, work[1 + B] = all items, work[0] = 0 (the counter),
+// and the item list at work + list_off: item prefix[b] + hk * nch_b + c is (b, hk << 16 | c).
+__global__ void decode_plan_kernel(const int32_t* lens, int64_t B, int64_t Smax, int64_t Hkv, int chunk, int* work,
+                                   int64_t list_off) {
     __shared__ int wsum[32];
     const int tid = threadIdx.x, nt = blockDim.x, lane = tid & 31, warp = tid >> 5;
     const int64_t per = (B + nt - 1) / nt;
@@ -221,9 +223,13 @@ __global__ void decode_plan_kernel(const int32_t* lens, int64_t B, int64_t Smax,
     }
     __syncthreads();
     int run = x - local + (warp > 0 ? wsum[warp - 1] : 0);
+    int2* list = (int2*)(work + list_off);
     for (int64_t b = b0; b < b1; ++b) {
         work[1 + b] = run;
-        run += seq_items(lens, b, Smax, Hkv, chunk);
+        const int n = seq_items(lens, b, Smax, Hkv, chunk);
+        const int nch = n / (int)Hkv;
+        for (int j = 0; j < n; ++j) list[run + j] = make_int2((int)b, ((j / nch) << 16) | (j % nch));
+        run += n;
     }
     if (tid == nt - 1) work[1 + B] = run;
     if (tid == 0) work[0] = 0;
@@ -687,7 +693,7 @@ int run_decode_sm100(const DecodeArgs& a, int* work, float* part, int64_t nchunk
 }  // namespace
 
 int launch_decode_plan(const DecodeArgs& a, int* work, cudaStream_t st) {
-    decode_plan_kernel<<<1, 1024, 0, st>>>(a.lens, a.B, a.Smax, a.Hkv, GTB_DECODE_CHUNK, work);
+    decode_plan_kernel<<<1, 1024, 0, st>>>(a.lens, a.B, a.Smax, a.Hkv, GTB_DECODE_CHUNK, work, decode_list_offset(a.B));
     return cuda_failed(cudaGetLastError(), "decode plan launch") ? -1 : 0;
 }
 
@@ -699,7 +705,8 @@ bool decode_sm100_supported(const DecodeArgs& a) {
     const int64_t G = a.Hkv > 0 ? a.H / a.Hkv : 0;
     return !force_simt && a.D == HD && a.q_dtype == F16 && (G == 1 || G == 2 || G == 4 || G == 8) &&
            a.Smax > 0 && a.Smax % 2 == 0 && ((uintptr_t)a.q % 16 == 0) && ((uintptr_t)a.k % 16 == 0) &&
-           ((uintptr_t)a.v % 16 == 0) && a.B * a.Hkv * decode_num_chunks(a.Smax) < (int64_t)INT32_MAX && a.B < INT32_MAX;
+           ((uintptr_t)a.v % 16 == 0) && a.B * a.Hkv * decode_num_chunks(a.Smax) < (int64_t)INT32_MAX && a.B < INT32_MAX &&
+           a.Hkv < 32768 && decode_num_chunks(a.Smax) < 65536;
 }
 
 int launch_decode_sm100(const DecodeArgs& a, int* work, float* part, int64_t nchunks, cudaStream_t st) {

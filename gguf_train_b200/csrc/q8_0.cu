@@ -478,14 +478,17 @@ int64_t decode_num_chunks(int64_t Smax) {
     return Smax <= 0 ? 1 : (Smax + GTB_DECODE_CHUNK - 1) / GTB_DECODE_CHUNK;
 }
 
-size_t decode_work_bytes(int64_t B) {
-    return (size_t)((B + 2) * sizeof(int) + 255) / 256 * 256;
+int64_t decode_list_offset(int64_t B) { return (B + 2 + 1) / 2 * 2; }  // in ints, 8-byte aligned
+
+size_t decode_work_bytes(int64_t B, int64_t Hkv, int64_t Smax) {
+    const int64_t items = B * Hkv * decode_num_chunks(Smax);
+    return (size_t)(decode_list_offset(B) * sizeof(int) + items * 2 * sizeof(int) + 255) / 256 * 256;
 }
 
 size_t decode_scratch_bytes(int64_t B, int64_t H, int64_t Hkv, int64_t Smax, int64_t D) {
     const int64_t nch = decode_num_chunks(Smax);
     const size_t part = nch <= 1 ? 0 : (size_t)B * Hkv * nch * (H / Hkv) * (D + 2) * sizeof(float);
-    return decode_work_bytes(B) + part;
+    return decode_work_bytes(B, Hkv, Smax) + part;
 }
 
 int launch_decode_q8_0(const DecodeArgs& a, void* scratch, cudaStream_t st) {
@@ -507,7 +510,7 @@ int launch_decode_q8_0(const DecodeArgs& a, void* scratch, cudaStream_t st) {
         set_error("decode_q8_0: scratch buffer missing");
         return -1;
     }
-    p.part = (float*)((char*)scratch + decode_work_bytes(a.B));
+    p.part = (float*)((char*)scratch + decode_work_bytes(a.B, a.Hkv, a.Smax));
     const bool mma = decode_mma_supported(a);
     if (mma || decode_sm100_supported(a)) {
         const int rc = mma ? launch_decode_mma(a, (int*)scratch, p.part, p.nchunks, st)

@@ -22,9 +22,11 @@ struct DecodeArgs {
 int launch_q8_0_quantize(const void* x, int x_dtype, int64_t nblocks, void* out, cudaStream_t st);
 int launch_q8_0_dequantize(const void* blocks, int64_t nblocks, void* out, int out_dtype, cudaStream_t st);
 int64_t decode_num_chunks(int64_t Smax);
-// Scratch of one decode call: a work area of decode_work_bytes(B) (the tensor-core kernel's item
-// counter and per-sequence item prefix), then the split-KV partials [B][Hkv][nchunks][G][D + 2] f32.
-size_t decode_work_bytes(int64_t B);
+// Scratch of one decode call: a work area of decode_work_bytes() for the persistent kernels (item
+// counter, per-sequence item prefix [B + 1], and at int offset decode_list_offset(B) the item list:
+// one int2 (b, hk << 16 | chunk) per item), then the split-KV partials [B][Hkv][nchunks][G][D + 2] f32.
+int64_t decode_list_offset(int64_t B);
+size_t decode_work_bytes(int64_t B, int64_t Hkv, int64_t Smax);
 size_t decode_scratch_bytes(int64_t B, int64_t H, int64_t Hkv, int64_t Smax, int64_t D);
 int launch_decode_q8_0(const DecodeArgs& a, void* scratch, cudaStream_t st);
 
@@ -32,7 +34,7 @@ int launch_decode_q8_0(const DecodeArgs& a, void* scratch, cudaStream_t st);
 // aligned q/k/v. Launches the plan kernel and the persistent kernel; partials as above.
 bool decode_sm100_supported(const DecodeArgs& a);
 int launch_decode_sm100(const DecodeArgs& a, int* work, float* part, int64_t nchunks, cudaStream_t st);
-// Plan kernel of both persistent decode kernels: per-sequence item prefix and a zeroed item counter.
+// Plan kernel of both persistent decode kernels: per-sequence item prefix, item list, zeroed counter.
 int launch_decode_plan(const DecodeArgs& a, int* work, cudaStream_t st);
 
 // Warp-MMA decode (decode_mma.cu): D = 128, f16 q, H/Hkv in {1, 2, 4}, even Smax, 16-byte aligned

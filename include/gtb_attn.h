@@ -78,7 +78,7 @@ GTB_API int gtb_q8_0_dequantize(const void *blocks, int64_t n_rows, int64_t row_
  *   [0, Smax]); out: (B,H,D) in q_dtype. D % 32 == 0 and D <= 256.
  * Split-KV: each (b, kv head) is cut into chunks of up to GTB_DECODE_CHUNK rows that run in
  * parallel; a second kernel merges the partial results. The partials, and a small work area
- * (per-sequence item prefix and item counter of the tensor-core kernel), live in scratch taken
+ * (item counter, per-sequence item prefix and item list of the tensor-core kernels), live in scratch taken
  * from the stream-ordered allocator. With D = 128, an f16 q, H/Hkv in {1,2,4,8}, an even Smax
  * and 16-byte aligned q/k/v the step runs on the tensor cores; otherwise on CUDA cores. */
 #define GTB_DECODE_CHUNK 1024
@@ -92,7 +92,8 @@ GTB_API int gtb_decode_q8_0(const void *q, int q_dtype, const void *k_q8, const 
  * nothing: the split-KV partial results go to a fixed device array of
  * GTB_DECODE_NOALLOC_SCRATCH_BYTES that every GPU loading this library holds until the process
  * exits. Calls needing more scratch than that, B*Hkv*ceil(Smax/GTB_DECODE_CHUNK)*(H/Hkv)*(D+2)*4
- * bytes plus a work area of 4*(B+2) bytes rounded up to 256, are rejected with an error
+ * bytes plus a work area of 4*(B+3) + 8*B*Hkv*ceil(Smax/GTB_DECODE_CHUNK) bytes rounded up to 256,
+ * are rejected with an error
  * (config 5a, B=64 Hkv=8 H=32 D=128 Smax=32768, needs 34.1 MB).
  * The first call on a device sets up the array's device address (call it once before any stream
  * capture). Calls share the array: calls whose kernels overlap on the GPU race.
