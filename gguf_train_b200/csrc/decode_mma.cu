@@ -50,10 +50,10 @@ namespace {
 using namespace sm100;
 
 #ifndef GTB_DECODE_GROUPS
-#define GTB_DECODE_GROUPS 2
+#define GTB_DECODE_GROUPS 3
 #endif
 #ifndef GTB_DECODE_SLICES
-#define GTB_DECODE_SLICES 2
+#define GTB_DECODE_SLICES 1
 #endif
 constexpr int HD = 128;             // head size
 constexpr int NBLK = HD / 32;       // Q8_0 blocks per row
@@ -64,7 +64,7 @@ constexpr int SPW = GTB_DECODE_SLICES;   // 16-row slices per warp and tile
 constexpr int TILE = GW * 16 * SPW; // cached rows per tile: warp wi owns rows [16 SPW wi, 16 SPW (wi + 1))
 constexpr int RAWB = TILE * ROWB;   // raw bytes of a K (or V) tile
 constexpr int NCW = NGRP * GW;
-constexpr int RS = 2;               // stages per group ring
+constexpr int RS = 3;               // stages per group ring
 constexpr int NTHREADS = (NCW + NGRP) * 32;  // + one producer warp per group
 static_assert(GTB_DECODE_CHUNK % TILE == 0, "tiles must divide a chunk");
 constexpr int SMEM_LIMIT = 232448;
@@ -80,13 +80,13 @@ struct MC {
     static constexpr int QB = G * HD * 2;                        // q rows of the item's heads
     static constexpr int STAGE = 2 * RAWB + ((QB + 127) / 128) * 128;
     static constexpr int VST = 16 * 256;                         // per warp: one 16-row slice of V as f16
-    static constexpr int MRG = GW * G * HD * 4 + 2 * GW * G * 4; // per group and item parity: out [w][h][d], m, l [w][h]
+    // at the end of an item a warp's VST holds its partial: out [h][d] f32, then m [h], l [h]
+    static_assert(G * HD * 4 + 2 * G * 4 <= VST, "decode_mma: partial does not fit the V slice buffer");
     static constexpr int OFF_RAW = 0;                            // [NGRP][RS] stages
     static constexpr int OFF_VST = OFF_RAW + NGRP * RS * STAGE;
-    static constexpr int OFF_MRG = OFF_VST + NCW * VST;          // [NGRP][2]
-    static constexpr int OFF_META = OFF_MRG + NGRP * 2 * MRG;    // TileMeta [NGRP][RS]
+    static constexpr int OFF_META = OFF_VST + NCW * VST;         // TileMeta [NGRP][RS]
     static constexpr int OFF_BAR = OFF_META + NGRP * RS * 32;
-    static constexpr int NBAR = 2 * NGRP * RS + 4 * NGRP;        // full, empty [NGRP][RS]; mrg_full, mrg_done [NGRP][2]
+    static constexpr int NBAR = 2 * NGRP * RS + 2 * NGRP;        // full, empty [NGRP][RS]; mrg_full, mrg_done [NGRP]
     static constexpr int SMEM = OFF_BAR + NBAR * 8 + 16 + 128;
     static_assert(SMEM <= SMEM_LIMIT, "decode_mma shared memory");
 };
@@ -199,14 +199,14 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_mma_kernel(const DecMmaPar
     uint64_t* bars = (uint64_t*)(smem + C::OFF_BAR);
     uint64_t* full = bars;                                         // [NGRP][RS] stage loaded
     uint64_t* empty = full + NGRP * RS;                            // [NGRP][RS] stage released (GW warps)
-    uint64_t* mrg_full = empty + NGRP * RS;                        // [NGRP][2] partials written (GW warps)
-    uint64_t* mrg_done = mrg_full + NGRP * 2;                      // [NGRP][2] merge done reading (GW warps)
+    uint64_t* mrg_full = empty + NGRP * RS;                        // [NGRP] partials written (GW warps)
+    uint64_t* mrg_done = mrg_full + NGRP;                          // [NGRP] merge done reading (GW warps)
     int* abort_flag = (int*)(bars + C::NBAR);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
         for (int i = 0; i < NGRP * RS; ++i) { mbar_init(&full[i], 1); mbar_init(&empty[i], GW); }
-        for (int i = 0; i < NGRP * 2; ++i) { mbar_init(&mrg_full[i], GW); mbar_init(&mrg_done[i], GW); }
+        for (int i = 0; i < NGRP; ++i) { mbar_init(&mrg_full[i], GW); mbar_init(&mrg_done[i], GW); }
         *abort_flag = 0;
         fence_mbar_init();
     }
@@ -485,12 +485,11 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_mma_kernel(const DecMmaPar
 
         if (m.flags & F_LAST) {
             // ---------------------------------------------------- merge the group's 4 partials of the item
-            const int ip = nitem & 1;
-            float* mo = (float*)(smem + C::OFF_MRG + (gp * 2 + ip) * C::MRG);  // [w][h][d]
-            float* mm = mo + GW * G * HD;                                     // [w][h]
-            float* ml = mm + GW * G;                                          // [w][h]
-            if (nitem >= 2) ok = warp_wait(&mrg_done[gp * 2 + ip], ((nitem - 2) >> 1) & 1, p.status, 52);
-            if (!ok) break;
+            // Each warp's partial goes to its own V slice buffer (free after its PV); two group barriers
+            // per item: partials written, and every warp done reading before any buffer is reused.
+            float* mo = (float*)(smem + C::OFF_VST + warp * C::VST);  // [h][d]
+            float* mm = mo + G * HD;                                  // [h]
+            float* ml = mm + G;                                       // [h]
             float lsum = l_run;
             lsum += __shfl_xor_sync(0xffffffffu, lsum, 1);
             lsum += __shfl_xor_sync(0xffffffffu, lsum, 2);
@@ -504,30 +503,33 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_mma_kernel(const DecMmaPar
                     const int r = R0 + 2 * c + e;
                     if (r < NR && r / G == blk) {
                         const int h = r % G;
-                        mo[(wi * G + h) * HD + 16 * mt + g] = ot[mt][e] * invf;
-                        mo[(wi * G + h) * HD + 16 * mt + g + 8] = ot[mt][2 + e] * invf;
+                        mo[h * HD + 16 * mt + g] = ot[mt][e] * invf;
+                        mo[h * HD + 16 * mt + g + 8] = ot[mt][2 + e] * invf;
                     }
                 }
             }
             if (v0 && b0 == 0 && c == 0) {  // one lane per head
-                mm[wi * G + hh] = m_run;
-                ml[wi * G + hh] = lsum;
+                mm[hh] = m_run;
+                ml[hh] = lsum;
             }
             __syncwarp();
-            if (lane == 0) mbar_arrive(&mrg_full[gp * 2 + ip]);
-            ok = warp_wait(&mrg_full[gp * 2 + ip], (nitem >> 1) & 1, p.status, 53);
+            if (lane == 0) mbar_arrive(&mrg_full[gp]);
+            ok = warp_wait(&mrg_full[gp], nitem & 1, p.status, 53);
             if (!ok) break;
+            const float* gbase = (const float*)(smem + C::OFF_VST + gp * GW * C::VST);
+            constexpr int WSTRIDE = C::VST / 4;  // floats between the group's warps' buffers
             for (int pr2 = wi * 32 + lane; pr2 < G * HD; pr2 += GW * 32) {
                 const int h = pr2 / HD, d = pr2 % HD;
                 float M = -INFINITY;
 #pragma unroll
-                for (int w = 0; w < GW; ++w) M = fmaxf(M, mm[w * G + h]);
+                for (int w = 0; w < GW; ++w) M = fmaxf(M, gbase[w * WSTRIDE + G * HD + h]);
                 float L = 0.0f, O = 0.0f;
 #pragma unroll
                 for (int w = 0; w < GW; ++w) {
-                    const float a = mm[w * G + h] == -INFINITY ? 0.0f : ex2(mm[w * G + h] - M);
-                    L = fmaf(ml[w * G + h], a, L);
-                    O = fmaf(mo[(w * G + h) * HD + d], a, O);
+                    const float mw = gbase[w * WSTRIDE + G * HD + h];
+                    const float a = mw == -INFINITY ? 0.0f : ex2(mw - M);
+                    L = fmaf(gbase[w * WSTRIDE + G * HD + G + h], a, L);
+                    O = fmaf(gbase[w * WSTRIDE + h * HD + d], a, O);
                 }
                 const int64_t head = (int64_t)m.hk * G + h;
                 if (p.nchunks == 1) {
@@ -539,7 +541,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_mma_kernel(const DecMmaPar
                 }
             }
             __syncwarp();
-            if (lane == 0) mbar_arrive(&mrg_done[gp * 2 + ip]);
+            if (lane == 0) mbar_arrive(&mrg_done[gp]);
+            ok = warp_wait(&mrg_done[gp], nitem & 1, p.status, 52);
+            if (!ok) break;
 #pragma unroll
             for (int mt = 0; mt < 8; ++mt) ot[mt][0] = ot[mt][1] = ot[mt][2] = ot[mt][3] = 0.0f;
             ++nitem;
