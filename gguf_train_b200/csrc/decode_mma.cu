@@ -17,8 +17,9 @@
 //   P~[r, t]  = p_h(t) * dV(t, b) * f                         (f = 2^k per warp keeps P~ in the f16 range)
 //   O[r, d]  += P~[r, t] * Vx[t, d]                           (head dim d keeps row b(d)*G + h)
 //
-// The quants are exact integers in f16 (int8 -> f16 by a byte permute into 1024.0 + u and one
-// subtraction), so the products with the f16 query are exact; accumulation is f32.
+// The quants are exact integers in f16 (int8 -> f16 by a byte permute into 1024.0 + u; for K the
+// bias 1152 is left in and removed after the MMA), so the products with the f16 query are exact;
+// accumulation is f32.
 //
 // PV runs transposed, O^T[d, r] = Vx^T[d, t] P~^T[t, r], so that P~ (in the accumulator layout of
 // S') is directly the B operand and each 16 head dims need one MMA with the 8 operand rows of their
@@ -141,13 +142,11 @@ __device__ __forceinline__ uint32_t lds_u16(const unsigned char* p) {
     return v;
 }
 
-// two int8 (low 16 bits of x) -> f16x2 of the same integers: flip the sign bits (u = x + 128), place
-// u in the low byte of 1024.0 (0x6400 | u) and subtract 1152. Exact for every int8.
-__device__ __forceinline__ uint32_t i8x2_to_f16x2(uint32_t x) {
-    const uint32_t u = __byte_perm(x ^ 0x8080u, 0x64u, 0x4140u);
-    uint32_t r;
-    asm("sub.f16x2 %0, %1, %2;" : "=r"(r) : "r"(u), "r"(0x64806480u));
-    return r;
+// two int8 (low 16 bits of x) -> f16x2 of the biased integers 1152 + x: flip the sign bits
+// (u = x + 128) and place u in the low byte of 1024.0 (0x6400 | u = 1024 + u). Exact for every int8;
+// the bias is removed after the MMA (1152 * the sum of the other operand over the reduction).
+__device__ __forceinline__ uint32_t i8x2_to_f16x2_biased(uint32_t x) {
+    return __byte_perm(x ^ 0x8080u, 0x64u, 0x4140u);
 }
 
 // Half of a cached row (Q8_0 blocks 2*hb and 2*hb+1: 68 bytes starting at row + 68*hb) -> 64 f16
@@ -307,6 +306,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_mma_kernel(const DecMmaPar
     for (int mt = 0; mt < 8; ++mt) ot[mt][0] = ot[mt][1] = ot[mt][2] = ot[mt][3] = 0.0f;
     float m_run = -INFINITY, l_run = 0.0f;
     float f = 0.0f;  // power of two for P~; 0 = not chosen yet in this item
+    float qbias0 = 0.0f, qbias1 = 0.0f;  // -1152 * sum of q over the block of row g / row g + 8
     int nitem = 0;
     bool ok = true;
 
@@ -329,6 +329,22 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_mma_kernel(const DecMmaPar
                 qg8[e][0] = v1 ? q0[d1 >> 1] : 0u;
                 qg8[e][1] = v1 ? q0[(d1 + 8) >> 1] : 0u;
             }
+            // sum of each operand row over its block: the K operand carries +1152 per element
+            float qs0 = 0.0f, qs1 = 0.0f;
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+#pragma unroll
+                for (int j = 0; j < 2; ++j) {
+                    qs0 += half_lo(qg[e][j]) + half_hi(qg[e][j]);
+                    qs1 += half_lo(qg8[e][j]) + half_hi(qg8[e][j]);
+                }
+            }
+            qs0 += __shfl_xor_sync(0xffffffffu, qs0, 1);
+            qs0 += __shfl_xor_sync(0xffffffffu, qs0, 2);
+            qs1 += __shfl_xor_sync(0xffffffffu, qs1, 1);
+            qs1 += __shfl_xor_sync(0xffffffffu, qs1, 2);
+            qbias0 = -1152.0f * qs0;
+            qbias1 = -1152.0f * qs1;
             m_run = -INFINITY;
             l_run = 0.0f;
             f = 0.0f;
@@ -362,7 +378,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_mma_kernel(const DecMmaPar
                     // column tile nt holds the slice's rows 2n + nt (row order inside an MMA is free; rows
                     // 2 apart start 4 banks apart, so the 8 rows' 2-byte reads never share a bank)
                     const unsigned char* kr = st + (rb + 2 * g + nt) * ROWB + off;
-                    mma16816(sacc[nt][ks & 1], qa, i8x2_to_f16x2(lds_u16(kr)), i8x2_to_f16x2(lds_u16(kr + 8)));
+                    mma16816(sacc[nt][ks & 1], qa, i8x2_to_f16x2_biased(lds_u16(kr)), i8x2_to_f16x2_biased(lds_u16(kr + 8)));
                 }
             }
 #pragma unroll
@@ -375,8 +391,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_mma_kernel(const DecMmaPar
                 const int t = 4 * c + 2 * (k & 1) + (k >> 1);
                 const unsigned char* kr = st + (rb + t) * ROWB;
                 const unsigned char* vr = kr + RAWB;
-                const float s0 = sacc[k >> 1][0][k & 1] + sacc[k >> 1][1][k & 1];
-                const float s1 = sacc[k >> 1][0][2 + (k & 1)] + sacc[k >> 1][1][2 + (k & 1)];
+                const float s0 = sacc[k >> 1][0][k & 1] + sacc[k >> 1][1][k & 1] + qbias0;
+                const float s1 = sacc[k >> 1][0][2 + (k & 1)] + sacc[k >> 1][1][2 + (k & 1)] + qbias1;
                 float x = 0.0f;
                 dv0[k] = dv1[k] = 0.0f;
                 if (v0) {
