@@ -85,7 +85,13 @@ def cpu_sample(reps: int = 1, rows: int = 256):
 
     from oracle import oracle as O
 
-    threads = O.num_threads()
+    # every host core this process may run on (torchrun sets OMP_NUM_THREADS=1 for its ranks; the
+    # thread count is passed to the oracle explicitly)
+    try:
+        threads = len(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        threads = O.num_threads()
+    threads = max(1, threads)
     L, D, H = CFG["L"], CFG["D"], threads
     rng = np.random.default_rng(0)
     q = rng.standard_normal((1, H, rows, D)) * 0.5
