@@ -309,6 +309,70 @@ def run_train(args, rank: int, world: int, dev, max_over_ranks=lambda x: x) -> d
     return line
 
 
+# ------------------------------------------------------------------ long-context workload (config 5b)
+
+RING = dict(B=1, H=32, Hkv=8, L=131072, D=128)
+
+
+def run_ring(args, rank: int, world: int, dev, max_over_ranks=lambda x: x) -> dict:
+    """Config 5b: causal GQA forward of one 131072-token sequence, bf16, Hq=32 Hkv=8 D=128. One GPU
+    runs the whole sequence in one launch; N GPUs hold zig-zag shards and run the K/V ring
+    (gguf_train_b200.ring: N steps of native forwards on chunk pairs, log-sum-exp merges, K/V shards
+    passed on over NVLink with NCCL send/receive beside the compute). FLOPs: 4*Hq*D*L(L+1)/2."""
+    import torch
+
+    from gguf_train_b200 import _C
+    from gguf_train_b200 import functional as Fn
+    from gguf_train_b200 import ring
+
+    B, H, Hkv, L, D = RING["B"], RING["H"], RING["Hkv"], RING["L"], RING["D"]
+    g = torch.Generator(device=dev)
+    g.manual_seed(2024)  # the same sequence on every rank; each keeps its shard
+    q = (torch.randn((B, H, L, D), generator=g, device=dev) * 0.5).to(torch.bfloat16)
+    k = (torch.randn((B, Hkv, L, D), generator=g, device=dev) * 0.5).to(torch.bfloat16)
+    v = (torch.randn((B, Hkv, L, D), generator=g, device=dev) * 0.5).to(torch.bfloat16)
+    scale = 1.0 / math.sqrt(D)
+    if world > 1:
+        qs, ks, vs = (ring.shard_zigzag(t, world, rank) for t in (q, k, v))
+        del q, k, v
+
+        def step():
+            return ring.ring_attention(qs, ks, vs, scale)
+    else:
+        def step():
+            return Fn.sdpa_forward(q, k, v, None, scale, True, need_lse=False)[0]
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize(dev)
+    steps = max(3, min(args.steps, 10))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = max_over_ranks(e0.elapsed_time(e1) / steps)
+    flops = fwd_flops(B, H, L, D)
+    tf = flops / (ms * 1e-3) / 1e12
+    peaks = load_peaks()
+    kv_bytes = 2 * B * Hkv * L * D * 2
+    line = {
+        "workload": "config 5b: causal GQA prefill of one long sequence, bf16, B=1 Hq=32 Hkv=8 L=131072 D=128",
+        "value": tf, "unit": "TFLOP/s", "ms_per_step": ms, "steps": steps, "flops_per_step": flops,
+        "parallelism": (f"zig-zag sequence shards, K/V ring over {world} GPUs (NCCL send/recv beside the compute)"
+                        if world > 1 else "one GPU, one launch"),
+        "scaling": "strong",
+        "nvlink_bytes_per_rank_per_step": kv_bytes // world * (world - 1),
+        "roofline": {"bound": "tensor", "achieved": tf / world, "peak": peaks["bf16_tflops_sustained"],
+                     "unit": "TFLOP/s per GPU", "frac": tf / world / peaks["bf16_tflops_sustained"],
+                     "peak_source": peaks["source"] + " bf16 dense (sustained)"},
+        "status": _C.device_status(),
+    }
+    torch.cuda.empty_cache()
+    return line
+
+
 # ------------------------------------------------------------------ GPU arm
 
 def main() -> None:
@@ -321,8 +385,9 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--decode-batch", type=int, default=None,
                     help="sequences of the decode workload (default: config 5a's 64; smaller for profiling)")
-    ap.add_argument("--workload", default="prefill", choices=["prefill", "decode", "train"],
-                    help="prefill: config 3 (the default line); train: config 4 fwd+bwd; decode: config 5a")
+    ap.add_argument("--workload", default="prefill", choices=["prefill", "decode", "train", "ring"],
+                    help="prefill: config 3 (the default line); train: config 4 fwd+bwd; decode: config 5a; "
+                         "ring: config 5b (one long sequence, K/V ring over the GPUs)")
     ap.add_argument("--no-extra", action="store_true",
                     help="default line without the fwd+bwd (config 4) and decode (config 5a) measurements")
     args = ap.parse_args()
@@ -358,13 +423,14 @@ def main() -> None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    if args.workload in ("decode", "train"):
+    if args.workload in ("decode", "train", "ring"):
         barrier()
-        runner = run_decode if args.workload == "decode" else run_train
+        runner = {"decode": run_decode, "train": run_train, "ring": run_ring}[args.workload]
         res = runner(args, rank, world, dev, max_over_ranks)
-        if args.workload == "train":
-            res = dict(metric=METRIC, n_gpus=world, steps=max(3, min(args.steps, 20)), warmup=max(args.warmup, 3),
-                       higher_is_better=True, scaling="weak", vs_baseline=None, dtype="bf16",
+        if args.workload in ("train", "ring"):
+            scaling = res.pop("scaling", "weak")
+            res = dict(metric=METRIC, n_gpus=world, steps=res.pop("steps", max(3, min(args.steps, 20))),
+                       warmup=max(args.warmup, 3), higher_is_better=True, scaling=scaling, vs_baseline=None, dtype="bf16",
                        data="synthetic: seeded normal inputs generated on the device",
                        config={"workload": res.pop("workload")}, **res)
         if world > 1:
@@ -476,6 +542,8 @@ def main() -> None:
         line["extra"] = {"fwd_bwd": run_train(args, rank, world, dev, max_over_ranks)}
         barrier()
         line["extra"]["decode_q8_0"] = run_decode(args, rank, world, dev, max_over_ranks)
+        barrier()
+        line["extra"]["long_context_ring"] = run_ring(args, rank, world, dev, max_over_ranks)
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
         cv, threads, desc = cpu_sample(2)
         line["cpu_baseline"] = {"value": cv, "unit": "TFLOP/s", "cores": threads, "kind": "port", "sample": desc}

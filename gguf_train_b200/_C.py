@@ -59,6 +59,9 @@ def _configure(lib: ctypes.CDLL) -> ctypes.CDLL:
     lib.gtb_decode_q8_0.restype = c_int
     lib.gtb_decode_q8_0_noalloc.argtypes = list(lib.gtb_decode_q8_0.argtypes)
     lib.gtb_decode_q8_0_noalloc.restype = c_int
+    lib.gtb_attn_merge.argtypes = [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int64, c_int64, c_int64, c_int64,
+                                   c_int64, c_void_p]
+    lib.gtb_attn_merge.restype = c_int
     lib.gtb_last_error.argtypes = []
     lib.gtb_last_error.restype = c_char_p
     lib.gtb_clear_error.argtypes = []

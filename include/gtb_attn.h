@@ -103,6 +103,16 @@ GTB_API int gtb_decode_q8_0_noalloc(const void *q, int q_dtype, const void *k_q8
                                     const int32_t *seq_lens, int64_t B, int64_t H, int64_t Hkv,
                                     int64_t Smax, int64_t D, float scale, void *out, void *stream);
 
+/* Log-sum-exp merge of a partial attention result into an accumulator (the combine step of the
+ * long-context K/V ring: a causal attention over a sequence sharded across GPUs):
+ *   o_acc: groups x rows x D float32, lse_acc: groups x rows float32 (contiguous; start at 0 / -inf),
+ *   o_part: element g*part_gstride + r*D + d of part_dtype (f32/f16/bf16), lse_part: g*lse_gstride + r
+ *   (natural-log sums as gtb_sdpa_fwd writes them). Rows with lse -inf contribute nothing.
+ * No counterpart in the reference, which has no multi-device path. */
+GTB_API int gtb_attn_merge(float *o_acc, float *lse_acc, const void *o_part, const float *lse_part,
+                           int part_dtype, int64_t groups, int64_t rows, int64_t D, int64_t part_gstride,
+                           int64_t lse_gstride, void *stream);
+
 /* Thread-local message of the last failure ("" if none). */
 GTB_API const char *gtb_last_error(void);
 GTB_API void gtb_clear_error(void);
