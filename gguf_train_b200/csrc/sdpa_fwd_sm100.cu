@@ -222,17 +222,25 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
             constexpr uint32_t IDESC_S = idesc_f16(BM, BN, BF16, false);
             constexpr uint32_t IDESC_PV = idesc_f16(BM, D, BF16, true);
             bool ok = mbar_wait(q_full, 0, p.status, 21);
+            // operand descriptors of every buffer, built once: per MMA only a constant is added to the
+            // start address
+            static_assert(C::KS == 2 && C::VS == 2, "descriptor selection below assumes two K and two V stages");
+            const uint64_t qd0 = desc_sw128(smem_u32(smem + C::OFF_Q), 16, 1024);
+            const uint64_t qd1 = desc_sw128(smem_u32(smem + C::OFF_Q + C::TILE), 16, 1024);
+            const uint64_t kd0 = desc_sw128(smem_u32(smem + C::OFF_K), 16, 1024);
+            const uint64_t kd1 = desc_sw128(smem_u32(smem + C::OFF_K + C::TILE), 16, 1024);
+            const uint64_t vd0 = desc_sw128(smem_u32(smem + C::OFF_V), C::ATOM_BYTES, 1024);
+            const uint64_t vd1 = desc_sw128(smem_u32(smem + C::OFF_V + C::TILE), C::ATOM_BYTES, 1024);
             auto issue_s = [&](int t, int j) -> bool {
                 const int ks = j % C::KS;
                 if (!mbar_wait(&k_full[ks], (j / C::KS) & 1, p.status, 22)) return false;
                 tc_fence_after();
-                const uint32_t q_addr = smem_u32(smem + C::OFF_Q + t * C::TILE);
-                const uint32_t k_addr = smem_u32(smem + C::OFF_K + ks * C::TILE);
+                const uint64_t qb = t ? qd1 : qd0, kb = ks ? kd1 : kd0;
+                const uint32_t dst = tmem + s_col(t);
 #pragma unroll
                 for (int kk = 0; kk < D / 16; ++kk) {
                     const uint32_t off = (uint32_t)((kk / 4) * C::ATOM_BYTES + (kk % 4) * 32);
-                    mma_ss(tmem + s_col(t), desc_sw128(q_addr + off, 16, 1024), desc_sw128(k_addr + off, 16, 1024),
-                           IDESC_S, kk > 0 ? 1u : 0u);
+                    mma_ss(dst, desc_advance(qb, off), desc_advance(kb, off), IDESC_S, kk > 0 ? 1u : 0u);
                 }
                 mma_commit(&s_full[t]);
                 return true;
@@ -242,13 +250,12 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
                 const int vs = j % C::VS;
                 if (!mbar_wait(&v_full[vs], (j / C::VS) & 1, p.status, 24)) return false;
                 tc_fence_after();
-                const uint32_t v_addr = smem_u32(smem + C::OFF_V + vs * C::TILE);
+                const uint64_t vb = vs ? vd1 : vd0;
+                const uint32_t dst = tmem + o_col(t), pa = tmem + s_col(t) + P_OFF;
 #pragma unroll
                 for (int kk = 0; kk < BN / 16; ++kk) {
-                    const uint64_t bdesc = desc_sw128(v_addr + kk * 2048, C::ATOM_BYTES, 1024);
                     // A = P_t(j): 16-bit values packed two per TMEM column, 8 columns per K step
-                    mma_ts(tmem + o_col(t), tmem + s_col(t) + P_OFF + kk * 8, bdesc, IDESC_PV,
-                           (j > 0 || kk > 0) ? 1u : 0u);
+                    mma_ts(dst, pa + kk * 8, desc_advance(vb, kk * 2048), IDESC_PV, (j > 0 || kk > 0) ? 1u : 0u);
                 }
                 return true;
             };

@@ -220,6 +220,10 @@ __device__ __forceinline__ uint64_t desc_sw128(uint32_t saddr, uint32_t lbo, uin
     return d;
 }
 
+// The descriptor of the same operand `bytes` further on (bytes a multiple of 16): only the start
+// address field changes, and shared-memory addresses stay below 2^18, so the 14-bit field cannot carry.
+__device__ __forceinline__ uint64_t desc_advance(uint64_t desc, uint32_t bytes) { return desc + (uint64_t)(bytes >> 4); }
+
 // Instruction descriptor of tcgen05.mma kind::f16 with f32 accumulation:
 //   [4,6) D format (1 = f32), [7,10) A format, [10,13) B format (0 = f16, 1 = bf16),
 //   [15] A major (0 = K), [16] B major (0 = K, 1 = MN), [17,23) N >> 3, [24,29) M >> 4.
