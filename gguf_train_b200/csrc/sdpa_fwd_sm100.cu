@@ -98,6 +98,26 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
     return r;
 }
 
+// two f32 lanes in one 64-bit register, and the packed two-lane FMA / add of sm_100
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& lo, float& hi) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t r;
+    asm("fma.rn.ftz.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("add.rn.ftz.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+
 // the same bounded wait taken by a whole warp: every lane gets the same answer
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* status, int code) {
     const bool ok = mbar_wait(bar, parity, status, code);
@@ -339,17 +359,19 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
                 m_used = m_new;
             }
             const float neg_m = (m_used == -INFINITY) ? 0.0f : -m_used;
-            float ps[4] = {0.f, 0.f, 0.f, 0.f};
-            // pass 2: exponentials, 32 columns at a time, P into S's columns [64, 128)
+            // pass 2: exponentials, 32 columns at a time, P into S's columns [64, 128); the scale-and-
+            // subtract and the row sum run as packed two-lane f32 operations
+            const uint64_t sc2 = f2_pack(p.scale_log2, p.scale_log2), nm2 = f2_pack(neg_m, neg_m);
+            uint64_t ps2[2] = {0ull, 0ull};
             auto emit = [&](const float* x, int c) {
                 uint32_t pk[16];
 #pragma unroll
                 for (int i = 0; i < 32; i += 2) {
-                    const float a0 = fmaf(x[i], p.scale_log2, neg_m);
-                    const float a1 = fmaf(x[i + 1], p.scale_log2, neg_m);
+                    float a0, a1;
+                    f2_unpack(f2_fma(f2_pack(x[i], x[i + 1]), sc2, nm2), a0, a1);
                     const float p0 = (i & 7) < EMU ? exp2_poly(a0) : ex2(a0);
                     const float p1 = ((i + 1) & 7) < EMU ? exp2_poly(a1) : ex2(a1);
-                    ps[(i >> 1) & 3] += p0 + p1;
+                    ps2[(i >> 1) & 1] = f2_add(ps2[(i >> 1) & 1], f2_pack(p0, p1));
                     pk[i / 2] = pack2<BF16>(p0, p1);
                 }
                 tmem_st16(s_tmem + P_OFF + c * 16, pk);
@@ -364,7 +386,12 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
             if (need_mask) { mask_chunk(xa, kv0, lim); mask_chunk(xb, kv0 + 32, lim); }
             emit(xa, 0);
             emit(xb, 1);
-            lsum += (ps[0] + ps[1]) + (ps[2] + ps[3]);
+            {
+                float s0, s1, s2, s3;
+                f2_unpack(ps2[0], s0, s1);
+                f2_unpack(ps2[1], s2, s3);
+                lsum += (s0 + s1) + (s2 + s3);
+            }
             tmem_st_wait();
             tc_fence_before();
             mbar_arrive(&p_full[t]);
