@@ -118,6 +118,13 @@ __device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
     return r;
 }
 
+// max of three (one instruction on sm_100)
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+    float r;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
+}
+
 // the same bounded wait taken by a whole warp: every lane gets the same answer
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* status, int code) {
     const bool ok = mbar_wait(bar, parity, status, code);
@@ -330,15 +337,14 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
 #pragma unroll
             for (int u = 0; u < 8; ++u) pm[u] = fmaxf(xa[u], xb[u]);
 #pragma unroll
-            for (int i = 8; i < 32; ++i) pm[i & 7] = fmaxf(pm[i & 7], fmaxf(xa[i], xb[i]));
+            for (int i = 8; i < 32; ++i) pm[i & 7] = fmax3(pm[i & 7], xa[i], xb[i]);
             tmem_ld32(s_tmem + 64, ra);
             tmem_ld32(s_tmem + 96, rb);
             tmem_ld_wait();
             if (need_mask) { mask_chunk(xa, kv0 + 64, lim); mask_chunk(xb, kv0 + 96, lim); }
 #pragma unroll
-            for (int i = 0; i < 32; ++i) pm[i & 7] = fmaxf(pm[i & 7], fmaxf(xa[i], xb[i]));
-            const float mx = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])),
-                                   fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7])));
+            for (int i = 0; i < 32; ++i) pm[i & 7] = fmax3(pm[i & 7], xa[i], xb[i]);
+            const float mx = fmax3(fmax3(pm[0], pm[1], pm[2]), fmax3(pm[3], pm[4], pm[5]), fmaxf(pm[6], pm[7]));
             const float m_new = fmaxf(m_used, mx * p.scale_log2);
             const bool rescale = m_new > m_used + 8.0f;  // false while the row has no finite score
             if (__any_sync(0xffffffffu, rescale && j > 0)) {
