@@ -219,21 +219,29 @@ bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
         if (lane == 0 && nit > 0) {
             constexpr uint32_t IDESC_S = idesc_f16(BT, BT, BF16, false);
             constexpr uint32_t IDESC_ACC = idesc_f16(BT, D, BF16, true);
-            const uint32_t k_addr = smem_u32(smem + OFF_K), v_addr = smem_u32(smem + OFF_V);
+            // operand descriptors built once; per MMA only a constant is added to the start address
+            const uint64_t kdk = kmajor(smem_u32(smem + OFF_K), 0, C::SLAB), vdk = kmajor(smem_u32(smem + OFF_V), 0, C::SLAB);
+            const uint64_t qk0 = kmajor(smem_u32(smem + OFF_ST), 0, C::SLAB);
+            const uint64_t qk1 = kmajor(smem_u32(smem + OFF_ST + ST_BYTES), 0, C::SLAB);
+            const uint64_t qm0 = mnmajor(smem_u32(smem + OFF_ST), 0, C::SLAB);
+            const uint64_t qm1 = mnmajor(smem_u32(smem + OFF_ST + ST_BYTES), 0, C::SLAB);
             bool ok = mbar_wait(kv_full, 0, p.status, 42);
             for (int it = 0; it < nit && ok; ++it) {
                 const int st = it & 1;
                 ok = mbar_wait(&st_full[st], (it >> 1) & 1, p.status, 43);
                 if (!ok || *(volatile int*)abort_flag) break;
                 tc_fence_after();
-                const uint32_t q_addr = smem_u32(smem + OFF_ST + st * ST_BYTES);
-                const uint32_t g_addr = q_addr + C::TILE;
+                const uint64_t qk = st ? qk1 : qk0, qm = st ? qm1 : qm0;
 #pragma unroll
-                for (int kk = 0; kk < D / 16; ++kk)
-                    mma_ss(tmem + 256, kmajor(k_addr, kk, C::SLAB), kmajor(q_addr, kk, C::SLAB), IDESC_S, kk > 0);
+                for (int kk = 0; kk < D / 16; ++kk) {
+                    const uint32_t off = (uint32_t)((kk / 4) * C::SLAB + (kk % 4) * 32);
+                    mma_ss(tmem + 256, desc_advance(kdk, off), desc_advance(qk, off), IDESC_S, kk > 0);
+                }
 #pragma unroll
-                for (int kk = 0; kk < D / 16; ++kk)
-                    mma_ss(tmem + 384, kmajor(v_addr, kk, C::SLAB), kmajor(g_addr, kk, C::SLAB), IDESC_S, kk > 0);
+                for (int kk = 0; kk < D / 16; ++kk) {
+                    const uint32_t off = (uint32_t)((kk / 4) * C::SLAB + (kk % 4) * 32);
+                    mma_ss(tmem + 384, desc_advance(vdk, off), desc_advance(qk, off + C::TILE), IDESC_S, kk > 0);
+                }
                 mma_commit(s_full);
                 ok = mbar_wait(p_full, it & 1, p.status, 44);
                 if (!ok) break;
@@ -241,8 +249,8 @@ bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
 #pragma unroll
                 for (int kk = 0; kk < BT / 16; ++kk) {
                     const uint32_t acc = (it > 0 || kk > 0) ? 1u : 0u;
-                    mma_ts(tmem + 0, tmem + 256 + kk * 8, mnmajor(g_addr, kk, C::SLAB), IDESC_ACC, acc);   // dV
-                    mma_ts(tmem + 128, tmem + 384 + kk * 8, mnmajor(q_addr, kk, C::SLAB), IDESC_ACC, acc); // dK
+                    mma_ts(tmem + 0, tmem + 256 + kk * 8, desc_advance(qm, kk * 2048 + C::TILE), IDESC_ACC, acc);  // dV
+                    mma_ts(tmem + 128, tmem + 384 + kk * 8, desc_advance(qm, kk * 2048), IDESC_ACC, acc);          // dK
                 }
                 mma_commit(&st_empty[st]);
             }
@@ -269,6 +277,7 @@ bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
             tc_fence_after();
             const float* lse_s = (const float*)(smem + OFF_ST + st * ST_BYTES + 2 * C::TILE);
             const float* dl_s = lse_s + 128;
+            const uint64_t sc2 = f2_pack(p.scale_log2, p.scale_log2);
             const bool need_mask = p.causal && (q0 < key0 + BT - 1);
 #pragma unroll
             for (int c = 0; c < 4; ++c) {
@@ -278,17 +287,22 @@ bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
                 tmem_ld_wait();
 #pragma unroll
                 for (int i = 0; i < 32; i += 2) {
-                    float pv[2], dsv[2];
-#pragma unroll
-                    for (int u = 0; u < 2; ++u) {
-                        const int qc = c * 32 + i + u;
-                        float pr = ex2(fmaf(__uint_as_float(ra[i + u]), p.scale_log2, -lse_s[qc]));
-                        if (need_mask && key > q0 + qc) pr = 0.0f;
-                        pv[u] = pr;
-                        dsv[u] = pr * (__uint_as_float(rb[i + u]) - dl_s[qc]);
-                    }
-                    pk[i / 2] = pack2<BF16>(pv[0], pv[1]);
-                    dk[i / 2] = pack2<BF16>(dsv[0], dsv[1]);
+                    // packed two-lane f32: a = S * scale - lse2, ds = p * (dP - delta)
+                    const int qc = c * 32 + i;
+                    const float2 ls2 = *(const float2*)(lse_s + qc);
+                    const float2 dl2 = *(const float2*)(dl_s + qc);
+                    float a0, a1;
+                    f2_unpack(f2_fma(f2_pack(__uint_as_float(ra[i]), __uint_as_float(ra[i + 1])), sc2,
+                                     f2_pack(-ls2.x, -ls2.y)), a0, a1);
+                    float p0 = ex2(a0), p1 = ex2(a1);
+                    if (need_mask && key > q0 + qc) p0 = 0.0f;
+                    if (need_mask && key > q0 + qc + 1) p1 = 0.0f;
+                    const uint64_t pp = f2_pack(p0, p1);
+                    float d0, d1;
+                    f2_unpack(f2_mul(pp, f2_add(f2_pack(__uint_as_float(rb[i]), __uint_as_float(rb[i + 1])),
+                                                f2_pack(-dl2.x, -dl2.y))), d0, d1);
+                    pk[i / 2] = pack2<BF16>(p0, p1);
+                    dk[i / 2] = pack2<BF16>(d0, d1);
                 }
                 tmem_st16(tmem + lane_addr + 256 + c * 16, pk);
                 tmem_st16(tmem + lane_addr + 384 + c * 16, dk);
@@ -438,6 +452,7 @@ bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
             constexpr uint32_t IDESC_DQ = idesc_f16(BT, D, BF16, true);
             const uint32_t q_addr = smem_u32(smem + OFF_Q), g_addr = smem_u32(smem + OFF_G);
             bool ok = mbar_wait(qg_full, 0, p.status, 53);
+            const uint64_t qk0 = kmajor(q_addr, 0, C::SLAB), gk0 = kmajor(g_addr, 0, C::SLAB);
             for (int j = 0; j < nblk && ok; ++j) {
                 const int s = j & 1;
                 const uint32_t k_addr = smem_u32(smem + OFF_K + s * C::TILE);
@@ -445,15 +460,21 @@ bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
                 ok = mbar_wait(&k_full[s], (j >> 1) & 1, p.status, 54);
                 if (!ok || *(volatile int*)abort_flag) break;
                 tc_fence_after();
+                const uint64_t kk0 = kmajor(k_addr, 0, C::SLAB), vk0 = kmajor(v_addr, 0, C::SLAB);
+                const uint64_t km0 = mnmajor(k_addr, 0, C::SLAB);
 #pragma unroll
-                for (int kk = 0; kk < D / 16; ++kk)
-                    mma_ss(tmem + 0, kmajor(q_addr, kk, C::SLAB), kmajor(k_addr, kk, C::SLAB), IDESC_S, kk > 0);
+                for (int kk = 0; kk < D / 16; ++kk) {
+                    const uint32_t off = (uint32_t)((kk / 4) * C::SLAB + (kk % 4) * 32);
+                    mma_ss(tmem + 0, desc_advance(qk0, off), desc_advance(kk0, off), IDESC_S, kk > 0);
+                }
                 ok = mbar_wait(&v_full[s], (j >> 1) & 1, p.status, 55);
                 if (!ok) break;
                 tc_fence_after();
 #pragma unroll
-                for (int kk = 0; kk < D / 16; ++kk)
-                    mma_ss(tmem + 128, kmajor(g_addr, kk, C::SLAB), kmajor(v_addr, kk, C::SLAB), IDESC_S, kk > 0);
+                for (int kk = 0; kk < D / 16; ++kk) {
+                    const uint32_t off = (uint32_t)((kk / 4) * C::SLAB + (kk % 4) * 32);
+                    mma_ss(tmem + 128, desc_advance(gk0, off), desc_advance(vk0, off), IDESC_S, kk > 0);
+                }
                 mma_commit(s_full);
                 mma_commit(&v_empty[s]);
                 ok = mbar_wait(ds_full, j & 1, p.status, 56);
@@ -461,7 +482,7 @@ bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
                 tc_fence_after();
 #pragma unroll
                 for (int kk = 0; kk < BT / 16; ++kk)
-                    mma_ts(tmem + 256, tmem + 0 + kk * 8, mnmajor(k_addr, kk, C::SLAB), IDESC_DQ, (j > 0 || kk > 0) ? 1u : 0u);
+                    mma_ts(tmem + 256, tmem + 0 + kk * 8, desc_advance(km0, kk * 2048), IDESC_DQ, (j > 0 || kk > 0) ? 1u : 0u);
                 mma_commit(&k_empty[s]);
             }
             if (!ok) *(volatile int*)abort_flag = 1;
@@ -480,6 +501,7 @@ bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
         const int64_t prow = ((int64_t)b * p.H + h) * p.Lpad + row;  // row < Lpad
         const float lse2 = p.lse2[prow];
         const float dl = p.delta[prow];
+        const uint64_t sc2 = f2_pack(p.scale_log2, p.scale_log2), nl2 = f2_pack(-lse2, -lse2), nd2 = f2_pack(-dl, -dl);
         const int lim_s = (int)min(p.S, (int64_t)INT32_MAX) - 1;
         const int lim = p.causal ? min(lim_s, row) : lim_s;  // last key this row may see
         bool ok = true;
@@ -497,14 +519,16 @@ bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
                 tmem_ld_wait();
 #pragma unroll
                 for (int i = 0; i < 32; i += 2) {
-                    float dsv[2];
-#pragma unroll
-                    for (int u = 0; u < 2; ++u) {
-                        float pr = ex2(fmaf(__uint_as_float(ra[i + u]), p.scale_log2, -lse2));
-                        if (need_mask && kv0 + c * 32 + i + u > lim) pr = 0.0f;
-                        dsv[u] = pr * (__uint_as_float(rb[i + u]) - dl);
-                    }
-                    pk[i / 2] = pack2<BF16>(dsv[0], dsv[1]);
+                    // packed two-lane f32: a = S * scale - lse2, ds = p * (dP - delta)
+                    float a0, a1;
+                    f2_unpack(f2_fma(f2_pack(__uint_as_float(ra[i]), __uint_as_float(ra[i + 1])), sc2, nl2), a0, a1);
+                    float p0 = ex2(a0), p1 = ex2(a1);
+                    if (need_mask && kv0 + c * 32 + i > lim) p0 = 0.0f;
+                    if (need_mask && kv0 + c * 32 + i + 1 > lim) p1 = 0.0f;
+                    float d0, d1;
+                    f2_unpack(f2_mul(f2_pack(p0, p1), f2_add(f2_pack(__uint_as_float(rb[i]), __uint_as_float(rb[i + 1])), nd2)),
+                              d0, d1);
+                    pk[i / 2] = pack2<BF16>(d0, d1);
                 }
                 tmem_st16(tmem + lane_addr + c * 16, pk);
             }
