@@ -186,53 +186,101 @@ __device__ __forceinline__ uint2 dequant_row(const unsigned char* row, unsigned 
     return scales;
 }
 
-// items of sequence b: Hkv kv heads x max(1, ceil(len / chunk)) chunks
-__device__ __forceinline__ int seq_items(const int32_t* lens, int64_t b, int64_t Smax, int64_t Hkv, int chunk) {
-    int64_t len = lens[b];
-    len = len < 0 ? 0 : (len > Smax ? Smax : len);
-    const int64_t nch = len == 0 ? 1 : (len + chunk - 1) / chunk;
-    return (int)(Hkv * nch);
-}
-
-// One block: work[1 + b] = items of sequences < b, work[1 + B] = all items, work[0] = 0 (the counter),
-// and the item list at work + list_off: item prefix[b] + hk * nch_b + c is (b, hk << 16 | c).
-__global__ void decode_plan_kernel(const int32_t* lens, int64_t B, int64_t Smax, int64_t Hkv, int chunk, int* work,
-                                   int64_t list_off) {
-    __shared__ int wsum[32];
-    const int tid = threadIdx.x, nt = blockDim.x, lane = tid & 31, warp = tid >> 5;
-    const int64_t per = (B + nt - 1) / nt;
-    const int64_t b0 = (int64_t)tid * per, b1 = min(B, b0 + per);
-    int local = 0;
-    for (int64_t b = b0; b < b1; ++b) local += seq_items(lens, b, Smax, Hkv, chunk);
-    int x = local;
+// Block-wide exclusive scan of one int64 per thread (blockDim.x a multiple of 32, at most 1024);
+// returns the exclusive prefix, *total gets the sum.
+__device__ __forceinline__ long long block_scan_excl(long long v, long long* wsum, long long* total) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    long long x = v;
 #pragma unroll
     for (int off = 1; off < 32; off <<= 1) {
-        const int y = __shfl_up_sync(0xffffffffu, x, off);
+        const long long y = __shfl_up_sync(0xffffffffu, x, off);
         if (lane >= off) x += y;
     }
     if (lane == 31) wsum[warp] = x;
     __syncthreads();
     if (warp == 0) {
-        int s = lane < (nt >> 5) ? wsum[lane] : 0;
+        long long s = lane < nw ? wsum[lane] : 0;
 #pragma unroll
         for (int off = 1; off < 32; off <<= 1) {
-            const int y = __shfl_up_sync(0xffffffffu, s, off);
+            const long long y = __shfl_up_sync(0xffffffffu, s, off);
             if (lane >= off) s += y;
         }
         wsum[lane] = s;
     }
     __syncthreads();
-    int run = x - local + (warp > 0 ? wsum[warp - 1] : 0);
-    int2* list = (int2*)(work + list_off);
+    *total = wsum[nw - 1];
+    return x - v + (warp > 0 ? wsum[warp - 1] : 0);
+}
+
+// One block plans the items of a decode call. work[0] = 0 (the claim counter); work[1 + b] = items of
+// sequences < b and work[1 + B] = all items (the tcgen05 kernel maps an item index to its sequence
+// with these); work[B + 2 + b] = full-chunk items of sequences < b. The item list at work + list_off
+// holds (b, hk << 16 | c): first every full chunk (sequence-major), then the last, partial chunk of
+// every sequence, by decreasing size (16 size classes), so that the persistent kernels end on small
+// items and their groups run out of work at nearly the same time. Each warp writes the list entries
+// of one sequence at a time.
+__global__ void decode_plan_kernel(const int32_t* lens, int64_t B, int64_t Smax, int64_t Hkv, int chunk, int* work,
+                                   int64_t list_off) {
+    constexpr int NCLS = 17;  // size classes of a partial chunk: ceil(16 * rows / chunk), 0 .. 16
+    __shared__ long long wsum[32];
+    __shared__ int hist[NCLS], cursor[NCLS];
+    const int tid = threadIdx.x, nt = blockDim.x, lane = tid & 31, warp = tid >> 5;
+    if (tid < NCLS) hist[tid] = 0;
+    __syncthreads();
+    const int64_t per = (B + nt - 1) / nt;
+    const int64_t b0 = (int64_t)tid * per, b1 = min(B, b0 + per);
+    auto seq_len = [&](int64_t b) -> int64_t {
+        const int64_t len = lens[b];
+        return len < 0 ? 0 : (len > Smax ? Smax : len);
+    };
+    // per sequence: nch = max(1, ceil(len / chunk)) chunks, of which `full` hold chunk rows
+    long long la = 0, lf = 0;
     for (int64_t b = b0; b < b1; ++b) {
-        work[1 + b] = run;
-        const int n = seq_items(lens, b, Smax, Hkv, chunk);
-        const int nch = n / (int)Hkv;
-        for (int j = 0; j < n; ++j) list[run + j] = make_int2((int)b, ((j / nch) << 16) | (j % nch));
-        run += n;
+        const int64_t len = seq_len(b);
+        const int64_t nch = len == 0 ? 1 : (len + chunk - 1) / chunk;
+        const int64_t full = len / chunk;
+        la += Hkv * nch;
+        lf += Hkv * full;
+        if (nch > full) atomicAdd(&hist[(int)((16 * (len - full * chunk) + chunk - 1) / chunk)], (int)Hkv);
     }
-    if (tid == nt - 1) work[1 + B] = run;
-    if (tid == 0) work[0] = 0;
+    long long tot_all, tot_full;
+    const long long pa = block_scan_excl((la << 32) | lf, wsum, &tot_all);  // both halves stay below 2^31
+    tot_full = tot_all & 0xffffffffll;
+    tot_all >>= 32;
+    long long ra = pa >> 32, rf = pa & 0xffffffffll;
+    for (int64_t b = b0; b < b1; ++b) {
+        const int64_t len = seq_len(b);
+        work[1 + b] = (int)ra;
+        work[B + 2 + b] = (int)rf;
+        ra += Hkv * (len == 0 ? 1 : (len + chunk - 1) / chunk);
+        rf += Hkv * (len / chunk);
+    }
+    if (tid == 0) {
+        work[0] = 0;
+        work[1 + B] = (int)tot_all;
+        work[2 * B + 2] = (int)tot_full;
+        int start = (int)tot_full;  // partial chunks after the full ones, largest class first
+        for (int k = NCLS - 1; k >= 0; --k) {
+            cursor[k] = start;
+            start += hist[k];
+        }
+    }
+    __syncthreads();  // the prefixes (global, written by this block) and the cursors are visible
+    int2* list = (int2*)(work + list_off);
+    for (int64_t b = warp; b < B; b += nt >> 5) {
+        const int64_t len = seq_len(b);
+        const int full = (int)(len / chunk);
+        const int nfull = full * (int)Hkv;
+        const int base = work[B + 2 + b];
+        for (int j = lane; j < nfull; j += 32) list[base + j] = make_int2((int)b, ((j / full) << 16) | (j % full));
+        const int64_t nch = len == 0 ? 1 : (len + chunk - 1) / chunk;
+        if (nch > full) {
+            int pos = 0;
+            if (lane == 0) pos = atomicAdd(&cursor[(int)((16 * (len - (int64_t)full * chunk) + chunk - 1) / chunk)], (int)Hkv);
+            pos = __shfl_sync(0xffffffffu, pos, 0);
+            for (int hk = lane; hk < Hkv; hk += 32) list[pos + hk] = make_int2((int)b, (hk << 16) | full);
+        }
+    }
 }
 
 template <int G>

@@ -394,6 +394,72 @@ __global__ void decode_combine_kernel(DecP p) {
     else ((float*)p.out)[oi] = r;
 }
 
+// The same merge for D = 128, one warp per (b, query head): the lanes first take one chunk each for
+// the maximum and the weights 2^(m_c - M), then every lane accumulates its d pairs (2 lane, 2 lane + 1)
+// and (64 + 2 lane, 65 + 2 lane) over the chunks with independent loads (the weight of chunk j comes
+// from lane j by shuffle). Latency-bound work, so many loads in flight per lane.
+__global__ void __launch_bounds__(256) decode_combine128_kernel(DecP p) {
+    constexpr int D = 128, ST = D + 2;
+    const int lane = threadIdx.x & 31;
+    const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (row >= p.B * p.H) return;
+    const int64_t b = row / p.H, h = row % p.H, hk = h / p.G, g = h % p.G;
+    int64_t len = p.lens[b];
+    len = len < 0 ? 0 : (len > p.Smax ? p.Smax : len);
+    const int nch = (int)max((int64_t)1, (len + p.chunk - 1) / p.chunk);
+    const float* base = p.part + (((b * p.Hkv + hk) * p.nchunks) * p.G + g) * ST;
+    const int64_t cst = p.G * ST;  // floats between consecutive chunks of one head
+    float mm = -INFINITY;
+    for (int c = lane; c < nch; c += 32) mm = fmaxf(mm, base[c * cst + D]);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) mm = fmaxf(mm, __shfl_xor_sync(0xffffffffu, mm, off));
+    float ll = 0.0f, o0 = 0.0f, o1 = 0.0f, o2 = 0.0f, o3 = 0.0f;
+    for (int c0 = 0; c0 < nch; c0 += 32) {
+        const int c = c0 + lane;
+        float w = 0.0f;
+        if (c < nch) {
+            const float mc = base[c * cst + D];
+            w = mc == -INFINITY ? 0.0f : fast_exp2(mc - mm);
+            ll = fmaf(w, base[c * cst + D + 1], ll);
+        }
+        const int n = min(32, nch - c0);
+#pragma unroll 4
+        for (int j = 0; j < n; ++j) {
+            const float wj = __shfl_sync(0xffffffffu, w, j);
+            const float* e = base + (c0 + j) * cst;
+            const float2 x0 = *(const float2*)(e + 2 * lane);
+            const float2 x1 = *(const float2*)(e + 64 + 2 * lane);
+            o0 = fmaf(wj, x0.x, o0);
+            o1 = fmaf(wj, x0.y, o1);
+            o2 = fmaf(wj, x1.x, o2);
+            o3 = fmaf(wj, x1.y, o3);
+        }
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) ll += __shfl_xor_sync(0xffffffffu, ll, off);
+    const float inv = ll > 0.0f ? 1.0f / ll : 0.0f;
+    const float r[4] = {o0 * inv, o1 * inv, o2 * inv, o3 * inv};
+    const int dd[4] = {2 * lane, 2 * lane + 1, 64 + 2 * lane, 65 + 2 * lane};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int64_t oi = row * D + dd[i];
+        if (p.q_dtype == F16) ((__half*)p.out)[oi] = __float2half_rn(r[i]);
+        else if (p.q_dtype == BF16) ((__nv_bfloat16*)p.out)[oi] = __float2bfloat16_rn(r[i]);
+        else ((float*)p.out)[oi] = r[i];
+    }
+}
+
+int launch_decode_combine(const DecP& p, cudaStream_t st) {
+    if (p.D == 128) {
+        const int64_t rows = p.B * p.H;
+        decode_combine128_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(p);
+    } else {
+        dim3 g2((unsigned)p.H, (unsigned)p.B);
+        decode_combine_kernel<<<g2, (unsigned)p.D, 0, st>>>(p);
+    }
+    return cuda_failed(cudaGetLastError(), "decode_q8_0 combine launch") ? -1 : 0;
+}
+
 template <int D, int GH>
 size_t decode_smem() {
     constexpr int ROWB = D / QK * QBYTES;
@@ -416,11 +482,7 @@ int run_decode_gh(DecP p, cudaStream_t st) {
     dim3 grid((unsigned)p.nchunks, (unsigned)(p.Hkv * p.nhg), (unsigned)p.B);
     decode_q8_0_kernel<D, GH><<<grid, DEC_WARPS * 32, smem, st>>>(p);
     if (cuda_failed(cudaGetLastError(), "decode_q8_0 launch")) return -1;
-    if (p.nchunks > 1) {
-        dim3 g2((unsigned)p.H, (unsigned)p.B);
-        decode_combine_kernel<<<g2, (unsigned)p.D, 0, st>>>(p);
-        if (cuda_failed(cudaGetLastError(), "decode_q8_0 combine launch")) return -1;
-    }
+    if (p.nchunks > 1 && launch_decode_combine(p, st) != 0) return -1;
     return 0;
 }
 
@@ -478,7 +540,7 @@ int64_t decode_num_chunks(int64_t Smax) {
     return Smax <= 0 ? 1 : (Smax + GTB_DECODE_CHUNK - 1) / GTB_DECODE_CHUNK;
 }
 
-int64_t decode_list_offset(int64_t B) { return (B + 2 + 1) / 2 * 2; }  // in ints, 8-byte aligned
+int64_t decode_list_offset(int64_t B) { return 2 * B + 4; }  // in ints, 8-byte aligned: counter, 2 prefixes
 
 size_t decode_work_bytes(int64_t B, int64_t Hkv, int64_t Smax) {
     const int64_t items = B * Hkv * decode_num_chunks(Smax);
@@ -516,11 +578,7 @@ int launch_decode_q8_0(const DecodeArgs& a, void* scratch, cudaStream_t st) {
         const int rc = mma ? launch_decode_mma(a, (int*)scratch, p.part, p.nchunks, st)
                            : launch_decode_sm100(a, (int*)scratch, p.part, p.nchunks, st);
         if (rc != 0) return -1;
-        if (p.nchunks > 1) {
-            dim3 g2((unsigned)p.H, (unsigned)p.B);
-            decode_combine_kernel<<<g2, (unsigned)p.D, 0, st>>>(p);
-            if (cuda_failed(cudaGetLastError(), "decode_q8_0 combine launch")) return -1;
-        }
+        if (p.nchunks > 1 && launch_decode_combine(p, st) != 0) return -1;
         return 0;
     }
     switch (a.D) {

@@ -23,7 +23,9 @@ int launch_q8_0_quantize(const void* x, int x_dtype, int64_t nblocks, void* out,
 int launch_q8_0_dequantize(const void* blocks, int64_t nblocks, void* out, int out_dtype, cudaStream_t st);
 int64_t decode_num_chunks(int64_t Smax);
 // Scratch of one decode call: a work area of decode_work_bytes() for the persistent kernels (item
-// counter, per-sequence item prefix [B + 1], and at int offset decode_list_offset(B) the item list:
+// counter, per-sequence item prefix [B + 1], per-sequence prefix of full-chunk items [B + 1], and at
+// int offset decode_list_offset(B) the item list (full chunks first, then last partial chunks by
+// decreasing size):
 // one int2 (b, hk << 16 | chunk) per item), then the split-KV partials [B][Hkv][nchunks][G][D + 2] f32.
 int64_t decode_list_offset(int64_t B);
 size_t decode_work_bytes(int64_t B, int64_t Hkv, int64_t Smax);

@@ -92,7 +92,7 @@ GTB_API int gtb_decode_q8_0(const void *q, int q_dtype, const void *k_q8, const 
  * nothing: the split-KV partial results go to a fixed device array of
  * GTB_DECODE_NOALLOC_SCRATCH_BYTES that every GPU loading this library holds until the process
  * exits. Calls needing more scratch than that, B*Hkv*ceil(Smax/GTB_DECODE_CHUNK)*(H/Hkv)*(D+2)*4
- * bytes plus a work area of 4*(B+3) + 8*B*Hkv*ceil(Smax/GTB_DECODE_CHUNK) bytes rounded up to 256,
+ * bytes plus a work area of 8*(B+2) + 8*B*Hkv*ceil(Smax/GTB_DECODE_CHUNK) bytes rounded up to 256,
  * are rejected with an error
  * (config 5a, B=64 Hkv=8 H=32 D=128 Smax=32768, needs 34.1 MB).
  * The first call on a device sets up the array's device address (call it once before any stream
