@@ -81,7 +81,7 @@ GTB_API int gtb_q8_0_dequantize(const void *blocks, int64_t n_rows, int64_t row_
  * (item counter, per-sequence item prefix and item list of the tensor-core kernels), live in scratch taken
  * from the stream-ordered allocator. With D = 128, an f16 q, H/Hkv in {1,2,4,8}, an even Smax
  * and 16-byte aligned q/k/v the step runs on the tensor cores; otherwise on CUDA cores. */
-#define GTB_DECODE_CHUNK 1024
+#define GTB_DECODE_CHUNK 2048
 GTB_API int gtb_decode_q8_0(const void *q, int q_dtype, const void *k_q8, const void *v_q8,
                             const int32_t *seq_lens, int64_t B, int64_t H, int64_t Hkv, int64_t Smax,
                             int64_t D, float scale, void *out, void *stream);
@@ -94,7 +94,7 @@ GTB_API int gtb_decode_q8_0(const void *q, int q_dtype, const void *k_q8, const 
  * exits. Calls needing more scratch than that, B*Hkv*ceil(Smax/GTB_DECODE_CHUNK)*(H/Hkv)*(D+2)*4
  * bytes plus a work area of 8*(B+2) + 8*B*Hkv*ceil(Smax/GTB_DECODE_CHUNK) bytes rounded up to 256,
  * are rejected with an error
- * (config 5a, B=64 Hkv=8 H=32 D=128 Smax=32768, needs 34.1 MB).
+ * (config 5a, B=64 Hkv=8 H=32 D=128 Smax=32768, needs 17.1 MB).
  * The first call on a device sets up the array's device address (call it once before any stream
  * capture). Calls share the array: calls whose kernels overlap on the GPU race.
  * No counterpart in the reference: it is an addition of this engine. */
