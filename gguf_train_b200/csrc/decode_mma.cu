@@ -150,7 +150,7 @@ __device__ __forceinline__ uint32_t i8x2_to_f16x2_biased(uint32_t x) {
 }
 
 // Half of a cached row (Q8_0 blocks 2*hb and 2*hb+1: 68 bytes starting at row + 68*hb) -> 64 f16
-// integers at row r of a 16-row tile of 256-byte rows whose 16-byte chunks are XOR-swizzled by
+// biased integers 1152 + x (exact; the bias is removed once per item, see vbias) at row r of a 16-row tile of 256-byte rows whose 16-byte chunks are XOR-swizzled by
 // (r >> 1) & 7 (ldmatrix reads the even and the odd rows as separate 8-row matrices); returns the
 // two scales.
 __device__ __forceinline__ float2 dequant_half_row(const unsigned char* row, int hb, uint32_t out_row, int r) {
@@ -173,9 +173,9 @@ __device__ __forceinline__ float2 dequant_half_row(const unsigned char* row, int
             uint32_t h[4];
 #pragma unroll
             for (int k = 0; k < 2; ++k) {
-                const uint32_t u = qw[2 * cc + k] ^ 0x80808080u;
-                asm("sub.f16x2 %0, %1, %2;" : "=r"(h[2 * k]) : "r"(__byte_perm(u, 0x64u, 0x4140u)), "r"(0x64806480u));
-                asm("sub.f16x2 %0, %1, %2;" : "=r"(h[2 * k + 1]) : "r"(__byte_perm(u, 0x64u, 0x4342u)), "r"(0x64806480u));
+                const uint32_t u = qw[2 * cc + k] ^ 0x80808080u;  // x + 128 in each byte
+                h[2 * k] = __byte_perm(u, 0x64u, 0x4140u);          // 1024 + (x + 128) as f16
+                h[2 * k + 1] = __byte_perm(u, 0x64u, 0x4342u);
             }
             const int chunk = 4 * (2 * hb + j) + cc;
             const uint32_t addr = out_row + (uint32_t)((chunk ^ ((r >> 1) & 7)) << 4);
@@ -304,6 +304,13 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_mma_kernel(const DecMmaPar
     float ot[8][4];
 #pragma unroll
     for (int mt = 0; mt < 8; ++mt) ot[mt][0] = ot[mt][1] = ot[mt][2] = ot[mt][3] = 0.0f;
+    // vbias: the V operand holds 1152 + x, so O^T carries 1152 * sum_t P~[r, t] in every row of column
+    // r; that sum comes from one more MMA per column tile with an all-ones A operand (rescaled with
+    // O), and is subtracted at the end of the item. Same layout as ot: [column tile][c0..c3].
+    constexpr int NTL = ((3 * G) >> 3) + 1;  // column tiles of operand rows in use
+    float ps[NTL][4];
+#pragma unroll
+    for (int nt = 0; nt < NTL; ++nt) ps[nt][0] = ps[nt][1] = ps[nt][2] = ps[nt][3] = 0.0f;
     float m_run = -INFINITY, l_run = 0.0f;
     float f = 0.0f;  // power of two for P~; 0 = not chosen yet in this item
     float qbias0 = 0.0f, qbias1 = 0.0f;  // -1152 * sum of q over the block of row g / row g + 8
@@ -454,6 +461,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_mma_kernel(const DecMmaPar
                 for (int mt = 0; mt < 8; ++mt) {
                     ot[mt][0] *= a0; ot[mt][1] *= a1; ot[mt][2] *= a0; ot[mt][3] *= a1;
                 }
+#pragma unroll
+                for (int nt = 0; nt < NTL; ++nt) {
+                    ps[nt][0] *= a0; ps[nt][1] *= a1; ps[nt][2] *= a0; ps[nt][3] *= a1;
+                }
             }
             const float neg = m_run == -INFINITY ? 0.0f : -m_run;
             float pr[4];
@@ -494,6 +505,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_mma_kernel(const DecMmaPar
                     const int ntile = ((mt >> 1) * G) >> 3;
                     mma16816(ot[mt], a, ntile ? pa[1] : pa[0], ntile ? pa[3] : pa[2]);
                 }
+                const uint32_t ones[4] = {0x3C003C00u, 0x3C003C00u, 0x3C003C00u, 0x3C003C00u};  // f16 1.0
+#pragma unroll
+                for (int nt = 0; nt < NTL; ++nt) mma16816(ps[nt], ones, pa[nt], pa[2 + nt]);
             }
             __syncwarp();  // done with the slice's f16 V rows
         }
@@ -519,8 +533,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_mma_kernel(const DecMmaPar
                     const int r = R0 + 2 * c + e;
                     if (r < NR && r / G == blk) {
                         const int h = r % G;
-                        mo[h * HD + 16 * mt + g] = ot[mt][e] * invf;
-                        mo[h * HD + 16 * mt + g + 8] = ot[mt][2 + e] * invf;
+                        const float bias = 1152.0f * ps[R0 >> 3][e];
+                        mo[h * HD + 16 * mt + g] = (ot[mt][e] - bias) * invf;
+                        mo[h * HD + 16 * mt + g + 8] = (ot[mt][2 + e] - bias) * invf;
                     }
                 }
             }
@@ -562,6 +577,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_mma_kernel(const DecMmaPar
             if (!ok) break;
 #pragma unroll
             for (int mt = 0; mt < 8; ++mt) ot[mt][0] = ot[mt][1] = ot[mt][2] = ot[mt][3] = 0.0f;
+#pragma unroll
+            for (int nt = 0; nt < NTL; ++nt) ps[nt][0] = ps[nt][1] = ps[nt][2] = ps[nt][3] = 0.0f;
             ++nitem;
         }
     }
