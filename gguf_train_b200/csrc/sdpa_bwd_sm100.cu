@@ -9,19 +9,26 @@
 //               (B, H, Lpad) buffers, Lpad = L rounded up to 128, so tiles load with bulk copies.
 //   dK/dV       one CTA per 128-key block of one (batch, kv head); it loops over the 128-row query
 //               tiles of every query head of the kv head's group, so dK and dV are complete when the
-//               CTA ends (no cross-CTA reduction). Per query tile, in TMEM (lane = key):
-//                 S^T = K Q^T, dP^T = V dO^T                      (M=128 keys, N=128 queries, K=D)
+//               CTA ends (no cross-CTA reduction). Each query tile is two sub-items of 64 queries;
+//               per sub-item h, in TMEM (lane = key):
+//                 S^T = K Q_h^T, dP^T = V dO_h^T                  (M=128 keys, N=64 queries, K=D)
 //                 P^T = exp2(S^T * scale*log2e - lse2), dS^T = P^T * (dP^T - delta)
-//                 dV += P^T dO, dK += dS^T Q                       (M=128, N=D, K=128; A from TMEM)
-//   dQ          one CTA per 128-row query tile; it loops over the key blocks the tile attends:
-//                 S = Q K^T, dP = dO V^T, dS = P * (dP - delta), dQ += dS K  (A from TMEM)
-// TMEM columns: dK/dV kernel: dV [0,D), dK [128,128+D), S^T [256,384), dP^T [384,512);
-//               dQ kernel: S [0,128), dP [128,256), dQ [256,256+D).
-// P^T / dS^T / dS (bf16 or f16, packed two per column) are written back over the S / dP columns
-// they were computed from: chunk c (32 columns) lands in columns 16c..16c+15, which were read before.
+//                 dV += P^T dO_h, dK += dS^T Q_h                   (M=128, N=D, K=64; A from TMEM)
+//   dQ          one CTA per 128-row query tile; it loops over the 128-key blocks the tile attends,
+//               each two sub-items of 64 keys:
+//                 S = Q K_h^T, dP = dO V_h^T, dS = P * (dP - delta), dQ += dS K_h  (A from TMEM)
+// TMEM columns: dK/dV kernel: dV [0,D), dK [128,128+D), S^T of sub-item h [256+64h, 320+64h),
+//               dP^T of sub-item h [384+64h, 448+64h); dQ kernel: S_h [64h, 64h+64),
+//               dP_h [128+64h, 192+64h), dQ [256,256+D).
+// P^T / dS^T / dS (bf16 or f16, packed two per column) are written back over the first 32 of the
+// S / dP columns of their sub-item: chunk c (32 columns) lands in columns 16c..16c+15, read before.
 //
-// Warps (both main kernels): 0 = TMA producer, 1 = TMEM owner and MMA issuer (one thread), 2-5 =
-// compute, one key (dK/dV) or query (dQ) row per thread. Causal masking is top-left (key s masked for
+// Warps (both main kernels): 0 = TMA producer, 1 = TMEM owner and MMA issuer (one thread), 2-9 =
+// two compute warpgroups, one key (dK/dV) or query (dQ) row per thread: warpgroup h computes
+// sub-item h of every tile (ping-pong). While one warpgroup exponentiates, the tensor core runs the
+// other sub-item's MMAs; the MMA thread issues sub-item h of the next tile right after the
+// gradient MMAs of sub-item h of this one (tcgen05 MMAs of one thread run in issue order, which
+// is what lets them reuse the columns those MMAs read). Causal masking is top-left (key s masked for
 // query l when s > l), as in gt_flash_attention (csrc/gt_ops_nn.cpp:2476). Every wait is bounded as in
 // the forward kernel: a timeout records a status code, drains, frees TMEM and returns.
 
@@ -37,7 +44,8 @@ namespace {
 using namespace sm100;
 
 constexpr int BT = 128;        // rows of a query tile and of a key block
-constexpr int NTHREADS = 192;  // 6 warps
+constexpr int NTHREADS = 320;  // 10 warps: TMA, MMA, two compute warpgroups
+constexpr int HB = BT / 2;     // rows of a sub-item
 constexpr uint32_t TMEM_COLS = 512;
 constexpr float LOG2E = 1.4426950408889634f;
 
@@ -150,11 +158,11 @@ bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
     uint64_t* kv_full = bars;
     uint64_t* st_full = bars + 1;     // [2]
     uint64_t* st_empty = bars + 3;    // [2]
-    uint64_t* s_full = bars + 5;      // S^T, dP^T of the current tile computed
-    uint64_t* p_full = bars + 6;      // P^T, dS^T written (128 arrivals)
-    uint64_t* acc_final = bars + 7;   // every MMA done
-    uint64_t* drain = bars + 8;
-    uint32_t* tmem_slot = (uint32_t*)(bars + 9);
+    uint64_t* s_full = bars + 5;      // [2] S^T, dP^T of sub-item h computed
+    uint64_t* p_full = bars + 7;      // [2] P^T, dS^T of sub-item h written (128 arrivals)
+    uint64_t* acc_final = bars + 9;   // every MMA done
+    uint64_t* drain = bars + 10;
+    uint32_t* tmem_slot = (uint32_t*)(bars + 11);
     int* abort_flag = (int*)(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -168,8 +176,7 @@ bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
     if (threadIdx.x == 0) {
         mbar_init(kv_full, 1);
         for (int i = 0; i < 2; ++i) { mbar_init(&st_full[i], 1); mbar_init(&st_empty[i], 1); }
-        mbar_init(s_full, 1);
-        mbar_init(p_full, 128);
+        for (int h = 0; h < 2; ++h) { mbar_init(&s_full[h], 1); mbar_init(&p_full[h], 128); }
         mbar_init(acc_final, 1);
         mbar_init(drain, 1);
         *abort_flag = 0;
@@ -217,7 +224,7 @@ bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
         }
     } else if (warp == 1) {
         if (lane == 0 && nit > 0) {
-            constexpr uint32_t IDESC_S = idesc_f16(BT, BT, BF16, false);
+            constexpr uint32_t IDESC_S = idesc_f16(BT, HB, BF16, false);
             constexpr uint32_t IDESC_ACC = idesc_f16(BT, D, BF16, true);
             // operand descriptors built once; per MMA only a constant is added to the start address
             const uint64_t kdk = kmajor(smem_u32(smem + OFF_K), 0, C::SLAB), vdk = kmajor(smem_u32(smem + OFF_V), 0, C::SLAB);
@@ -225,34 +232,61 @@ bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
             const uint64_t qk1 = kmajor(smem_u32(smem + OFF_ST + ST_BYTES), 0, C::SLAB);
             const uint64_t qm0 = mnmajor(smem_u32(smem + OFF_ST), 0, C::SLAB);
             const uint64_t qm1 = mnmajor(smem_u32(smem + OFF_ST + ST_BYTES), 0, C::SLAB);
+            // S^T, dP^T of sub-item h (queries 64h.. of the stage's tile: 64 rows = 8 KB into each slab)
+            auto issue_sdp = [&](int st, int h) {
+                const uint64_t qk = st ? qk1 : qk0;
+#pragma unroll
+                for (int kk = 0; kk < D / 16; ++kk) {
+                    const uint32_t off = (uint32_t)((kk / 4) * C::SLAB + (kk % 4) * 32);
+                    mma_ss(tmem + 256 + HB * h, desc_advance(kdk, off), desc_advance(qk, off + h * HB * 128), IDESC_S, kk > 0);
+                }
+#pragma unroll
+                for (int kk = 0; kk < D / 16; ++kk) {
+                    const uint32_t off = (uint32_t)((kk / 4) * C::SLAB + (kk % 4) * 32);
+                    mma_ss(tmem + 384 + HB * h, desc_advance(vdk, off), desc_advance(qk, off + h * HB * 128 + C::TILE),
+                           IDESC_S, kk > 0);
+                }
+                mma_commit(&s_full[h]);
+            };
+            // dV += P^T dO_h, dK += dS^T Q_h (k-steps over the sub-item's 64 queries)
+            auto issue_grad = [&](int st, int h, bool first) {
+                const uint64_t qm = st ? qm1 : qm0;
+#pragma unroll
+                for (int kk = 0; kk < HB / 16; ++kk) {
+                    const uint32_t acc = (!first || kk > 0) ? 1u : 0u;
+                    const uint32_t rows = (uint32_t)((h * (HB / 16) + kk) * 2048);
+                    mma_ts(tmem + 0, tmem + 256 + HB * h + kk * 8, desc_advance(qm, rows + C::TILE), IDESC_ACC, acc);  // dV
+                    mma_ts(tmem + 128, tmem + 384 + HB * h + kk * 8, desc_advance(qm, rows), IDESC_ACC, acc);          // dK
+                }
+            };
             bool ok = mbar_wait(kv_full, 0, p.status, 42);
+            if (ok) ok = mbar_wait(&st_full[0], 0, p.status, 43);
+            if (ok && !*(volatile int*)abort_flag) {
+                tc_fence_after();
+                issue_sdp(0, 0);
+                issue_sdp(0, 1);
+            } else {
+                ok = false;
+            }
             for (int it = 0; it < nit && ok; ++it) {
                 const int st = it & 1;
-                ok = mbar_wait(&st_full[st], (it >> 1) & 1, p.status, 43);
-                if (!ok || *(volatile int*)abort_flag) break;
-                tc_fence_after();
-                const uint64_t qk = st ? qk1 : qk0, qm = st ? qm1 : qm0;
-#pragma unroll
-                for (int kk = 0; kk < D / 16; ++kk) {
-                    const uint32_t off = (uint32_t)((kk / 4) * C::SLAB + (kk % 4) * 32);
-                    mma_ss(tmem + 256, desc_advance(kdk, off), desc_advance(qk, off), IDESC_S, kk > 0);
-                }
-#pragma unroll
-                for (int kk = 0; kk < D / 16; ++kk) {
-                    const uint32_t off = (uint32_t)((kk / 4) * C::SLAB + (kk % 4) * 32);
-                    mma_ss(tmem + 384, desc_advance(vdk, off), desc_advance(qk, off + C::TILE), IDESC_S, kk > 0);
-                }
-                mma_commit(s_full);
-                ok = mbar_wait(p_full, it & 1, p.status, 44);
+                const bool more = it + 1 < nit;
+                ok = mbar_wait(&p_full[0], it & 1, p.status, 44);
                 if (!ok) break;
                 tc_fence_after();
-#pragma unroll
-                for (int kk = 0; kk < BT / 16; ++kk) {
-                    const uint32_t acc = (it > 0 || kk > 0) ? 1u : 0u;
-                    mma_ts(tmem + 0, tmem + 256 + kk * 8, desc_advance(qm, kk * 2048 + C::TILE), IDESC_ACC, acc);  // dV
-                    mma_ts(tmem + 128, tmem + 384 + kk * 8, desc_advance(qm, kk * 2048), IDESC_ACC, acc);          // dK
+                issue_grad(st, 0, it == 0);
+                if (more) {  // sub-item 0 of the next tile, into the columns just read
+                    ok = mbar_wait(&st_full[st ^ 1], ((it + 1) >> 1) & 1, p.status, 43);
+                    if (!ok || *(volatile int*)abort_flag) { ok = false; break; }
+                    tc_fence_after();
+                    issue_sdp(st ^ 1, 0);
                 }
-                mma_commit(&st_empty[st]);
+                ok = mbar_wait(&p_full[1], it & 1, p.status, 44);
+                if (!ok) break;
+                tc_fence_after();
+                issue_grad(st, 1, false);
+                mma_commit(&st_empty[st]);  // this tile's Q / dO are read by every MMA issued so far
+                if (more) issue_sdp(st ^ 1, 1);
             }
             if (!ok) *(volatile int*)abort_flag = 1;
             if (ok && !*(volatile int*)abort_flag) {
@@ -263,6 +297,7 @@ bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
             }
         }
     } else {
+        const int wg = (warp - 2) >> 2;  // compute warpgroup = sub-item: queries [64 wg, 64 wg + 64) of a tile
         const int quad = warp & 3;
         const int r = quad * 32 + lane;
         const int key = key0 + r;
@@ -270,20 +305,20 @@ bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
         bool ok = true;
         for (int it = 0; it < nit; ++it) {
             const int st = it & 1;
-            const int q0 = (i_start + it % nq) * BT;
+            const int q0 = (i_start + it % nq) * BT + wg * HB;  // first query of the sub-item
             ok = warp_wait(&st_full[st], (it >> 1) & 1, p.status, 45);  // lse2 / delta of this tile
-            if (ok) ok = warp_wait(s_full, it & 1, p.status, 46);
+            if (ok) ok = warp_wait(&s_full[wg], it & 1, p.status, 46);
             if (!ok || __any_sync(0xffffffffu, *(volatile int*)abort_flag)) break;
             tc_fence_after();
-            const float* lse_s = (const float*)(smem + OFF_ST + st * ST_BYTES + 2 * C::TILE);
+            const float* lse_s = (const float*)(smem + OFF_ST + st * ST_BYTES + 2 * C::TILE) + wg * HB;
             const float* dl_s = lse_s + 128;
             const uint64_t sc2 = f2_pack(p.scale_log2, p.scale_log2);
             const bool need_mask = p.causal && (q0 < key0 + BT - 1);
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
+            for (int c = 0; c < 2; ++c) {
                 uint32_t ra[32], rb[32], pk[16], dk[16];
-                tmem_ld32(tmem + lane_addr + 256 + c * 32, ra);
-                tmem_ld32(tmem + lane_addr + 384 + c * 32, rb);
+                tmem_ld32(tmem + lane_addr + 256 + HB * wg + c * 32, ra);
+                tmem_ld32(tmem + lane_addr + 384 + HB * wg + c * 32, rb);
                 tmem_ld_wait();
 #pragma unroll
                 for (int i = 0; i < 32; i += 2) {
@@ -304,12 +339,12 @@ bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
                     pk[i / 2] = pack2<BF16>(p0, p1);
                     dk[i / 2] = pack2<BF16>(d0, d1);
                 }
-                tmem_st16(tmem + lane_addr + 256 + c * 16, pk);
-                tmem_st16(tmem + lane_addr + 384 + c * 16, dk);
+                tmem_st16(tmem + lane_addr + 256 + HB * wg + c * 16, pk);
+                tmem_st16(tmem + lane_addr + 384 + HB * wg + c * 16, dk);
             }
             tmem_st_wait();
             tc_fence_before();
-            mbar_arrive(p_full);
+            mbar_arrive(&p_full[wg]);
         }
         if (!ok) *(volatile int*)abort_flag = 1;
         if (nit > 0 && ok && !*(volatile int*)abort_flag) {
@@ -319,7 +354,8 @@ bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
                 T* dvrow = (T*)p.dv + (int64_t)b * p.vs0 + (int64_t)hk * p.vs1 + (int64_t)key * p.vs2;
                 T* dkrow = (T*)p.dk + (int64_t)b * p.ks0 + (int64_t)hk * p.ks1 + (int64_t)key * p.ks2;
 #pragma unroll
-                for (int c = 0; c < D / 32; ++c) {
+                for (int c2 = 0; c2 < D / 64; ++c2) {
+                    const int c = wg * (D / 64) + c2;  // this warpgroup's half of the D columns
                     uint32_t v[32];
                     tmem_ld32(tmem + lane_addr + c * 32, v);
                     tmem_ld_wait();
@@ -335,7 +371,7 @@ bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
             // no query sees this key block: its gradients are zero
             T* dvrow = (T*)p.dv + (int64_t)b * p.vs0 + (int64_t)hk * p.vs1 + (int64_t)key * p.vs2;
             T* dkrow = (T*)p.dk + (int64_t)b * p.ks0 + (int64_t)hk * p.ks1 + (int64_t)key * p.ks2;
-            for (int d = 0; d < D; d += 8) {
+            for (int d = wg * (D / 2); d < (wg + 1) * (D / 2); d += 8) {
                 *(uint4*)(dvrow + d) = make_uint4(0, 0, 0, 0);
                 *(uint4*)(dkrow + d) = make_uint4(0, 0, 0, 0);
             }
@@ -379,11 +415,11 @@ bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
     uint64_t* k_empty = bars + 3;   // [2]
     uint64_t* v_full = bars + 5;    // [2]
     uint64_t* v_empty = bars + 7;   // [2]
-    uint64_t* s_full = bars + 9;    // S and dP computed
-    uint64_t* ds_full = bars + 10;  // dS written (128 arrivals)
-    uint64_t* dq_final = bars + 11;
-    uint64_t* drain = bars + 12;
-    uint32_t* tmem_slot = (uint32_t*)(bars + 13);
+    uint64_t* s_full = bars + 9;    // [2] S, dP of sub-item h computed
+    uint64_t* ds_full = bars + 11;  // [2] dS of sub-item h written (128 arrivals)
+    uint64_t* dq_final = bars + 13;
+    uint64_t* drain = bars + 14;
+    uint32_t* tmem_slot = (uint32_t*)(bars + 15);
     int* abort_flag = (int*)(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -400,8 +436,7 @@ bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
             mbar_init(&k_full[i], 1); mbar_init(&k_empty[i], 1);
             mbar_init(&v_full[i], 1); mbar_init(&v_empty[i], 1);
         }
-        mbar_init(s_full, 1);
-        mbar_init(ds_full, 128);
+        for (int h = 0; h < 2; ++h) { mbar_init(&s_full[h], 1); mbar_init(&ds_full[h], 128); }
         mbar_init(dq_final, 1);
         mbar_init(drain, 1);
         *abort_flag = 0;
@@ -448,42 +483,69 @@ bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
         }
     } else if (warp == 1) {
         if (lane == 0) {
-            constexpr uint32_t IDESC_S = idesc_f16(BT, BT, BF16, false);
+            constexpr uint32_t IDESC_S = idesc_f16(BT, HB, BF16, false);
             constexpr uint32_t IDESC_DQ = idesc_f16(BT, D, BF16, true);
             const uint32_t q_addr = smem_u32(smem + OFF_Q), g_addr = smem_u32(smem + OFF_G);
-            bool ok = mbar_wait(qg_full, 0, p.status, 53);
             const uint64_t qk0 = kmajor(q_addr, 0, C::SLAB), gk0 = kmajor(g_addr, 0, C::SLAB);
+            const uint64_t kb0 = kmajor(smem_u32(smem + OFF_K), 0, C::SLAB), kb1 = kmajor(smem_u32(smem + OFF_K + C::TILE), 0, C::SLAB);
+            const uint64_t vb0 = kmajor(smem_u32(smem + OFF_V), 0, C::SLAB), vb1 = kmajor(smem_u32(smem + OFF_V + C::TILE), 0, C::SLAB);
+            const uint64_t km0 = mnmajor(smem_u32(smem + OFF_K), 0, C::SLAB), km1 = mnmajor(smem_u32(smem + OFF_K + C::TILE), 0, C::SLAB);
+            // S_h = Q K_h^T (keys 64h.. of the block: 64 rows = 8 KB into each slab)
+            auto issue_s = [&](int s, int h) {
+                const uint64_t kb = s ? kb1 : kb0;
+#pragma unroll
+                for (int kk = 0; kk < D / 16; ++kk) {
+                    const uint32_t off = (uint32_t)((kk / 4) * C::SLAB + (kk % 4) * 32);
+                    mma_ss(tmem + HB * h, desc_advance(qk0, off), desc_advance(kb, off + h * HB * 128), IDESC_S, kk > 0);
+                }
+            };
+            // dP_h = dO V_h^T
+            auto issue_dp = [&](int s, int h) {
+                const uint64_t vb = s ? vb1 : vb0;
+#pragma unroll
+                for (int kk = 0; kk < D / 16; ++kk) {
+                    const uint32_t off = (uint32_t)((kk / 4) * C::SLAB + (kk % 4) * 32);
+                    mma_ss(tmem + 128 + HB * h, desc_advance(gk0, off), desc_advance(vb, off + h * HB * 128), IDESC_S, kk > 0);
+                }
+                mma_commit(&s_full[h]);
+            };
+            // dQ += dS_h K_h (k-steps over the sub-item's 64 keys)
+            auto issue_dq = [&](int s, int h, bool first) {
+                const uint64_t km = s ? km1 : km0;
+#pragma unroll
+                for (int kk = 0; kk < HB / 16; ++kk)
+                    mma_ts(tmem + 256, tmem + HB * h + kk * 8, desc_advance(km, (uint32_t)((h * (HB / 16) + kk) * 2048)), IDESC_DQ,
+                           (!first || kk > 0) ? 1u : 0u);
+            };
+            // both sub-items of block j: S needs K, dP needs V
+            auto issue_block_sdp = [&](int j, int h) -> bool {
+                const int s = j & 1;
+                if (h == 0) {
+                    if (!mbar_wait(&k_full[s], (j >> 1) & 1, p.status, 54) || *(volatile int*)abort_flag) return false;
+                    if (!mbar_wait(&v_full[s], (j >> 1) & 1, p.status, 55)) return false;
+                    tc_fence_after();
+                }
+                issue_s(s, h);
+                issue_dp(s, h);
+                if (h == 1) mma_commit(&v_empty[s]);  // V of block j is read by both dP MMAs
+                return true;
+            };
+            bool ok = mbar_wait(qg_full, 0, p.status, 53);
+            if (ok && nblk > 0) ok = issue_block_sdp(0, 0) && issue_block_sdp(0, 1);
             for (int j = 0; j < nblk && ok; ++j) {
                 const int s = j & 1;
-                const uint32_t k_addr = smem_u32(smem + OFF_K + s * C::TILE);
-                const uint32_t v_addr = smem_u32(smem + OFF_V + s * C::TILE);
-                ok = mbar_wait(&k_full[s], (j >> 1) & 1, p.status, 54);
-                if (!ok || *(volatile int*)abort_flag) break;
-                tc_fence_after();
-                const uint64_t kk0 = kmajor(k_addr, 0, C::SLAB), vk0 = kmajor(v_addr, 0, C::SLAB);
-                const uint64_t km0 = mnmajor(k_addr, 0, C::SLAB);
-#pragma unroll
-                for (int kk = 0; kk < D / 16; ++kk) {
-                    const uint32_t off = (uint32_t)((kk / 4) * C::SLAB + (kk % 4) * 32);
-                    mma_ss(tmem + 0, desc_advance(qk0, off), desc_advance(kk0, off), IDESC_S, kk > 0);
-                }
-                ok = mbar_wait(&v_full[s], (j >> 1) & 1, p.status, 55);
+                const bool more = j + 1 < nblk;
+                ok = mbar_wait(&ds_full[0], j & 1, p.status, 56);
                 if (!ok) break;
                 tc_fence_after();
-#pragma unroll
-                for (int kk = 0; kk < D / 16; ++kk) {
-                    const uint32_t off = (uint32_t)((kk / 4) * C::SLAB + (kk % 4) * 32);
-                    mma_ss(tmem + 128, desc_advance(gk0, off), desc_advance(vk0, off), IDESC_S, kk > 0);
-                }
-                mma_commit(s_full);
-                mma_commit(&v_empty[s]);
-                ok = mbar_wait(ds_full, j & 1, p.status, 56);
+                issue_dq(s, 0, j == 0);
+                if (more && !(ok = issue_block_sdp(j + 1, 0))) break;  // into the columns just read
+                ok = mbar_wait(&ds_full[1], j & 1, p.status, 56);
                 if (!ok) break;
                 tc_fence_after();
-#pragma unroll
-                for (int kk = 0; kk < BT / 16; ++kk)
-                    mma_ts(tmem + 256, tmem + 0 + kk * 8, desc_advance(km0, kk * 2048), IDESC_DQ, (j > 0 || kk > 0) ? 1u : 0u);
-                mma_commit(&k_empty[s]);
+                issue_dq(s, 1, false);
+                mma_commit(&k_empty[s]);  // K of block j is read by every MMA issued so far
+                if (more) issue_block_sdp(j + 1, 1);
             }
             if (!ok) *(volatile int*)abort_flag = 1;
             if (ok && !*(volatile int*)abort_flag) {
@@ -494,6 +556,7 @@ bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
             }
         }
     } else {
+        const int wg = (warp - 2) >> 2;  // compute warpgroup = sub-item: keys [64 wg, 64 wg + 64) of a block
         const int quad = warp & 3;
         const int r = quad * 32 + lane;
         const int row = row0 + r;
@@ -506,16 +569,16 @@ bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
         const int lim = p.causal ? min(lim_s, row) : lim_s;  // last key this row may see
         bool ok = true;
         for (int j = 0; j < nblk; ++j) {
-            ok = warp_wait(s_full, j & 1, p.status, 57);
+            ok = warp_wait(&s_full[wg], j & 1, p.status, 57);
             if (!ok || __any_sync(0xffffffffu, *(volatile int*)abort_flag)) break;
             tc_fence_after();
-            const int kv0 = j * BT;
-            const bool need_mask = (kv0 + BT > p.S) || (p.causal && kv0 + BT - 1 > row0);
+            const int kv0 = j * BT + wg * HB;  // first key of the sub-item
+            const bool need_mask = (kv0 + HB > p.S) || (p.causal && kv0 + HB - 1 > row0);
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
+            for (int c = 0; c < 2; ++c) {
                 uint32_t ra[32], rb[32], pk[16];
-                tmem_ld32(tmem + lane_addr + c * 32, ra);
-                tmem_ld32(tmem + lane_addr + 128 + c * 32, rb);
+                tmem_ld32(tmem + lane_addr + HB * wg + c * 32, ra);
+                tmem_ld32(tmem + lane_addr + 128 + HB * wg + c * 32, rb);
                 tmem_ld_wait();
 #pragma unroll
                 for (int i = 0; i < 32; i += 2) {
@@ -530,11 +593,11 @@ bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
                               d0, d1);
                     pk[i / 2] = pack2<BF16>(d0, d1);
                 }
-                tmem_st16(tmem + lane_addr + c * 16, pk);
+                tmem_st16(tmem + lane_addr + HB * wg + c * 16, pk);
             }
             tmem_st_wait();
             tc_fence_before();
-            mbar_arrive(ds_full);
+            mbar_arrive(&ds_full[wg]);
         }
         if (!ok) *(volatile int*)abort_flag = 1;
         if (ok && !*(volatile int*)abort_flag) {
@@ -543,7 +606,8 @@ bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
                 tc_fence_after();
                 T* qrow = (T*)p.dq + (int64_t)b * p.s0 + (int64_t)h * p.s1 + (int64_t)row * p.s2;
 #pragma unroll
-                for (int c = 0; c < D / 32; ++c) {
+                for (int c2 = 0; c2 < D / 64; ++c2) {
+                    const int c = wg * (D / 64) + c2;  // this warpgroup's half of the D columns
                     uint32_t v[32];
                     tmem_ld32(tmem + lane_addr + 256 + c * 32, v);
                     tmem_ld_wait();
