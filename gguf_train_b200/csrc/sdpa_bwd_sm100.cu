@@ -4,9 +4,10 @@
 // the probabilities with separate matmul / softmax / elementwise ops and materialises several
 // (B, H, L, S) tensors. Here it is three kernels that never hold more than 128x128 tiles:
 //
-//   preprocess  per query row: delta = sum(dO * O), lse2 = lse * log2(e) (+inf for rows that are
-//               padding or had no allowed key, so their probabilities come out 0); both stored in
-//               (B, H, Lpad) buffers, Lpad = L rounded up to 128, so tiles load with bulk copies.
+//   preprocess  per query row: -delta = -sum(dO * O), -lse2 = -lse * log2(e) (-inf for rows that are
+//               padding or had no allowed key, so their probabilities come out 0); both stored negated
+//               (the main kernels add them) in (B, H, Lpad) buffers, Lpad = L rounded up to 128, so
+//               tiles load with bulk copies.
 //   dK/dV       one CTA per 128-key block of one (batch, kv head); it loops over the 128-row query
 //               tiles of every query head of the kv head's group, so dK and dV are complete when the
 //               CTA ends (no cross-CTA reduction). Each query tile is two sub-items of 64 queries;
@@ -33,6 +34,7 @@
 // the forward kernel: a timeout records a status code, drains, frees TMEM and returns.
 
 #include <cmath>
+#include <type_traits>
 
 #include "gtb_common.cuh"
 #include "sdpa_args.h"
@@ -97,8 +99,8 @@ struct PreP {
     int64_t os0, os1, os2;    // strides of O (b, h, l); d stride 1
     int64_t gs0, gs1, gs2;    // strides of dO
     const float* lse;         // (B, H, L)
-    float* lse2;              // (B, H, Lpad)
-    float* delta;             // (B, H, Lpad)
+    float* lse2;              // (B, H, Lpad): -lse * log2(e)
+    float* delta;             // (B, H, Lpad): -sum(dO * O)
     int64_t B, H, L, Lpad, D;
 };
 
@@ -117,13 +119,13 @@ __global__ void __launch_bounds__(128) bwd_pre_kernel(PreP p) {
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
     if (lane == 0) {
-        float l2 = INFINITY;  // padding rows and rows without an allowed key: probabilities 0
+        float nl2 = -INFINITY;  // padding rows and rows without an allowed key: probabilities 0
         if (l < p.L) {
             const float lse = p.lse[bh * p.L + l];
-            if (lse != -INFINITY) l2 = lse * LOG2E;
+            if (lse != -INFINITY) nl2 = -lse * LOG2E;
         }
-        p.lse2[row] = l2;
-        p.delta[row] = acc;
+        p.lse2[row] = nl2;
+        p.delta[row] = -acc;
     }
 }
 
@@ -310,38 +312,42 @@ bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
             if (ok) ok = warp_wait(&s_full[wg], it & 1, p.status, 46);
             if (!ok || __any_sync(0xffffffffu, *(volatile int*)abort_flag)) break;
             tc_fence_after();
-            const float* lse_s = (const float*)(smem + OFF_ST + st * ST_BYTES + 2 * C::TILE) + wg * HB;
-            const float* dl_s = lse_s + 128;
+            const float* lse_s = (const float*)(smem + OFF_ST + st * ST_BYTES + 2 * C::TILE) + wg * HB;  // -lse2
+            const float* dl_s = lse_s + 128;                                                                 // -delta
             const uint64_t sc2 = f2_pack(p.scale_log2, p.scale_log2);
-            const bool need_mask = p.causal && (q0 < key0 + BT - 1);
+            // masking only where the causal diagonal crosses the sub-item: one branch per sub-item
+            auto chunks = [&](auto masked) {
+                constexpr bool MASK = decltype(masked)::value;
 #pragma unroll
-            for (int c = 0; c < 2; ++c) {
-                uint32_t ra[32], rb[32], pk[16], dk[16];
-                tmem_ld32(tmem + lane_addr + 256 + HB * wg + c * 32, ra);
-                tmem_ld32(tmem + lane_addr + 384 + HB * wg + c * 32, rb);
-                tmem_ld_wait();
+                for (int c = 0; c < 2; ++c) {
+                    uint32_t ra[32], rb[32], pk[16], dk[16];
+                    tmem_ld32(tmem + lane_addr + 256 + HB * wg + c * 32, ra);
+                    tmem_ld32(tmem + lane_addr + 384 + HB * wg + c * 32, rb);
+                    tmem_ld_wait();
 #pragma unroll
-                for (int i = 0; i < 32; i += 2) {
-                    // packed two-lane f32: a = S * scale - lse2, ds = p * (dP - delta)
-                    const int qc = c * 32 + i;
-                    const float2 ls2 = *(const float2*)(lse_s + qc);
-                    const float2 dl2 = *(const float2*)(dl_s + qc);
-                    float a0, a1;
-                    f2_unpack(f2_fma(f2_pack(__uint_as_float(ra[i]), __uint_as_float(ra[i + 1])), sc2,
-                                     f2_pack(-ls2.x, -ls2.y)), a0, a1);
-                    float p0 = ex2(a0), p1 = ex2(a1);
-                    if (need_mask && key > q0 + qc) p0 = 0.0f;
-                    if (need_mask && key > q0 + qc + 1) p1 = 0.0f;
-                    const uint64_t pp = f2_pack(p0, p1);
-                    float d0, d1;
-                    f2_unpack(f2_mul(pp, f2_add(f2_pack(__uint_as_float(rb[i]), __uint_as_float(rb[i + 1])),
-                                                f2_pack(-dl2.x, -dl2.y))), d0, d1);
-                    pk[i / 2] = pack2<BF16>(p0, p1);
-                    dk[i / 2] = pack2<BF16>(d0, d1);
+                    for (int i = 0; i < 32; i += 2) {
+                        // packed two-lane f32: a = S * scale - lse2, ds = p * (dP - delta)
+                        const int qc = c * 32 + i;
+                        float a0, a1;
+                        f2_unpack(f2_fma(f2_pack(__uint_as_float(ra[i]), __uint_as_float(ra[i + 1])), sc2,
+                                         *(const uint64_t*)(lse_s + qc)), a0, a1);
+                        float p0 = ex2(a0), p1 = ex2(a1);
+                        if constexpr (MASK) {
+                            if (key > q0 + qc) p0 = 0.0f;
+                            if (key > q0 + qc + 1) p1 = 0.0f;
+                        }
+                        float d0, d1;
+                        f2_unpack(f2_mul(f2_pack(p0, p1), f2_add(f2_pack(__uint_as_float(rb[i]), __uint_as_float(rb[i + 1])),
+                                                                 *(const uint64_t*)(dl_s + qc))), d0, d1);
+                        pk[i / 2] = pack2<BF16>(p0, p1);
+                        dk[i / 2] = pack2<BF16>(d0, d1);
+                    }
+                    tmem_st16(tmem + lane_addr + 256 + HB * wg + c * 16, pk);
+                    tmem_st16(tmem + lane_addr + 384 + HB * wg + c * 16, dk);
                 }
-                tmem_st16(tmem + lane_addr + 256 + HB * wg + c * 16, pk);
-                tmem_st16(tmem + lane_addr + 384 + HB * wg + c * 16, dk);
-            }
+            };
+            if (p.causal && (q0 < key0 + BT - 1)) chunks(std::true_type{});
+            else chunks(std::false_type{});
             tmem_st_wait();
             tc_fence_before();
             mbar_arrive(&p_full[wg]);
@@ -562,9 +568,9 @@ bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
         const int row = row0 + r;
         const uint32_t lane_addr = (uint32_t)(quad * 32) << 16;
         const int64_t prow = ((int64_t)b * p.H + h) * p.Lpad + row;  // row < Lpad
-        const float lse2 = p.lse2[prow];
-        const float dl = p.delta[prow];
-        const uint64_t sc2 = f2_pack(p.scale_log2, p.scale_log2), nl2 = f2_pack(-lse2, -lse2), nd2 = f2_pack(-dl, -dl);
+        const float nlse2 = p.lse2[prow];  // stored negated
+        const float ndl = p.delta[prow];
+        const uint64_t sc2 = f2_pack(p.scale_log2, p.scale_log2), nl2 = f2_pack(nlse2, nlse2), nd2 = f2_pack(ndl, ndl);
         const int lim_s = (int)min(p.S, (int64_t)INT32_MAX) - 1;
         const int lim = p.causal ? min(lim_s, row) : lim_s;  // last key this row may see
         bool ok = true;
@@ -573,28 +579,35 @@ bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
             if (!ok || __any_sync(0xffffffffu, *(volatile int*)abort_flag)) break;
             tc_fence_after();
             const int kv0 = j * BT + wg * HB;  // first key of the sub-item
-            const bool need_mask = (kv0 + HB > p.S) || (p.causal && kv0 + HB - 1 > row0);
+            // masking only on ragged or diagonal blocks: one branch per sub-item
+            auto chunks = [&](auto masked) {
+                constexpr bool MASK = decltype(masked)::value;
 #pragma unroll
-            for (int c = 0; c < 2; ++c) {
-                uint32_t ra[32], rb[32], pk[16];
-                tmem_ld32(tmem + lane_addr + HB * wg + c * 32, ra);
-                tmem_ld32(tmem + lane_addr + 128 + HB * wg + c * 32, rb);
-                tmem_ld_wait();
+                for (int c = 0; c < 2; ++c) {
+                    uint32_t ra[32], rb[32], pk[16];
+                    tmem_ld32(tmem + lane_addr + HB * wg + c * 32, ra);
+                    tmem_ld32(tmem + lane_addr + 128 + HB * wg + c * 32, rb);
+                    tmem_ld_wait();
 #pragma unroll
-                for (int i = 0; i < 32; i += 2) {
-                    // packed two-lane f32: a = S * scale - lse2, ds = p * (dP - delta)
-                    float a0, a1;
-                    f2_unpack(f2_fma(f2_pack(__uint_as_float(ra[i]), __uint_as_float(ra[i + 1])), sc2, nl2), a0, a1);
-                    float p0 = ex2(a0), p1 = ex2(a1);
-                    if (need_mask && kv0 + c * 32 + i > lim) p0 = 0.0f;
-                    if (need_mask && kv0 + c * 32 + i + 1 > lim) p1 = 0.0f;
-                    float d0, d1;
-                    f2_unpack(f2_mul(f2_pack(p0, p1), f2_add(f2_pack(__uint_as_float(rb[i]), __uint_as_float(rb[i + 1])), nd2)),
-                              d0, d1);
-                    pk[i / 2] = pack2<BF16>(d0, d1);
+                    for (int i = 0; i < 32; i += 2) {
+                        // packed two-lane f32: a = S * scale - lse2, ds = p * (dP - delta)
+                        float a0, a1;
+                        f2_unpack(f2_fma(f2_pack(__uint_as_float(ra[i]), __uint_as_float(ra[i + 1])), sc2, nl2), a0, a1);
+                        float p0 = ex2(a0), p1 = ex2(a1);
+                        if constexpr (MASK) {
+                            if (kv0 + c * 32 + i > lim) p0 = 0.0f;
+                            if (kv0 + c * 32 + i + 1 > lim) p1 = 0.0f;
+                        }
+                        float d0, d1;
+                        f2_unpack(f2_mul(f2_pack(p0, p1), f2_add(f2_pack(__uint_as_float(rb[i]), __uint_as_float(rb[i + 1])), nd2)),
+                                  d0, d1);
+                        pk[i / 2] = pack2<BF16>(d0, d1);
+                    }
+                    tmem_st16(tmem + lane_addr + HB * wg + c * 16, pk);
                 }
-                tmem_st16(tmem + lane_addr + HB * wg + c * 16, pk);
-            }
+            };
+            if ((kv0 + HB > p.S) || (p.causal && kv0 + HB - 1 > row0)) chunks(std::true_type{});
+            else chunks(std::false_type{});
             tmem_st_wait();
             tc_fence_before();
             mbar_arrive(&ds_full[wg]);
