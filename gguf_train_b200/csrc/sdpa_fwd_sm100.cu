@@ -70,23 +70,30 @@ __device__ __forceinline__ uint32_t s_col(int t) { return (uint32_t)t * 128u; }
 __device__ __forceinline__ uint32_t o_col(int t) { return 256u + (uint32_t)t * 128u; }
 constexpr uint32_t P_OFF = 64;  // P_t lives in S_t's columns [64, 128)
 
-// 2^x on the FMA/ALU pipes, to take part of the softmax's exponentials off the MUFU unit.
-// Range reduction x = n + f with n = round(x) (adding 1.5 * 2^23 rounds to an integer held in
-// the low mantissa bits) and f in [-1/2, 1/2]; 2^f from a cubic fitted for this kernel (minimax in
-// relative error on [-1/2, 1/2], max error 7.5e-5, far below the 2^-9 of the bf16 P it feeds);
-// 2^n is added to the exponent field. x is clamped below at -126 so the exponent cannot wrap.
-__device__ __forceinline__ float exp2_poly(float x) {
+// 2^x on the FMA/ALU pipes, to take part of the softmax's exponentials off the MUFU unit, for a
+// packed pair of floats. Range reduction x = n + f with n = round(x) (adding 1.5 * 2^23 rounds to an
+// integer held in the low mantissa bits) and f in [-1/2, 1/2]; 2^f from a cubic fitted for this
+// kernel (minimax in relative error on [-1/2, 1/2], max error 7.5e-5, far below the 2^-9 of the
+// bf16 P it feeds); 2^n is added to the exponent field. x is clamped below at -126 so the exponent
+// cannot wrap. The reduction and the cubic run as two-lane f32 operations.
+__device__ __forceinline__ uint64_t exp2_poly2(uint64_t x2) {
     constexpr float C0 = 0.9999280571937561f, C1 = 0.6932609677314758f;
     constexpr float C2 = 0.2426111400127411f, C3 = 0.0551716573536396f;
     constexpr float SHIFT = 12582912.0f;  // 1.5 * 2^23
-    x = fmaxf(x, -126.0f);
-    const float t = x + SHIFT;
-    const int n = __float_as_int(t) - 0x4B400000;
-    const float f = x - (t - SHIFT);
-    float q = fmaf(C3, f, C2);
-    q = fmaf(q, f, C1);
-    q = fmaf(q, f, C0);
-    return __int_as_float(__float_as_int(q) + (n << 23));
+    float x0, x1;
+    f2_unpack(x2, x0, x1);
+    x2 = f2_pack(fmaxf(x0, -126.0f), fmaxf(x1, -126.0f));
+    const uint64_t t2 = f2_add(x2, f2_pack(SHIFT, SHIFT));
+    const uint64_t f2 = f2_add(x2, f2_add(t2, f2_pack(-SHIFT, -SHIFT)) ^ 0x8000000080000000ull);  // x - (t - SHIFT)
+    uint64_t q2 = f2_fma(f2_pack(C3, C3), f2, f2_pack(C2, C2));
+    q2 = f2_fma(q2, f2, f2_pack(C1, C1));
+    q2 = f2_fma(q2, f2, f2_pack(C0, C0));
+    float q0, q1, t0, t1;
+    f2_unpack(q2, q0, q1);
+    f2_unpack(t2, t0, t1);
+    // n = bits(t) - bits(1.5 * 2^23); n << 23 == bits(t) << 23 (mod 2^32): the low 9 bits of the shift's bits are 0
+    return f2_pack(__uint_as_float(__float_as_uint(q0) + (__float_as_uint(t0) << 23)),
+                   __uint_as_float(__float_as_uint(q1) + (__float_as_uint(t1) << 23)));
 }
 
 // two floats -> one 32-bit word of two 16-bit values (lo in the low half), round to nearest even
@@ -353,11 +360,18 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
                 uint32_t pk[16];
 #pragma unroll
                 for (int i = 0; i < 32; i += 2) {
-                    float a0, a1;
-                    f2_unpack(f2_fma(f2_pack(x[i], x[i + 1]), sc2, nm2), a0, a1);
-                    const float p0 = (i & 7) < EMU ? exp2_poly(a0) : ex2(a0);
-                    const float p1 = ((i + 1) & 7) < EMU ? exp2_poly(a1) : ex2(a1);
-                    ps2[(i >> 1) & 1] = f2_add(ps2[(i >> 1) & 1], f2_pack(p0, p1));
+                    const uint64_t a2 = f2_fma(f2_pack(x[i], x[i + 1]), sc2, nm2);
+                    uint64_t p2;
+                    if ((i & 7) < EMU) {  // this pair on the FMA pipe
+                        p2 = exp2_poly2(a2);
+                    } else {
+                        float a0, a1;
+                        f2_unpack(a2, a0, a1);
+                        p2 = f2_pack(ex2(a0), ex2(a1));
+                    }
+                    ps2[(i >> 1) & 1] = f2_add(ps2[(i >> 1) & 1], p2);
+                    float p0, p1;
+                    f2_unpack(p2, p0, p1);
                     pk[i / 2] = pack2<BF16>(p0, p1);
                 }
                 tmem_st16(s_tmem + P_OFF + c * 16, pk);
@@ -506,13 +520,13 @@ int run(const FwdArgs& a, const CUtensorMap& mq, const CUtensorMap& mk, const CU
     return cuda_failed(cudaGetLastError(), "flash_attention (sm100) launch") ? -1 : 0;
 }
 
-// Exponentials computed by exp2_poly per 8 (GTB_FWD_EMU=0|2|3, default 0).
+// Exponentials computed by exp2_poly2 per 8 (GTB_FWD_EMU=0|2|4, default 0).
 int emu_setting() {
     static int v = -1;
     if (v < 0) {
         const char* e = getenv("GTB_FWD_EMU");
         v = e ? atoi(e) : 0;
-        if (v != 0 && v != 2 && v != 3) v = 0;
+        if (v != 0 && v != 2 && v != 4) v = 0;
     }
     return v;
 }
@@ -520,7 +534,7 @@ int emu_setting() {
 template <int D, bool BF16>
 int run_emu(const FwdArgs& a, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, cudaStream_t st) {
     switch (emu_setting()) {
-        case 3: return run<D, BF16, 3>(a, mq, mk, mv, st);
+        case 4: return run<D, BF16, 4>(a, mq, mk, mv, st);
         case 2: return run<D, BF16, 2>(a, mq, mk, mv, st);
         default: return run<D, BF16, 0>(a, mq, mk, mv, st);
     }
