@@ -84,12 +84,15 @@ def test_decode_matches_oracle(B, H, Hkv, Smax, D, lens):
     _decode_case(B, H, Hkv, Smax, D, lens)
 
 
-# D = 128 with an f16 query, H/Hkv in {1, 2, 4, 8} and an even Smax run on the tensor-core kernel
-# (persistent CTAs, 128-row tiles, chunks of 1024 rows): tile and chunk edges, group sizes, and
-# rows past the end of a sequence inside a tile.
+# D = 128 with an f16 query, H/Hkv in {1, 2, 4, 8} and an even Smax run on the tensor-core kernels
+# (persistent CTAs, 64- or 128-row tiles, split-KV chunks of GTB_DECODE_CHUNK = 2048 rows; the plan
+# lists full chunks first, then each sequence's partial last chunk by decreasing size): tile and
+# chunk edges, group sizes, and rows past the end of a sequence inside a tile.
 @pytest.mark.parametrize("B,H,Hkv,Smax,D,lens", [
     (4, 8, 8, 2050, 128, [1, 127, 128, 129]),           # group of 1, ragged first tiles
-    (4, 16, 2, 2050, 128, [1023, 1024, 1025, 2050]),    # group of 8, chunk edges
+    (4, 16, 2, 2050, 128, [1023, 1024, 1025, 2050]),    # group of 8, tile edges, one full chunk + 2 rows
+    (5, 32, 8, 6144, 128, [2047, 2048, 2049, 6144, 0]),  # group of 4, chunk edges: only full, only partial, both, empty
+    (3, 8, 4, 4100, 128, [4100, 4094, 2]),              # group of 2, two full chunks + a partial one
     (3, 32, 8, 4096, 128, [4096, 2049, 640]),           # the config-5a group (4), several chunks
     (2, 4, 2, 256, 128, [256, 255]),                    # one chunk: normalised directly
 ])
