@@ -20,7 +20,9 @@
 //                 S = Q K_h^T, dP = dO V_h^T, dS = P * (dP - delta), dQ += dS K_h  (A from TMEM)
 // TMEM columns: dK/dV kernel: dV [0,D), dK [128,128+D), S^T of sub-item h [256+64h, 320+64h),
 //               dP^T of sub-item h [384+64h, 448+64h); dQ kernel: S_h [64h, 64h+64),
-//               dP_h [128+64h, 192+64h), dQ [256,256+D).
+//               dP_h [128+64h, 192+64h), dQ [256,256+D), and the tile's Q [384, 384+D/2) and
+//               dO [448, 448+D/2) (16-bit pairs), the A operands of S and dP (TS-form MMAs: Q and
+//               dO are the same for every key block, so they are read from TMEM, not shared memory).
 // P^T / dS^T / dS (bf16 or f16, packed two per column) are written back over the first 32 of the
 // S / dP columns of their sub-item: chunk c (32 columns) lands in columns 16c..16c+15, read before.
 //
@@ -48,6 +50,7 @@ using namespace sm100;
 constexpr int BT = 128;        // rows of a query tile and of a key block
 constexpr int NTHREADS = 320;  // 10 warps: TMA, MMA, two compute warpgroups
 constexpr int HB = BT / 2;     // rows of a sub-item
+constexpr int NCOMP = 256;     // compute threads (two warpgroups)
 constexpr uint32_t TMEM_COLS = 512;
 constexpr float LOG2E = 1.4426950408889634f;
 
@@ -425,7 +428,8 @@ bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
     uint64_t* ds_full = bars + 11;  // [2] dS of sub-item h written (128 arrivals)
     uint64_t* dq_final = bars + 13;
     uint64_t* drain = bars + 14;
-    uint32_t* tmem_slot = (uint32_t*)(bars + 15);
+    uint64_t* qt_full = bars + 15;  // Q and dO copied into TMEM (NCOMP arrivals)
+    uint32_t* tmem_slot = (uint32_t*)(bars + 16);
     int* abort_flag = (int*)(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -445,6 +449,7 @@ bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
         for (int h = 0; h < 2; ++h) { mbar_init(&s_full[h], 1); mbar_init(&ds_full[h], 128); }
         mbar_init(dq_final, 1);
         mbar_init(drain, 1);
+        mbar_init(qt_full, NCOMP);
         *abort_flag = 0;
         fence_mbar_init();
     }
@@ -453,6 +458,7 @@ bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    constexpr uint32_t QCOL = 384, GCOL = 448;  // Q, dO in TMEM (16-bit pairs)
 
     if (warp == 0) {
         if (lane == 0) {
@@ -491,8 +497,6 @@ bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
         if (lane == 0) {
             constexpr uint32_t IDESC_S = idesc_f16(BT, HB, BF16, false);
             constexpr uint32_t IDESC_DQ = idesc_f16(BT, D, BF16, true);
-            const uint32_t q_addr = smem_u32(smem + OFF_Q), g_addr = smem_u32(smem + OFF_G);
-            const uint64_t qk0 = kmajor(q_addr, 0, C::SLAB), gk0 = kmajor(g_addr, 0, C::SLAB);
             const uint64_t kb0 = kmajor(smem_u32(smem + OFF_K), 0, C::SLAB), kb1 = kmajor(smem_u32(smem + OFF_K + C::TILE), 0, C::SLAB);
             const uint64_t vb0 = kmajor(smem_u32(smem + OFF_V), 0, C::SLAB), vb1 = kmajor(smem_u32(smem + OFF_V + C::TILE), 0, C::SLAB);
             const uint64_t km0 = mnmajor(smem_u32(smem + OFF_K), 0, C::SLAB), km1 = mnmajor(smem_u32(smem + OFF_K + C::TILE), 0, C::SLAB);
@@ -502,7 +506,7 @@ bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
 #pragma unroll
                 for (int kk = 0; kk < D / 16; ++kk) {
                     const uint32_t off = (uint32_t)((kk / 4) * C::SLAB + (kk % 4) * 32);
-                    mma_ss(tmem + HB * h, desc_advance(qk0, off), desc_advance(kb, off + h * HB * 128), IDESC_S, kk > 0);
+                    mma_ts(tmem + HB * h, tmem + QCOL + kk * 8, desc_advance(kb, off + h * HB * 128), IDESC_S, kk > 0);
                 }
             };
             // dP_h = dO V_h^T
@@ -511,7 +515,7 @@ bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
 #pragma unroll
                 for (int kk = 0; kk < D / 16; ++kk) {
                     const uint32_t off = (uint32_t)((kk / 4) * C::SLAB + (kk % 4) * 32);
-                    mma_ss(tmem + 128 + HB * h, desc_advance(gk0, off), desc_advance(vb, off + h * HB * 128), IDESC_S, kk > 0);
+                    mma_ts(tmem + 128 + HB * h, tmem + GCOL + kk * 8, desc_advance(vb, off + h * HB * 128), IDESC_S, kk > 0);
                 }
                 mma_commit(&s_full[h]);
             };
@@ -536,7 +540,8 @@ bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
                 if (h == 1) mma_commit(&v_empty[s]);  // V of block j is read by both dP MMAs
                 return true;
             };
-            bool ok = mbar_wait(qg_full, 0, p.status, 53);
+            bool ok = mbar_wait(qt_full, 0, p.status, 53);  // Q and dO in TMEM
+            if (ok) tc_fence_after();
             if (ok && nblk > 0) ok = issue_block_sdp(0, 0) && issue_block_sdp(0, 1);
             for (int j = 0; j < nblk && ok; ++j) {
                 const int s = j & 1;
@@ -573,8 +578,26 @@ bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
         const uint64_t sc2 = f2_pack(p.scale_log2, p.scale_log2), nl2 = f2_pack(nlse2, nlse2), nd2 = f2_pack(ndl, ndl);
         const int lim_s = (int)min(p.S, (int64_t)INT32_MAX) - 1;
         const int lim = p.causal ? min(lim_s, row) : lim_s;  // last key this row may see
-        bool ok = true;
-        for (int j = 0; j < nblk; ++j) {
+        // warpgroup 0 copies its row of Q, warpgroup 1 its row of dO, from the 128-byte-swizzled tile
+        // into TMEM (16-byte chunk c of row r of a 64-column slab sits at chunk c ^ (r & 7))
+        bool ok = warp_wait(qg_full, 0, p.status, 59);
+        if (ok) {
+            const unsigned char* src = smem + (wg ? OFF_G : OFF_Q) + r * 128;
+#pragma unroll
+            for (int a = 0; a < C::ATOMS; ++a) {
+                uint32_t w[32];
+#pragma unroll
+                for (int c = 0; c < 8; ++c) {
+                    const uint4 v = *(const uint4*)(src + a * C::SLAB + ((c ^ (r & 7)) << 4));
+                    w[4 * c] = v.x; w[4 * c + 1] = v.y; w[4 * c + 2] = v.z; w[4 * c + 3] = v.w;
+                }
+                tmem_st32(tmem + lane_addr + (wg ? GCOL : QCOL) + a * 32, w);
+            }
+            tmem_st_wait();
+            tc_fence_before();
+            mbar_arrive(qt_full);
+        }
+        for (int j = 0; j < nblk && ok; ++j) {
             ok = warp_wait(&s_full[wg], j & 1, p.status, 57);
             if (!ok || __any_sync(0xffffffffu, *(volatile int*)abort_flag)) break;
             tc_fence_after();
@@ -679,8 +702,8 @@ int run_bwd(const BwdArgs& a, cudaStream_t st) {
     const float scale_log2 = a.scale * LOG2E;
 
     static bool attr_set = false;
-    constexpr int SMEM_KV = 2 * C::TILE + 2 * (2 * C::TILE + 1024) + 16 * 8 + 1024;
-    constexpr int SMEM_DQ = 6 * C::TILE + 16 * 8 + 1024;
+    constexpr int SMEM_KV = 2 * C::TILE + 2 * (2 * C::TILE + 1024) + 32 * 8 + 1024;  // + barriers, TMEM slot, flag
+    constexpr int SMEM_DQ = 6 * C::TILE + 32 * 8 + 1024;  // + barriers, TMEM slot, flag
     if (!attr_set) {
         if (cuda_failed(cudaFuncSetAttribute(bwd_dkdv_kernel<D, BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              SMEM_KV), "cudaFuncSetAttribute(bwd dkdv)") ||
