@@ -72,6 +72,13 @@ constexpr int SMEM_LIMIT = 232448;
 
 enum : int { F_FIRST = 1, F_LAST = 2, F_END = 4 };
 
+// In-kernel plan (batches of at most FOLD_MAX_B sequences): every CTA derives the item order of the
+// plan kernel (decode_sm100.cu) from the lengths in shared memory, so the step needs no plan launch,
+// only a zeroed claim counter. Tables: full chunks [B], size class [B], full-item prefix [B + 1],
+// partial-chunk sequences in list order [B], class starts [17], then full items and all items.
+constexpr int FOLD_MAX_B = 256;
+constexpr int PLAN_INTS = 4 * FOLD_MAX_B + 1 + 17 + 2;
+
 struct TileMeta {
     int b, hk, chunk, nrows, flags, seq, pad0, pad1;
 };
@@ -88,7 +95,8 @@ struct MC {
     static constexpr int OFF_META = OFF_VST + NCW * VST;         // TileMeta [NGRP][RS]
     static constexpr int OFF_BAR = OFF_META + NGRP * RS * 32;
     static constexpr int NBAR = 2 * NGRP * RS + 2 * NGRP;        // full, empty [NGRP][RS]; mrg_full, mrg_done [NGRP]
-    static constexpr int SMEM = OFF_BAR + NBAR * 8 + 16 + 128;
+    static constexpr int OFF_PLAN = OFF_BAR + NBAR * 8 + 16;     // item tables of the in-kernel plan
+    static constexpr int SMEM = OFF_PLAN + PLAN_INTS * 4 + 128;
     static_assert(SMEM <= SMEM_LIMIT, "decode_mma shared memory");
 };
 
@@ -100,6 +108,7 @@ struct DecMmaParams {
     __half* out;
     float* part;  // [B][Hkv][nchunks][G][HD + 2] when nchunks > 1
     int* work;    // [0] item counter, [1 .. B+1] prefix of items per sequence (plan kernel)
+    int fold;     // 1: no plan kernel ran; the item order is derived in the kernel (B <= FOLD_MAX_B)
     const int2* items;  // item list (b, hk << 16 | chunk), written by the plan kernel
     int64_t B, H, Hkv, Smax;
     int nchunks, chunk;
@@ -209,24 +218,101 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_mma_kernel(const DecMmaPar
         *abort_flag = 0;
         fence_mbar_init();
     }
+    // in-kernel plan: the same order as the plan kernel's list (full chunks sequence-major, then
+    // each sequence's partial last chunk by decreasing size class, sequences in order within a class)
+    int* s_full = (int*)(smem + C::OFF_PLAN);  // full chunks of sequence b
+    int* s_cls = s_full + FOLD_MAX_B;          // size class of its partial chunk, -1: none
+    int* s_fpre = s_cls + FOLD_MAX_B;          // full items of sequences < b
+    int* s_tail = s_fpre + FOLD_MAX_B + 1;     // sequences with a partial chunk, in list order
+    int* s_cs = s_tail + FOLD_MAX_B;           // [17] class starts, [17] full items, [18] all items
+    if (p.fold) {
+        const int B = (int)p.B, ch = p.chunk, hkv = (int)p.Hkv;
+        for (int b = threadIdx.x; b < B; b += NTHREADS) {
+            int64_t len = p.lens[b];
+            len = len < 0 ? 0 : (len > p.Smax ? p.Smax : len);
+            const int fc = (int)(len / ch);
+            const int nch = len == 0 ? 1 : (int)((len + ch - 1) / ch);
+            s_full[b] = fc;
+            s_cls[b] = nch > fc ? (int)((16 * (len - (int64_t)fc * ch) + ch - 1) / ch) : -1;
+        }
+        __syncthreads();
+        if (warp == 0) {
+            const int per = (B + 31) / 32, b0 = min(B, lane * per), b1 = min(B, b0 + per);
+            int loc = 0;
+            for (int b = b0; b < b1; ++b) loc += s_full[b];
+            int x = loc;
+#pragma unroll
+            for (int off = 1; off < 32; off <<= 1) {
+                const int y = __shfl_up_sync(0xffffffffu, x, off);
+                if (lane >= off) x += y;
+            }
+            int run = x - loc;
+            for (int b = b0; b < b1; ++b) {
+                s_fpre[b] = run * hkv;
+                run += s_full[b];
+            }
+            const int fitems = __shfl_sync(0xffffffffu, x, 31) * hkv;
+            int cnt = 0;
+            if (lane < 17)
+                for (int b = 0; b < B; ++b) cnt += (s_cls[b] == lane);
+            int suf = cnt;  // sequences in classes >= lane (larger classes come first)
+#pragma unroll
+            for (int off = 1; off < 32; off <<= 1) {
+                const int y = __shfl_down_sync(0xffffffffu, suf, off);
+                if (lane + off < 17) suf += y;
+            }
+            if (lane < 17) s_cs[lane] = suf - cnt;  // first list slot (in sequences) of class lane
+            const int ntail = __shfl_sync(0xffffffffu, suf, 0);
+            if (lane == 0) {
+                s_fpre[B] = fitems;
+                s_cs[17] = fitems;
+                s_cs[18] = fitems + ntail * hkv;
+            }
+        }
+        __syncthreads();
+        for (int b = threadIdx.x; b < B; b += NTHREADS) {
+            const int k = s_cls[b];
+            if (k >= 0) {
+                int r = 0;
+                for (int b2 = 0; b2 < b; ++b2) r += (s_cls[b2] == k);
+                s_tail[s_cs[k] + r] = b;
+            }
+        }
+    }
     __syncthreads();
 
     if (warp >= NCW) {
         // ------------------------------------------------------------ producer of group warp - NCW
         if (lane == 0) {
             const int gp = warp - NCW;
-            const int total = p.work[1 + p.B];
+            const int total = p.fold ? s_cs[18] : p.work[1 + p.B];
+            // item n -> (b, hk << 16 | chunk): from the plan kernel's list, or from the tables
+            auto item = [&](int n) -> int2 {
+                if (!p.fold) return p.items[n];
+                const int hkv = (int)p.Hkv;
+                if (n < s_cs[17]) {  // full chunk: the sequence with s_fpre[b] <= n < s_fpre[b + 1]
+                    int lo = 0, hi = (int)p.B;
+                    while (hi - lo > 1) {
+                        const int mid = (lo + hi) >> 1;
+                        if (s_fpre[mid] <= n) lo = mid; else hi = mid;
+                    }
+                    const int w = n - s_fpre[lo], fc = s_full[lo];
+                    return make_int2(lo, ((w / fc) << 16) | (w % fc));
+                }
+                const int t = n - s_cs[17], b = s_tail[t / hkv];
+                return make_int2(b, ((t % hkv) << 16) | s_full[b]);
+            };
             // claims run two deep: the counter for item k+2 and the list entry of item k+1 are fetched
             // while item k's tiles are issued, so neither latency stalls the ring
             int n1 = atomicAdd(p.work, 1);
             int n2 = atomicAdd(p.work, 1);
-            int2 d1 = n1 < total ? p.items[n1] : make_int2(0, 0);
+            int2 d1 = n1 < total ? item(n1) : make_int2(0, 0);
             int n = 0, seq = 0;
             bool ok = true;
             while (ok && n1 < total) {  // claims only grow: once n1 is past the end, so is n2
                 const int b = d1.x, hk = d1.y >> 16, chunk = d1.y & 0xFFFF;
                 n1 = n2;
-                d1 = n1 < total ? p.items[n1] : make_int2(0, 0);
+                d1 = n1 < total ? item(n1) : make_int2(0, 0);
                 n2 = atomicAdd(p.work, 1);
                 int64_t len = p.lens[b];
                 len = len < 0 ? 0 : (len > p.Smax ? p.Smax : len);
@@ -602,8 +688,15 @@ int run_decode_mma(const DecodeArgs& a, int* work, float* part, int64_t nchunks,
     if (cuda_failed(cudaFuncSetAttribute(decode_mma_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM),
                     "cudaFuncSetAttribute(decode_mma)"))
         return -1;
-    if (launch_decode_plan(a, work, st) != 0) return -1;
+    // small batches plan inside the kernel: only the claim counter needs zeroing
+    const bool fold = a.B <= FOLD_MAX_B;
+    if (fold) {
+        if (cuda_failed(cudaMemsetAsync(work, 0, sizeof(int), st), "decode_mma counter reset")) return -1;
+    } else if (launch_decode_plan(a, work, st) != 0) {
+        return -1;
+    }
     DecMmaParams p;
+    p.fold = fold ? 1 : 0;
     p.q = (const __half*)a.q;
     p.k = (const uint8_t*)a.k;
     p.v = (const uint8_t*)a.v;
