@@ -173,6 +173,9 @@ int env_int(const char* name, int dflt) {
 }
 
 }  // namespace
+
+void retain_pool_memory(int dev) { keep_pool_memory(dev); }
+
 }  // namespace gtb
 
 using namespace gtb;

@@ -40,6 +40,9 @@ bool cuda_failed(cudaError_t e, const char* what);
 // Per-device status word that kernels set when a bounded wait runs out (never trap, never hang).
 int* device_status_word(int device);
 
+// Keep freed memory in the device's stream-ordered pool (per-call scratch stays allocation-free).
+void retain_pool_memory(int dev);
+
 template <typename T> struct Elem;
 template <> struct Elem<float> {
     __device__ static float load(const float* p) { return *p; }

@@ -62,7 +62,7 @@ struct Cfg {
     static constexpr int OFF_K = 2 * TILE;
     static constexpr int OFF_V = OFF_K + KS * TILE;
     static constexpr int OFF_BAR = OFF_V + VS * TILE;
-    static constexpr int NBAR = 1 + 2 * KS + 2 * VS + 2 + 2 + 2 + 1;
+    static constexpr int NBAR = 1 + 2 * KS + 2 * VS + 2 + 2 + 2 + 1 + 1 + 2 + 4;
     static constexpr int SMEM = OFF_BAR + NBAR * 8 + 16 + 1024;  // + TMEM slot and flag, + alignment slack
 };
 
@@ -121,7 +121,10 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* s
 struct Params {
     int64_t H, Hkv, L, S;
     int group;
-    int n_pairs;  // CTAs along the query dimension (two 128-row tiles each)
+    int n_pairs;  // work items along the query dimension (two 128-row tiles each)
+    int n_items;  // n_pairs * H * B: item i = (pair, head, batch), heaviest pairs first
+    int64_t B;
+    int* claim;   // zeroed item counter: CTAs claim items in order
     float scale_log2;
     int causal;
     void* o;
@@ -164,23 +167,50 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
     uint64_t* p_full = s_full + 2;           // [2] per tile: P_t(j) written (128 arrivals)
     uint64_t* o_final = p_full + 2;          // [2] per tile: every MMA of the tile done
     uint64_t* drain = o_final + 2;           // error path only
+    uint64_t* q_empty = drain + 1;           // every S MMA of an item done: its Q buffers are free
+    uint64_t* o_empty = q_empty + 1;         // [2] per tile: the epilogue has read O_t (128 arrivals)
+    uint64_t* item_full = o_empty + 2;       // [2] ring of claimed items: index written
+    uint64_t* item_empty = item_full + 2;    // [2] ... read by the MMA warp and the 8 softmax warps
     uint32_t* tmem_slot = (uint32_t*)(bars + C::NBAR);
     int* abort_flag = (int*)(tmem_slot + 1);
+    int* item_slot = abort_flag + 1;         // [2] claimed item index, -1: no more items
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int pair = p.causal ? (p.n_pairs - 1 - (int)blockIdx.x) : (int)blockIdx.x;  // heavy pairs first
-    const int h = blockIdx.y, b = blockIdx.z;
-    const int hk = h / p.group;
     const int n_kv = (int)((p.S + BN - 1) / BN);
-    const int row0[2] = {pair * 2 * BM, pair * 2 * BM + BM};
-    const int nblk[2] = {tile_blocks(row0[0], p, n_kv), tile_blocks(row0[1], p, n_kv)};
-    const int n = max(nblk[0], nblk[1]);  // nblk[0] >= 1: the CTA exists because row0[0] < L
+    // Persistent CTAs (one per SM) claim items from a counter in order; item i = (pair, head h,
+    // batch b), the pairs heaviest first (causal), heads fastest, so that the CTAs take the longest
+    // work first and the query heads of a kv head run side by side (K/V re-reads hit L2). The TMA
+    // warp claims and passes each item on through a two-slot ring in shared memory. The K/V ring,
+    // the barrier phases and TMEM carry over from item to item: the next item's K/V loads start as
+    // soon as ring slots free up, its Q load as soon as the previous item's S MMAs are done.
+    struct Item {
+        int h, b, hk, row0[2], nblk[2], n;
+    };
+    auto item_of = [&](int i) {
+        Item it;
+        const int hb = (int)(p.H * p.B);
+        const int pr = i / hb, rem = i - pr * hb;
+        const int pair = p.causal ? (p.n_pairs - 1 - pr) : pr;
+        it.h = (int)(rem % p.H);
+        it.b = (int)(rem / p.H);
+        it.hk = it.h / p.group;
+        it.row0[0] = pair * 2 * BM;
+        it.row0[1] = pair * 2 * BM + BM;
+        it.nblk[0] = tile_blocks(it.row0[0], p, n_kv);  // >= 1: row0[0] < L for every pair
+        it.nblk[1] = tile_blocks(it.row0[1], p, n_kv);
+        it.n = max(it.nblk[0], it.nblk[1]);
+        return it;
+    };
 
     if (threadIdx.x == 0) {
         mbar_init(q_full, 1);
         for (int i = 0; i < C::KS; ++i) { mbar_init(&k_full[i], 1); mbar_init(&k_empty[i], 1); }
         for (int i = 0; i < C::VS; ++i) { mbar_init(&v_full[i], 1); mbar_init(&v_empty[i], 1); }
-        for (int t = 0; t < 2; ++t) { mbar_init(&s_full[t], 1); mbar_init(&p_full[t], 128); mbar_init(&o_final[t], 1); }
+        for (int t = 0; t < 2; ++t) {
+            mbar_init(&s_full[t], 1); mbar_init(&p_full[t], 128); mbar_init(&o_final[t], 1); mbar_init(&o_empty[t], 128);
+        }
+        mbar_init(q_empty, 1);
+        for (int i = 0; i < 2; ++i) { mbar_init(&item_full[i], 1); mbar_init(&item_empty[i], 9); }
         mbar_init(drain, 1);
         *abort_flag = 0;
         fence_mbar_init();
@@ -197,37 +227,57 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
             prefetch_tmap(&tmQ);
             prefetch_tmap(&tmK);
             prefetch_tmap(&tmV);
-            int last_k = -1, last_v = -1;
+            int J = 0, nitem = 0;  // K/V blocks and items started so far
+            int nk = 0, nv = 0, nql = 0;  // K, V and Q loads issued
             bool ok = true;
-            const int nq = nblk[1] > 0 ? 2 : 1;
-            mbar_expect_tx(q_full, nq * C::TILE);
-            for (int t = 0; t < nq; ++t)
-                for (int a = 0; a < C::ATOMS; ++a)
-                    tma_load_4d(smem + C::OFF_Q + t * C::TILE + a * C::ATOM_BYTES, &tmQ, a * 64, row0[t], h, b, q_full);
-            for (int j = 0; j < n && ok; ++j) {
-                const int ks = j % C::KS;
-                if (j >= C::KS) ok = mbar_wait(&k_empty[ks], ((j / C::KS) - 1) & 1, p.status, 11);
-                if (!ok || *(volatile int*)abort_flag) break;
-                mbar_expect_tx(&k_full[ks], C::TILE);
-                for (int a = 0; a < C::ATOMS; ++a)
-                    tma_load_4d(smem + C::OFF_K + ks * C::TILE + a * C::ATOM_BYTES, &tmK, a * 64, j * BN, hk, b, &k_full[ks]);
-                last_k = j;
-                const int vs = j % C::VS;
-                if (j >= C::VS) ok = mbar_wait(&v_empty[vs], ((j / C::VS) - 1) & 1, p.status, 12);
-                if (!ok || *(volatile int*)abort_flag) break;
-                mbar_expect_tx(&v_full[vs], C::TILE);
-                for (int a = 0; a < C::ATOMS; ++a)
-                    tma_load_4d(smem + C::OFF_V + vs * C::TILE + a * C::ATOM_BYTES, &tmV, a * 64, j * BN, hk, b, &v_full[vs]);
-                last_v = j;
+            int next = atomicAdd(p.claim, 1);  // claims run one item ahead: the atomic's latency is hidden
+            for (;; ++nitem) {
+                const int slot = nitem & 1;
+                if (nitem >= 2) ok = mbar_wait(&item_empty[slot], ((nitem >> 1) - 1) & 1, p.status, 14);
+                if (!ok || *(volatile int*)abort_flag) { ok = false; break; }
+                const int i = next;
+                item_slot[slot] = i < p.n_items ? i : -1;
+                mbar_arrive(&item_full[slot]);
+                if (i >= p.n_items) break;
+                next = atomicAdd(p.claim, 1);
+                const Item it = item_of(i);
+                for (int j = 0; j < it.n && ok; ++j, ++J) {
+                    const int ks = J % C::KS;
+                    if (J >= C::KS) ok = mbar_wait(&k_empty[ks], ((J / C::KS) - 1) & 1, p.status, 11);
+                    if (!ok || *(volatile int*)abort_flag) { ok = false; break; }
+                    mbar_expect_tx(&k_full[ks], C::TILE);
+                    for (int a = 0; a < C::ATOMS; ++a)
+                        tma_load_4d(smem + C::OFF_K + ks * C::TILE + a * C::ATOM_BYTES, &tmK, a * 64, j * BN, it.hk, it.b,
+                                    &k_full[ks]);
+                    ++nk;
+                    const int vs = J % C::VS;
+                    if (J >= C::VS) ok = mbar_wait(&v_empty[vs], ((J / C::VS) - 1) & 1, p.status, 12);
+                    if (!ok || *(volatile int*)abort_flag) { ok = false; break; }
+                    mbar_expect_tx(&v_full[vs], C::TILE);
+                    for (int a = 0; a < C::ATOMS; ++a)
+                        tma_load_4d(smem + C::OFF_V + vs * C::TILE + a * C::ATOM_BYTES, &tmV, a * 64, j * BN, it.hk, it.b,
+                                    &v_full[vs]);
+                    ++nv;
+                    if (j == 0) {
+                        // Q of the item, once the previous item's S MMAs have read theirs
+                        if (nitem > 0) ok = mbar_wait(q_empty, (nitem - 1) & 1, p.status, 13);
+                        if (!ok || *(volatile int*)abort_flag) { ok = false; break; }
+                        const int nq = it.nblk[1] > 0 ? 2 : 1;
+                        mbar_expect_tx(q_full, nq * C::TILE);
+                        for (int t = 0; t < nq; ++t)
+                            for (int a = 0; a < C::ATOMS; ++a)
+                                tma_load_4d(smem + C::OFF_Q + t * C::TILE + a * C::ATOM_BYTES, &tmQ, a * 64, it.row0[t],
+                                            it.h, it.b, q_full);
+                        ++nql;
+                    }
+                }
             }
             if (!ok) *(volatile int*)abort_flag = 1;
             if (*(volatile int*)abort_flag) {
-                // drain our own copies before the CTA exits (bounded)
-                mbar_wait(q_full, 0, nullptr, 0);
-                for (int j = max(0, last_k - C::KS + 1); j <= last_k; ++j)
-                    mbar_wait(&k_full[j % C::KS], (j / C::KS) & 1, nullptr, 0);
-                for (int j = max(0, last_v - C::VS + 1); j <= last_v; ++j)
-                    mbar_wait(&v_full[j % C::VS], (j / C::VS) & 1, nullptr, 0);
+                // drain our own copies before the CTA exits (bounded): the last Q and the last K/V blocks
+                if (nql > 0) mbar_wait(q_full, (nql - 1) & 1, nullptr, 0);
+                for (int jj = max(0, nk - C::KS); jj < nk; ++jj) mbar_wait(&k_full[jj % C::KS], (jj / C::KS) & 1, nullptr, 0);
+                for (int jj = max(0, nv - C::VS); jj < nv; ++jj) mbar_wait(&v_full[jj % C::VS], (jj / C::VS) & 1, nullptr, 0);
             }
         }
     } else if (warp == 1) {
@@ -235,7 +285,6 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
         if (lane == 0) {
             constexpr uint32_t IDESC_S = idesc_f16(BM, BN, BF16, false);
             constexpr uint32_t IDESC_PV = idesc_f16(BM, D, BF16, true);
-            bool ok = mbar_wait(q_full, 0, p.status, 21);
             // operand descriptors of every buffer, built once: per MMA only a constant is added to the
             // start address
             static_assert(C::KS == 2 && C::VS == 2, "descriptor selection below assumes two K and two V stages");
@@ -245,9 +294,12 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
             const uint64_t kd1 = desc_sw128(smem_u32(smem + C::OFF_K + C::TILE), 16, 1024);
             const uint64_t vd0 = desc_sw128(smem_u32(smem + C::OFF_V), C::ATOM_BYTES, 1024);
             const uint64_t vd1 = desc_sw128(smem_u32(smem + C::OFF_V + C::TILE), C::ATOM_BYTES, 1024);
-            auto issue_s = [&](int t, int j) -> bool {
-                const int ks = j % C::KS;
-                if (!mbar_wait(&k_full[ks], (j / C::KS) & 1, p.status, 22)) return false;
+            // J: K/V block of the ring (over all items); u[t]: blocks of tile t so far (s_full / p_full
+            // phases); nf[t]: items with a tile t so far (o_final / o_empty phases)
+            int J = 0, u[2] = {0, 0}, nf[2] = {0, 0}, nitem = 0;
+            auto issue_s = [&](int t, int jg) -> bool {  // S_t of ring block jg
+                const int ks = jg % C::KS;
+                if (!mbar_wait(&k_full[ks], (jg / C::KS) & 1, p.status, 22)) return false;
                 tc_fence_after();
                 const uint64_t qb = t ? qd1 : qd0, kb = ks ? kd1 : kd0;
                 const uint32_t dst = tmem + s_col(t);
@@ -259,33 +311,54 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
                 mma_commit(&s_full[t]);
                 return true;
             };
-            auto issue_pv = [&](int t, int j) -> bool {
-                if (!mbar_wait(&p_full[t], j & 1, p.status, 23)) return false;
-                const int vs = j % C::VS;
-                if (!mbar_wait(&v_full[vs], (j / C::VS) & 1, p.status, 24)) return false;
+            auto issue_pv = [&](int t, int jg, int ut, bool first) -> bool {  // PV_t of ring block jg
+                if (!mbar_wait(&p_full[t], ut & 1, p.status, 23)) return false;
+                const int vs = jg % C::VS;
+                if (!mbar_wait(&v_full[vs], (jg / C::VS) & 1, p.status, 24)) return false;
                 tc_fence_after();
                 const uint64_t vb = vs ? vd1 : vd0;
                 const uint32_t dst = tmem + o_col(t), pa = tmem + s_col(t) + P_OFF;
 #pragma unroll
                 for (int kk = 0; kk < BN / 16; ++kk) {
                     // A = P_t(j): 16-bit values packed two per TMEM column, 8 columns per K step
-                    mma_ts(dst, pa + kk * 8, desc_advance(vb, kk * 2048), IDESC_PV, (j > 0 || kk > 0) ? 1u : 0u);
+                    mma_ts(dst, pa + kk * 8, desc_advance(vb, kk * 2048), IDESC_PV, (!first || kk > 0) ? 1u : 0u);
                 }
                 return true;
             };
-            for (int t = 0; t < 2 && ok; ++t)
-                if (nblk[t] > 0) ok = issue_s(t, 0);
-            if (ok) mma_commit(&k_empty[0]);
-            for (int j = 0; j < n && ok; ++j) {
-                for (int t = 0; t < 2 && ok; ++t) {
-                    if (j >= nblk[t]) continue;
-                    ok = issue_pv(t, j);
-                    if (ok && j + 1 < nblk[t]) ok = issue_s(t, j + 1);
-                    if (ok && j + 1 == nblk[t]) mma_commit(&o_final[t]);
+            bool ok = true;
+            for (;; ++nitem) {
+                const int slot = nitem & 1;
+                ok = mbar_wait(&item_full[slot], (nitem >> 1) & 1, p.status, 27);
+                if (!ok) break;
+                const int i = item_slot[slot];
+                mbar_arrive(&item_empty[slot]);
+                if (i < 0) break;
+                const Item it = item_of(i);
+                ok = mbar_wait(q_full, nitem & 1, p.status, 21);
+                for (int t = 0; t < 2 && ok; ++t)
+                    if (it.nblk[t] > 0) ok = issue_s(t, J);
+                if (!ok) break;
+                mma_commit(&k_empty[J % C::KS]);
+                if (it.n == 1) mma_commit(q_empty);  // every S of the item issued
+                for (int j = 0; j < it.n && ok; ++j) {
+                    for (int t = 0; t < 2 && ok; ++t) {
+                        if (j >= it.nblk[t]) continue;
+                        // the first PV of an item overwrites O_t: the previous item's epilogue must have read it
+                        if (j == 0 && nf[t] > 0) ok = mbar_wait(&o_empty[t], (nf[t] - 1) & 1, p.status, 26);
+                        if (ok) ok = issue_pv(t, J + j, u[t] + j, j == 0);
+                        if (ok && j + 1 < it.nblk[t]) ok = issue_s(t, J + j + 1);
+                        if (ok && j + 1 == it.nblk[t]) mma_commit(&o_final[t]);
+                    }
+                    if (!ok || *(volatile int*)abort_flag) { ok = false; break; }
+                    mma_commit(&v_empty[(J + j) % C::VS]);
+                    if (j + 1 < it.n) mma_commit(&k_empty[(J + j + 1) % C::KS]);
+                    if (j + 2 == it.n) mma_commit(q_empty);  // the item's last S MMAs were issued at this j
                 }
-                if (!ok || *(volatile int*)abort_flag) break;
-                mma_commit(&v_empty[j % C::VS]);
-                if (j + 1 < n) mma_commit(&k_empty[(j + 1) % C::KS]);
+                J += it.n;
+                for (int t = 0; t < 2; ++t) {
+                    u[t] += it.nblk[t];
+                    nf[t] += it.nblk[t] > 0 ? 1 : 0;
+                }
             }
             if (!ok) *(volatile int*)abort_flag = 1;
             if (*(volatile int*)abort_flag) {
@@ -298,20 +371,34 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
         const int t = (warp - 4) >> 2;
         const int quad = warp & 3;                    // TMEM lanes this warp may access
         const int r = quad * 32 + lane;               // row of the tile
-        const int grow = row0[t] + r;                 // query index
         const uint32_t lane_addr = (uint32_t)(quad * 32) << 16;
         const uint32_t s_tmem = tmem + lane_addr + s_col(t);
         const uint32_t o_tmem = tmem + lane_addr + o_col(t);
         const int lim_s = (int)min(p.S, (int64_t)INT32_MAX) - 1;
+        int u = 0, nf = 0;  // blocks and items of tile t so far (barrier phases)
+        bool ok = true;
+        for (int nitem = 0; ok; ++nitem) {
+        const int slot = nitem & 1;
+        ok = warp_wait(&item_full[slot], (nitem >> 1) & 1, p.status, 34);
+        if (!ok) break;
+        const int i = item_slot[slot];
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&item_empty[slot]);
+        if (i < 0) break;
+        const Item it = item_of(i);
+        const int nb = it.nblk[t];
+        if (nb == 0) continue;
+        const int h = it.h, b = it.b;
+        const int row0t = it.row0[t];
+        const int grow = row0t + r;                   // query index
         const int lim = p.causal ? min(lim_s, grow) : lim_s;  // last key this row may see
         float m_used = -INFINITY, lsum = 0.0f;
-        bool ok = true;
-        for (int j = 0; j < nblk[t]; ++j) {
-            ok = warp_wait(&s_full[t], j & 1, p.status, 31);
+        for (int j = 0; j < nb; ++j) {
+            ok = warp_wait(&s_full[t], (u + j) & 1, p.status, 31);
             if (!ok || __any_sync(0xffffffffu, *(volatile int*)abort_flag)) break;
             tc_fence_after();
             const int kv0 = j * BN;
-            const bool need_mask = (kv0 + BN > p.S) || (p.causal && kv0 + BN - 1 > row0[t]);
+            const bool need_mask = (kv0 + BN > p.S) || (p.causal && kv0 + BN - 1 > row0t);
             // pass 1: row maximum, 64 columns at a time; columns 64..127 stay in registers for pass 2
             uint32_t ra[32], rb[32];
             float* xa = (float*)ra;
@@ -396,9 +483,10 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
             tc_fence_before();
             mbar_arrive(&p_full[t]);
         }
-        if (!ok) *(volatile int*)abort_flag = 1;
-        if (nblk[t] > 0 && ok && !*(volatile int*)abort_flag) {
-            ok = warp_wait(&o_final[t], 0, p.status, 33);
+        u += nb;
+        if (!ok) break;
+        if (!*(volatile int*)abort_flag) {
+            ok = warp_wait(&o_final[t], nf & 1, p.status, 33);
             if (ok) {
                 tc_fence_after();
                 const float inv = lsum > 0.0f ? 1.0f / lsum : 0.0f;
@@ -421,10 +509,15 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
                 if (p.lse && grow < p.L)
                     p.lse[((int64_t)b * p.H + h) * p.L + grow] =
                         lsum > 0.0f ? (m_used + log2f(lsum)) * 0.69314718055994531f : -INFINITY;
-            } else {
-                *(volatile int*)abort_flag = 1;
+                tc_fence_before();
+                mbar_arrive(&o_empty[t]);  // O_t has been read: the next item's PV may overwrite it
+                ++nf;
             }
+        } else {
+            ok = false;
         }
+        }
+        if (!ok) *(volatile int*)abort_flag = 1;
     }
 
     tc_fence_before();
@@ -515,9 +608,28 @@ int run(const FwdArgs& a, const CUtensorMap& mq, const CUtensorMap& mk, const CU
     int dev = 0;
     cudaGetDevice(&dev);
     p.status = device_status_word(dev);
-    dim3 grid((unsigned)p.n_pairs, (unsigned)a.sh.H, (unsigned)a.sh.B);
+    p.B = a.sh.B;
+    const int64_t items = (int64_t)p.n_pairs * a.sh.H * a.sh.B;
+    if (items >= INT32_MAX) {
+        set_error("flash_attention (sm100): too many work items");
+        return -1;
+    }
+    p.n_items = (int)items;
+    static int n_sm = 0;
+    if (n_sm == 0 && (cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n_sm <= 0))
+        n_sm = 148;
+    const int grid = (int)min((int64_t)n_sm, items);  // persistent: one CTA per SM
+    // the item counter: 4 bytes of the stream-ordered pool, zeroed on the stream
+    retain_pool_memory(dev);
+    int* claim = nullptr;
+    if (cuda_failed(cudaMallocAsync((void**)&claim, sizeof(int), st), "flash_attention (sm100): item counter") ||
+        cuda_failed(cudaMemsetAsync(claim, 0, sizeof(int), st), "flash_attention (sm100): item counter reset"))
+        return -1;
+    p.claim = claim;
     kern<<<grid, NTHREADS, C::SMEM, st>>>(mq, mk, mv, p);
-    return cuda_failed(cudaGetLastError(), "flash_attention (sm100) launch") ? -1 : 0;
+    const bool bad = cuda_failed(cudaGetLastError(), "flash_attention (sm100) launch");
+    cudaFreeAsync(claim, st);
+    return bad ? -1 : 0;
 }
 
 // Exponentials computed by exp2_poly2 per 8 (GTB_FWD_EMU=0|2|4, default 0).
