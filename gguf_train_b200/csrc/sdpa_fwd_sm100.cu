@@ -122,9 +122,9 @@ struct Params {
     int64_t H, Hkv, L, S;
     int group;
     int n_pairs;  // work items along the query dimension (two 128-row tiles each)
-    int n_items;  // n_pairs * H * B: item i = (pair, head, batch), heaviest pairs first
+    int n_items;  // n_pairs * H * B: item i = (batch, kv head, pair heaviest first, query head)
     int64_t B;
-    int* claim;   // zeroed item counter: CTAs claim items in order
+    int* claim;   // zeroed item counter: CTAs claim items in order (persistent launch)
     float scale_log2;
     int causal;
     void* o;
@@ -149,7 +149,7 @@ __device__ __forceinline__ void mask_chunk(float* x, int kv0, int lim) {
         if (kv0 + i > lim) x[i] = -INFINITY;
 }
 
-template <int D, bool BF16, int EMU>
+template <int D, bool BF16, int EMU, bool PERSIST>
 __global__ void __launch_bounds__(NTHREADS, 1)
 fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                  const __grid_constant__ CUtensorMap tmV, const Params p) {
@@ -177,22 +177,32 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n_kv = (int)((p.S + BN - 1) / BN);
-    // Persistent CTAs (one per SM) claim items from a counter in order; item i = (pair, head h,
-    // batch b), the pairs heaviest first (causal), heads fastest, so that the CTAs take the longest
-    // work first and the query heads of a kv head run side by side (K/V re-reads hit L2). The TMA
-    // warp claims and passes each item on through a two-slot ring in shared memory. The K/V ring,
-    // the barrier phases and TMEM carry over from item to item: the next item's K/V loads start as
-    // soon as ring slots free up, its Q load as soon as the previous item's S MMAs are done.
+    // Work item = (pair of 128-row query tiles, head, batch). Persistent launch (short sequences):
+    // one CTA per SM claims items from a counter, pairs heaviest first and (batch, head) fastest, so
+    // that the CTAs take the longest work first; the TMA warp claims and passes each item on through
+    // a two-slot ring in shared memory, and the K/V ring, the barrier phases and TMEM carry over from
+    // item to item (the next item's K/V loads start as soon as ring slots free up, its Q load as soon
+    // as the previous item's S MMAs are done), which hides each item's start-up. One CTA per item
+    // (long sequences): blockIdx order, (batch, head) major and pairs heaviest first, so that the
+    // CTAs running together stream the same head's K/V and share it through L2; measured faster
+    // when a sequence's K/V is far larger than L2.
     struct Item {
         int h, b, hk, row0[2], nblk[2], n;
     };
     auto item_of = [&](int i) {
         Item it;
-        const int hb = (int)(p.H * p.B);
-        const int pr = i / hb, rem = i - pr * hb;
+        int pr, bh;
+        if constexpr (PERSIST) {  // pairs heaviest first, (batch, head) fastest
+            const int hb = (int)(p.H * p.B);
+            pr = i / hb;
+            bh = i - pr * hb;
+        } else {             // (batch, head) major, pairs heaviest first
+            bh = i / p.n_pairs;
+            pr = i - bh * p.n_pairs;
+        }
         const int pair = p.causal ? (p.n_pairs - 1 - pr) : pr;
-        it.h = (int)(rem % p.H);
-        it.b = (int)(rem / p.H);
+        it.b = (int)(bh / p.H);
+        it.h = (int)(bh % p.H);
         it.hk = it.h / p.group;
         it.row0[0] = pair * 2 * BM;
         it.row0[1] = pair * 2 * BM + BM;
@@ -230,17 +240,30 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
             int J = 0, nitem = 0;  // K/V blocks and items started so far
             int nk = 0, nv = 0, nql = 0;  // K, V and Q loads issued
             bool ok = true;
-            int next = atomicAdd(p.claim, 1);  // claims run one item ahead: the atomic's latency is hidden
+            // claims run one item ahead (the atomic's latency is hidden); one item per CTA otherwise
+            int next = PERSIST ? atomicAdd(p.claim, 1) : (int)blockIdx.x;
             for (;; ++nitem) {
-                const int slot = nitem & 1;
-                if (nitem >= 2) ok = mbar_wait(&item_empty[slot], ((nitem >> 1) - 1) & 1, p.status, 14);
-                if (!ok || *(volatile int*)abort_flag) { ok = false; break; }
                 const int i = next;
-                item_slot[slot] = i < p.n_items ? i : -1;
-                mbar_arrive(&item_full[slot]);
+                if constexpr (PERSIST) {
+                    const int slot = nitem & 1;
+                    if (nitem >= 2) ok = mbar_wait(&item_empty[slot], ((nitem >> 1) - 1) & 1, p.status, 14);
+                    if (!ok || *(volatile int*)abort_flag) { ok = false; break; }
+                    item_slot[slot] = i < p.n_items ? i : -1;
+                    mbar_arrive(&item_full[slot]);
+                }
                 if (i >= p.n_items) break;
-                next = atomicAdd(p.claim, 1);
+                next = PERSIST ? atomicAdd(p.claim, 1) : p.n_items;
                 const Item it = item_of(i);
+                const int nq = it.nblk[1] > 0 ? 2 : 1;
+                auto load_q = [&]() {
+                    mbar_expect_tx(q_full, nq * C::TILE);
+                    for (int t = 0; t < nq; ++t)
+                        for (int a = 0; a < C::ATOMS; ++a)
+                            tma_load_4d(smem + C::OFF_Q + t * C::TILE + a * C::ATOM_BYTES, &tmQ, a * 64, it.row0[t], it.h,
+                                        it.b, q_full);
+                    ++nql;
+                };
+                if (nitem == 0) load_q();  // the CTA's first item: nothing to wait for, Q first
                 for (int j = 0; j < it.n && ok; ++j, ++J) {
                     const int ks = J % C::KS;
                     if (J >= C::KS) ok = mbar_wait(&k_empty[ks], ((J / C::KS) - 1) & 1, p.status, 11);
@@ -258,17 +281,12 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
                         tma_load_4d(smem + C::OFF_V + vs * C::TILE + a * C::ATOM_BYTES, &tmV, a * 64, j * BN, it.hk, it.b,
                                     &v_full[vs]);
                     ++nv;
-                    if (j == 0) {
-                        // Q of the item, once the previous item's S MMAs have read theirs
-                        if (nitem > 0) ok = mbar_wait(q_empty, (nitem - 1) & 1, p.status, 13);
+                    if (j == 0 && nitem > 0) {
+                        // Q of a later item, once the previous item's S MMAs have read theirs (after this
+                        // item's first K/V block, whose slots may free up earlier)
+                        ok = mbar_wait(q_empty, (nitem - 1) & 1, p.status, 13);
                         if (!ok || *(volatile int*)abort_flag) { ok = false; break; }
-                        const int nq = it.nblk[1] > 0 ? 2 : 1;
-                        mbar_expect_tx(q_full, nq * C::TILE);
-                        for (int t = 0; t < nq; ++t)
-                            for (int a = 0; a < C::ATOMS; ++a)
-                                tma_load_4d(smem + C::OFF_Q + t * C::TILE + a * C::ATOM_BYTES, &tmQ, a * 64, it.row0[t],
-                                            it.h, it.b, q_full);
-                        ++nql;
+                        load_q();
                     }
                 }
             }
@@ -327,11 +345,16 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
             };
             bool ok = true;
             for (;; ++nitem) {
-                const int slot = nitem & 1;
-                ok = mbar_wait(&item_full[slot], (nitem >> 1) & 1, p.status, 27);
-                if (!ok) break;
-                const int i = item_slot[slot];
-                mbar_arrive(&item_empty[slot]);
+                int i;
+                if constexpr (PERSIST) {
+                    const int slot = nitem & 1;
+                    ok = mbar_wait(&item_full[slot], (nitem >> 1) & 1, p.status, 27);
+                    if (!ok) break;
+                    i = item_slot[slot];
+                    mbar_arrive(&item_empty[slot]);
+                } else {
+                    i = nitem == 0 ? (int)blockIdx.x : -1;
+                }
                 if (i < 0) break;
                 const Item it = item_of(i);
                 ok = mbar_wait(q_full, nitem & 1, p.status, 21);
@@ -378,12 +401,17 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
         int u = 0, nf = 0;  // blocks and items of tile t so far (barrier phases)
         bool ok = true;
         for (int nitem = 0; ok; ++nitem) {
-        const int slot = nitem & 1;
-        ok = warp_wait(&item_full[slot], (nitem >> 1) & 1, p.status, 34);
-        if (!ok) break;
-        const int i = item_slot[slot];
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&item_empty[slot]);
+        int i;
+        if constexpr (PERSIST) {
+            const int slot = nitem & 1;
+            ok = warp_wait(&item_full[slot], (nitem >> 1) & 1, p.status, 34);
+            if (!ok) break;
+            i = item_slot[slot];
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&item_empty[slot]);
+        } else {
+            i = nitem == 0 ? (int)blockIdx.x : -1;
+        }
         if (i < 0) break;
         const Item it = item_of(i);
         const int nb = it.nblk[t];
@@ -588,10 +616,13 @@ bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
 template <int D, bool BF16, int EMU>
 int run(const FwdArgs& a, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, cudaStream_t st) {
     using C = Cfg<D>;
-    auto kern = fwd_sm100_kernel<D, BF16, EMU>;
+    auto kern_p = fwd_sm100_kernel<D, BF16, EMU, true>;
+    auto kern_1 = fwd_sm100_kernel<D, BF16, EMU, false>;
     static bool attr_set = false;  // benign race: setting the same attribute twice is harmless
     if (!attr_set) {
-        if (cuda_failed(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM),
+        if (cuda_failed(cudaFuncSetAttribute(kern_p, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM),
+                        "cudaFuncSetAttribute(fwd_sm100)") ||
+            cuda_failed(cudaFuncSetAttribute(kern_1, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM),
                         "cudaFuncSetAttribute(fwd_sm100)"))
             return -1;
         attr_set = true;
@@ -618,7 +649,14 @@ int run(const FwdArgs& a, const CUtensorMap& mq, const CUtensorMap& mk, const CU
     static int n_sm = 0;
     if (n_sm == 0 && (cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n_sm <= 0))
         n_sm = 148;
-    const int grid = (int)min((int64_t)n_sm, items);  // persistent: one CTA per SM
+    // persistent for sequences of up to 32 tile pairs (8192 rows): there the start-up of each short
+    // item is worth hiding; longer ones keep the blockIdx order (see the kernel's comment)
+    p.claim = nullptr;
+    if (p.n_pairs > 32) {
+        kern_1<<<(unsigned)items, NTHREADS, C::SMEM, st>>>(mq, mk, mv, p);
+        return cuda_failed(cudaGetLastError(), "flash_attention (sm100) launch") ? -1 : 0;
+    }
+    const int grid = (int)min((int64_t)n_sm, items);  // one CTA per SM
     // the item counter: 4 bytes of the stream-ordered pool, zeroed on the stream
     retain_pool_memory(dev);
     int* claim = nullptr;
@@ -626,7 +664,7 @@ int run(const FwdArgs& a, const CUtensorMap& mq, const CUtensorMap& mk, const CU
         cuda_failed(cudaMemsetAsync(claim, 0, sizeof(int), st), "flash_attention (sm100): item counter reset"))
         return -1;
     p.claim = claim;
-    kern<<<grid, NTHREADS, C::SMEM, st>>>(mq, mk, mv, p);
+    kern_p<<<grid, NTHREADS, C::SMEM, st>>>(mq, mk, mv, p);
     const bool bad = cuda_failed(cudaGetLastError(), "flash_attention (sm100) launch");
     cudaFreeAsync(claim, st);
     return bad ? -1 : 0;
