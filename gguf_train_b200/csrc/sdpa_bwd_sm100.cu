@@ -36,6 +36,7 @@
 // the forward kernel: a timeout records a status code, drains, frees TMEM and returns.
 
 #include <cmath>
+#include <mutex>
 #include <type_traits>
 
 #include "gtb_common.cuh"
@@ -676,6 +677,18 @@ bool fast_view(const gtb_tensor4& t, int dtype) {
 
 int64_t lpad_of(int64_t L) { return (L + BT - 1) / BT * BT; }
 
+// A non-blocking stream per device for the dQ kernel (created once, kept for the process).
+cudaStream_t side_stream(int dev) {
+    static cudaStream_t streams[64] = {};
+    static std::once_flag once[64];
+    if (dev < 0 || dev >= 64) return nullptr;
+    std::call_once(once[dev], [dev] {
+        if (cudaStreamCreateWithFlags(&streams[dev], cudaStreamNonBlocking) != cudaSuccess) streams[dev] = nullptr;
+        cudaGetLastError();
+    });
+    return streams[dev];
+}
+
 template <int D, bool BF16>
 int run_bwd(const BwdArgs& a, cudaStream_t st) {
     using C = BCfg<D>;
@@ -715,13 +728,34 @@ int run_bwd(const BwdArgs& a, cudaStream_t st) {
     KvP kp{H, a.sh.Hkv, L, S, Lpad, group, n_qt, n_kvt, scale_log2, a.scale, a.causal,
            a.dk.data, a.dk.stride[0], a.dk.stride[1], a.dk.stride[2],
            a.dv.data, a.dv.stride[0], a.dv.stride[1], a.dv.stride[2], lse2, delta, status};
-    bwd_dkdv_kernel<D, BF16><<<dim3((unsigned)n_kvt, (unsigned)a.sh.Hkv, (unsigned)B), NTHREADS, SMEM_KV, st>>>(
-        mq, mk, mv, mg, kp);
-    if (cuda_failed(cudaGetLastError(), "flash_attention_backward: dK/dV launch")) return -1;
     DqP dp{H, a.sh.Hkv, L, S, Lpad, group, n_qt, n_kvt, scale_log2, a.scale, a.causal,
            a.dq.data, a.dq.stride[0], a.dq.stride[1], a.dq.stride[2], lse2, delta, status};
-    bwd_dq_kernel<D, BF16><<<dim3((unsigned)n_qt, (unsigned)H, (unsigned)B), NTHREADS, SMEM_DQ, st>>>(mq, mk, mv, mg, dp);
-    return cuda_failed(cudaGetLastError(), "flash_attention_backward: dQ launch") ? -1 : 0;
+    // dK/dV and dQ only share the preprocess output: dQ runs on a side stream, forked after the
+    // preprocess and joined before returning, so that each kernel's last partial wave of CTAs leaves
+    // no SM idle while the other still has work
+    cudaStream_t side = side_stream(dev);
+    cudaEvent_t fork = nullptr, join = nullptr;
+    const bool two = side && cudaEventCreateWithFlags(&fork, cudaEventDisableTiming) == cudaSuccess &&
+                     cudaEventCreateWithFlags(&join, cudaEventDisableTiming) == cudaSuccess &&
+                     cudaEventRecord(fork, st) == cudaSuccess && cudaStreamWaitEvent(side, fork, 0) == cudaSuccess;
+    cudaGetLastError();  // a failed fork falls back to one stream
+    cudaStream_t dq_st = two ? side : st;
+    bwd_dkdv_kernel<D, BF16><<<dim3((unsigned)n_kvt, (unsigned)a.sh.Hkv, (unsigned)B), NTHREADS, SMEM_KV, st>>>(
+        mq, mk, mv, mg, kp);
+    bool bad = cuda_failed(cudaGetLastError(), "flash_attention_backward: dK/dV launch");
+    if (!bad) {
+        bwd_dq_kernel<D, BF16><<<dim3((unsigned)n_qt, (unsigned)H, (unsigned)B), NTHREADS, SMEM_DQ, dq_st>>>(mq, mk, mv, mg, dp);
+        bad = cuda_failed(cudaGetLastError(), "flash_attention_backward: dQ launch");
+    }
+    if (two) {
+        // join even after a failed launch: later work on st (the scratch's release) must follow dQ
+        if (cuda_failed(cudaEventRecord(join, side), "flash_attention_backward: join record") ||
+            cuda_failed(cudaStreamWaitEvent(st, join, 0), "flash_attention_backward: join wait"))
+            bad = true;
+    }
+    if (fork) cudaEventDestroy(fork);
+    if (join) cudaEventDestroy(join);
+    return bad ? -1 : 0;
 }
 
 }  // namespace
