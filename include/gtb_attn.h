@@ -42,7 +42,9 @@ typedef struct gtb_tensor4 {
  *   per row (-inf for a row with no allowed key, whose output is 0): float64 for f64 inputs,
  *   float32 otherwise.
  * Kernel choice: bf16/f16 with D == Dv in {64,128}, unit inner stride and no mask runs the
- * tcgen05/TMA kernel; everything else runs the SIMT kernel (f32/f64 accumulate as the input). */
+ * tcgen05/TMA kernel; everything else runs the SIMT kernel (f32/f64 accumulate as the input).
+ * For L <= 8192 the tcgen05 kernel runs persistent CTAs that claim work from a 4-byte counter taken
+ * from the stream-ordered allocator and zeroed on the stream. */
 GTB_API int gtb_sdpa_fwd(const gtb_tensor4 *q, const gtb_tensor4 *k, const gtb_tensor4 *v,
                          const gtb_tensor4 *mask, float scale, int is_causal,
                          gtb_tensor4 *out, void *lse, void *stream);
@@ -51,7 +53,9 @@ GTB_API int gtb_sdpa_fwd(const gtb_tensor4 *q, const gtb_tensor4 *k, const gtb_t
  * Replaces FlashAttentionFn.backward (reference gguf_train/_functions.py:1934-1965), which
  * recomputes the probabilities with a chain of separate ops. dk/dv are summed over the query
  * heads of each kv head, as that function does (:1958-1962). Scratch (rowsum(dout*out) per row)
- * is taken from the stream-ordered allocator. */
+ * is taken from the stream-ordered allocator. On the tcgen05 path the dq kernel runs on an internal
+ * per-device stream, forked from and joined back into `stream` within the call, so the call's
+ * work stays ordered on `stream` (and under stream capture, in the captured graph). */
 GTB_API int gtb_sdpa_bwd(const gtb_tensor4 *dout, const gtb_tensor4 *q, const gtb_tensor4 *k,
                          const gtb_tensor4 *v, const gtb_tensor4 *mask, const gtb_tensor4 *out,
                          const void *lse, float scale, int is_causal,
