@@ -133,6 +133,49 @@ __global__ void __launch_bounds__(128) bwd_pre_kernel(PreP p) {
     }
 }
 
+// The same for 16-bit rows of D = 128 whose starts are 8-byte aligned: a warp takes 4 consecutive
+// rows (l .. l+3 of one (b, h)) and issues all 8 of a lane's 8-byte loads before reducing, so that
+// enough bytes are in flight to stream O and dO at HBM speed.
+template <typename T>
+__global__ void __launch_bounds__(128) bwd_pre128_kernel(PreP p) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t r0 = ((int64_t)blockIdx.x * 4 + warp) * 4;  // over B*H*Lpad; Lpad % 4 == 0
+    if (r0 >= p.B * p.H * p.Lpad) return;
+    const int64_t l0 = r0 % p.Lpad, bh = r0 / p.Lpad, h = bh % p.H, b = bh / p.H;
+    uint2 ov[4], gv[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+        ov[u] = make_uint2(0u, 0u);
+        gv[u] = make_uint2(0u, 0u);
+        if (l0 + u < p.L) {
+            ov[u] = *(const uint2*)((const T*)p.o + b * p.os0 + h * p.os1 + (l0 + u) * p.os2 + 4 * lane);
+            gv[u] = *(const uint2*)((const T*)p.g + b * p.gs0 + h * p.gs1 + (l0 + u) * p.gs2 + 4 * lane);
+        }
+    }
+    float acc[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+        const T* oe = (const T*)&ov[u];
+        const T* ge = (const T*)&gv[u];
+        acc[u] = 0.0f;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[u] = fmaf((float)Elem<T>::load(oe + e), (float)Elem<T>::load(ge + e), acc[u]);
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) acc[u] += __shfl_xor_sync(0xffffffffu, acc[u], off);
+    }
+    if (lane < 4) {
+        const int64_t l = l0 + lane;
+        const float a = lane == 0 ? acc[0] : lane == 1 ? acc[1] : lane == 2 ? acc[2] : acc[3];
+        float nl2 = -INFINITY;  // padding rows and rows without an allowed key: probabilities 0
+        if (l < p.L) {
+            const float lse = p.lse[bh * p.L + l];
+            if (lse != -INFINITY) nl2 = -lse * LOG2E;
+        }
+        p.lse2[r0 + lane] = nl2;
+        p.delta[r0 + lane] = l < p.L ? -a : 0.0f;
+    }
+}
+
 // ------------------------------------------------------------------ dK / dV
 
 struct KvP {
@@ -703,7 +746,12 @@ int run_bwd(const BwdArgs& a, cudaStream_t st) {
             a.dout.stride[2], (const float*)a.lse, lse2, delta, B, H, L, Lpad, a.sh.Dv};
     const int64_t rows = B * H * Lpad;
     using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
-    bwd_pre_kernel<T><<<(unsigned)((rows + 3) / 4), 128, 0, st>>>(pp);
+    // 8-byte vector loads need every row of O and dO to start on an 8-byte boundary
+    const bool vec = a.sh.Dv == 128 && (uintptr_t)a.o.data % 8 == 0 && (uintptr_t)a.dout.data % 8 == 0 &&
+                     a.o.stride[0] % 4 == 0 && a.o.stride[1] % 4 == 0 && a.o.stride[2] % 4 == 0 &&
+                     a.dout.stride[0] % 4 == 0 && a.dout.stride[1] % 4 == 0 && a.dout.stride[2] % 4 == 0;
+    if (vec) bwd_pre128_kernel<T><<<(unsigned)((rows / 4 + 3) / 4), 128, 0, st>>>(pp);
+    else bwd_pre_kernel<T><<<(unsigned)((rows + 3) / 4), 128, 0, st>>>(pp);
     if (cuda_failed(cudaGetLastError(), "flash_attention_backward: preprocess launch")) return -1;
 
     CUtensorMap mq, mk, mv, mg;
