@@ -52,6 +52,7 @@ constexpr int BT = 128;        // rows of a query tile and of a key block
 constexpr int NTHREADS = 320;  // 10 warps: TMA, MMA, two compute warpgroups
 constexpr int HB = BT / 2;     // rows of a sub-item
 constexpr int NCOMP = 256;     // compute threads (two warpgroups)
+constexpr int SB_UNITS = 4;    // (batch, head) units per superblock of the block order
 constexpr uint32_t TMEM_COLS = 512;
 constexpr float LOG2E = 1.4426950408889634f;
 
@@ -215,7 +216,22 @@ bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
     int* abort_flag = (int*)(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int jt = blockIdx.x, hk = blockIdx.y, b = blockIdx.z;
+    // Block order: superblocks of SB_UNITS (batch, kv head) units, key blocks outer (block 0, the
+    // heaviest under a causal mask, first) and the units inner. Every heavy CTA starts early, so no
+    // long CTA is still running after the rest of the grid is done, and a superblock's Q/dO streams
+    // (about 16 MB per unit at L = 8192) stay in L2 for all of its CTAs.
+    int jt, hk, b;
+    {
+        const int nunits = (int)(gridDim.y * gridDim.z);
+        const int lin = (int)(blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z));
+        const int per_sb = SB_UNITS * (int)gridDim.x;
+        const int sb = lin / per_sb, r = lin - sb * per_sb;
+        const int sbsize = min(SB_UNITS, nunits - sb * SB_UNITS);
+        jt = r / sbsize;
+        const int unit = sb * SB_UNITS + r % sbsize;
+        hk = unit % (int)gridDim.y;
+        b = unit / (int)gridDim.y;
+    }
     const int key0 = jt * BT;
     // query tiles that see this key block: rows l >= key0 when causal (top-left)
     const int i_start = p.causal ? min(p.n_qt, key0 / BT) : 0;
@@ -477,8 +493,22 @@ bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
     int* abort_flag = (int*)(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int tile = p.causal ? (p.n_qt - 1 - (int)blockIdx.x) : (int)blockIdx.x;  // heavy tiles first
-    const int h = blockIdx.y, b = blockIdx.z;
+    // Block order: superblocks of SB_UNITS (batch, head) units (the query heads of one kv head when
+    // H / Hkv = SB_UNITS), query tiles outer (the heaviest, last tile first under a causal mask) and
+    // the units inner, for the same reason as in the dK/dV kernel.
+    int tile, h, b;
+    {
+        const int nunits = (int)(gridDim.y * gridDim.z);
+        const int lin = (int)(blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z));
+        const int per_sb = SB_UNITS * (int)gridDim.x;
+        const int sb = lin / per_sb, r = lin - sb * per_sb;
+        const int sbsize = min(SB_UNITS, nunits - sb * SB_UNITS);
+        const int ti = r / sbsize;
+        const int unit = sb * SB_UNITS + r % sbsize;
+        tile = p.causal ? (p.n_qt - 1 - ti) : ti;
+        h = unit % (int)gridDim.y;
+        b = unit / (int)gridDim.y;
+    }
     const int hk = h / p.group;
     const int row0 = tile * BT;
     const int last_row = (int)min((int64_t)row0 + BT - 1, p.L - 1);
