@@ -401,149 +401,150 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
         int u = 0, nf = 0;  // blocks and items of tile t so far (barrier phases)
         bool ok = true;
         for (int nitem = 0; ok; ++nitem) {
-        int i;
-        if constexpr (PERSIST) {
-            const int slot = nitem & 1;
-            ok = warp_wait(&item_full[slot], (nitem >> 1) & 1, p.status, 34);
-            if (!ok) break;
-            i = item_slot[slot];
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&item_empty[slot]);
-        } else {
-            i = nitem == 0 ? (int)blockIdx.x : -1;
-        }
-        if (i < 0) break;
-        const Item it = item_of(i);
-        const int nb = it.nblk[t];
-        if (nb == 0) continue;
-        const int h = it.h, b = it.b;
-        const int row0t = it.row0[t];
-        const int grow = row0t + r;                   // query index
-        const int lim = p.causal ? min(lim_s, grow) : lim_s;  // last key this row may see
-        float m_used = -INFINITY, lsum = 0.0f;
-        for (int j = 0; j < nb; ++j) {
-            ok = warp_wait(&s_full[t], (u + j) & 1, p.status, 31);
-            if (!ok || __any_sync(0xffffffffu, *(volatile int*)abort_flag)) break;
-            tc_fence_after();
-            const int kv0 = j * BN;
-            const bool need_mask = (kv0 + BN > p.S) || (p.causal && kv0 + BN - 1 > row0t);
-            // pass 1: row maximum, 64 columns at a time; columns 64..127 stay in registers for pass 2
-            uint32_t ra[32], rb[32];
-            float* xa = (float*)ra;
-            float* xb = (float*)rb;
-            float pm[8];
-            tmem_ld32(s_tmem + 0, ra);
-            tmem_ld32(s_tmem + 32, rb);
-            tmem_ld_wait();
-            if (need_mask) { mask_chunk(xa, kv0, lim); mask_chunk(xb, kv0 + 32, lim); }
-#pragma unroll
-            for (int u = 0; u < 8; ++u) pm[u] = fmaxf(xa[u], xb[u]);
-#pragma unroll
-            for (int i = 8; i < 32; ++i) pm[i & 7] = fmax3(pm[i & 7], xa[i], xb[i]);
-            tmem_ld32(s_tmem + 64, ra);
-            tmem_ld32(s_tmem + 96, rb);
-            tmem_ld_wait();
-            if (need_mask) { mask_chunk(xa, kv0 + 64, lim); mask_chunk(xb, kv0 + 96, lim); }
-#pragma unroll
-            for (int i = 0; i < 32; ++i) pm[i & 7] = fmax3(pm[i & 7], xa[i], xb[i]);
-            const float mx = fmax3(fmax3(pm[0], pm[1], pm[2]), fmax3(pm[3], pm[4], pm[5]), fmaxf(pm[6], pm[7]));
-            const float m_new = fmaxf(m_used, mx * p.scale_log2);
-            const bool rescale = m_new > m_used + 8.0f;  // false while the row has no finite score
-            if (__any_sync(0xffffffffu, rescale && j > 0)) {
-                // PV_t(j-1) is complete: it was issued before S_t(j), whose completion we just saw
-                const float alpha = rescale ? ex2(m_used - m_new) : 1.0f;
-#pragma unroll
-                for (int c = 0; c < D / 32; ++c) {
-                    uint32_t ov[32];
-                    tmem_ld32(o_tmem + c * 32, ov);
-                    tmem_ld_wait();
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
-                    tmem_st32(o_tmem + c * 32, ov);
-                }
+            int i;
+            if constexpr (PERSIST) {
+                const int slot = nitem & 1;
+                ok = warp_wait(&item_full[slot], (nitem >> 1) & 1, p.status, 34);
+                if (!ok) break;
+                i = item_slot[slot];
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&item_empty[slot]);
+            } else {
+                i = nitem == 0 ? (int)blockIdx.x : -1;
             }
-            if (rescale) {
-                lsum *= ex2(m_used - m_new);
-                m_used = m_new;
-            }
-            const float neg_m = (m_used == -INFINITY) ? 0.0f : -m_used;
-            // pass 2: exponentials, 32 columns at a time, P into S's columns [64, 128); the scale-and-
-            // subtract and the row sum run as packed two-lane f32 operations
-            const uint64_t sc2 = f2_pack(p.scale_log2, p.scale_log2), nm2 = f2_pack(neg_m, neg_m);
-            uint64_t ps2[2] = {0ull, 0ull};
-            auto emit = [&](const float* x, int c) {
-                uint32_t pk[16];
-#pragma unroll
-                for (int i = 0; i < 32; i += 2) {
-                    const uint64_t a2 = f2_fma(f2_pack(x[i], x[i + 1]), sc2, nm2);
-                    uint64_t p2;
-                    if ((i & 7) < EMU) {  // this pair on the FMA pipe
-                        p2 = exp2_poly2(a2);
-                    } else {
-                        float a0, a1;
-                        f2_unpack(a2, a0, a1);
-                        p2 = f2_pack(ex2(a0), ex2(a1));
-                    }
-                    ps2[(i >> 1) & 1] = f2_add(ps2[(i >> 1) & 1], p2);
-                    float p0, p1;
-                    f2_unpack(p2, p0, p1);
-                    pk[i / 2] = pack2<BF16>(p0, p1);
-                }
-                tmem_st16(s_tmem + P_OFF + c * 16, pk);
-            };
-            // P chunk c (keys 32c..32c+31) goes to columns 64+16c. Chunks 2, 3 come from the registers
-            // first (their P lands on columns already read), then columns 0..63 are read again.
-            emit(xa, 2);
-            emit(xb, 3);
-            tmem_ld32(s_tmem + 0, ra);
-            tmem_ld32(s_tmem + 32, rb);
-            tmem_ld_wait();
-            if (need_mask) { mask_chunk(xa, kv0, lim); mask_chunk(xb, kv0 + 32, lim); }
-            emit(xa, 0);
-            emit(xb, 1);
-            {
-                float s0, s1, s2, s3;
-                f2_unpack(ps2[0], s0, s1);
-                f2_unpack(ps2[1], s2, s3);
-                lsum += (s0 + s1) + (s2 + s3);
-            }
-            tmem_st_wait();
-            tc_fence_before();
-            mbar_arrive(&p_full[t]);
-        }
-        u += nb;
-        if (!ok) break;
-        if (!*(volatile int*)abort_flag) {
-            ok = warp_wait(&o_final[t], nf & 1, p.status, 33);
-            if (ok) {
+            if (i < 0) break;
+            const Item it = item_of(i);
+            const int nb = it.nblk[t];
+            if (nb == 0) continue;
+            const int h = it.h, b = it.b;
+            const int row0t = it.row0[t];
+            const int grow = row0t + r;                   // query index
+            const int lim = p.causal ? min(lim_s, grow) : lim_s;  // last key this row may see
+            float m_used = -INFINITY, lsum = 0.0f;
+            for (int j = 0; j < nb; ++j) {
+                ok = warp_wait(&s_full[t], (u + j) & 1, p.status, 31);
+                if (!ok || __any_sync(0xffffffffu, *(volatile int*)abort_flag)) break;
                 tc_fence_after();
-                const float inv = lsum > 0.0f ? 1.0f / lsum : 0.0f;
-                T* orow = (T*)p.o + (int64_t)b * p.os0 + (int64_t)h * p.os1 + (int64_t)grow * p.os2;
+                const int kv0 = j * BN;
+                const bool need_mask = (kv0 + BN > p.S) || (p.causal && kv0 + BN - 1 > row0t);
+                // pass 1: row maximum, 64 columns at a time; columns 64..127 stay in registers for pass 2
+                uint32_t ra[32], rb[32];
+                float* xa = (float*)ra;
+                float* xb = (float*)rb;
+                float pm[8];
+                tmem_ld32(s_tmem + 0, ra);
+                tmem_ld32(s_tmem + 32, rb);
+                tmem_ld_wait();
+                if (need_mask) { mask_chunk(xa, kv0, lim); mask_chunk(xb, kv0 + 32, lim); }
 #pragma unroll
-                for (int c = 0; c < D / 32; ++c) {
-                    uint32_t ov[32];
-                    tmem_ld32(o_tmem + c * 32, ov);
-                    tmem_ld_wait();
-                    if (grow < p.L) {
-                        uint32_t w[16];
+                for (int u = 0; u < 8; ++u) pm[u] = fmaxf(xa[u], xb[u]);
 #pragma unroll
-                        for (int i = 0; i < 32; i += 2)
-                            w[i / 2] = pack2<BF16>(__uint_as_float(ov[i]) * inv, __uint_as_float(ov[i + 1]) * inv);
-                        uint4* dst = (uint4*)(orow + c * 32);
+                for (int i = 8; i < 32; ++i) pm[i & 7] = fmax3(pm[i & 7], xa[i], xb[i]);
+                tmem_ld32(s_tmem + 64, ra);
+                tmem_ld32(s_tmem + 96, rb);
+                tmem_ld_wait();
+                if (need_mask) { mask_chunk(xa, kv0 + 64, lim); mask_chunk(xb, kv0 + 96, lim); }
 #pragma unroll
-                        for (int q4 = 0; q4 < 4; ++q4) dst[q4] = make_uint4(w[4 * q4], w[4 * q4 + 1], w[4 * q4 + 2], w[4 * q4 + 3]);
+                for (int i = 0; i < 32; ++i) pm[i & 7] = fmax3(pm[i & 7], xa[i], xb[i]);
+                const float mx = fmax3(fmax3(pm[0], pm[1], pm[2]), fmax3(pm[3], pm[4], pm[5]), fmaxf(pm[6], pm[7]));
+                const float m_new = fmaxf(m_used, mx * p.scale_log2);
+                const bool rescale = m_new > m_used + 8.0f;  // false while the row has no finite score
+                if (__any_sync(0xffffffffu, rescale && j > 0)) {
+                    // PV_t(j-1) is complete: it was issued before S_t(j), whose completion we just saw
+                    const float alpha = rescale ? ex2(m_used - m_new) : 1.0f;
+#pragma unroll
+                    for (int c = 0; c < D / 32; ++c) {
+                        uint32_t ov[32];
+                        tmem_ld32(o_tmem + c * 32, ov);
+                        tmem_ld_wait();
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
+                        tmem_st32(o_tmem + c * 32, ov);
                     }
                 }
-                if (p.lse && grow < p.L)
-                    p.lse[((int64_t)b * p.H + h) * p.L + grow] =
-                        lsum > 0.0f ? (m_used + log2f(lsum)) * 0.69314718055994531f : -INFINITY;
+                if (rescale) {
+                    lsum *= ex2(m_used - m_new);
+                    m_used = m_new;
+                }
+                const float neg_m = (m_used == -INFINITY) ? 0.0f : -m_used;
+                // pass 2: exponentials, 32 columns at a time, P into S's columns [64, 128); the scale-and-
+                // subtract and the row sum run as packed two-lane f32 operations
+                const uint64_t sc2 = f2_pack(p.scale_log2, p.scale_log2), nm2 = f2_pack(neg_m, neg_m);
+                uint64_t ps2[2] = {0ull, 0ull};
+                auto emit = [&](const float* x, int c) {
+                    uint32_t pk[16];
+#pragma unroll
+                    for (int i = 0; i < 32; i += 2) {
+                        const uint64_t a2 = f2_fma(f2_pack(x[i], x[i + 1]), sc2, nm2);
+                        uint64_t p2;
+                        if ((i & 7) < EMU) {  // this pair on the FMA pipe
+                            p2 = exp2_poly2(a2);
+                        } else {
+                            float a0, a1;
+                            f2_unpack(a2, a0, a1);
+                            p2 = f2_pack(ex2(a0), ex2(a1));
+                        }
+                        ps2[(i >> 1) & 1] = f2_add(ps2[(i >> 1) & 1], p2);
+                        float p0, p1;
+                        f2_unpack(p2, p0, p1);
+                        pk[i / 2] = pack2<BF16>(p0, p1);
+                    }
+                    tmem_st16(s_tmem + P_OFF + c * 16, pk);
+                };
+                // P chunk c (keys 32c..32c+31) goes to columns 64+16c. Chunks 2, 3 come from the registers
+                // first (their P lands on columns already read), then columns 0..63 are read again.
+                emit(xa, 2);
+                emit(xb, 3);
+                tmem_ld32(s_tmem + 0, ra);
+                tmem_ld32(s_tmem + 32, rb);
+                tmem_ld_wait();
+                if (need_mask) { mask_chunk(xa, kv0, lim); mask_chunk(xb, kv0 + 32, lim); }
+                emit(xa, 0);
+                emit(xb, 1);
+                {
+                    float s0, s1, s2, s3;
+                    f2_unpack(ps2[0], s0, s1);
+                    f2_unpack(ps2[1], s2, s3);
+                    lsum += (s0 + s1) + (s2 + s3);
+                }
+                tmem_st_wait();
                 tc_fence_before();
-                mbar_arrive(&o_empty[t]);  // O_t has been read: the next item's PV may overwrite it
-                ++nf;
+                mbar_arrive(&p_full[t]);
             }
-        } else {
-            ok = false;
-        }
+            u += nb;
+            if (!ok) break;
+            if (!*(volatile int*)abort_flag) {
+                ok = warp_wait(&o_final[t], nf & 1, p.status, 33);
+                if (ok) {
+                    tc_fence_after();
+                    const float inv = lsum > 0.0f ? 1.0f / lsum : 0.0f;
+                    T* orow = (T*)p.o + (int64_t)b * p.os0 + (int64_t)h * p.os1 + (int64_t)grow * p.os2;
+#pragma unroll
+                    for (int c = 0; c < D / 32; ++c) {
+                        uint32_t ov[32];
+                        tmem_ld32(o_tmem + c * 32, ov);
+                        tmem_ld_wait();
+                        if (grow < p.L) {
+                            uint32_t w[16];
+#pragma unroll
+                            for (int i = 0; i < 32; i += 2)
+                                w[i / 2] = pack2<BF16>(__uint_as_float(ov[i]) * inv, __uint_as_float(ov[i + 1]) * inv);
+                            uint4* dst = (uint4*)(orow + c * 32);
+#pragma unroll
+                            for (int q4 = 0; q4 < 4; ++q4)
+                                dst[q4] = make_uint4(w[4 * q4], w[4 * q4 + 1], w[4 * q4 + 2], w[4 * q4 + 3]);
+                        }
+                    }
+                    if (p.lse && grow < p.L)
+                        p.lse[((int64_t)b * p.H + h) * p.L + grow] =
+                            lsum > 0.0f ? (m_used + log2f(lsum)) * 0.69314718055994531f : -INFINITY;
+                    tc_fence_before();
+                    mbar_arrive(&o_empty[t]);  // O_t has been read: the next item's PV may overwrite it
+                    ++nf;
+                }
+            } else {
+                ok = false;
+            }
         }
         if (!ok) *(volatile int*)abort_flag = 1;
     }
