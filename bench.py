@@ -242,7 +242,9 @@ def run_decode(args, rank: int, world: int, dev, max_over_ranks=lambda x: x) -> 
         "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": gbs / peaks["hbm_gbs"], "traffic": profile_traffic("decode_q8_0_config5a"),
                      "peak_source": peaks["source"] + " HBM copy"},
-        "gpu_launches": 3 * args.steps,  # plan, decode, combine
+        # per step: decode_mma_kernel and the split-KV combine (after a 4-byte memset of the claim
+        # counter); above 256 sequences a plan kernel runs first
+        "gpu_launches": (2 if B <= 256 else 3) * args.steps,
         "clocks": sampler.summary(), "status": _C.device_status(),
     }
     del kq, vq, flush
