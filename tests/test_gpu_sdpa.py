@@ -243,3 +243,61 @@ def test_backward_sampled_group_at_larger_size():
     assert_close(tk.grad[b:b + 1, hk:hk + 1], dk, 2e-2, 1e-2, "dk sampled group")
     assert_close(tv.grad[b:b + 1, hk:hk + 1], dv, 2e-2, 1e-2, "dv sampled group")
     del torch
+
+
+def test_forward_persistent_ctas_over_many_items():
+    """Causal GQA bf16 forward with more work items (pairs of 128-row query tiles x heads x batch) than
+    SMs, so that each persistent CTA of the tcgen05 kernel runs several items in a row and its K/V
+    ring, barrier phases and TMEM carry over between them: B=4, H=16, Hkv=4, L=S=2048 is 512 items
+    for 148 CTAs. Three (batch, head) slices checked against the oracle at full length, the lse too."""
+    import torch
+
+    import gguf_train_b200 as gtb
+    from gguf_train_b200 import _C
+    from gguf_train_b200 import functional as Fn
+
+    O.manual_seed(21)
+    B, H, Hkv, L, D = 4, 16, 4, 2048, 128
+    q = seeded((B, H, L, D), "bf16", 0.5)
+    k = seeded((B, Hkv, L, D), "bf16", 0.5)
+    v = seeded((B, Hkv, L, D), "bf16", 0.5)
+    tq, tk, tv = (to_dev(x, "bf16") for x in (q, k, v))
+    out, lse = Fn.sdpa_forward(tq, tk, tv, None, D ** -0.5, True, need_lse=True)
+    torch.cuda.synchronize()
+    assert _C.device_status() == 0
+    G = H // Hkv
+    for b, h in ((0, 0), (2, 6), (3, 15)):
+        hk = h // G
+        want = O.sdpa_fwd(q[b:b + 1, h:h + 1], k[b:b + 1, hk:hk + 1], v[b:b + 1, hk:hk + 1], is_causal=True)
+        assert_close(out[b:b + 1, h:h + 1], want, *TOL["bf16"], f"out (b={b}, h={h})")
+        # lse = log sum_k exp(scale * q.k) over the allowed keys, from a float64 restatement
+        qf, kf = q[b, h].astype(np.float64), k[b, hk].astype(np.float64)
+        rows = np.array([0, 1, 777, L - 1])
+        s = (qf[rows] @ kf.T) * float(np.float32(D ** -0.5))
+        s[np.arange(L)[None, :] > rows[:, None]] = -np.inf
+        mx = s.max(axis=1, keepdims=True)
+        want_lse = (mx + np.log(np.exp(s - mx).sum(axis=1, keepdims=True)))[:, 0]
+        assert_close(lse[b, h, rows], want_lse, 1e-3, 1e-4, f"lse (b={b}, h={h})")
+
+
+def test_forward_just_past_the_persistent_limit():
+    """L = S = 8448 (33 tile pairs) is one CTA per item in blockIdx order, the mode used for
+    sequences longer than 8192 rows; the last 256 query rows of one head checked against the
+    oracle's row-range forward (causal masking uses absolute rows)."""
+    import torch
+
+    import gguf_train_b200 as gtb
+    from gguf_train_b200 import _C
+
+    O.manual_seed(22)
+    B, H, Hkv, L, D = 1, 4, 2, 8448, 128
+    q = seeded((B, H, L, D), "bf16", 0.5)
+    k = seeded((B, Hkv, L, D), "bf16", 0.5)
+    v = seeded((B, Hkv, L, D), "bf16", 0.5)
+    out = gtb.scaled_dot_product_attention(*(to_dev(x, "bf16") for x in (q, k, v)), is_causal=True)
+    torch.cuda.synchronize()
+    assert _C.device_status() == 0
+    h, hk, off = 3, 1, L - 256
+    want = O.sdpa_fwd_reforder(q[:, h:h + 1, off:], k[:, hk:hk + 1], v[:, hk:hk + 1], float(np.float32(D ** -0.5)),
+                               True, 0, off)
+    assert_close(out[:, h:h + 1, off:], want, *TOL["bf16"], "out, last 256 rows of head 3")
