@@ -2,7 +2,7 @@
 //
 // The reference's backward (FlashAttentionFn.backward, gguf_train/_functions.py:1934-1965) recomputes
 // the probabilities with separate matmul / softmax / elementwise ops and materialises several
-// (B, H, L, S) tensors. Here it is three kernels that never hold more than 128x128 tiles:
+// (B, H, L, S) tensors. Here it is a few kernels that never hold more than 128x128 tiles:
 //
 //   preprocess  per query row: -delta = -sum(dO * O), -lse2 = -lse * log2(e) (-inf for rows that are
 //               padding or had no allowed key, so their probabilities come out 0); both stored negated
@@ -14,17 +14,25 @@
 //               per sub-item h, in TMEM (lane = key):
 //                 S^T = K Q_h^T, dP^T = V dO_h^T                  (M=128 keys, N=64 queries, K=D)
 //                 P^T = exp2(S^T * scale*log2e - lse2), dS^T = P^T * (dP^T - delta)
-//                 dV += P^T dO_h, dK += dS^T Q_h                   (M=128, N=D, K=64; A from TMEM)
-//   dQ          one CTA per 128-row query tile; it loops over the 128-key blocks the tile attends,
-//               each two sub-items of 64 keys:
+//                 dV += P^T dO_h, dK += dS^T Q_h                   (M=128, N=D, K=64; P^T from TMEM)
+//               With D = 128 the same CTA also forms the sub-item's share of dQ (fused dQ):
+//                 dQ_h^T = K^T dS^T                                (M=128 head dims, N=64, K=128 keys)
+//               with dS^T written to shared memory (the B operand here and the A operand of dK) and
+//               dQ_h^T accumulated into the dP^T columns it no longer needs; the compute warps add it
+//               to f32 sums (B, H, Lpad, D) in global memory with reductions performed at L2, and a
+//               conversion kernel writes dq = scale * sums. Five GEMM-shaped products per tile
+//               instead of seven; the bits of dq may vary in the last place from run to run.
+//   dQ          (D = 64, or GTB_BWD_SPLIT_DQ=1) one CTA per 128-row query tile; it loops over the
+//               128-key blocks the tile attends, each two sub-items of 64 keys:
 //                 S = Q K_h^T, dP = dO V_h^T, dS = P * (dP - delta), dQ += dS K_h  (A from TMEM)
 // TMEM columns: dK/dV kernel: dV [0,D), dK [128,128+D), S^T of sub-item h [256+64h, 320+64h),
-//               dP^T of sub-item h [384+64h, 448+64h); dQ kernel: S_h [64h, 64h+64),
+//               dP^T (then dQ_h^T) of sub-item h [384+64h, 448+64h); dQ kernel: S_h [64h, 64h+64),
 //               dP_h [128+64h, 192+64h), dQ [256,256+D), and the tile's Q [384, 384+D/2) and
 //               dO [448, 448+D/2) (16-bit pairs), the A operands of S and dP (TS-form MMAs: Q and
 //               dO are the same for every key block, so they are read from TMEM, not shared memory).
 // P^T / dS^T / dS (bf16 or f16, packed two per column) are written back over the first 32 of the
-// S / dP columns of their sub-item: chunk c (32 columns) lands in columns 16c..16c+15, read before.
+// S / dP columns of their sub-item: chunk c (32 columns) lands in columns 16c..16c+15, read before
+// (dS^T goes to shared memory instead when dQ is fused).
 //
 // Warps (both main kernels): 0 = TMA producer, 1 = TMEM owner and MMA issuer (one thread), 2-9 =
 // two compute warpgroups, one key (dK/dV) or query (dQ) row per thread: warpgroup h computes
@@ -190,20 +198,45 @@ struct KvP {
     int64_t vs0, vs1, vs2;
     const float* lse2;
     const float* delta;
+    float* dqacc;  // (B, H, Lpad, D) f32, zeroed: unscaled dQ sums (fused dQ only)
     int* status;
 };
 
-template <int D, bool BF16>
+// Shared memory of the dK/dV kernel: K, V, two stages of (Q, dO, lse2, delta), with the fused dQ
+// two 16 KB dS^T tiles, then the barrier block. The fused layout uses all 227 KB a block may have,
+// so its base may sit at most SMEM_SLACK bytes past the start of dynamic shared memory.
+template <int D, bool FUSE>
+struct KvSmem {
+    static constexpr int ST_BYTES = 2 * BCfg<D>::TILE + 1024;  // Q, dO, lse2[128], delta[128]
+    static constexpr int OFF_ST = 2 * BCfg<D>::TILE;
+    static constexpr int OFF_DS = OFF_ST + 2 * ST_BYTES;       // dS^T of sub-item h: 128 keys x 64 queries
+    static constexpr int DS_BYTES = BT * HB * 2;
+    static constexpr int OFF_BAR = OFF_DS + (FUSE ? 2 * DS_BYTES : 0);
+    static constexpr int USED = OFF_BAR + 32 * 8;              // + barriers, TMEM slot, flag
+    static constexpr int ALLOC = FUSE ? 232448 : USED + 1024;  // 232448 = 227 KB, the per-block maximum
+    static constexpr int SLACK = ALLOC - USED;
+};
+
+template <int D, bool BF16, bool FUSE>
 __global__ void __launch_bounds__(NTHREADS, 1)
 bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                 const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmG, const KvP p) {
+    static_assert(!FUSE || D == 128, "the fused dQ needs M = D = 128");
     using C = BCfg<D>;
+    using M = KvSmem<D, FUSE>;
     using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
-    constexpr int OFF_K = 0, OFF_V = C::TILE, OFF_ST = 2 * C::TILE;
-    constexpr int ST_BYTES = 2 * C::TILE + 1024;  // Q, dO, lse2[128], delta[128]
-    constexpr int OFF_BAR = OFF_ST + 2 * ST_BYTES;
+    constexpr int OFF_K = 0, OFF_V = C::TILE, OFF_ST = M::OFF_ST;
+    constexpr int ST_BYTES = M::ST_BYTES;
+    constexpr int OFF_BAR = M::OFF_BAR;
     extern __shared__ unsigned char smem_raw[];
     unsigned char* smem = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    if constexpr (M::SLACK < 1023) {
+        // the tiles need 1024-byte alignment and the fused layout leaves less slack than that
+        if ((uintptr_t)(smem - smem_raw) > (uintptr_t)M::SLACK) {
+            if (threadIdx.x == 0) atomicCAS(p.status, 0, 40);
+            return;
+        }
+    }
     uint64_t* bars = (uint64_t*)(smem + OFF_BAR);
     uint64_t* kv_full = bars;
     uint64_t* st_full = bars + 1;     // [2]
@@ -212,7 +245,9 @@ bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
     uint64_t* p_full = bars + 7;      // [2] P^T, dS^T of sub-item h written (128 arrivals)
     uint64_t* acc_final = bars + 9;   // every MMA done
     uint64_t* drain = bars + 10;
-    uint32_t* tmem_slot = (uint32_t*)(bars + 11);
+    uint64_t* dq_full = bars + 11;    // [2] dQ^T of sub-item h computed (fused dQ)
+    uint64_t* dq_empty = bars + 13;   // [2] dQ^T of sub-item h read out of TMEM (128 arrivals)
+    uint32_t* tmem_slot = (uint32_t*)(bars + 15);
     int* abort_flag = (int*)(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -241,7 +276,10 @@ bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
     if (threadIdx.x == 0) {
         mbar_init(kv_full, 1);
         for (int i = 0; i < 2; ++i) { mbar_init(&st_full[i], 1); mbar_init(&st_empty[i], 1); }
-        for (int h = 0; h < 2; ++h) { mbar_init(&s_full[h], 1); mbar_init(&p_full[h], 128); }
+        for (int h = 0; h < 2; ++h) {
+            mbar_init(&s_full[h], 1); mbar_init(&p_full[h], 128);
+            mbar_init(&dq_full[h], 1); mbar_init(&dq_empty[h], 128);
+        }
         mbar_init(acc_final, 1);
         mbar_init(drain, 1);
         *abort_flag = 0;
@@ -297,14 +335,18 @@ bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
             const uint64_t qk1 = kmajor(smem_u32(smem + OFF_ST + ST_BYTES), 0, C::SLAB);
             const uint64_t qm0 = mnmajor(smem_u32(smem + OFF_ST), 0, C::SLAB);
             const uint64_t qm1 = mnmajor(smem_u32(smem + OFF_ST + ST_BYTES), 0, C::SLAB);
-            // S^T, dP^T of sub-item h (queries 64h.. of the stage's tile: 64 rows = 8 KB into each slab)
-            auto issue_sdp = [&](int st, int h) {
+            // S^T of sub-item h (queries 64h.. of the stage's tile: 64 rows = 8 KB into each slab)
+            auto issue_s = [&](int st, int h) {
                 const uint64_t qk = st ? qk1 : qk0;
 #pragma unroll
                 for (int kk = 0; kk < D / 16; ++kk) {
                     const uint32_t off = (uint32_t)((kk / 4) * C::SLAB + (kk % 4) * 32);
                     mma_ss(tmem + 256 + HB * h, desc_advance(kdk, off), desc_advance(qk, off + h * HB * 128), IDESC_S, kk > 0);
                 }
+            };
+            // dP^T of sub-item h; the commit covers S^T as well
+            auto issue_dp = [&](int st, int h) {
+                const uint64_t qk = st ? qk1 : qk0;
 #pragma unroll
                 for (int kk = 0; kk < D / 16; ++kk) {
                     const uint32_t off = (uint32_t)((kk / 4) * C::SLAB + (kk % 4) * 32);
@@ -313,6 +355,12 @@ bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
                 }
                 mma_commit(&s_full[h]);
             };
+            auto issue_sdp = [&](int st, int h) {
+                issue_s(st, h);
+                issue_dp(st, h);
+            };
+            // dS^T of sub-item h in shared memory (fused dQ): rows = keys, 64 queries per 128-byte row
+            const uint32_t ds0 = smem_u32(smem + M::OFF_DS), ds1 = ds0 + M::DS_BYTES;
             // dV += P^T dO_h, dK += dS^T Q_h (k-steps over the sub-item's 64 queries)
             auto issue_grad = [&](int st, int h, bool first) {
                 const uint64_t qm = st ? qm1 : qm0;
@@ -321,8 +369,23 @@ bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
                     const uint32_t acc = (!first || kk > 0) ? 1u : 0u;
                     const uint32_t rows = (uint32_t)((h * (HB / 16) + kk) * 2048);
                     mma_ts(tmem + 0, tmem + 256 + HB * h + kk * 8, desc_advance(qm, rows + C::TILE), IDESC_ACC, acc);  // dV
-                    mma_ts(tmem + 128, tmem + 384 + HB * h + kk * 8, desc_advance(qm, rows), IDESC_ACC, acc);          // dK
+                    if constexpr (FUSE)  // A = dS^T from shared memory (K-major)
+                        mma_ss(tmem + 128, kmajor(h ? ds1 : ds0, kk, 0), desc_advance(qm, rows), IDESC_ACC, acc);  // dK
+                    else
+                        mma_ts(tmem + 128, tmem + 384 + HB * h + kk * 8, desc_advance(qm, rows), IDESC_ACC, acc);  // dK
                 }
+            };
+            // dQ^T_h = K^T dS^T_h (M = 128 head dims, N = 64 queries, K = 128 keys; both operands
+            // MN-major) into the columns of dP^T_h, which the compute warps have read by now
+            auto issue_dq = [&](int h) {
+                constexpr uint32_t IDESC_DQ = idesc_f16_amn(BT, HB, BF16, true);
+                const uint64_t km = mnmajor(smem_u32(smem + OFF_K), 0, C::SLAB);
+                const uint64_t dm = desc_sw128(h ? ds1 : ds0, 8192, 1024);  // one 64-query atom: LBO unused
+#pragma unroll
+                for (int kk = 0; kk < BT / 16; ++kk)
+                    mma_ss(tmem + 384 + HB * h, desc_advance(km, (uint32_t)(kk * 2048)), desc_advance(dm, (uint32_t)(kk * 2048)),
+                           IDESC_DQ, kk > 0);
+                mma_commit(&dq_full[h]);
             };
             bool ok = mbar_wait(kv_full, 0, p.status, 42);
             if (ok) ok = mbar_wait(&st_full[0], 0, p.status, 43);
@@ -340,18 +403,39 @@ bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
                 if (!ok) break;
                 tc_fence_after();
                 issue_grad(st, 0, it == 0);
+                if constexpr (FUSE) issue_dq(0);
                 if (more) {  // sub-item 0 of the next tile, into the columns just read
                     ok = mbar_wait(&st_full[st ^ 1], ((it + 1) >> 1) & 1, p.status, 43);
                     if (!ok || *(volatile int*)abort_flag) { ok = false; break; }
                     tc_fence_after();
-                    issue_sdp(st ^ 1, 0);
+                    if constexpr (FUSE) {
+                        // dP^T waits for dQ^T_0 to leave its columns; S^T keeps the tensor core busy meanwhile
+                        issue_s(st ^ 1, 0);
+                        ok = mbar_wait(&dq_empty[0], it & 1, p.status, 49);
+                        if (!ok) break;
+                        tc_fence_after();
+                        issue_dp(st ^ 1, 0);
+                    } else {
+                        issue_sdp(st ^ 1, 0);
+                    }
                 }
                 ok = mbar_wait(&p_full[1], it & 1, p.status, 44);
                 if (!ok) break;
                 tc_fence_after();
                 issue_grad(st, 1, false);
+                if constexpr (FUSE) issue_dq(1);
                 mma_commit(&st_empty[st]);  // this tile's Q / dO are read by every MMA issued so far
-                if (more) issue_sdp(st ^ 1, 1);
+                if (more) {
+                    if constexpr (FUSE) {
+                        issue_s(st ^ 1, 1);
+                        ok = mbar_wait(&dq_empty[1], it & 1, p.status, 49);
+                        if (!ok) break;
+                        tc_fence_after();
+                        issue_dp(st ^ 1, 1);
+                    } else {
+                        issue_sdp(st ^ 1, 1);
+                    }
+                }
             }
             if (!ok) *(volatile int*)abort_flag = 1;
             if (ok && !*(volatile int*)abort_flag) {
@@ -367,6 +451,7 @@ bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
         const int r = quad * 32 + lane;
         const int key = key0 + r;
         const uint32_t lane_addr = (uint32_t)(quad * 32) << 16;
+        unsigned char* const ds_row = smem + M::OFF_DS + wg * M::DS_BYTES + r * 128;
         bool ok = true;
         for (int it = 0; it < nit; ++it) {
             const int st = it & 1;
@@ -406,14 +491,42 @@ bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
                         dk[i / 2] = pack2<BF16>(d0, d1);
                     }
                     tmem_st16(tmem + lane_addr + 256 + HB * wg + c * 16, pk);
-                    tmem_st16(tmem + lane_addr + 384 + HB * wg + c * 16, dk);
+                    if constexpr (FUSE) {
+                        // row r of the 128-byte-swizzled dS^T tile: 16-byte chunk j sits at j ^ (r & 7)
+                        unsigned char* row = ds_row;
+#pragma unroll
+                        for (int j = 0; j < 4; ++j)
+                            *(uint4*)(row + (((4 * c + j) ^ (r & 7)) << 4)) =
+                                make_uint4(dk[4 * j], dk[4 * j + 1], dk[4 * j + 2], dk[4 * j + 3]);
+                    } else {
+                        tmem_st16(tmem + lane_addr + 384 + HB * wg + c * 16, dk);
+                    }
                 }
             };
             if (p.causal && (q0 < key0 + BT - 1)) chunks(std::true_type{});
             else chunks(std::false_type{});
             tmem_st_wait();
+            if constexpr (FUSE) fence_proxy_async_smem();  // dS^T is read by the tensor core
             tc_fence_before();
             mbar_arrive(&p_full[wg]);
+            if constexpr (FUSE) {
+                // dQ^T of the sub-item (lane = head dim r, column = query): read it out of TMEM, free the
+                // columns for the next dP^T, and add it to the f32 sums in global memory (each warp's
+                // reduction covers 32 consecutive head dims of one query row: 128 contiguous bytes)
+                ok = warp_wait(&dq_full[wg], it & 1, p.status, 48);
+                if (!ok) break;
+                tc_fence_after();
+                uint32_t v[64];
+                tmem_ld32(tmem + lane_addr + 384 + HB * wg, v);
+                tmem_ld32(tmem + lane_addr + 384 + HB * wg + 32, v + 32);
+                tmem_ld_wait();
+                tc_fence_before();
+                mbar_arrive(&dq_empty[wg]);
+                const int hq = hk * p.group + it / nq;
+                float* dst = p.dqacc + (((int64_t)b * p.H + hq) * p.Lpad + q0) * D + r;
+#pragma unroll
+                for (int q = 0; q < HB; ++q) red_add_f32(dst + (int64_t)q * D, __uint_as_float(v[q]));
+            }
         }
         if (!ok) *(volatile int*)abort_flag = 1;
         if (nit > 0 && ok && !*(volatile int*)abort_flag) {
@@ -737,6 +850,28 @@ bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
     }
 }
 
+// ------------------------------------------------------------------ dQ from the fused sums
+
+// dq[b, h, l, :] = scale * dqacc[b, h, l, :] in the 16-bit type; 16 threads per row of D = 128,
+// each converting 8 values (two 16-byte loads, one 16-byte store)
+template <typename T>
+__global__ void __launch_bounds__(256) bwd_dq_convert_kernel(const float* __restrict__ acc, T* __restrict__ dq, int64_t s0,
+                                                             int64_t s1, int64_t s2, int64_t H, int64_t L, int64_t Lpad,
+                                                             int64_t n, float scale) {
+    const int64_t idx = (int64_t)blockIdx.x * 256 + threadIdx.x;  // over B*H*L*16
+    if (idx >= n) return;
+    const int seg = (int)(idx & 15);
+    const int64_t row = idx >> 4, l = row % L, bh = row / L, h = bh % H, b = bh / H;
+    const float4* src = (const float4*)(acc + ((bh * Lpad + l) * 128 + seg * 8));
+    const float4 x = src[0], y = src[1];
+    uint32_t w[4];
+    w[0] = pack2<std::is_same<T, __nv_bfloat16>::value>(x.x * scale, x.y * scale);
+    w[1] = pack2<std::is_same<T, __nv_bfloat16>::value>(x.z * scale, x.w * scale);
+    w[2] = pack2<std::is_same<T, __nv_bfloat16>::value>(y.x * scale, y.y * scale);
+    w[3] = pack2<std::is_same<T, __nv_bfloat16>::value>(y.z * scale, y.w * scale);
+    *(uint4*)(dq + b * s0 + h * s1 + l * s2 + seg * 8) = make_uint4(w[0], w[1], w[2], w[3]);
+}
+
 // ------------------------------------------------------------------ host side
 
 bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
@@ -750,6 +885,17 @@ bool fast_view(const gtb_tensor4& t, int dtype) {
 
 int64_t lpad_of(int64_t L) { return (L + BT - 1) / BT * BT; }
 
+// dQ summed inside the dK/dV kernel (D = 128): f32 reductions in global memory, so the bits of dQ
+// may differ from run to run in the last place. GTB_BWD_SPLIT_DQ=1 selects the separate dQ kernel
+// instead (recomputes S and dP per query tile; deterministic).
+bool fused_dq(const BwdArgs& a) {
+    static const bool split = [] {
+        const char* e = getenv("GTB_BWD_SPLIT_DQ");
+        return e && e[0] == '1';
+    }();
+    return a.sh.D == 128 && !split;
+}
+
 // A non-blocking stream per device for the dQ kernel (created once, kept for the process).
 cudaStream_t side_stream(int dev) {
     static cudaStream_t streams[64] = {};
@@ -762,7 +908,7 @@ cudaStream_t side_stream(int dev) {
     return streams[dev];
 }
 
-template <int D, bool BF16>
+template <int D, bool BF16, bool FUSE>
 int run_bwd(const BwdArgs& a, cudaStream_t st) {
     using C = BCfg<D>;
     const int64_t B = a.sh.B, H = a.sh.H, L = a.sh.L, S = a.sh.S, Lpad = lpad_of(L);
@@ -793,19 +939,32 @@ int run_bwd(const BwdArgs& a, cudaStream_t st) {
     const float scale_log2 = a.scale * LOG2E;
 
     static bool attr_set = false;
-    constexpr int SMEM_KV = 2 * C::TILE + 2 * (2 * C::TILE + 1024) + 32 * 8 + 1024;  // + barriers, TMEM slot, flag
+    constexpr int SMEM_KV = KvSmem<D, FUSE>::ALLOC;
     constexpr int SMEM_DQ = 6 * C::TILE + 32 * 8 + 1024;  // + barriers, TMEM slot, flag
     if (!attr_set) {
-        if (cuda_failed(cudaFuncSetAttribute(bwd_dkdv_kernel<D, BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        if (cuda_failed(cudaFuncSetAttribute(bwd_dkdv_kernel<D, BF16, FUSE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              SMEM_KV), "cudaFuncSetAttribute(bwd dkdv)") ||
-            cuda_failed(cudaFuncSetAttribute(bwd_dq_kernel<D, BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             SMEM_DQ), "cudaFuncSetAttribute(bwd dq)"))
+            (!FUSE && cuda_failed(cudaFuncSetAttribute(bwd_dq_kernel<D, BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                       SMEM_DQ), "cudaFuncSetAttribute(bwd dq)")))
             return -1;
         attr_set = true;
     }
+    float* dqacc = FUSE ? delta + B * H * Lpad : nullptr;
     KvP kp{H, a.sh.Hkv, L, S, Lpad, group, n_qt, n_kvt, scale_log2, a.scale, a.causal,
            a.dk.data, a.dk.stride[0], a.dk.stride[1], a.dk.stride[2],
-           a.dv.data, a.dv.stride[0], a.dv.stride[1], a.dv.stride[2], lse2, delta, status};
+           a.dv.data, a.dv.stride[0], a.dv.stride[1], a.dv.stride[2], lse2, delta, dqacc, status};
+    if constexpr (FUSE) {
+        if (cuda_failed(cudaMemsetAsync(dqacc, 0, sizeof(float) * (size_t)(B * H * Lpad * D), st),
+                        "flash_attention_backward: dQ sums reset"))
+            return -1;
+        bwd_dkdv_kernel<D, BF16, true><<<dim3((unsigned)n_kvt, (unsigned)a.sh.Hkv, (unsigned)B), NTHREADS, SMEM_KV, st>>>(
+            mq, mk, mv, mg, kp);
+        if (cuda_failed(cudaGetLastError(), "flash_attention_backward: dK/dV/dQ launch")) return -1;
+        const int64_t n = B * H * L * 16;
+        bwd_dq_convert_kernel<T><<<(unsigned)((n + 255) / 256), 256, 0, st>>>(dqacc, (T*)a.dq.data, a.dq.stride[0],
+                                                                          a.dq.stride[1], a.dq.stride[2], H, L, Lpad, n, a.scale);
+        return cuda_failed(cudaGetLastError(), "flash_attention_backward: dQ conversion launch") ? -1 : 0;
+    }
     DqP dp{H, a.sh.Hkv, L, S, Lpad, group, n_qt, n_kvt, scale_log2, a.scale, a.causal,
            a.dq.data, a.dq.stride[0], a.dq.stride[1], a.dq.stride[2], lse2, delta, status};
     // dK/dV and dQ only share the preprocess output: dQ runs on a side stream, forked after the
@@ -818,7 +977,7 @@ int run_bwd(const BwdArgs& a, cudaStream_t st) {
                      cudaEventRecord(fork, st) == cudaSuccess && cudaStreamWaitEvent(side, fork, 0) == cudaSuccess;
     cudaGetLastError();  // a failed fork falls back to one stream
     cudaStream_t dq_st = two ? side : st;
-    bwd_dkdv_kernel<D, BF16><<<dim3((unsigned)n_kvt, (unsigned)a.sh.Hkv, (unsigned)B), NTHREADS, SMEM_KV, st>>>(
+    bwd_dkdv_kernel<D, BF16, false><<<dim3((unsigned)n_kvt, (unsigned)a.sh.Hkv, (unsigned)B), NTHREADS, SMEM_KV, st>>>(
         mq, mk, mv, mg, kp);
     bool bad = cuda_failed(cudaGetLastError(), "flash_attention_backward: dK/dV launch");
     if (!bad) {
@@ -852,13 +1011,17 @@ bool bwd_sm100_supported(const BwdArgs& a) {
 }
 
 size_t bwd_sm100_scratch_bytes(const BwdArgs& a) {
-    return 2 * sizeof(float) * (size_t)(a.sh.B * a.sh.H * lpad_of(a.sh.L));
+    const size_t rows = (size_t)(a.sh.B * a.sh.H * lpad_of(a.sh.L));
+    return sizeof(float) * rows * (2 + (fused_dq(a) ? (size_t)a.sh.D : 0));  // lse2, delta (+ dQ sums)
 }
 
 int launch_bwd_sm100(const BwdArgs& a, cudaStream_t st) {
     const bool bf16 = a.q.dtype == BF16;
-    if (a.sh.D == 128) return bf16 ? run_bwd<128, true>(a, st) : run_bwd<128, false>(a, st);
-    return bf16 ? run_bwd<64, true>(a, st) : run_bwd<64, false>(a, st);
+    if (a.sh.D == 128) {
+        if (fused_dq(a)) return bf16 ? run_bwd<128, true, true>(a, st) : run_bwd<128, false, true>(a, st);
+        return bf16 ? run_bwd<128, true, false>(a, st) : run_bwd<128, false, false>(a, st);
+    }
+    return bf16 ? run_bwd<64, true, false>(a, st) : run_bwd<64, false, false>(a, st);
 }
 
 }  // namespace gtb

@@ -101,6 +101,11 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+// fire-and-forget f32 addition in global memory (performed at L2; no value returned)
+__device__ __forceinline__ void red_add_f32(float* addr, float v) {
+    asm volatile("red.relaxed.gpu.global.add.f32 [%0], %1;" ::"l"(addr), "f"(v) : "memory");
+}
+
 // ------------------------------------------------------------------ tcgen05
 
 __device__ __forceinline__ void tmem_alloc(uint32_t* slot, uint32_t ncols) {  // whole warp
