@@ -301,3 +301,65 @@ def test_forward_just_past_the_persistent_limit():
     want = O.sdpa_fwd_reforder(q[:, h:h + 1, off:], k[:, hk:hk + 1], v[:, hk:hk + 1], float(np.float32(D ** -0.5)),
                                True, 0, off)
     assert_close(out[:, h:h + 1, off:], want, *TOL["bf16"], "out, last 256 rows of head 3")
+
+
+_SPLIT_SCRIPT = r"""
+import sys
+import numpy as np
+sys.path.insert(0, {root!r})
+from oracle import oracle as O
+from tests._util import seeded, to_dev
+import gguf_train_b200 as gtb
+from gguf_train_b200 import _C
+O.manual_seed(4242)
+B, H, Hkv, L, D = 1, 4, 1, 384, 128
+q = seeded((B, H, L, D), "bf16", 0.5)
+k = seeded((B, Hkv, L, D), "bf16", 0.5)
+v = seeded((B, Hkv, L, D), "bf16", 0.5)
+g = seeded((B, H, L, D), "bf16")
+want = O.sdpa_bwd(q, k, v, g, None, None, is_causal=True)
+tq, tk, tv = (to_dev(x, "bf16", True) for x in (q, k, v))
+gtb.scaled_dot_product_attention(tq, tk, tv, is_causal=True).backward(to_dev(g, "bf16"))
+assert _C.device_status() == 0
+for name, got, ref in zip(("dq", "dk", "dv"), (tq.grad, tk.grad, tv.grad), want):
+    err = np.abs(got.float().cpu().numpy() - ref)
+    assert np.all(err <= 2e-2 + 1e-2 * np.abs(ref)), (name, float(err.max()))
+print("SPLIT-OK")
+"""
+
+
+def test_backward_split_dq_kernel_matches_oracle():
+    """GTB_BWD_SPLIT_DQ=1 selects the separate (deterministic) dQ kernel instead of the dQ sums
+    inside the dK/dV kernel; the variable is read once per process, so the check runs in a child."""
+    import os
+    import subprocess
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = dict(os.environ, GTB_BWD_SPLIT_DQ="1")
+    r = subprocess.run([sys.executable, "-c", _SPLIT_SCRIPT.format(root=root)], env=env, cwd=root,
+                       capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0 and "SPLIT-OK" in r.stdout, r.stdout + r.stderr
+
+
+def test_backward_fused_dq_repeats_within_rounding():
+    """The fused dQ adds f32 partial sums in whatever order the CTAs reach L2: two runs of the same
+    backward agree to f32 rounding of the sums (well inside the bf16 output's ulp), dK and dV exactly."""
+    import torch
+
+    import gguf_train_b200 as gtb
+
+    O.manual_seed(99)
+    B, H, Hkv, L, D = 2, 8, 2, 1024, 128
+    q = seeded((B, H, L, D), "bf16", 0.5)
+    k = seeded((B, Hkv, L, D), "bf16", 0.5)
+    v = seeded((B, Hkv, L, D), "bf16", 0.5)
+    g = to_dev(seeded((B, H, L, D), "bf16"), "bf16")
+    grads = []
+    for _ in range(2):
+        tq, tk, tv = (to_dev(x, "bf16", True) for x in (q, k, v))
+        gtb.scaled_dot_product_attention(tq, tk, tv, is_causal=True).backward(g)
+        grads.append((tq.grad.float(), tk.grad, tv.grad))
+    (q1, k1, v1), (q2, k2, v2) = grads
+    assert torch.equal(k1, k2) and torch.equal(v1, v2)
+    assert torch.allclose(q1, q2, atol=1e-3, rtol=1e-2)
