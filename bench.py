@@ -301,11 +301,11 @@ def run_train(args, rank: int, world: int, dev, max_over_ranks=lambda x: x) -> d
                      "frac": tf / peaks["bf16_tflops_sustained"],
                      "peak_source": peaks["source"] + " bf16 dense (sustained)",
                      "backward_tflops": 2 * fwd / (b_ms * 1e-3) / 1e12, "forward_tflops": fwd / (f_ms * 1e-3) / 1e12},
-        "launches_per_step": "forward 1, backward 3 (preprocess, dK/dV, dQ)",
+        "launches_per_step": "forward 1, backward 3 (preprocess, dK/dV with the dQ sums, dQ conversion)",
         "gpu_launches": 4 * steps, "status": _C.device_status(),
     }
     line["roofline"]["traffic_bwd_dkdv"] = profile_traffic("bwd_sm100_config4", "dkdv")
-    line["roofline"]["traffic_bwd_dq"] = profile_traffic("bwd_sm100_config4", "dq")
+    line["roofline"]["traffic_bwd_dq_convert"] = profile_traffic("bwd_sm100_config4", "dq_convert")
     del q, k, v, gd, out, lse
     torch.cuda.empty_cache()
     return line

@@ -52,10 +52,14 @@ GTB_API int gtb_sdpa_fwd(const gtb_tensor4 *q, const gtb_tensor4 *k, const gtb_t
 /* Attention backward: dq, dk, dv from dout, the forward inputs, the forward output and its lse.
  * Replaces FlashAttentionFn.backward (reference gguf_train/_functions.py:1934-1965), which
  * recomputes the probabilities with a chain of separate ops. dk/dv are summed over the query
- * heads of each kv head, as that function does (:1958-1962). Scratch (rowsum(dout*out) per row)
- * is taken from the stream-ordered allocator. On the tcgen05 path the dq kernel runs on an internal
- * per-device stream, forked from and joined back into `stream` within the call, so the call's
- * work stays ordered on `stream` (and under stream capture, in the captured graph). */
+ * heads of each kv head, as that function does (:1958-1962). Scratch (rowsum(dout*out) per row;
+ * on the tcgen05 path with D = 128 also f32 dq sums, B*H*Lpad*128*4 bytes, Lpad = L rounded up to
+ * 128) is taken from the stream-ordered allocator. With D = 128 dq is summed with f32 reductions
+ * in global memory, so its bits may differ from run to run in the last place; the environment
+ * variable GTB_BWD_SPLIT_DQ=1 (read once per process) selects a separate, deterministic dq kernel,
+ * which then runs on an internal per-device stream forked from and joined back into `stream`
+ * within the call, so the call's work stays ordered on `stream` (and under stream capture, in the
+ * captured graph). */
 GTB_API int gtb_sdpa_bwd(const gtb_tensor4 *dout, const gtb_tensor4 *q, const gtb_tensor4 *k,
                          const gtb_tensor4 *v, const gtb_tensor4 *mask, const gtb_tensor4 *out,
                          const void *lse, float scale, int is_causal,
