@@ -11,7 +11,8 @@ is an ImportError, never a silent fallback.
 from . import _C
 from . import functional
 from . import handles
-from .functional import FlashAttentionFn, decode_q8_0, dequantize_q8_0, quantize_q8_0, scaled_dot_product_attention
+from .functional import (FlashAttentionFn, decode_q8_0, dequantize_q8_0, quantize_q8_0, scaled_dot_product_attention,
+                         sdpa_from_host)
 from .modules import MultiheadAttention
 
 __all__ = [
@@ -21,6 +22,7 @@ __all__ = [
     "FlashAttentionFn",
     "MultiheadAttention",
     "scaled_dot_product_attention",
+    "sdpa_from_host",
     "quantize_q8_0",
     "dequantize_q8_0",
     "decode_q8_0",

@@ -75,3 +75,19 @@ def test_q8_0_python_checks():
 
     with pytest.raises(RuntimeError, match="CUDA tensors only"):
         gtb.quantize_q8_0(torch.zeros(4, 64))
+
+
+def test_sdpa_from_host_argument_checks():
+    """sdpa_from_host takes host tensors, no mask, and a host `out` of the result's shape; the checks
+    fire before any device work."""
+    import gguf_train_b200 as gtb
+
+    q = torch.randn(2, 2, 4, 8)
+    with pytest.raises(RuntimeError, match="attn_mask is not supported"):
+        gtb.sdpa_from_host(q, q, q, attn_mask=torch.ones(4, 4, dtype=torch.bool))
+    with pytest.raises(RuntimeError, match="expects 4D"):
+        gtb.sdpa_from_host(q[0], q[0], q[0])
+    with pytest.raises(RuntimeError, match="out must be"):
+        gtb.sdpa_from_host(q, q, q, out=torch.empty(2, 2, 4, 4))
+    with pytest.raises(RuntimeError, match="same batch size"):
+        gtb.sdpa_from_host(q, q[:1], q[:1])

@@ -363,3 +363,28 @@ def test_backward_fused_dq_repeats_within_rounding():
     (q1, k1, v1), (q2, k2, v2) = grads
     assert torch.equal(k1, k2) and torch.equal(v1, v2)
     assert torch.allclose(q1, q2, atol=1e-3, rtol=1e-2)
+
+
+@pytest.mark.parametrize("dtype,B,H,Hkv,L,S,D,causal,chunk", [
+    ("bf16", 5, 4, 2, 300, 300, 128, True, 2),    # three chunks, the last one ragged; tcgen05 path
+    ("f32", 3, 2, 1, 70, 90, 64, False, None),    # default chunking (one sequence per chunk); SIMT path
+    ("bf16", 2, 12, 3, 260, 260, 128, True, None),  # default chunking over kv heads (3 per sequence)
+    ("bf16", 3, 10, 5, 129, 129, 128, False, None), # kv heads in ragged groups (3, 2 per sequence)
+])
+def test_sdpa_from_host_matches_the_device_call(dtype, B, H, Hkv, L, S, D, causal, chunk):
+    """sdpa_from_host (pinned host tensors in and out, batch chunks pipelined over three streams)
+    gives bit for bit what scaled_dot_product_attention gives on the same inputs in device memory."""
+    import torch
+
+    import gguf_train_b200 as gtb
+
+    O.manual_seed(515 + B + L)
+    q = to_dev(seeded((B, H, L, D), dtype, 0.5), dtype)
+    k = to_dev(seeded((B, Hkv, S, D), dtype, 0.5), dtype)
+    v = to_dev(seeded((B, Hkv, S, D), dtype, 0.5), dtype)
+    want = gtb.scaled_dot_product_attention(q, k, v, is_causal=causal)
+    qh, kh, vh = (x.cpu().pin_memory() for x in (q, k, v))
+    got = gtb.sdpa_from_host(qh, kh, vh, is_causal=causal, chunk=chunk)
+    torch.cuda.current_stream().synchronize()
+    assert got.device.type == "cpu" and got.is_pinned()
+    assert torch.equal(got, want.cpu())
