@@ -13,9 +13,10 @@ The process group is used only for barriers and the max-over-ranks of the timed 
 Reported on one JSON line by rank 0:
   value        whole-job TFLOP/s with inputs resident in HBM (CUDA events on the launching
                stream, K steps between barriers + synchronize, max over ranks);
-  e2e          the same through the public API (gguf_train_b200.sdpa_from_host) with the inputs
-               copied from pinned host memory and the output copied back inside every timed step
-               (batch chunks, the copies overlapped with the kernels);
+  e2e          the same through the public API (gguf_train_b200.sdpa_from_host, i.e. the C ABI's
+               gtb_sdpa_fwd_host) with the inputs copied from pinned host memory and the output
+               copied back inside every timed step (pieces of the batch, the copies overlapped with
+               the kernels);
   roofline     the tcgen05 forward kernel against the measured bf16 dense peak;
   cpu_baseline the reference's CPU forward (restated loop, float64, OpenMP on every host
                core) on a bounded sample of the same workload, rank 0 at N=1 only;
@@ -529,8 +530,9 @@ def main() -> None:
                      "flops_per_launch": flops, "launch_ms": launch_ms},
         "e2e": {"value": flops * world / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "api": "gguf_train_b200.sdpa_from_host (pinned host q, k, v, out; 8 chunks of one sequence, "
-                       "copies in both directions overlapped with the tcgen05 forward on three streams)"},
+                "api": "gguf_train_b200.sdpa_from_host -> C ABI gtb_sdpa_fwd_host (pinned host q, k, v, out; "
+                       "8 pieces of one sequence, copies in both directions overlapped with the tcgen05 forward "
+                       "on three streams)"},
         "gpu_launches": args.steps,
         "clocks": sampler.summary(),
         "status": status,

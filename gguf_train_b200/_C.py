@@ -48,6 +48,8 @@ def _configure(lib: ctypes.CDLL) -> ctypes.CDLL:
     # raw-pointer ABI (gtb_attn.h)
     lib.gtb_sdpa_fwd.argtypes = [P4, P4, P4, P4, c_float, c_int, P4, c_void_p, c_void_p]
     lib.gtb_sdpa_fwd.restype = c_int
+    lib.gtb_sdpa_fwd_host.argtypes = [P4, P4, P4, c_float, c_int, P4, c_int, c_void_p]
+    lib.gtb_sdpa_fwd_host.restype = c_int
     lib.gtb_sdpa_bwd.argtypes = [P4, P4, P4, P4, P4, P4, c_void_p, c_float, c_int, P4, P4, P4, c_void_p]
     lib.gtb_sdpa_bwd.restype = c_int
     lib.gtb_q8_0_quantize.argtypes = [c_void_p, c_int, c_int64, c_int64, c_void_p, c_void_p]

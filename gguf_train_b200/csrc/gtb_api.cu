@@ -5,11 +5,13 @@
 // (csrc/gt_ops_nn.cpp:2425-2454) where the same condition is tested, so callers that match on
 // them (tests/test_pooling_and_attention.py:381,386 look for "cannot be broadcast") keep working.
 
+#include <algorithm>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
 #include <mutex>
 #include <string>
+#include <vector>
 
 #include "gtb_common.cuh"
 #include "q8_0_internal.h"
@@ -172,6 +174,52 @@ int env_int(const char* name, int dflt) {
     return e ? atoi(e) : dflt;
 }
 
+// The two side streams of gtb_sdpa_fwd_host on a device (host -> device and device -> host copies),
+// non-blocking, created once and kept for the process.
+struct HostCopyStreams {
+    cudaStream_t in = nullptr, out = nullptr;
+};
+
+HostCopyStreams host_copy_streams(int dev) {
+    static HostCopyStreams hs[64];
+    static std::once_flag once[64];
+    if (dev < 0 || dev >= 64) return HostCopyStreams{};
+    std::call_once(once[dev], [dev] {
+        if (cudaStreamCreateWithFlags(&hs[dev].in, cudaStreamNonBlocking) != cudaSuccess ||
+            cudaStreamCreateWithFlags(&hs[dev].out, cudaStreamNonBlocking) != cudaSuccess)
+            hs[dev] = HostCopyStreams{};
+        cudaGetLastError();
+    });
+    return hs[dev];
+}
+
+// host memory, pinned or not (not CUDA device or managed memory)
+bool check_host_ptr(const void* p, const char* ctx, const char* name) {
+    if (!p) {
+        set_errorf("%s: %s is NULL", ctx, name);
+        return false;
+    }
+    cudaPointerAttributes attr;
+    if (cudaPointerGetAttributes(&attr, p) != cudaSuccess) {
+        cudaGetLastError();
+        return true;
+    }
+    if (attr.type == cudaMemoryTypeDevice || attr.type == cudaMemoryTypeManaged) {
+        set_errorf("%s: %s is CUDA memory; this call takes host memory (use gtb_sdpa_fwd for device tensors)", ctx, name);
+        return false;
+    }
+    return true;
+}
+
+bool row_major(const gtb_tensor4& t) {
+    int64_t s = 1;
+    for (int i = 3; i >= 0; --i) {
+        if (t.shape[i] > 1 && t.stride[i] != s) return false;
+        s *= t.shape[i];
+    }
+    return true;
+}
+
 }  // namespace
 
 void retain_pool_memory(int dev) { keep_pool_memory(dev); }
@@ -229,6 +277,132 @@ GTB_API int gtb_sdpa_fwd(const gtb_tensor4* q, const gtb_tensor4* k, const gtb_t
     static const int force_simt = env_int("GTB_FWD_SIMT", 0);
     if (!force_simt && fwd_sm100_supported(a)) return launch_fwd_sm100(a, st);
     return launch_fwd_simt(a, st);
+}
+
+GTB_API int gtb_sdpa_fwd_host(const gtb_tensor4* q, const gtb_tensor4* k, const gtb_tensor4* v, float scale, int is_causal,
+                              gtb_tensor4* out, int pieces, void* stream) {
+    const char* ctx = "flash_attention_host";
+    AttnShape sh;
+    if (!check_attn(ctx, q, k, v, nullptr, sh)) return -1;
+    if (!out) {
+        set_errorf("%s: out is NULL", ctx);
+        return -1;
+    }
+    const int64_t osh[4] = {sh.B, sh.H, sh.L, sh.Dv};
+    if (!same_shape(*out, osh) || out->dtype != q->dtype) {
+        set_errorf("%s: out must be %s in q's dtype", ctx, shape_str(osh, 4).c_str());
+        return -1;
+    }
+    if (!row_major(*q) || !row_major(*k) || !row_major(*v) || !row_major(*out)) {
+        set_errorf("%s: q, k, v and out must be contiguous (row-major) host tensors", ctx);
+        return -1;
+    }
+    if (numel4(*out) == 0) return 0;
+    if (!check_host_ptr(q->data, ctx, "q") || !check_host_ptr(out->data, ctx, "out")) return -1;
+    if (sh.S > 0 && (!check_host_ptr(k->data, ctx, "k") || !check_host_ptr(v->data, ctx, "v"))) return -1;
+    int dev = 0;
+    if (cuda_failed(cudaGetDevice(&dev), ctx)) return -1;
+    const HostCopyStreams hs = host_copy_streams(dev);
+    if (!hs.in || !hs.out) {
+        set_errorf("%s: could not create the copy streams", ctx);
+        return -1;
+    }
+    cudaStream_t st = (cudaStream_t)stream;
+    const int64_t G = sh.H / sh.Hkv, P = pieces > 0 ? pieces : 8;
+    // pieces of work: whole sequences, or one sequence's kv heads in groups (with their query heads);
+    // either way each piece of q, k, v and out is one contiguous range of the host tensors
+    struct Piece { int64_t b0, m, h0, mh; };
+    std::vector<Piece> ps;
+    if (sh.B >= P) {
+        const int64_t n = sh.B / P;
+        for (int64_t b0 = 0; b0 < sh.B; b0 += n) ps.push_back({b0, std::min(n, sh.B - b0), 0, sh.Hkv});
+    } else {
+        const int64_t parts = std::max<int64_t>(1, std::min<int64_t>(sh.Hkv, P / sh.B));
+        const int64_t nh = (sh.Hkv + parts - 1) / parts;
+        for (int64_t b = 0; b < sh.B; ++b)
+            for (int64_t h0 = 0; h0 < sh.Hkv; h0 += nh) ps.push_back({b, 1, h0, std::min(nh, sh.Hkv - h0)});
+    }
+    int64_t nb = 0, nh = 0;
+    for (const Piece& x : ps) { nb = std::max(nb, x.m); nh = std::max(nh, x.mh); }
+    const size_t es = dtype_size(q->dtype);
+    auto up = [](size_t b) { return (b + 255) / 256 * 256; };
+    const size_t bq = up(es * nb * nh * G * sh.L * sh.D), bk = up(es * nb * nh * sh.S * sh.D),
+                 bv = up(es * nb * nh * sh.S * sh.Dv), bo = up(es * nb * nh * G * sh.L * sh.Dv);
+    const size_t slot = bq + bk + bv + bo;
+    keep_pool_memory(dev);
+    unsigned char* mem = nullptr;
+    if (cuda_failed(cudaMallocAsync((void**)&mem, 2 * slot, st), "flash_attention_host: device slots")) return -1;
+    const size_t ne = 3 * ps.size() + 3;
+    std::vector<cudaEvent_t> ev(ne, nullptr);
+    bool bad = false;
+    for (size_t i = 0; i < ne && !bad; ++i) bad = cuda_failed(cudaEventCreateWithFlags(&ev[i], cudaEventDisableTiming), ctx);
+    cudaEvent_t* ev_in = ev.data();
+    cudaEvent_t* ev_comp = ev_in + ps.size();
+    cudaEvent_t* ev_out = ev_comp + ps.size();
+    cudaEvent_t ev_start = ev[ne - 3], ev_join_in = ev[ne - 2], ev_join_out = ev[ne - 1];
+    // the slots were allocated on `st`: the copy streams start after that point
+    if (!bad) bad = cuda_failed(cudaEventRecord(ev_start, st), ctx) || cuda_failed(cudaStreamWaitEvent(hs.in, ev_start, 0), ctx) ||
+                    cuda_failed(cudaStreamWaitEvent(hs.out, ev_start, 0), ctx);
+    const unsigned char* hq = (const unsigned char*)q->data;
+    const unsigned char* hk = (const unsigned char*)k->data;
+    const unsigned char* hv = (const unsigned char*)v->data;
+    unsigned char* ho = (unsigned char*)out->data;
+    for (size_t i = 0; i < ps.size() && !bad; ++i) {
+        const Piece& x = ps[i];
+        unsigned char* base = mem + (i & 1) * slot;
+        const int64_t nq = x.m * x.mh * G;  // query heads of the piece (one range: m == 1 or mh == Hkv)
+        const size_t oq = es * (x.b0 * sh.H + x.h0 * G) * sh.L * sh.D, nbq = es * nq * sh.L * sh.D;
+        const size_t okv = (x.b0 * sh.Hkv + x.h0), nkv = x.m * x.mh;
+        const size_t oo = es * (x.b0 * sh.H + x.h0 * G) * sh.L * sh.Dv, nbo = es * nq * sh.L * sh.Dv;
+        if (i >= 2) bad = cuda_failed(cudaStreamWaitEvent(hs.in, ev_comp[i - 2], 0), ctx);  // slot read by piece i-2
+        bad = bad || cuda_failed(cudaMemcpyAsync(base, hq + oq, nbq, cudaMemcpyHostToDevice, hs.in), ctx) ||
+              cuda_failed(cudaMemcpyAsync(base + bq, hk + es * okv * sh.S * sh.D, es * nkv * sh.S * sh.D,
+                                          cudaMemcpyHostToDevice, hs.in), ctx) ||
+              cuda_failed(cudaMemcpyAsync(base + bq + bk, hv + es * okv * sh.S * sh.Dv, es * nkv * sh.S * sh.Dv,
+                                          cudaMemcpyHostToDevice, hs.in), ctx) ||
+              cuda_failed(cudaEventRecord(ev_in[i], hs.in), ctx) || cuda_failed(cudaStreamWaitEvent(st, ev_in[i], 0), ctx);
+        if (!bad && i >= 2) bad = cuda_failed(cudaStreamWaitEvent(st, ev_out[i - 2], 0), ctx);  // slot's output copied out
+        if (bad) break;
+        gtb_tensor4 tq, tk, tv, to;
+        const int64_t qs[4] = {x.m, x.mh * G, sh.L, sh.D}, ks[4] = {x.m, x.mh, sh.S, sh.D}, vs[4] = {x.m, x.mh, sh.S, sh.Dv},
+                      os[4] = {x.m, x.mh * G, sh.L, sh.Dv};
+        auto dense = [&](gtb_tensor4& t, void* p, const int64_t* s4) {
+            t.data = p;
+            t.dtype = q->dtype;
+            int64_t str = 1;
+            for (int d = 3; d >= 0; --d) {
+                t.shape[d] = s4[d];
+                t.stride[d] = str;
+                str *= s4[d];
+            }
+        };
+        dense(tq, base, qs);
+        dense(tk, base + bq, ks);
+        dense(tv, base + bq + bk, vs);
+        dense(to, base + bq + bk + bv, os);
+        if (gtb_sdpa_fwd(&tq, &tk, &tv, nullptr, scale, is_causal, &to, nullptr, st) != 0) {
+            bad = true;
+            break;
+        }
+        bad = cuda_failed(cudaEventRecord(ev_comp[i], st), ctx) || cuda_failed(cudaStreamWaitEvent(hs.out, ev_comp[i], 0), ctx) ||
+              cuda_failed(cudaMemcpyAsync(ho + oo, base + bq + bk + bv, nbo, cudaMemcpyDeviceToHost, hs.out), ctx) ||
+              cuda_failed(cudaEventRecord(ev_out[i], hs.out), ctx);
+    }
+    // join both copy streams into `st` (after an error too: the slots are released on `st`)
+    const bool joined = ev_join_in && ev_join_out && cudaEventRecord(ev_join_in, hs.in) == cudaSuccess &&
+                        cudaEventRecord(ev_join_out, hs.out) == cudaSuccess &&
+                        cudaStreamWaitEvent(st, ev_join_in, 0) == cudaSuccess &&
+                        cudaStreamWaitEvent(st, ev_join_out, 0) == cudaSuccess;
+    if (!joined) {
+        cudaGetLastError();
+        cudaStreamSynchronize(hs.in);
+        cudaStreamSynchronize(hs.out);
+        bad = true;
+    }
+    cudaFreeAsync(mem, st);
+    for (cudaEvent_t e : ev)
+        if (e) cudaEventDestroy(e);
+    return bad ? -1 : 0;
 }
 
 GTB_API int gtb_sdpa_bwd(const gtb_tensor4* dout, const gtb_tensor4* q, const gtb_tensor4* k, const gtb_tensor4* v,

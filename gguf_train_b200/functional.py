@@ -189,34 +189,20 @@ def scaled_dot_product_attention(
     return _sdpa_dropout(query, key, value, attn_mask, dropout_p, is_causal, sc)
 
 
-_HOST_STREAMS: dict = {}
-_HOST_PIECES = 8  # pieces per sdpa_from_host call when the caller gives no chunk size
-
-
-def _host_streams(dev: torch.device):
-    """The two side streams of `sdpa_from_host` on `dev` (host -> device and device -> host copies),
-    created once per device."""
-    key = dev.index
-    if key not in _HOST_STREAMS:
-        _HOST_STREAMS[key] = (torch.cuda.Stream(dev), torch.cuda.Stream(dev))
-    return _HOST_STREAMS[key]
-
-
 def sdpa_from_host(query: torch.Tensor, key: torch.Tensor, value: torch.Tensor, out: torch.Tensor | None = None,
                    attn_mask: torch.Tensor | None = None, is_causal: bool = False, scale: float | None = None,
                    chunk: int | None = None, device=None) -> torch.Tensor:
     """Scaled dot-product attention of q (B, H, L, D), k (B, Hkv, S, D), v (B, Hkv, S, Dv) held in host
-    memory (pinned, for the copies to be asynchronous), computed on the GPU; the result lands in `out`
-    (host, (B, H, L, Dv), pinned and allocated when not given), which is returned.
+    memory (pinned, for the copies to be asynchronous), computed on the GPU by the native
+    gtb_sdpa_fwd_host; the result lands in `out` (host, (B, H, L, Dv), pinned and allocated when not
+    given), which is returned.
 
-    The work is cut into chunks: `chunk` whole sequences each when given, else about 8 pieces (whole
-    sequences when the batch has 8 or more, otherwise each sequence's kv heads in groups, with their
-    query heads; on config 3, 8 and 12 pieces measured 8.99 / 8.96 ms per call, 16 and 24 pieces
-    9.33 / 9.97, the Python work per piece then showing). Chunk i's q, k, v are copied to the device on one side stream while chunk i-1 is
-    attended on the caller's current stream and chunk i-2's output is copied back on a second side
-    stream, so both directions of PCIe are busy at once and the kernels run behind the copies. Two
-    device slots of each of q, k, v and out are reused in turn. Like any non_blocking copy, `out` is
-    complete once the caller's current stream has passed this call (e.g. after
+    The work is cut into ceil(B / chunk) pieces when `chunk` is given, else 8 (whole sequences when
+    the batch has that many, otherwise each sequence's kv heads in groups, with their query heads).
+    Piece i's q, k, v are copied to the device on one internal stream while piece i-1 is attended on
+    the caller's current stream and piece i-2's output is copied back on another, so both directions
+    of PCIe are busy at once and the kernels run behind the copies. Like any non_blocking copy, `out`
+    is complete once the caller's current stream has passed this call (e.g. after
     torch.cuda.current_stream().synchronize()). Masks are not taken here: copy the tensors and use
     scaled_dot_product_attention."""
     if attn_mask is not None:
@@ -229,62 +215,24 @@ def sdpa_from_host(query: torch.Tensor, key: torch.Tensor, value: torch.Tensor, 
     if query.ndim != 4 or key.ndim != 4 or value.ndim != 4:
         raise RuntimeError("flash_attention expects 4D q, k, v tensors (B, H, L, D)")
     B, H, L, D = query.shape
-    Hkv, Dv = key.shape[1], value.shape[3]
+    Dv = value.shape[3]
     if key.shape[0] != B or value.shape[0] != B:
         raise RuntimeError("sdpa_from_host: q, k, v must have the same batch size")
-    if Hkv < 1 or H % Hkv != 0:
-        raise RuntimeError("num_heads must be divisible by num_kv_heads")
     if out is None:
         out = torch.empty((B, H, L, Dv), dtype=query.dtype, pin_memory=True)
-    elif tuple(out.shape) != (B, H, L, Dv) or out.dtype != query.dtype:
-        raise RuntimeError(f"sdpa_from_host: out must be {(B, H, L, Dv)} of {query.dtype}")
-    if B == 0:
+    elif tuple(out.shape) != (B, H, L, Dv) or out.dtype != query.dtype or not out.is_contiguous():
+        raise RuntimeError(f"sdpa_from_host: out must be a contiguous {(B, H, L, Dv)} tensor of {query.dtype}")
+    if out.numel() == 0:
         return out
-    G = H // Hkv
-    # pieces: (first sequence, sequences, first kv head, kv heads)
-    if chunk or B >= _HOST_PIECES:
-        n = max(1, min(B, chunk if chunk else B // _HOST_PIECES))
-        pieces = [(b0, min(n, B - b0), 0, Hkv) for b0 in range(0, B, n)]
-    else:
-        nh = -(-Hkv // max(1, min(Hkv, _HOST_PIECES // B)))  # kv heads per piece
-        pieces = [(b, 1, h0, min(nh, Hkv - h0)) for b in range(B) for h0 in range(0, Hkv, nh)]
-    nb = max(p[1] for p in pieces)
-    nh = max(p[3] for p in pieces)
+    q, k, v = (t.contiguous() for t in (query, key, value))
+    pieces = -(-B // chunk) if chunk else 0
     dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
-    sc = (1.0 / math.sqrt(D)) if scale is None else float(scale)
-    comp = torch.cuda.current_stream(dev)
-    s_in, s_out = _host_streams(dev)
-    slots = [(torch.empty((nb, nh * G, L, D), dtype=query.dtype, device=dev),
-              torch.empty((nb, nh) + tuple(key.shape[2:]), dtype=key.dtype, device=dev),
-              torch.empty((nb, nh) + tuple(value.shape[2:]), dtype=value.dtype, device=dev),
-              torch.empty((nb, nh * G, L, Dv), dtype=query.dtype, device=dev)) for _ in range(2)]
-    s_in.wait_stream(comp)  # the slots were allocated on the current stream
-    s_out.wait_stream(comp)
-    ev_comp, ev_out = [], []
-    for i, (b0, m, h0, mh) in enumerate(pieces):
-        sq, sk, sv, so = slots[i % 2]
-        qd, kd, vd, od = sq[:m, :mh * G], sk[:m, :mh], sv[:m, :mh], so[:m, :mh * G]
-        with torch.cuda.stream(s_in):
-            if i >= 2:
-                s_in.wait_event(ev_comp[i - 2])  # chunk i-2's kernel has read this slot
-            qd.copy_(query[b0:b0 + m, h0 * G:(h0 + mh) * G], non_blocking=True)
-            kd.copy_(key[b0:b0 + m, h0:h0 + mh], non_blocking=True)
-            vd.copy_(value[b0:b0 + m, h0:h0 + mh], non_blocking=True)
-            ev_in = s_in.record_event()
-        comp.wait_event(ev_in)
-        if i >= 2:
-            comp.wait_event(ev_out[i - 2])  # chunk i-2's output has left this slot
-        tq, tk, tv, to = _t4(qd), _t4(kd), _t4(vd), _t4(od)
-        rc = _C.lib.gtb_sdpa_fwd(ctypes.byref(tq), ctypes.byref(tk), ctypes.byref(tv), None, sc,
-                                 1 if is_causal else 0, ctypes.byref(to), None, comp.cuda_stream)
-        _C.check_rc(rc, "flash_attention")
-        ev_comp.append(comp.record_event())
-        with torch.cuda.stream(s_out):
-            s_out.wait_event(ev_comp[i])
-            out[b0:b0 + m, h0 * G:(h0 + mh) * G].copy_(od, non_blocking=True)
-            ev_out.append(s_out.record_event())
-    comp.wait_event(ev_out[-1])
-    comp.wait_stream(s_in)
+    with torch.cuda.device(dev):
+        tq, tk, tv, to = _t4(q), _t4(k), _t4(v), _t4(out)
+        rc = _C.lib.gtb_sdpa_fwd_host(ctypes.byref(tq), ctypes.byref(tk), ctypes.byref(tv),
+                                      -1.0 if scale is None else float(scale), 1 if is_causal else 0,
+                                      ctypes.byref(to), pieces, torch.cuda.current_stream(dev).cuda_stream)
+    _C.check_rc(rc, "flash_attention")
     return out
 
 

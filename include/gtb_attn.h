@@ -49,6 +49,18 @@ GTB_API int gtb_sdpa_fwd(const gtb_tensor4 *q, const gtb_tensor4 *k, const gtb_t
                          const gtb_tensor4 *mask, float scale, int is_causal,
                          gtb_tensor4 *out, void *lse, void *stream);
 
+/* The forward for q, k, v and out in HOST memory (contiguous, row-major; pinned for the copies to
+ * overlap, pageable works with serialised copies), no mask. New export for callers whose tensors live
+ * on the host, as the reference's do (gt_flash_attention, csrc/gt_ops_nn.cpp:2423-2525, reads and
+ * writes host tensors). The work is cut into `pieces` (<= 0: 8) pieces — whole sequences, or one
+ * sequence's kv heads in groups when the batch is smaller than that — and on the calling thread's
+ * device piece i's q, k, v are copied in on one internal stream while piece i-1 is attended on
+ * `stream` and piece i-2's output is copied out on another; two device slots from the stream-ordered
+ * allocator are reused in turn. Asynchronous like the other calls: `out` is complete once `stream`
+ * has passed the call. Results are bit for bit those of gtb_sdpa_fwd on the same values. */
+GTB_API int gtb_sdpa_fwd_host(const gtb_tensor4 *q, const gtb_tensor4 *k, const gtb_tensor4 *v, float scale,
+                              int is_causal, gtb_tensor4 *out, int pieces, void *stream);
+
 /* Attention backward: dq, dk, dv from dout, the forward inputs, the forward output and its lse.
  * Replaces FlashAttentionFn.backward (reference gguf_train/_functions.py:1934-1965), which
  * recomputes the probabilities with a chain of separate ops. dk/dv are summed over the query
