@@ -117,3 +117,33 @@ def test_raw_abi_rejects_host_pointers_and_bad_shapes():
     assert rc != 0 and "cannot be broadcast" in _C.lib.gtb_last_error().decode()
     rc = _C.lib.gtb_q8_0_quantize(host.ctypes.data, _C.GT_F32, 1, 33, host.ctypes.data, None)
     assert rc != 0 and "multiple of ggml quantization block size" in _C.lib.gtb_last_error().decode()
+
+
+def test_host_forward_argument_checks():
+    """gtb_sdpa_fwd_host (host q, k, v, out) checks shapes, dtypes and layout before any device work."""
+    from gguf_train_b200 import _C
+
+    def t4(arr, shape=None, strides=None):
+        t = _C.Tensor4()
+        t.data = arr.ctypes.data
+        sts = strides or [int(s) for s in np.array(arr.strides) // arr.itemsize]
+        for i, (s, st) in enumerate(zip(shape or arr.shape, sts)):
+            t.shape[i], t.stride[i] = s, st
+        t.dtype = _C.GT_F32
+        return t
+
+    q = np.zeros((1, 2, 4, 8), np.float32)
+    k3 = np.zeros((1, 3, 4, 8), np.float32)
+
+    def call(qq, kk, vv, oo):
+        rc = _C.lib.gtb_sdpa_fwd_host(ctypes.byref(qq), ctypes.byref(kk), ctypes.byref(vv), 0.0, 0, ctypes.byref(oo),
+                                      0, None)
+        return rc, _C.lib.gtb_last_error().decode()
+
+    rc, msg = call(t4(q), t4(k3), t4(k3), t4(q.copy()))
+    assert rc != 0 and "num_heads must be divisible by num_kv_heads" in msg
+    rc, msg = call(t4(q), t4(q), t4(q), t4(np.zeros((1, 2, 4, 4), np.float32)))
+    assert rc != 0 and "out must be" in msg
+    # a (B, H, L, D) view whose L and D strides are swapped is not row-major
+    rc, msg = call(t4(q, (1, 2, 4, 8), [64, 32, 1, 4]), t4(q), t4(q), t4(q.copy()))
+    assert rc != 0 and "contiguous (row-major)" in msg
