@@ -402,8 +402,10 @@ bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
                 ok = mbar_wait(&p_full[0], it & 1, p.status, 44);
                 if (!ok) break;
                 tc_fence_after();
-                issue_grad(st, 0, it == 0);
+                // dQ^T first: the compute warps read it out while the gradient MMAs run, so the next
+                // tile's dP^T rarely waits for its columns
                 if constexpr (FUSE) issue_dq(0);
+                issue_grad(st, 0, it == 0);
                 if (more) {  // sub-item 0 of the next tile, into the columns just read
                     ok = mbar_wait(&st_full[st ^ 1], ((it + 1) >> 1) & 1, p.status, 43);
                     if (!ok || *(volatile int*)abort_flag) { ok = false; break; }
@@ -422,8 +424,8 @@ bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
                 ok = mbar_wait(&p_full[1], it & 1, p.status, 44);
                 if (!ok) break;
                 tc_fence_after();
-                issue_grad(st, 1, false);
                 if constexpr (FUSE) issue_dq(1);
+                issue_grad(st, 1, false);
                 mma_commit(&st_empty[st]);  // this tile's Q / dO are read by every MMA issued so far
                 if (more) {
                     if constexpr (FUSE) {
