@@ -54,6 +54,9 @@ def _configure(lib: ctypes.CDLL) -> ctypes.CDLL:
     lib.gtb_sdpa_bwd.restype = c_int
     lib.gtb_q8_0_quantize.argtypes = [c_void_p, c_int, c_int64, c_int64, c_void_p, c_void_p]
     lib.gtb_q8_0_quantize.restype = c_int
+    lib.gtb_q8_0_append.argtypes = [c_void_p, c_int, c_int64, c_int64, c_int64, c_int64, c_void_p, c_int64, c_void_p,
+                                    c_int, c_void_p]
+    lib.gtb_q8_0_append.restype = c_int
     lib.gtb_q8_0_dequantize.argtypes = [c_void_p, c_int64, c_int64, c_void_p, c_int, c_void_p]
     lib.gtb_q8_0_dequantize.restype = c_int
     lib.gtb_decode_q8_0.argtypes = [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64,

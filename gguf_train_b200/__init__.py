@@ -11,8 +11,8 @@ is an ImportError, never a silent fallback.
 from . import _C
 from . import functional
 from . import handles
-from .functional import (FlashAttentionFn, decode_q8_0, dequantize_q8_0, quantize_q8_0, scaled_dot_product_attention,
-                         sdpa_from_host)
+from .functional import (FlashAttentionFn, decode_q8_0, dequantize_q8_0, q8_0_append, quantize_q8_0,
+                         scaled_dot_product_attention, sdpa_from_host)
 from .modules import MultiheadAttention
 
 __all__ = [
@@ -24,6 +24,7 @@ __all__ = [
     "scaled_dot_product_attention",
     "sdpa_from_host",
     "quantize_q8_0",
+    "q8_0_append",
     "dequantize_q8_0",
     "decode_q8_0",
 ]

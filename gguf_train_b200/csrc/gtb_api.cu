@@ -470,6 +470,33 @@ GTB_API int gtb_q8_0_quantize(const void* x, int x_dtype, int64_t n_rows, int64_
     return launch_q8_0_quantize(x, x_dtype, n / 32, out, (cudaStream_t)stream);
 }
 
+GTB_API int gtb_q8_0_append(const void* x, int x_dtype, int64_t B, int64_t Hkv, int64_t n_new, int64_t D, void* cache,
+                            int64_t Smax, int32_t* pos, int advance, void* stream) {
+    const char* ctx = "q8_0_append";
+    if (B < 0 || Hkv < 0 || n_new < 0 || D < 0 || Smax < 0) {
+        set_errorf("%s: negative size", ctx);
+        return -1;
+    }
+    if (D % 32 != 0) {
+        set_error("Tensor size must be a multiple of ggml quantization block size");
+        return -1;
+    }
+    if (n_new > INT32_MAX) {
+        set_errorf("%s: n_new must fit in int32", ctx);
+        return -1;
+    }
+    if (x_dtype != F32 && x_dtype != F16 && x_dtype != BF16) {
+        set_errorf("%s: the new rows must be f32, f16 or bf16", ctx);
+        return -1;
+    }
+    if (B == 0 || n_new == 0) return 0;
+    if (D > 0 && Hkv > 0) {
+        if (!check_device_ptr(x, ctx, "x") || !check_device_ptr(cache, ctx, "cache")) return -1;
+    }
+    if (!check_device_ptr(pos, ctx, "pos")) return -1;
+    return launch_q8_0_append(x, x_dtype, B, Hkv, n_new, D, cache, Smax, pos, advance != 0, (cudaStream_t)stream);
+}
+
 GTB_API int gtb_q8_0_dequantize(const void* blocks, int64_t n_rows, int64_t row_len, void* out, int out_dtype,
                                 void* stream) {
     const int64_t n = n_rows * row_len;

@@ -29,11 +29,9 @@ constexpr int QBYTES = 34;
 
 // ------------------------------------------------------------------ quantise / dequantise
 
+// one 32-value block of x into the 34-byte block at `dst` (2-byte aligned)
 template <typename T>
-__global__ void q8_0_quantize_kernel(const T* __restrict__ x, int64_t nblocks, uint8_t* __restrict__ out) {
-    const int64_t blk = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (blk >= nblocks) return;
-    const T* xb = x + blk * QK;
+__device__ __forceinline__ void quantize_block(const T* __restrict__ xb, uint8_t* __restrict__ dst) {
     float v[QK];
     float amax = 0.0f;
 #pragma unroll
@@ -44,7 +42,7 @@ __global__ void q8_0_quantize_kernel(const T* __restrict__ x, int64_t nblocks, u
     const float d = __fdiv_rn(amax, 127.0f);
     const float id = d != 0.0f ? __frcp_rn(d) : 0.0f;
     // the 34-byte block as 17 little-endian 16-bit words (blocks start 2-byte aligned)
-    uint16_t* ob = (uint16_t*)(out + blk * QBYTES);
+    uint16_t* ob = (uint16_t*)dst;
     ob[0] = __half_as_ushort(__float2half_rn(d));
 #pragma unroll
     for (int j = 0; j < QK; j += 2) {
@@ -52,6 +50,37 @@ __global__ void q8_0_quantize_kernel(const T* __restrict__ x, int64_t nblocks, u
         const uint32_t hi = (uint32_t)(uint8_t)(int8_t)roundf(__fmul_rn(v[j + 1], id));
         ob[1 + j / 2] = (uint16_t)(lo | (hi << 8));
     }
+}
+
+template <typename T>
+__global__ void q8_0_quantize_kernel(const T* __restrict__ x, int64_t nblocks, uint8_t* __restrict__ out) {
+    const int64_t blk = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (blk >= nblocks) return;
+    quantize_block(x + blk * QK, out + blk * QBYTES);
+}
+
+// KV-cache append: block j of row t of (sequence b, kv head hk) of x (B, Hkv, n_new, D) goes to
+// cache row pos[b] + t of (B, Hkv, Smax, D/32 blocks). A row outside [0, Smax) is not written and
+// records status 60.
+template <typename T>
+__global__ void q8_0_append_kernel(const T* __restrict__ x, int64_t Hkv, int64_t n_new, int64_t nb_row,
+                                   uint8_t* __restrict__ cache, int64_t Smax, const int32_t* __restrict__ pos,
+                                   int64_t nblocks, int* status) {
+    const int64_t blk = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (blk >= nblocks) return;
+    const int64_t j = blk % nb_row, r = blk / nb_row;  // r over (b, hk, t)
+    const int64_t t = r % n_new, bh = r / n_new, b = bh / Hkv;
+    const int64_t row = (int64_t)pos[b] + t;
+    if (row < 0 || row >= Smax) {
+        if (status) atomicCAS(status, 0, 60);
+        return;
+    }
+    quantize_block(x + blk * QK, cache + ((bh * Smax + row) * nb_row + j) * QBYTES);
+}
+
+__global__ void q8_0_advance_kernel(int32_t* pos, int64_t B, int32_t n_new) {
+    const int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (b < B) pos[b] += n_new;
 }
 
 template <typename T>
@@ -521,6 +550,30 @@ int launch_q8_0_quantize(const void* x, int x_dtype, int64_t nblocks, void* out,
         default: set_error("quantize: Q8_0 input must be f32, f16 or bf16"); return -1;
     }
     return cuda_failed(cudaGetLastError(), "q8_0 quantize launch") ? -1 : 0;
+}
+
+int launch_q8_0_append(const void* x, int x_dtype, int64_t B, int64_t Hkv, int64_t n_new, int64_t D, void* cache,
+                       int64_t Smax, int32_t* pos, bool advance, cudaStream_t st) {
+    const int64_t nb_row = D / QK, nblocks = B * Hkv * n_new * nb_row;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    int* status = device_status_word(dev);
+    if (nblocks > 0) {
+        const unsigned grid = (unsigned)((nblocks + 127) / 128);
+        uint8_t* c = (uint8_t*)cache;
+        switch (x_dtype) {
+            case F32: q8_0_append_kernel<float><<<grid, 128, 0, st>>>((const float*)x, Hkv, n_new, nb_row, c, Smax, pos, nblocks, status); break;
+            case F16: q8_0_append_kernel<__half><<<grid, 128, 0, st>>>((const __half*)x, Hkv, n_new, nb_row, c, Smax, pos, nblocks, status); break;
+            case BF16: q8_0_append_kernel<__nv_bfloat16><<<grid, 128, 0, st>>>((const __nv_bfloat16*)x, Hkv, n_new, nb_row, c, Smax, pos, nblocks, status); break;
+            default: set_error("q8_0_append: the new rows must be f32, f16 or bf16"); return -1;
+        }
+        if (cuda_failed(cudaGetLastError(), "q8_0 append launch")) return -1;
+    }
+    if (advance && n_new > 0 && B > 0) {
+        q8_0_advance_kernel<<<(unsigned)((B + 255) / 256), 256, 0, st>>>(pos, B, (int32_t)n_new);
+        if (cuda_failed(cudaGetLastError(), "q8_0 append: length update launch")) return -1;
+    }
+    return 0;
 }
 
 int launch_q8_0_dequantize(const void* blocks, int64_t nblocks, void* out, int out_dtype, cudaStream_t st) {

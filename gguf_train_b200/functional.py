@@ -276,6 +276,32 @@ def quantize_q8_0(x: torch.Tensor) -> torch.Tensor:
     return out
 
 
+def q8_0_append(cache: torch.Tensor, x: torch.Tensor, pos: torch.Tensor, advance: bool = True) -> torch.Tensor:
+    """Append new rows to a Q8_0 KV cache on the device: x (B, Hkv, n_new, D) is quantised (bit for bit
+    as quantize_q8_0) into rows pos[b] .. pos[b] + n_new - 1 of cache (B, Hkv, Smax, D/32*34) uint8,
+    the layout decode_q8_0 reads; pos (B) int32 holds the sequences' current lengths (decode_q8_0's
+    seq_lens) and, with `advance`, is increased by n_new afterwards. Rows that would fall outside
+    the cache are skipped and leave status 60 in the device status word (_C.device_status()).
+    Returns cache."""
+    _require_cuda("q8_0_append", cache, x, pos)
+    if x.ndim != 4 or cache.ndim != 4:
+        raise RuntimeError("q8_0_append: x must be (B, Hkv, n_new, D) and cache (B, Hkv, Smax, D/32*34)")
+    B, Hkv, n_new, D = x.shape
+    if D % 32:
+        raise RuntimeError("Tensor size must be a multiple of ggml quantization block size")
+    if cache.dtype != torch.uint8 or tuple(cache.shape[:2]) != (B, Hkv) or cache.shape[3] != D // 32 * 34 \
+            or not cache.is_contiguous():
+        raise RuntimeError(f"q8_0_append: cache must be a contiguous uint8 tensor ({B}, {Hkv}, Smax, {D // 32 * 34})")
+    if pos.dtype != torch.int32 or tuple(pos.shape) != (B,) or not pos.is_contiguous():
+        raise RuntimeError(f"q8_0_append: pos must be a contiguous int32 tensor of shape ({B},)")
+    x = x.contiguous()
+    rc = _C.lib.gtb_q8_0_append(x.data_ptr() if x.numel() else None, _code(x), B, Hkv, n_new, D,
+                                cache.data_ptr() if cache.numel() else None, cache.shape[2],
+                                pos.data_ptr() if pos.numel() else None, 1 if advance else 0, _stream(x.device))
+    _C.check_rc(rc, "q8_0_append")
+    return cache
+
+
 def dequantize_q8_0(blocks: torch.Tensor, dtype=torch.float32) -> torch.Tensor:
     """Inverse of quantize_q8_0: x = q * d, in `dtype`."""
     _require_cuda("dequantize", blocks)

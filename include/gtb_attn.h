@@ -85,6 +85,16 @@ GTB_API int gtb_sdpa_bwd(const gtb_tensor4 *dout, const gtb_tensor4 *q, const gt
 GTB_API int gtb_q8_0_quantize(const void *x, int x_dtype, int64_t n_rows, int64_t row_len,
                               void *out, void *stream);
 
+/* KV-cache append on the device (new export; the reference appends by quantising on the host through
+ * gt_tensor_to_dtype, csrc/gt_core.cpp:792-840, and concatenating). x: contiguous (B, Hkv, n_new, D)
+ * f32/f16/bf16, D % 32 == 0; row t of (b, hk) is quantised exactly as gtb_q8_0_quantize does into
+ * row pos[b] + t of cache (B, Hkv, Smax, D/32*34 bytes, the layout gtb_decode_q8_0 reads). pos:
+ * device int32 (B), the sequences' current lengths (gtb_decode_q8_0's seq_lens); with advance != 0 a
+ * second kernel then adds n_new to every pos[b]. A destination row outside [0, Smax) is skipped and
+ * sets the device status word to 60 (read with gtb_device_status). */
+GTB_API int gtb_q8_0_append(const void *x, int x_dtype, int64_t B, int64_t Hkv, int64_t n_new, int64_t D,
+                            void *cache, int64_t Smax, int32_t *pos, int advance, void *stream);
+
 /* Q8_0 -> f32/f16/bf16 (out_dtype), x = q * d. Replaces gt_dequantize (csrc/gt_ops_extra.cpp:2006). */
 GTB_API int gtb_q8_0_dequantize(const void *blocks, int64_t n_rows, int64_t row_len,
                                 void *out, int out_dtype, void *stream);

@@ -147,3 +147,21 @@ def test_host_forward_argument_checks():
     # a (B, H, L, D) view whose L and D strides are swapped is not row-major
     rc, msg = call(t4(q, (1, 2, 4, 8), [64, 32, 1, 4]), t4(q), t4(q), t4(q.copy()))
     assert rc != 0 and "contiguous (row-major)" in msg
+
+
+def test_q8_0_append_argument_checks():
+    """gtb_q8_0_append rejects a row length that is not whole Q8_0 blocks, negative sizes and
+    non-float rows before any device work."""
+    from gguf_train_b200 import _C
+
+    def call(D=64, dtype=_C.GT_F32, n_new=1):
+        rc = _C.lib.gtb_q8_0_append(None, dtype, 1, 1, n_new, D, None, 8, None, 1, None)
+        return rc, _C.lib.gtb_last_error().decode()
+
+    rc, msg = call(D=33)
+    assert rc != 0 and "multiple of ggml quantization block size" in msg
+    rc, msg = call(n_new=-1)
+    assert rc != 0 and "negative size" in msg
+    rc, msg = call(dtype=_C.GT_F64)
+    assert rc != 0 and "f32, f16 or bf16" in msg
+    assert call(n_new=0)[0] == 0  # nothing to append

@@ -121,3 +121,63 @@ def test_decode_bf16_and_f32_queries():
 def test_decode_empty_sequence_gives_zero():
     got = _decode_case(2, 4, 2, 1100, 128, [0, 1100])
     assert float(got[0].abs().max()) == 0.0
+
+
+def test_append_writes_the_quantised_rows_at_each_length():
+    """q8_0_append quantises new rows into each sequence's cache rows [len, len + n_new), bit for bit
+    as quantize_q8_0 (and so as ggml), leaves every other row alone and advances the lengths; a
+    decode step then reads the appended rows (checked against the oracle)."""
+    import torch
+
+    import gguf_train_b200 as gtb
+    from gguf_train_b200 import _C
+
+    O.manual_seed(61)
+    B, H, Hkv, Smax, D, n_new = 3, 8, 2, 300, 128, 7
+    lens = [5, 0, 290]
+    base = (O.randn(B, Hkv, Smax, D) * 0.7).astype(np.float32)
+    new = (O.randn(B, Hkv, n_new, D) * 0.7).astype(np.float32)
+    cache = gtb.quantize_q8_0(torch.tensor(base).cuda())
+    pos = torch.tensor(lens, dtype=torch.int32, device="cuda")
+    gtb.q8_0_append(cache, torch.tensor(new).cuda().to(torch.bfloat16), pos)
+    assert _C.device_status() == 0
+    full = base.copy()
+    new_bf = torch.tensor(new).to(torch.bfloat16).float().numpy()
+    for b in range(B):
+        full[b, :, lens[b]:lens[b] + n_new] = new_bf[b]
+    want = O.q8_0_quantize(full.reshape(-1, D)).reshape(B, Hkv, Smax, D // 32 * 34)
+    assert np.array_equal(cache.cpu().numpy(), want)
+    assert pos.cpu().tolist() == [n + n_new for n in lens]
+    # a decode step over the appended cache, against the oracle's dequantise-then-attend
+    vq = O.q8_0_quantize(full.reshape(-1, D))
+    vcache = torch.tensor(vq.reshape(B, Hkv, Smax, D // 32 * 34)).cuda()
+    q = seeded((B, H, 1, D), "f16")
+    got = gtb.decode_q8_0(to_dev(q, "f16"), cache, vcache, pos)
+    assert _C.device_status() == 0
+    ref = O.decode_q8_0(q, want.reshape(-1), vq, np.asarray(lens, np.int32) + n_new, Hkv, Smax)
+    assert_close(got.double(), ref, 2e-2, 1e-2, "decode after append")
+
+
+def test_append_past_the_cache_end_is_skipped_and_reported():
+    """Rows that would land at or past Smax are not written; the kernel records status 60 and the
+    rows that fit are written."""
+    import torch
+
+    import gguf_train_b200 as gtb
+    from gguf_train_b200 import _C
+
+    O.manual_seed(62)
+    B, Hkv, Smax, D, n_new = 1, 2, 64, 64, 4
+    base = (O.randn(B, Hkv, Smax, D)).astype(np.float32)
+    new = (O.randn(B, Hkv, n_new, D)).astype(np.float32)
+    cache = gtb.quantize_q8_0(torch.tensor(base).cuda())
+    before = cache.cpu().numpy().copy()
+    pos = torch.tensor([Smax - 2], dtype=torch.int32, device="cuda")
+    gtb.q8_0_append(cache, torch.tensor(new).cuda(), pos, advance=False)
+    assert _C.device_status() == 60
+    assert _C.device_status() == 0  # read and cleared
+    got = cache.cpu().numpy()
+    want_rows = O.q8_0_quantize(new[:, :, :2].reshape(-1, D)).reshape(B, Hkv, 2, D // 32 * 34)
+    assert np.array_equal(got[:, :, Smax - 2:], want_rows)
+    assert np.array_equal(got[:, :, :Smax - 2], before[:, :, :Smax - 2])
+    assert pos.cpu().tolist() == [Smax - 2]
