@@ -538,7 +538,7 @@ def main() -> None:
         "status": status,
     }
     if not args.no_extra:
-        del q, k, v, qh, kh, vh, oh, qd, kd, vd
+        del q, k, v, qh, kh, vh, oh
         torch.cuda.empty_cache()
         barrier()
         line["extra"] = {"fwd_bwd": run_train(args, rank, world, dev, max_over_ranks)}
