@@ -57,6 +57,12 @@ def _configure(lib: ctypes.CDLL) -> ctypes.CDLL:
     lib.gtb_q8_0_append.argtypes = [c_void_p, c_int, c_int64, c_int64, c_int64, c_int64, c_void_p, c_int64, c_void_p,
                                     c_int, c_void_p]
     lib.gtb_q8_0_append.restype = c_int
+    lib.gtb_q8_0_append_rope.argtypes = [c_void_p, c_int, c_int64, c_int64, c_int64, c_int64, c_void_p, c_int64,
+                                         c_void_p, c_int, c_int, c_int, c_float, c_float, c_void_p]
+    lib.gtb_q8_0_append_rope.restype = c_int
+    lib.gtb_rope.argtypes = [c_void_p, c_int, c_int64, c_int64, c_int64, c_int64, c_void_p, c_int64, c_int, c_int,
+                             c_float, c_float, c_int, c_void_p, c_void_p]
+    lib.gtb_rope.restype = c_int
     lib.gtb_q8_0_dequantize.argtypes = [c_void_p, c_int64, c_int64, c_void_p, c_int, c_void_p]
     lib.gtb_q8_0_dequantize.restype = c_int
     lib.gtb_decode_q8_0.argtypes = [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64,

@@ -11,7 +11,7 @@ is an ImportError, never a silent fallback.
 from . import _C
 from . import functional
 from . import handles
-from .functional import (FlashAttentionFn, decode_q8_0, dequantize_q8_0, q8_0_append, quantize_q8_0,
+from .functional import (FlashAttentionFn, RoPEFn, decode_q8_0, dequantize_q8_0, q8_0_append, quantize_q8_0, rope,
                          scaled_dot_product_attention, sdpa_from_host)
 from .modules import MultiheadAttention
 
@@ -25,6 +25,8 @@ __all__ = [
     "sdpa_from_host",
     "quantize_q8_0",
     "q8_0_append",
+    "rope",
+    "RoPEFn",
     "dequantize_q8_0",
     "decode_q8_0",
 ]

@@ -15,6 +15,7 @@
 
 #include "gtb_common.cuh"
 #include "q8_0_internal.h"
+#include "rope.cuh"
 #include "sdpa_args.h"
 
 namespace gtb {
@@ -172,6 +173,29 @@ void keep_pool_memory(int dev) {
 int env_int(const char* name, int dflt) {
     const char* e = getenv(name);
     return e ? atoi(e) : dflt;
+}
+
+// RoPE arguments with the reference's checks and messages (gt_rope_check, csrc/gt_ops_nn.cpp:2316-2357)
+bool rope_args(int64_t D, int n_dims, int mode, float freq_base, float freq_scale, bool backward, RopeArgs& r) {
+    if (mode != 0 && mode != 2) {
+        set_errorf("rope: mode must be 0 (normal) or 2 (NeoX), got %d; the multi-dimensional modes need per-section "
+                   "position ids and are not supported", mode);
+        return false;
+    }
+    if (n_dims < 2 || n_dims % 2 != 0 || n_dims > D) {
+        set_errorf("rope: n_dims must be an even number between 2 and the head dimension %lld, got %d", (long long)D, n_dims);
+        return false;
+    }
+    if (!(freq_base > 0.0f) || !std::isfinite(freq_base) || !std::isfinite(freq_scale)) {
+        set_error("rope: freq_base must be positive and finite, and freq_scale finite");
+        return false;
+    }
+    r.n_dims = n_dims;
+    r.mode = mode;
+    r.theta_scale = powf(freq_base, -2.0f / (float)n_dims);
+    r.freq_scale = freq_scale;
+    r.sin_sign = backward ? -1.0f : 1.0f;
+    return true;
 }
 
 // The two side streams of gtb_sdpa_fwd_host on a device (host -> device and device -> host copies),
@@ -494,7 +518,58 @@ GTB_API int gtb_q8_0_append(const void* x, int x_dtype, int64_t B, int64_t Hkv, 
         if (!check_device_ptr(x, ctx, "x") || !check_device_ptr(cache, ctx, "cache")) return -1;
     }
     if (!check_device_ptr(pos, ctx, "pos")) return -1;
-    return launch_q8_0_append(x, x_dtype, B, Hkv, n_new, D, cache, Smax, pos, advance != 0, (cudaStream_t)stream);
+    return launch_q8_0_append(x, x_dtype, B, Hkv, n_new, D, cache, Smax, pos, advance != 0, nullptr, (cudaStream_t)stream);
+}
+
+GTB_API int gtb_q8_0_append_rope(const void* x, int x_dtype, int64_t B, int64_t Hkv, int64_t n_new, int64_t D,
+                                 void* cache, int64_t Smax, int32_t* pos, int advance, int n_dims, int mode,
+                                 float freq_base, float freq_scale, void* stream) {
+    const char* ctx = "q8_0_append";
+    if (B < 0 || Hkv < 0 || n_new < 0 || D < 0 || Smax < 0) {
+        set_errorf("%s: negative size", ctx);
+        return -1;
+    }
+    if (D % 32 != 0) {
+        set_error("Tensor size must be a multiple of ggml quantization block size");
+        return -1;
+    }
+    if (n_new > INT32_MAX) {
+        set_errorf("%s: n_new must fit in int32", ctx);
+        return -1;
+    }
+    RopeArgs ra;
+    if (!rope_args(D, n_dims, mode, freq_base, freq_scale, false, ra)) return -1;
+    if (B == 0 || n_new == 0) return 0;
+    if (D > 0 && Hkv > 0) {
+        if (!check_device_ptr(x, ctx, "x") || !check_device_ptr(cache, ctx, "cache")) return -1;
+    }
+    if (!check_device_ptr(pos, ctx, "pos")) return -1;
+    return launch_q8_0_append(x, x_dtype, B, Hkv, n_new, D, cache, Smax, pos, advance != 0, &ra, (cudaStream_t)stream);
+}
+
+GTB_API int gtb_rope(const void* x, int dtype, int64_t B, int64_t H, int64_t S, int64_t D, const int32_t* pos,
+                     int64_t n_pos, int n_dims, int mode, float freq_base, float freq_scale, int backward, void* out,
+                     void* stream) {
+    if (B < 0 || H < 0 || S < 0 || D < 0) {
+        set_error("rope: negative size");
+        return -1;
+    }
+    if (dtype != F32 && dtype != F16 && dtype != BF16) {
+        set_error("rope: x must be f32, f16 or bf16");
+        return -1;
+    }
+    RopeArgs ra;
+    if (!rope_args(D, n_dims, mode, freq_base, freq_scale, backward != 0, ra)) return -1;
+    if (n_pos < S) {
+        set_errorf("rope: pos must be a 1-D tensor with a position for each of the %lld sequence elements, got %lld",
+                   (long long)S, (long long)n_pos);
+        return -1;
+    }
+    const int64_t rows = B * H * S;
+    if (rows == 0 || D == 0) return 0;
+    if (!check_device_ptr(x, "rope", "x") || !check_device_ptr(out, "rope", "out") || !check_device_ptr(pos, "rope", "pos"))
+        return -1;
+    return launch_rope(x, dtype, rows, S, D, pos, ra, out, (cudaStream_t)stream);
 }
 
 GTB_API int gtb_q8_0_dequantize(const void* blocks, int64_t n_rows, int64_t row_len, void* out, int out_dtype,

@@ -20,6 +20,7 @@
 
 #include "gtb_common.cuh"
 #include "q8_0_internal.h"
+#include "rope.cuh"
 
 namespace gtb {
 namespace {
@@ -29,16 +30,11 @@ constexpr int QBYTES = 34;
 
 // ------------------------------------------------------------------ quantise / dequantise
 
-// one 32-value block of x into the 34-byte block at `dst` (2-byte aligned)
-template <typename T>
-__device__ __forceinline__ void quantize_block(const T* __restrict__ xb, uint8_t* __restrict__ dst) {
-    float v[QK];
+// 32 values into the 34-byte block at `dst` (2-byte aligned)
+__device__ __forceinline__ void quantize_floats(const float* v, uint8_t* __restrict__ dst) {
     float amax = 0.0f;
 #pragma unroll
-    for (int j = 0; j < QK; ++j) {
-        v[j] = (float)Elem<T>::load(xb + j);
-        amax = fmaxf(amax, fabsf(v[j]));
-    }
+    for (int j = 0; j < QK; ++j) amax = fmaxf(amax, fabsf(v[j]));
     const float d = __fdiv_rn(amax, 127.0f);
     const float id = d != 0.0f ? __frcp_rn(d) : 0.0f;
     // the 34-byte block as 17 little-endian 16-bit words (blocks start 2-byte aligned)
@@ -52,6 +48,15 @@ __device__ __forceinline__ void quantize_block(const T* __restrict__ xb, uint8_t
     }
 }
 
+// one 32-value block of x into the 34-byte block at `dst`
+template <typename T>
+__device__ __forceinline__ void quantize_block(const T* __restrict__ xb, uint8_t* __restrict__ dst) {
+    float v[QK];
+#pragma unroll
+    for (int j = 0; j < QK; ++j) v[j] = (float)Elem<T>::load(xb + j);
+    quantize_floats(v, dst);
+}
+
 template <typename T>
 __global__ void q8_0_quantize_kernel(const T* __restrict__ x, int64_t nblocks, uint8_t* __restrict__ out) {
     const int64_t blk = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -62,10 +67,12 @@ __global__ void q8_0_quantize_kernel(const T* __restrict__ x, int64_t nblocks, u
 // KV-cache append: block j of row t of (sequence b, kv head hk) of x (B, Hkv, n_new, D) goes to
 // cache row pos[b] + t of (B, Hkv, Smax, D/32 blocks). A row outside [0, Smax) is not written and
 // records status 60.
-template <typename T>
+// With ROPE, each new row is first rotated for its cache position pos[b] + t (rope.cuh), in f32,
+// so the cache holds the quantised rotated keys without an intermediate rounding.
+template <typename T, bool ROPE>
 __global__ void q8_0_append_kernel(const T* __restrict__ x, int64_t Hkv, int64_t n_new, int64_t nb_row,
                                    uint8_t* __restrict__ cache, int64_t Smax, const int32_t* __restrict__ pos,
-                                   int64_t nblocks, int* status) {
+                                   int64_t nblocks, int* status, RopeArgs ra) {
     const int64_t blk = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (blk >= nblocks) return;
     const int64_t j = blk % nb_row, r = blk / nb_row;  // r over (b, hk, t)
@@ -75,7 +82,30 @@ __global__ void q8_0_append_kernel(const T* __restrict__ x, int64_t Hkv, int64_t
         if (status) atomicCAS(status, 0, 60);
         return;
     }
-    quantize_block(x + blk * QK, cache + ((bh * Smax + row) * nb_row + j) * QBYTES);
+    uint8_t* dst = cache + ((bh * Smax + row) * nb_row + j) * QBYTES;
+    if constexpr (!ROPE) {
+        quantize_block(x + blk * QK, dst);
+    } else {
+        const T* xr = x + r * nb_row * QK;  // the whole row: a NeoX partner can sit in another block
+        float v[QK];
+#pragma unroll 4
+        for (int e = 0; e < QK; ++e) {
+            const int c = (int)(j * QK) + e;
+            float xc = (float)Elem<T>::load(xr + c);
+            if (c < ra.n_dims) {
+                const int half = ra.n_dims / 2;
+                const bool first = ra.mode == 2 ? c < half : (c & 1) == 0;
+                const int i = ra.mode == 2 ? (first ? c : c - half) : c >> 1;
+                const int partner = ra.mode == 2 ? (first ? c + half : c - half) : (c ^ 1);
+                const float xp = (float)Elem<T>::load(xr + partner);
+                float x0 = first ? xc : xp, x1 = first ? xp : xc;
+                rope_rotate(ra, (int)row, i, x0, x1);
+                xc = first ? x0 : x1;
+            }
+            v[e] = xc;
+        }
+        quantize_floats(v, dst);
+    }
 }
 
 __global__ void q8_0_advance_kernel(int32_t* pos, int64_t B, int32_t n_new) {
@@ -552,21 +582,31 @@ int launch_q8_0_quantize(const void* x, int x_dtype, int64_t nblocks, void* out,
     return cuda_failed(cudaGetLastError(), "q8_0 quantize launch") ? -1 : 0;
 }
 
+template <bool ROPE>
+void append_launch(const void* x, int x_dtype, unsigned grid, int64_t Hkv, int64_t n_new, int64_t nb_row, uint8_t* c,
+                   int64_t Smax, const int32_t* pos, int64_t nblocks, int* status, const RopeArgs& ra, cudaStream_t st) {
+    switch (x_dtype) {
+        case F32: q8_0_append_kernel<float, ROPE><<<grid, 128, 0, st>>>((const float*)x, Hkv, n_new, nb_row, c, Smax, pos, nblocks, status, ra); break;
+        case F16: q8_0_append_kernel<__half, ROPE><<<grid, 128, 0, st>>>((const __half*)x, Hkv, n_new, nb_row, c, Smax, pos, nblocks, status, ra); break;
+        default: q8_0_append_kernel<__nv_bfloat16, ROPE><<<grid, 128, 0, st>>>((const __nv_bfloat16*)x, Hkv, n_new, nb_row, c, Smax, pos, nblocks, status, ra); break;
+    }
+}
+
 int launch_q8_0_append(const void* x, int x_dtype, int64_t B, int64_t Hkv, int64_t n_new, int64_t D, void* cache,
-                       int64_t Smax, int32_t* pos, bool advance, cudaStream_t st) {
+                       int64_t Smax, int32_t* pos, bool advance, const RopeArgs* rope, cudaStream_t st) {
     const int64_t nb_row = D / QK, nblocks = B * Hkv * n_new * nb_row;
+    if (x_dtype != F32 && x_dtype != F16 && x_dtype != BF16) {
+        set_error("q8_0_append: the new rows must be f32, f16 or bf16");
+        return -1;
+    }
     int dev = 0;
     cudaGetDevice(&dev);
     int* status = device_status_word(dev);
     if (nblocks > 0) {
         const unsigned grid = (unsigned)((nblocks + 127) / 128);
         uint8_t* c = (uint8_t*)cache;
-        switch (x_dtype) {
-            case F32: q8_0_append_kernel<float><<<grid, 128, 0, st>>>((const float*)x, Hkv, n_new, nb_row, c, Smax, pos, nblocks, status); break;
-            case F16: q8_0_append_kernel<__half><<<grid, 128, 0, st>>>((const __half*)x, Hkv, n_new, nb_row, c, Smax, pos, nblocks, status); break;
-            case BF16: q8_0_append_kernel<__nv_bfloat16><<<grid, 128, 0, st>>>((const __nv_bfloat16*)x, Hkv, n_new, nb_row, c, Smax, pos, nblocks, status); break;
-            default: set_error("q8_0_append: the new rows must be f32, f16 or bf16"); return -1;
-        }
+        if (rope) append_launch<true>(x, x_dtype, grid, Hkv, n_new, nb_row, c, Smax, pos, nblocks, status, *rope, st);
+        else append_launch<false>(x, x_dtype, grid, Hkv, n_new, nb_row, c, Smax, pos, nblocks, status, RopeArgs{}, st);
         if (cuda_failed(cudaGetLastError(), "q8_0 append launch")) return -1;
     }
     if (advance && n_new > 0 && B > 0) {

@@ -23,8 +23,13 @@ int launch_q8_0_quantize(const void* x, int x_dtype, int64_t nblocks, void* out,
 int launch_q8_0_dequantize(const void* blocks, int64_t nblocks, void* out, int out_dtype, cudaStream_t st);
 // KV-cache append (x (B, Hkv, n_new, D) into cache rows pos[b] .. pos[b] + n_new - 1), then pos += n_new
 // when `advance` (a second kernel, so every row's destination is read before it changes)
+// (rope: rotate each new row for its cache position first; nullptr for none)
+struct RopeArgs;
 int launch_q8_0_append(const void* x, int x_dtype, int64_t B, int64_t Hkv, int64_t n_new, int64_t D, void* cache,
-                       int64_t Smax, int32_t* pos, bool advance, cudaStream_t st);
+                       int64_t Smax, int32_t* pos, bool advance, const RopeArgs* rope, cudaStream_t st);
+// RoPE of rows (rows = B*H*S of D values, position pos[row % S]) into out (rope.cu)
+int launch_rope(const void* x, int dtype, int64_t rows, int64_t S, int64_t D, const int32_t* pos, const RopeArgs& r,
+                void* out, cudaStream_t st);
 int64_t decode_num_chunks(int64_t Smax);
 // Scratch of one decode call: a work area of decode_work_bytes() for the persistent kernels (item
 // counter, per-sequence item prefix [B + 1], per-sequence prefix of full-chunk items [B + 1], and at

@@ -276,13 +276,15 @@ def quantize_q8_0(x: torch.Tensor) -> torch.Tensor:
     return out
 
 
-def q8_0_append(cache: torch.Tensor, x: torch.Tensor, pos: torch.Tensor, advance: bool = True) -> torch.Tensor:
+def q8_0_append(cache: torch.Tensor, x: torch.Tensor, pos: torch.Tensor, advance: bool = True,
+                rope: dict | None = None) -> torch.Tensor:
     """Append new rows to a Q8_0 KV cache on the device: x (B, Hkv, n_new, D) is quantised (bit for bit
     as quantize_q8_0) into rows pos[b] .. pos[b] + n_new - 1 of cache (B, Hkv, Smax, D/32*34) uint8,
     the layout decode_q8_0 reads; pos (B) int32 holds the sequences' current lengths (decode_q8_0's
-    seq_lens) and, with `advance`, is increased by n_new afterwards. Rows that would fall outside
-    the cache are skipped and leave status 60 in the device status word (_C.device_status()).
-    Returns cache."""
+    seq_lens) and, with `advance`, is increased by n_new afterwards. With `rope` (a dict of rope()'s
+    n_dims, mode, freq_base, freq_scale) each row is first rotated for its cache position, in f32.
+    Rows that would fall outside the cache are skipped and leave status 60 in the device status word
+    (_C.device_status()). Returns cache."""
     _require_cuda("q8_0_append", cache, x, pos)
     if x.ndim != 4 or cache.ndim != 4:
         raise RuntimeError("q8_0_append: x must be (B, Hkv, n_new, D) and cache (B, Hkv, Smax, D/32*34)")
@@ -295,11 +297,67 @@ def q8_0_append(cache: torch.Tensor, x: torch.Tensor, pos: torch.Tensor, advance
     if pos.dtype != torch.int32 or tuple(pos.shape) != (B,) or not pos.is_contiguous():
         raise RuntimeError(f"q8_0_append: pos must be a contiguous int32 tensor of shape ({B},)")
     x = x.contiguous()
-    rc = _C.lib.gtb_q8_0_append(x.data_ptr() if x.numel() else None, _code(x), B, Hkv, n_new, D,
-                                cache.data_ptr() if cache.numel() else None, cache.shape[2],
-                                pos.data_ptr() if pos.numel() else None, 1 if advance else 0, _stream(x.device))
+    args = (x.data_ptr() if x.numel() else None, _code(x), B, Hkv, n_new, D,
+            cache.data_ptr() if cache.numel() else None, cache.shape[2],
+            pos.data_ptr() if pos.numel() else None, 1 if advance else 0)
+    if rope is None:
+        rc = _C.lib.gtb_q8_0_append(*args, _stream(x.device))
+    else:
+        r = {"n_dims": D, "mode": 0, "freq_base": 10000.0, "freq_scale": 1.0}
+        r.update(rope)
+        rc = _C.lib.gtb_q8_0_append_rope(*args, int(r["n_dims"]), int(r["mode"]), float(r["freq_base"]),
+                                         float(r["freq_scale"]), _stream(x.device))
     _C.check_rc(rc, "q8_0_append")
     return cache
+
+
+def _rope_run(x, positions, n_dims, mode, freq_base, freq_scale, backward):
+    _require_cuda("rope", x, positions)
+    if x.ndim < 3 or x.ndim > 4:
+        raise RuntimeError(f"rope: expected x of shape (batch, heads, seq_len, head_dim) or (heads, seq_len, head_dim), "
+                           f"got {list(x.shape)}")
+    if x.dtype not in (torch.float32, torch.float16, torch.bfloat16):
+        raise RuntimeError("rope: x must be f32, f16 or bf16")
+    if positions.ndim != 1:
+        raise RuntimeError(f"rope: pos must be a 1-D tensor with a position for each of the {x.shape[-2]} sequence "
+                           f"elements, got shape {list(positions.shape)}")
+    B = x.shape[0] if x.ndim == 4 else 1
+    H, S, D = x.shape[-3], x.shape[-2], x.shape[-1]
+    x = x.contiguous()
+    pos = positions.to(torch.int32).contiguous()
+    out = torch.empty_like(x)
+    rc = _C.lib.gtb_rope(x.data_ptr() if x.numel() else None, _code(x), B, H, S, D,
+                         pos.data_ptr() if pos.numel() else None, pos.numel(), int(n_dims), int(mode),
+                         float(freq_base), float(freq_scale), 1 if backward else 0,
+                         out.data_ptr() if out.numel() else None, _stream(x.device))
+    _C.check_rc(rc, "rope")
+    return out
+
+
+class RoPEFn(torch.autograd.Function):
+    """gguf_train's RoPEFn (_functions.py:1906-1919): forward gt_rope, backward gt_rope_backward (the
+    rotation by -angle), both on the device."""
+
+    @staticmethod
+    def forward(ctx, x, pos, n_dims: int, mode: int, n_ctx_orig: int, freq_base: float, freq_scale: float):
+        ctx.args = (n_dims, mode, float(freq_base), float(freq_scale))
+        ctx.save_for_backward(pos)
+        return _rope_run(x, pos, n_dims, mode, freq_base, freq_scale, False)
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        (pos,) = ctx.saved_tensors
+        n_dims, mode, fb, fs = ctx.args
+        return _rope_run(grad_out, pos, n_dims, mode, fb, fs, True), None, None, None, None, None, None
+
+
+def rope(input: torch.Tensor, positions: torch.Tensor, n_dims: int | None = None, mode: int = 0, n_ctx_orig: int = 0,
+         freq_base: float = 10000.0, freq_scale: float = 1.0) -> torch.Tensor:
+    """gguf_train's F.rope (nn/functional.py:770-772) on CUDA tensors: rotary position embedding of x
+    (B, H, S, D) or (H, S, D) with one position per sequence element (n_ctx_orig is accepted and, as
+    with ggml's ext_factor 0 that the reference passes, has no effect)."""
+    nd = input.shape[-1] if n_dims is None else int(n_dims)
+    return RoPEFn.apply(input, positions, nd, int(mode), int(n_ctx_orig), float(freq_base), float(freq_scale))
 
 
 def dequantize_q8_0(blocks: torch.Tensor, dtype=torch.float32) -> torch.Tensor:

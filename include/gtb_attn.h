@@ -95,6 +95,24 @@ GTB_API int gtb_q8_0_quantize(const void *x, int x_dtype, int64_t n_rows, int64_
 GTB_API int gtb_q8_0_append(const void *x, int x_dtype, int64_t B, int64_t Hkv, int64_t n_new, int64_t D,
                             void *cache, int64_t Smax, int32_t *pos, int advance, void *stream);
 
+/* The same with each new row first rotated (RoPE, as gtb_rope with backward = 0) for its cache
+ * position pos[b] + t, in f32 before quantising: the rotated keys land in the cache without an
+ * intermediate rounding. Replaces gt_rope (csrc/gt_ops_nn.cpp:2409) followed by the quantising append. */
+GTB_API int gtb_q8_0_append_rope(const void *x, int x_dtype, int64_t B, int64_t Hkv, int64_t n_new, int64_t D,
+                                 void *cache, int64_t Smax, int32_t *pos, int advance, int n_dims, int mode,
+                                 float freq_base, float freq_scale, void *stream);
+
+/* Rotary position embedding on the device. Replaces gt_rope / gt_rope_backward (reference
+ * csrc/gt_ops_nn.cpp:2409-2421, ggml_rope_ext with ext_factor 0, attn_factor 1): x, out (B, H, S, D)
+ * contiguous f32/f16/bf16 (computed in f32, stored in x's type), pos device int32 with n_pos >= S
+ * entries (one per sequence element, shared by batch and heads), n_dims even in [2, D], mode 0
+ * (pairs 2i, 2i+1) or 2 (NeoX: pairs i, i + n_dims/2), angle of pair i = freq_scale * p *
+ * freq_base^(-2i/n_dims) accumulated as ggml's rope cache does; backward != 0 rotates by -angle.
+ * Error texts are the reference's. */
+GTB_API int gtb_rope(const void *x, int dtype, int64_t B, int64_t H, int64_t S, int64_t D, const int32_t *pos,
+                     int64_t n_pos, int n_dims, int mode, float freq_base, float freq_scale, int backward, void *out,
+                     void *stream);
+
 /* Q8_0 -> f32/f16/bf16 (out_dtype), x = q * d. Replaces gt_dequantize (csrc/gt_ops_extra.cpp:2006). */
 GTB_API int gtb_q8_0_dequantize(const void *blocks, int64_t n_rows, int64_t row_len,
                                 void *out, int out_dtype, void *stream);

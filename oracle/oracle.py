@@ -180,6 +180,36 @@ def sdpa_bwd(q, k, v, dout, mask=None, mask_is_bool=False, scale: float | None =
 
 # ------------------------------------------------------------------ Q8_0
 
+def rope(x, pos, n_dims: int, mode: int = 0, freq_base: float = 10000.0, freq_scale: float = 1.0,
+         backward: bool = False) -> np.ndarray:
+    """gt_rope / gt_rope_backward (reference csrc/gt_ops_nn.cpp:2359-2421): ggml_rope_ext with
+    ext_factor 0 and attn_factor 1 on x (..., S, D), one position per sequence element. Restates
+    ggml's CPU rope (llama.cpp b12283, not vendored: the rope cache loop and rope_yarn) in float32:
+    theta starts at p and is multiplied by theta_scale = powf(freq_base, -2/n_dims) after each pair,
+    rotated angle = freq_scale * theta, mode 0 pairs (2i, 2i+1), mode 2 (NeoX) pairs (i, i + n_dims/2),
+    x0' = x0 cos - x1 sin, x1' = x0 sin + x1 cos (sin negated for the backward); later dims copied.
+    powf, cosf and sinf are taken as glibc gives them, correctly rounded: evaluated in float64 and
+    rounded once (numpy's float32 power and trigonometry can be an ulp or more away)."""
+    x = np.asarray(x, np.float32)
+    out = x.copy()
+    f32 = np.float32
+    theta_scale = f32(np.float64(f32(freq_base)) ** (np.float64(f32(-2.0) / f32(n_dims))))
+    half = n_dims // 2
+    for s in range(x.shape[-2]):
+        theta = f32(pos[s])
+        for i in range(half):
+            t = f32(f32(freq_scale) * theta)
+            c, sn = f32(np.cos(np.float64(t))), f32(np.sin(np.float64(t)))
+            if backward:
+                sn = -sn
+            c0, c1 = (i, i + half) if mode == 2 else (2 * i, 2 * i + 1)
+            x0, x1 = x[..., s, c0], x[..., s, c1]
+            out[..., s, c0] = x0 * c - x1 * sn
+            out[..., s, c1] = x0 * sn + x1 * c
+            theta = f32(theta * theta_scale)
+    return out
+
+
 def q8_0_quantize(x) -> np.ndarray:
     """Q8_0 blocks (34 B per 32 values) of x, rows along the last dim (gt_core.cpp:792-840)."""
     x = np.ascontiguousarray(x, dtype=np.float32)

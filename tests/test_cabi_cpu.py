@@ -165,3 +165,24 @@ def test_q8_0_append_argument_checks():
     rc, msg = call(dtype=_C.GT_F64)
     assert rc != 0 and "f32, f16 or bf16" in msg
     assert call(n_new=0)[0] == 0  # nothing to append
+
+
+def test_rope_argument_checks_use_the_reference_messages():
+    """gtb_rope checks mode, n_dims, the frequencies and the positions with gt_rope_check's messages
+    (csrc/gt_ops_nn.cpp:2316-2357) before any device work."""
+    from gguf_train_b200 import _C
+
+    def call(mode=0, n_dims=8, base=10000.0, n_pos=4):
+        rc = _C.lib.gtb_rope(None, _C.GT_F32, 1, 1, 4, 8, None, n_pos, n_dims, mode, base, 1.0, 0, None, None)
+        return rc, _C.lib.gtb_last_error().decode()
+
+    rc, msg = call(mode=1)
+    assert rc != 0 and "mode must be 0 (normal) or 2 (NeoX)" in msg
+    rc, msg = call(n_dims=3)
+    assert rc != 0 and "n_dims must be an even number between 2 and the head dimension 8" in msg
+    rc, msg = call(n_dims=10)
+    assert rc != 0 and "n_dims must be an even number" in msg
+    rc, msg = call(base=0.0)
+    assert rc != 0 and "freq_base must be positive and finite" in msg
+    rc, msg = call(n_pos=3)
+    assert rc != 0 and "a position for each of the 4 sequence elements" in msg

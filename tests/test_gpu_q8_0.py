@@ -181,3 +181,58 @@ def test_append_past_the_cache_end_is_skipped_and_reported():
     assert np.array_equal(got[:, :, Smax - 2:], want_rows)
     assert np.array_equal(got[:, :, :Smax - 2], before[:, :, :Smax - 2])
     assert pos.cpu().tolist() == [Smax - 2]
+
+
+@pytest.mark.parametrize("dtype,B,H,S,D,n_dims,mode,base,fscale", [
+    ("f32", 2, 3, 40, 64, 64, 0, 10000.0, 1.0),
+    ("f32", 1, 4, 33, 128, 128, 2, 500000.0, 1.0),   # NeoX, llama-3 base
+    ("f32", 2, 2, 17, 96, 32, 0, 10000.0, 0.25),     # partial rotation, linear position scaling
+    ("bf16", 2, 8, 64, 128, 128, 2, 10000.0, 1.0),
+])
+def test_rope_matches_oracle(dtype, B, H, S, D, n_dims, mode, base, fscale):
+    """rope (forward) and its backward through RoPEFn against the oracle's restatement of ggml's
+    rope, at positions up to 5000 (f32: 2e-5 abs; the angles, a few thousand radians, agree to the
+    float ulp and CUDA's sincosf is within 2 ulp of the correctly rounded value; bf16: 2e-2 / 1e-2)."""
+    import torch
+
+    import gguf_train_b200 as gtb
+    from gguf_train_b200 import _C
+
+    O.manual_seed(71 + S)
+    x = seeded((B, H, S, D), dtype)
+    g = seeded((B, H, S, D), dtype)
+    pos = (np.arange(S) * 97 + 3) % 5000
+    tx = to_dev(x, dtype, True)
+    y = gtb.rope(tx, torch.tensor(pos, dtype=torch.int32).cuda(), n_dims, mode, 0, base, fscale)
+    y.backward(to_dev(g, dtype))
+    assert _C.device_status() == 0
+    want = O.rope(x, pos, n_dims, mode, base, fscale)
+    gwant = O.rope(g, pos, n_dims, mode, base, fscale, backward=True)
+    atol, rtol = (2e-5, 1e-5) if dtype == "f32" else (2e-2, 1e-2)
+    assert_close(y, want, atol, rtol, "rope forward")
+    assert_close(tx.grad, gwant, atol, rtol, "rope backward")
+
+
+def test_append_with_rope_equals_rope_then_quantise():
+    """q8_0_append with rope rotates each new row for its cache position and quantises the f32 result:
+    for f32 rows that is bit for bit rope() at those positions followed by quantize_q8_0."""
+    import torch
+
+    import gguf_train_b200 as gtb
+    from gguf_train_b200 import _C
+
+    O.manual_seed(73)
+    B, Hkv, Smax, D, n_new = 3, 2, 96, 128, 5
+    lens = [0, 17, 90]
+    cfg = dict(n_dims=128, mode=2, freq_base=10000.0, freq_scale=1.0)
+    new = torch.tensor(O.randn(B, Hkv, n_new, D).astype(np.float32)).cuda()
+    cache = torch.zeros((B, Hkv, Smax, D // 32 * 34), dtype=torch.uint8, device="cuda")
+    pos = torch.tensor(lens, dtype=torch.int32, device="cuda")
+    gtb.q8_0_append(cache, new, pos, rope=cfg)
+    assert _C.device_status() == 0
+    for b in range(B):
+        positions = torch.arange(lens[b], lens[b] + n_new, dtype=torch.int32, device="cuda")
+        rotated = gtb.rope(new[b:b + 1], positions, cfg["n_dims"], cfg["mode"], 0, cfg["freq_base"], cfg["freq_scale"])
+        want = gtb.quantize_q8_0(rotated)
+        assert torch.equal(cache[b:b + 1, :, lens[b]:lens[b] + n_new], want)
+    assert pos.cpu().tolist() == [n + n_new for n in lens]

@@ -176,3 +176,26 @@ def test_mha_oracle_matches_torch_float64():
     assert np.abs(dw_in - m.in_proj_weight.grad.numpy()).max() < 1e-6
     assert np.abs(db_in - m.in_proj_bias.grad.numpy()).max() < 1e-6
     assert np.abs(dw_out - m.out_proj.weight.grad.numpy()).max() < 1e-9
+
+
+def test_rope_oracle_properties():
+    """The RoPE restatement: position 0 is the identity, each pair keeps its length, the backward
+    undoes the forward, NeoX mode is normal mode on the interleaved dims, and dims past n_dims are
+    copied; theta_scale is powf's correctly rounded value (0.7498942 for base 10000, n_dims 64)."""
+    rs = np.random.RandomState(7)
+    x = rs.randn(2, 3, 6, 16).astype(np.float32)
+    pos = [0, 1, 5, 100, 4096, 7]
+    y = O.rope(x, pos, 16)
+    assert np.array_equal(y[:, :, 0], x[:, :, 0])
+    pair = lambda a: a[..., 0::2] ** 2 + a[..., 1::2] ** 2  # noqa: E731
+    assert np.allclose(pair(y), pair(x), rtol=1e-5, atol=1e-6)
+    assert np.allclose(O.rope(y, pos, 16, backward=True), x, atol=1e-5)
+    perm = np.concatenate([np.arange(0, 16, 2), np.arange(1, 16, 2)])  # interleaved -> halves
+    yn = O.rope(x[..., perm], pos, 16, mode=2)
+    assert np.allclose(yn, y[..., perm], atol=1e-6)
+    yp = O.rope(x, pos, 8)
+    assert np.array_equal(yp[..., 8:], x[..., 8:])
+    # pair 1 at position 1 turns by exactly theta_scale
+    e = np.zeros((1, 2, 64), np.float32)
+    e[0, 1, 2] = 1.0
+    assert O.rope(e, [0, 1], 64)[0, 1, 3] == np.float32(np.sin(np.float64(np.float32(0.7498942))))
