@@ -198,6 +198,39 @@ bool rope_args(int64_t D, int n_dims, int mode, float freq_base, float freq_scal
     return true;
 }
 
+// Sizes and dtype of a Q8_0 cache append (both entry points)
+bool append_args_ok(int x_dtype, int64_t B, int64_t Hkv, int64_t n_new, int64_t D, int64_t Smax) {
+    if (B < 0 || Hkv < 0 || n_new < 0 || D < 0 || Smax < 0) {
+        set_error("q8_0_append: negative size");
+        return false;
+    }
+    if (D % 32 != 0) {
+        set_error("Tensor size must be a multiple of ggml quantization block size");
+        return false;
+    }
+    if (n_new > INT32_MAX) {
+        set_error("q8_0_append: n_new must fit in int32");
+        return false;
+    }
+    if (x_dtype != F32 && x_dtype != F16 && x_dtype != BF16) {
+        set_error("q8_0_append: the new rows must be f32, f16 or bf16");
+        return false;
+    }
+    return true;
+}
+
+// pointers checked, then the append kernel (and the length update) on `stream`
+int append_run(const void* x, int x_dtype, int64_t B, int64_t Hkv, int64_t n_new, int64_t D, void* cache, int64_t Smax,
+               int32_t* pos, int advance, const RopeArgs* rope, void* stream) {
+    const char* ctx = "q8_0_append";
+    if (B == 0 || n_new == 0) return 0;
+    if (D > 0 && Hkv > 0) {
+        if (!check_device_ptr(x, ctx, "x") || !check_device_ptr(cache, ctx, "cache")) return -1;
+    }
+    if (!check_device_ptr(pos, ctx, "pos")) return -1;
+    return launch_q8_0_append(x, x_dtype, B, Hkv, n_new, D, cache, Smax, pos, advance != 0, rope, (cudaStream_t)stream);
+}
+
 // The two side streams of gtb_sdpa_fwd_host on a device (host -> device and device -> host copies),
 // non-blocking, created once and kept for the process.
 struct HostCopyStreams {
@@ -496,55 +529,17 @@ GTB_API int gtb_q8_0_quantize(const void* x, int x_dtype, int64_t n_rows, int64_
 
 GTB_API int gtb_q8_0_append(const void* x, int x_dtype, int64_t B, int64_t Hkv, int64_t n_new, int64_t D, void* cache,
                             int64_t Smax, int32_t* pos, int advance, void* stream) {
-    const char* ctx = "q8_0_append";
-    if (B < 0 || Hkv < 0 || n_new < 0 || D < 0 || Smax < 0) {
-        set_errorf("%s: negative size", ctx);
-        return -1;
-    }
-    if (D % 32 != 0) {
-        set_error("Tensor size must be a multiple of ggml quantization block size");
-        return -1;
-    }
-    if (n_new > INT32_MAX) {
-        set_errorf("%s: n_new must fit in int32", ctx);
-        return -1;
-    }
-    if (x_dtype != F32 && x_dtype != F16 && x_dtype != BF16) {
-        set_errorf("%s: the new rows must be f32, f16 or bf16", ctx);
-        return -1;
-    }
-    if (B == 0 || n_new == 0) return 0;
-    if (D > 0 && Hkv > 0) {
-        if (!check_device_ptr(x, ctx, "x") || !check_device_ptr(cache, ctx, "cache")) return -1;
-    }
-    if (!check_device_ptr(pos, ctx, "pos")) return -1;
-    return launch_q8_0_append(x, x_dtype, B, Hkv, n_new, D, cache, Smax, pos, advance != 0, nullptr, (cudaStream_t)stream);
+    if (!append_args_ok(x_dtype, B, Hkv, n_new, D, Smax)) return -1;
+    return append_run(x, x_dtype, B, Hkv, n_new, D, cache, Smax, pos, advance, nullptr, stream);
 }
 
 GTB_API int gtb_q8_0_append_rope(const void* x, int x_dtype, int64_t B, int64_t Hkv, int64_t n_new, int64_t D,
                                  void* cache, int64_t Smax, int32_t* pos, int advance, int n_dims, int mode,
                                  float freq_base, float freq_scale, void* stream) {
-    const char* ctx = "q8_0_append";
-    if (B < 0 || Hkv < 0 || n_new < 0 || D < 0 || Smax < 0) {
-        set_errorf("%s: negative size", ctx);
-        return -1;
-    }
-    if (D % 32 != 0) {
-        set_error("Tensor size must be a multiple of ggml quantization block size");
-        return -1;
-    }
-    if (n_new > INT32_MAX) {
-        set_errorf("%s: n_new must fit in int32", ctx);
-        return -1;
-    }
+    if (!append_args_ok(x_dtype, B, Hkv, n_new, D, Smax)) return -1;
     RopeArgs ra;
     if (!rope_args(D, n_dims, mode, freq_base, freq_scale, false, ra)) return -1;
-    if (B == 0 || n_new == 0) return 0;
-    if (D > 0 && Hkv > 0) {
-        if (!check_device_ptr(x, ctx, "x") || !check_device_ptr(cache, ctx, "cache")) return -1;
-    }
-    if (!check_device_ptr(pos, ctx, "pos")) return -1;
-    return launch_q8_0_append(x, x_dtype, B, Hkv, n_new, D, cache, Smax, pos, advance != 0, &ra, (cudaStream_t)stream);
+    return append_run(x, x_dtype, B, Hkv, n_new, D, cache, Smax, pos, advance, &ra, stream);
 }
 
 GTB_API int gtb_rope(const void* x, int dtype, int64_t B, int64_t H, int64_t S, int64_t D, const int32_t* pos,
