@@ -158,6 +158,10 @@ def _configure(lib: ctypes.CDLL) -> ctypes.CDLL:
     lib.gt_flash_attention_backward.restype = c_int
     lib.gt_flash_decode_q8_0.argtypes = [c_void_p, c_void_p, c_void_p, c_void_p, c_float]
     lib.gt_flash_decode_q8_0.restype = c_void_p
+    lib.gt_rope.argtypes = [c_void_p, c_void_p, c_int, c_int, c_int, c_float, c_float]
+    lib.gt_rope.restype = c_void_p
+    lib.gt_rope_backward.argtypes = [c_void_p, c_void_p, c_int, c_int, c_int, c_float, c_float]
+    lib.gt_rope_backward.restype = c_void_p
     lib.gt_quantize.argtypes = [c_void_p, c_int]
     lib.gt_quantize.restype = c_void_p
     lib.gt_dequantize.argtypes = [c_void_p, c_int]

@@ -767,6 +767,94 @@ GT_API int gt_flash_attention_backward(const gt_tensor* grad_out, const gt_tenso
     return 0;
 }
 
+// a 1-D CUDA tensor of positions as contiguous int32 (values truncated toward zero), through the host:
+// positions are one per sequence element, so this is a few KB at most
+static gt_tensor* positions_i32(const gt_tensor* pos) {
+    const int64_t n = pos->numel;
+    std::vector<unsigned char> raw(bytes_for(pos->dtype, n));
+    std::vector<int32_t> v((size_t)n);
+    if (!raw.empty() && !read_contiguous(pos, raw.data())) return nullptr;
+    for (int64_t i = 0; i < n; ++i) {
+        const unsigned char* e = raw.data() + (size_t)i * elem_size(pos->dtype);
+        double x;
+        switch (pos->dtype) {
+            case GT_F32: { float f; std::memcpy(&f, e, 4); x = f; break; }
+            case GT_F64: std::memcpy(&x, e, 8); break;
+            case GT_I32: { int32_t k; std::memcpy(&k, e, 4); x = k; break; }
+            case GT_I64: { int64_t k; std::memcpy(&k, e, 8); x = (double)k; break; }
+            default:
+                set_error("rope: pos must be an integer or float32/float64 tensor");
+                return nullptr;
+        }
+        v[(size_t)i] = (int32_t)x;
+    }
+    gt_tensor* r = alloc_tensor(1, &n, GT_I32, GT_DEV_CUDA, pos->device_index);
+    if (r && n > 0 && gt_tensor_copy_from_host(r, v.data(), v.size() * 4) != 0) {
+        gt_tensor_free(r);
+        return nullptr;
+    }
+    return r;
+}
+
+// gt_rope / gt_rope_backward on CUDA tensors: x (B, H, S, D) or (H, S, D), pos 1-D with a position per
+// sequence element (converted to int32 as the reference does, gt_ops_nn.cpp:2367-2371)
+static gt_tensor* rope_handle(const gt_tensor* x, const gt_tensor* pos, int n_dims, int mode, float freq_base,
+                              float freq_scale, int backward) {
+    if (!x || !pos) {
+        set_error("rope: x and pos are required");
+        return nullptr;
+    }
+    if (x->ndim < 3 || x->ndim > 4) {
+        std::string sh = "[";
+        for (int i = 0; i < x->ndim; ++i) sh += (i ? ", " : "") + std::to_string(x->shape[i]);
+        set_errorf("rope: expected x of shape (batch, heads, seq_len, head_dim) or (heads, seq_len, head_dim), got %s]",
+                   sh.c_str());
+        return nullptr;
+    }
+    if (x->device_type != GT_DEV_CUDA || pos->device_type != GT_DEV_CUDA) {
+        set_error("rope: this engine runs CUDA tensors only (move x and pos with .to('cuda'))");
+        return nullptr;
+    }
+    if (pos->ndim != 1) {
+        set_errorf("rope: pos must be a 1-D tensor with a position for each of the %lld sequence elements",
+                   (long long)x->shape[x->ndim - 2]);
+        return nullptr;
+    }
+    const bool four = x->ndim == 4;
+    const int64_t B = four ? x->shape[0] : 1, H = x->shape[four ? 1 : 0], S = x->shape[four ? 2 : 1],
+                  D = x->shape[four ? 3 : 2];
+    gt_tensor* xc = contiguous(x) ? nullptr : gt_tensor_contiguous(x);
+    gt_tensor* pc = (pos->dtype == GT_I32 && contiguous(pos)) ? nullptr : positions_i32(pos);
+    const gt_tensor* xs = xc ? xc : x;
+    const gt_tensor* ps = pc ? pc : pos;
+    gt_tensor* out = (xs && ps) ? alloc_tensor(x->ndim, x->shape, x->dtype, GT_DEV_CUDA, x->device_index) : nullptr;
+    int rc = -1;
+    if (out) {
+        DeviceGuard g(x->device_index);
+        rc = gtb_rope(data_of(xs), xs->dtype, B, H, S, D, (const int32_t*)data_of(ps), ps->shape[0], n_dims, mode,
+                      freq_base, freq_scale, backward, data_of(out), nullptr);
+    }
+    if (xc) gt_tensor_free(xc);
+    if (pc) gt_tensor_free(pc);
+    if (rc != 0) {
+        if (out) gt_tensor_free(out);
+        return nullptr;
+    }
+    return out;
+}
+
+GT_API gt_tensor* gt_rope(const gt_tensor* x, const gt_tensor* pos, int n_dims, int mode, int n_ctx_orig, float freq_base,
+                          float freq_scale) {
+    (void)n_ctx_orig;  // only read by ggml when ext_factor != 0, which the reference never passes
+    return rope_handle(x, pos, n_dims, mode, freq_base, freq_scale, 0);
+}
+
+GT_API gt_tensor* gt_rope_backward(const gt_tensor* grad_out, const gt_tensor* pos, int n_dims, int mode, int n_ctx_orig,
+                                   float freq_base, float freq_scale) {
+    (void)n_ctx_orig;
+    return rope_handle(grad_out, pos, n_dims, mode, freq_base, freq_scale, 1);
+}
+
 GT_API gt_tensor* gt_flash_decode_q8_0(const gt_tensor* q, const gt_tensor* k_q8, const gt_tensor* v_q8,
                                        const gt_tensor* seq_lens, float scale) {
     const char* ctx = "flash_decode_q8_0";

@@ -116,6 +116,12 @@ def flash_attention_backward(grad_out, q, k, v, mask, out, lse, scale: float = 0
     return Handle(dq.value), Handle(dk.value), Handle(dv.value)
 
 
+def rope(x: Handle, pos: Handle, n_dims: int, mode: int = 0, n_ctx_orig: int = 0, freq_base: float = 10000.0,
+         freq_scale: float = 1.0, backward: bool = False) -> Handle:
+    fn = _C.lib.gt_rope_backward if backward else _C.lib.gt_rope
+    return Handle(fn(x.ptr, pos.ptr, n_dims, mode, n_ctx_orig, freq_base, freq_scale), "rope")
+
+
 def quantize(t: Handle, qtype: int = _C.GT_Q8_0) -> Handle:
     return Handle(_C.lib.gt_quantize(t.ptr, qtype), "quantize")
 

@@ -101,6 +101,14 @@ GT_API int gt_flash_attention_backward(const gt_tensor *grad_out, const gt_tenso
 GT_API gt_tensor *gt_flash_decode_q8_0(const gt_tensor *q, const gt_tensor *k_q8, const gt_tensor *v_q8,
                                        const gt_tensor *seq_lens, float scale);
 
+/* ---- RoPE (the reference's gt_rope / gt_rope_backward, bound at _C.py:467-470, csrc/gt_ops_nn.cpp:
+ * 2409-2421): same signature and messages; CUDA tensors, x f32/f16/bf16 (B,H,S,D) or (H,S,D), pos 1-D
+ * (converted to int32). Returns a new tensor of x's shape and dtype. */
+GT_API gt_tensor *gt_rope(const gt_tensor *x, const gt_tensor *pos, int n_dims, int mode, int n_ctx_orig,
+                          float freq_base, float freq_scale);
+GT_API gt_tensor *gt_rope_backward(const gt_tensor *grad_out, const gt_tensor *pos, int n_dims, int mode,
+                                   int n_ctx_orig, float freq_base, float freq_scale);
+
 /* ---- Q8_0 (gguf_train.h:381-382, gt_ops_extra.cpp:2002-2008): CUDA tensors, rows along the last dim */
 GT_API gt_tensor *gt_quantize(const gt_tensor *t, int quant_dtype);
 GT_API gt_tensor *gt_dequantize(const gt_tensor *t, int target_dtype);

@@ -186,3 +186,18 @@ def test_rope_argument_checks_use_the_reference_messages():
     assert rc != 0 and "freq_base must be positive and finite" in msg
     rc, msg = call(n_pos=3)
     assert rc != 0 and "a position for each of the 4 sequence elements" in msg
+
+
+def test_handle_rope_checks():
+    """gt_rope (the reference's own ctypes signature) reports a bad rank with gt_rope_check's message
+    and refuses host tensors: the engine has no CPU path."""
+    import gguf_train_b200.handles as H
+    from gguf_train_b200 import _C
+
+    pos = H.Handle.from_numpy(np.arange(4, dtype=np.int32), device=_C.GT_DEV_CPU)
+    bad = H.Handle.from_numpy(np.zeros((4, 8), np.float32), device=_C.GT_DEV_CPU)
+    with pytest.raises(RuntimeError, match=r"rope: expected x of shape .* got \[4, 8\]"):
+        H.rope(bad, pos, 8)
+    x = H.Handle.from_numpy(np.zeros((1, 2, 4, 8), np.float32), device=_C.GT_DEV_CPU)
+    with pytest.raises(RuntimeError, match="CUDA tensors only"):
+        H.rope(x, pos, 8)

@@ -85,3 +85,21 @@ def test_handle_quantize_and_decode():
     out = H.flash_decode_q8_0(hq, hk, hv, H.Handle.from_numpy(lens))
     want = O.decode_q8_0(q, O.q8_0_quantize(kf), O.q8_0_quantize(vf), lens, Hkv, S)
     assert_close(out.to_numpy().astype(np.float64), want, 2e-2, 1e-2, "gt_flash_decode_q8_0")
+
+
+def test_handle_rope_matches_oracle():
+    """gt_rope and gt_rope_backward through handles, as the reference's RoPEFn calls them
+    (_functions.py:1906-1919), with float positions converted to int32 as the reference does."""
+    from gguf_train_b200 import _C
+    from gguf_train_b200.handles import Handle
+    import gguf_train_b200.handles as H
+
+    O.manual_seed(91)
+    x = seeded((2, 4, 24, 64), "f32")
+    pos = ((np.arange(24) * 131 + 7) % 3000).astype(np.float32)
+    hx, hp = _h(x, "f32"), Handle.from_numpy(pos)
+    got = H.rope(hx, hp, 64, 2, 0, 10000.0, 1.0).to_numpy()
+    back = H.rope(hx, hp, 64, 2, 0, 10000.0, 1.0, backward=True).to_numpy()
+    assert _C.device_status() == 0
+    assert_close(got, O.rope(x, pos.astype(np.int64), 64, 2), 2e-5, 1e-5, "gt_rope")
+    assert_close(back, O.rope(x, pos.astype(np.int64), 64, 2, backward=True), 2e-5, 1e-5, "gt_rope_backward")
