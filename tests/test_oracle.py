@@ -199,3 +199,27 @@ def test_rope_oracle_properties():
     e = np.zeros((1, 2, 64), np.float32)
     e[0, 1, 2] = 1.0
     assert O.rope(e, [0, 1], 64)[0, 1, 3] == np.float32(np.sin(np.float64(np.float32(0.7498942))))
+
+
+def test_rope_oracle_matches_transformers_rotations():
+    """The RoPE restatement against independent implementations of the two layouts: transformers'
+    Llama apply_rotary_pos_emb (rotate_half: pairs i, i + d/2, ggml's NeoX mode) and GPT-J's
+    (rotate_every_two: pairs 2i, 2i+1, ggml's normal mode), fed float64 angles p * base^(-2i/d).
+    Positions stay small because ggml accumulates each angle in float32 (theta *= theta_scale), which
+    drifts from the exact power by ~1e-6 relative at the last pairs: 1e-4 covers that at p < 16."""
+    import torch
+    from transformers.models.gptj.modeling_gptj import apply_rotary_pos_emb as gptj_rotary
+    from transformers.models.llama.modeling_llama import apply_rotary_pos_emb as llama_rotary
+
+    rs = np.random.RandomState(11)
+    B, H, S, D, base = 2, 3, 16, 64, 10000.0
+    x = rs.randn(B, H, S, D).astype(np.float32)
+    pos = np.arange(S)
+    inv = base ** (-np.arange(0, D, 2, dtype=np.float64) / D)
+    ang = torch.tensor(pos[:, None] * inv[None, :])                  # (S, D/2) float64
+    xt = torch.tensor(x, dtype=torch.float64)
+    emb = torch.cat([ang, ang], dim=-1)[None]                        # (1, S, D)
+    neox, _ = llama_rotary(xt, xt, emb.cos(), emb.sin(), unsqueeze_dim=1)
+    assert np.allclose(O.rope(x, pos, D, mode=2, freq_base=base), neox.numpy(), atol=1e-4, rtol=0)
+    gptj = gptj_rotary(xt.transpose(1, 2), ang.sin()[None], ang.cos()[None]).transpose(1, 2)
+    assert np.allclose(O.rope(x, pos, D, mode=0, freq_base=base), gptj.numpy(), atol=1e-4, rtol=0)
