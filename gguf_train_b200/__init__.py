@@ -10,6 +10,7 @@ is an ImportError, never a silent fallback.
 
 from . import _C
 from . import functional
+from . import gguf_io
 from . import handles
 from .functional import (FlashAttentionFn, RoPEFn, decode_q8_0, dequantize_q8_0, q8_0_append, quantize_q8_0, rope,
                          scaled_dot_product_attention, sdpa_from_host)
@@ -18,6 +19,7 @@ from .modules import MultiheadAttention
 __all__ = [
     "_C",
     "functional",
+    "gguf_io",
     "handles",
     "FlashAttentionFn",
     "MultiheadAttention",
