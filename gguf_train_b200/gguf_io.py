@@ -52,7 +52,7 @@ class GGUFFile:
 
     def __init__(self, path, dequantize: bool = False, device=None):
         self.path = Path(path)
-        self.metadata, infos, data_start, align = _read_header(self.path)
+        self.metadata, infos, data_start = _read_header(self.path)
         self.tensors = {}
         raw = np.memmap(self.path, dtype=np.uint8, mode="r")
         dev = torch.device(device) if device is not None else torch.device("cpu")
@@ -235,9 +235,8 @@ def _read_header(path: Path):
             if ggml_type not in _TYPES:
                 raise ValueError(f"load_gguf: tensor {name!r} has ggml type {ggml_type}, which this engine does not read")
             infos.append((name, tuple(int(d) for d in reversed(ne)), ggml_type, offset))
-        align = int(meta.get("general.alignment", _ALIGN))
-        data_start = _pad(f.tell(), align)
-    return meta, infos, data_start, align
+        data_start = _pad(f.tell(), int(meta.get("general.alignment", _ALIGN)))
+    return meta, infos, data_start
 
 
 def _to_torch(buf: np.ndarray, shape, ggml_type: int, dev: torch.device, dequantize: bool, name: str):
