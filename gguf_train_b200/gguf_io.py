@@ -33,7 +33,6 @@ _TYPES = {0: (1, 4, np.float32), 1: (1, 2, np.float16), 30: (1, 2, None), _Q8_0:
           24: (1, 1, np.int8), 25: (1, 2, np.int16), 26: (1, 4, np.int32), 27: (1, 8, np.int64), 28: (1, 8, np.float64)}
 _TORCH_TYPE = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 30, torch.int8: 24, torch.int16: 25,
                torch.int32: 26, torch.int64: 27, torch.float64: 28}
-_TYPE_TORCH = {v: k for k, v in _TORCH_TYPE.items()}
 
 # GGUF metadata value types
 _U8, _I8, _U16, _I16, _U32, _I32, _F32, _BOOL, _STR, _ARR, _U64, _I64, _F64 = range(13)
