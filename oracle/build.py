@@ -4,9 +4,11 @@ Compiles oracle/sdpa_oracle.cpp into oracle/liboracle_sdpa.so with the flags the
 for its native build (build_native.py:564-586: -O3 -fopenmp), except that -march is pinned to
 x86-64-v3 instead of "native": the library is built on one host and run on another.
 
-The reference itself cannot be compiled here: gt_ops_nn.cpp includes gt_internal.h, which needs
-ggml headers from a llama.cpp tree that build_native.py downloads (build_native.py:217-307), and
-this machine has no network. No oracle/_ref build therefore exists.
+The reference's native library as a whole cannot be compiled here (gt_ops_nn.cpp includes
+gt_internal.h, which needs ggml headers from a llama.cpp tree that build_native.py downloads,
+build_native.py:217-307). Its SDPA forward, gt_flash_attention, needs none of ggml: oracle/build_ref.py
+compiles that one function from the reference source into oracle/_ref/, and tests pin this
+restatement to it.
 """
 
 from __future__ import annotations

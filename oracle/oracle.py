@@ -4,8 +4,9 @@ Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg import this
 checker and as the timed CPU baseline. The product package (gguf_train_b200) never imports it.
 
 Each function names the reference behaviour it restates; the arithmetic lives in
-oracle/sdpa_oracle.cpp. Parity is "unpinned" against the reference binary (it cannot be built
-here: its ggml dependency is downloaded at build time); see the C++ file's header.
+oracle/sdpa_oracle.cpp. The forward is pinned to the reference's own gt_flash_attention, compiled
+from its source into oracle/_ref/ (oracle/build_ref.py, tests/test_oracle_ref.py); the backward
+and Q8_0 parts are pinned to independent implementations (see the C++ file's header).
 """
 
 from __future__ import annotations

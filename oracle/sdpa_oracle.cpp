@@ -5,12 +5,14 @@
 // Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg load it, and only as the
 // checker / the timed CPU baseline. The product library never links or calls it.
 //
-// Parity status: the reference cannot be built here (csrc/gt_internal.h:4-8 needs ggml headers
-// that build_native.py:217-307 downloads), and the reference's own tests carry no golden vectors.
-// The restatement is pinned against independent implementations instead (torch float64 SDPA and
-// autograd, gguf-py's Q8_0 codec, which states bit-exactness with ggml-quants.c) and against the
-// reference tests' self-consistency cases. Forward/backward parity is therefore "unpinned" with
-// respect to the reference binary itself.
+// Parity status: the reference's native library cannot be built here as a whole
+// (csrc/gt_internal.h:4-8 needs ggml headers that build_native.py:217-307 downloads), but its SDPA
+// forward, gt_flash_attention (csrc/gt_ops_nn.cpp:2423-2525), uses none of ggml: oracle/build_ref.py
+// compiles that function from the reference source into oracle/_ref/, and the forward below is
+// pinned to it (bit for bit for f32/f16/bf16 outputs, masks and causal included; tests/
+// test_oracle_ref.py and the fixture tests/golden/ref_flash_attention.npz). The backward (a chain of
+// ggml ops in the reference) and the Q8_0 codec are pinned against independent implementations
+// (torch float64 SDPA and autograd; gguf-py's Q8_0, which states bit-exactness with ggml-quants.c).
 //
 // Every routine cites the reference lines it follows. Nothing here is copied from the reference;
 // the loops are written from the behaviour those lines define.
