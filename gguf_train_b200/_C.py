@@ -79,6 +79,8 @@ def _configure(lib: ctypes.CDLL) -> ctypes.CDLL:
     lib.gtb_clear_error.restype = None
     lib.gtb_device_status.argtypes = []
     lib.gtb_device_status.restype = c_int
+    lib.gtb_selftest_wait_timeout.argtypes = [c_int64, c_void_p]
+    lib.gtb_selftest_wait_timeout.restype = c_int
     lib.gtb_version.argtypes = []
     lib.gtb_version.restype = c_char_p
 

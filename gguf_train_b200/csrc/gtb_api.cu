@@ -17,13 +17,18 @@
 #include "q8_0_internal.h"
 #include "rope.cuh"
 #include "sdpa_args.h"
+#include "sm100_ptx.cuh"
 
 namespace gtb {
+
+constexpr long long WAIT_LIMIT_HOST = sm100::WAIT_LIMIT;
 
 namespace {
 thread_local std::string g_err;
 std::mutex g_status_mtx;
 int* g_status[64] = {};
+constexpr int MAX_EXTRA_WORDS = 4;
+int* g_extra_status[64][MAX_EXTRA_WORDS] = {};
 }  // namespace
 
 void set_error(const std::string& msg) { g_err = msg; }
@@ -58,7 +63,43 @@ int* device_status_word(int device) {
     return g_status[device];
 }
 
+void register_status_word(int device, int* word) {
+    if (device < 0 || device >= 64 || !word) return;
+    std::lock_guard<std::mutex> lk(g_status_mtx);
+    for (int i = 0; i < MAX_EXTRA_WORDS; ++i) {
+        if (g_extra_status[device][i] == word) return;
+        if (!g_extra_status[device][i]) {
+            g_extra_status[device][i] = word;
+            return;
+        }
+    }
+}
+
 namespace {
+
+// Every status word of a device that exists so far (none is allocated here).
+int status_words(int device, int** out) {
+    if (device < 0 || device >= 64) return 0;
+    std::lock_guard<std::mutex> lk(g_status_mtx);
+    int n = 0;
+    if (g_status[device]) out[n++] = g_status[device];
+    for (int i = 0; i < MAX_EXTRA_WORDS; ++i)
+        if (g_extra_status[device][i]) out[n++] = g_extra_status[device][i];
+    return n;
+}
+
+// A kernel whose mbarrier nothing ever arrives at: its bounded wait (the same mbar_wait every
+// kernel uses) must give up after `limit` cycles, record code 90 in the status word and return.
+__global__ void selftest_wait_kernel(int* status, long long limit) {
+    __shared__ uint64_t bar;
+    if (threadIdx.x == 0) {
+        sm100::mbar_init(&bar, 1);
+        sm100::fence_mbar_init();
+    }
+    __syncthreads();
+    sm100::mbar_wait(&bar, 0, status, 90, limit);
+    __syncthreads();  // no thread leaves while another still waits on the shared barrier
+}
 
 std::string shape_str(const int64_t* s, int n) {
     std::string r = "[";
@@ -296,12 +337,35 @@ GTB_API int gtb_device_status(void) {
     int dev = 0;
     if (cuda_failed(cudaGetDevice(&dev), "gtb_device_status")) return -1;
     if (cuda_failed(cudaDeviceSynchronize(), "gtb_device_status: synchronize")) return -1;
+    int* words[1 + MAX_EXTRA_WORDS];
+    const int n = status_words(dev, words);
+    int first = 0;
+    for (int i = 0; i < n; ++i) {
+        int v = 0;
+        if (cuda_failed(cudaMemcpy(&v, words[i], sizeof(int), cudaMemcpyDeviceToHost), "gtb_device_status: read"))
+            return -1;
+        if (v) {
+            if (!first) first = v;
+            if (cuda_failed(cudaMemset(words[i], 0, sizeof(int)), "gtb_device_status: clear")) return -1;
+        }
+    }
+    return first;
+}
+
+GTB_API int gtb_selftest_wait_timeout(int64_t limit_cycles, void* stream) {
+    if (limit_cycles < 1000 || limit_cycles > WAIT_LIMIT_HOST) {
+        set_errorf("selftest_wait_timeout: limit_cycles must be in [1000, %lld]", (long long)WAIT_LIMIT_HOST);
+        return -1;
+    }
+    int dev = 0;
+    if (cuda_failed(cudaGetDevice(&dev), "selftest_wait_timeout")) return -1;
     int* w = device_status_word(dev);
-    if (!w) return 0;
-    int v = 0;
-    if (cuda_failed(cudaMemcpy(&v, w, sizeof(int), cudaMemcpyDeviceToHost), "gtb_device_status: read")) return -1;
-    if (v) cudaMemset(w, 0, sizeof(int));
-    return v;
+    if (!w) {
+        set_error("selftest_wait_timeout: no status word");
+        return -1;
+    }
+    selftest_wait_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(w, (long long)limit_cycles);
+    return cuda_failed(cudaGetLastError(), "selftest_wait_timeout launch") ? -1 : 0;
 }
 
 GTB_API int gtb_sdpa_fwd(const gtb_tensor4* q, const gtb_tensor4* k, const gtb_tensor4* v, const gtb_tensor4* mask,

@@ -38,7 +38,11 @@ void clear_error();
 bool cuda_failed(cudaError_t e, const char* what);
 
 // Per-device status word that kernels set when a bounded wait runs out (never trap, never hang).
+// Allocated on first use.
 int* device_status_word(int device);
+// A further status word of `device` that gtb_device_status() reads and clears with the main one
+// (the no-allocation decode entry point keeps its own, a file-scope device variable).
+void register_status_word(int device, int* word);
 
 // Keep freed memory in the device's stream-ordered pool (per-call scratch stays allocation-free).
 void retain_pool_memory(int dev);

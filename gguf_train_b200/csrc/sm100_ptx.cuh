@@ -57,15 +57,19 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
     return done != 0;
 }
 
-// Wait for the phase of `parity` to complete, for at most ~2^31 SM cycles (about a second).
-// On timeout: records `code` in the device status word (the first code since the word was last
-// cleared is kept) and returns false. Never traps or hangs.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int code) {
+// Longest wait on one mbarrier phase, in SM cycles (about a second at the B200's clocks).
+constexpr long long WAIT_LIMIT = 1ll << 31;
+
+// Wait for the phase of `parity` to complete, for at most `limit` SM cycles (WAIT_LIMIT unless a
+// self-test passes a shorter one). On timeout: records `code` in the device status word (the first
+// code since the word was last cleared is kept) and returns false. Never traps or hangs.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int code,
+                                          long long limit = WAIT_LIMIT) {
     const uint32_t addr = smem_u32(bar);
     if (mbar_try_wait(addr, parity)) return true;
     const long long t0 = clock64();
     while (!mbar_try_wait(addr, parity)) {
-        if (clock64() - t0 > (1ll << 31)) {
+        if (clock64() - t0 > limit) {
             if (status) atomicCAS(status, 0, code);
             return false;
         }

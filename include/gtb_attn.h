@@ -139,12 +139,14 @@ GTB_API int gtb_decode_q8_0(const void *q, int q_dtype, const void *k_q8, const 
  * cudaMalloc/cudaFree (they synchronise the device) or grow a memory pool mid-run. It allocates
  * nothing: the split-KV partial results go to a fixed device array of
  * GTB_DECODE_NOALLOC_SCRATCH_BYTES that every GPU loading this library holds until the process
- * exits. Calls needing more scratch than that, B*Hkv*ceil(Smax/GTB_DECODE_CHUNK)*(H/Hkv)*(D+2)*4
- * bytes plus a work area of 8*(B+2) + 8*B*Hkv*ceil(Smax/GTB_DECODE_CHUNK) bytes rounded up to 256,
- * are rejected with an error
- * (config 5a, B=64 Hkv=8 H=32 D=128 Smax=32768, needs 17.1 MB).
+ * exits. A call needs a work area of 8*(B+2) + 8*B*Hkv*ceil(Smax/GTB_DECODE_CHUNK) bytes rounded up
+ * to 256, plus B*Hkv*ceil(Smax/GTB_DECODE_CHUNK)*(H/Hkv)*(D+2)*4 bytes of partials when Smax spans
+ * more than one chunk; calls needing more than the array holds, or with B, Smax above 2^31 - 1, H
+ * above 65535 or D above 256, are rejected with an error before any kernel runs (config 5a, B=64
+ * Hkv=8 H=32 D=128 Smax=32768, needs 17.1 MB).
  * The first call on a device sets up the array's device address (call it once before any stream
- * capture). Calls share the array: calls whose kernels overlap on the GPU race.
+ * capture). Calls share the array: calls whose kernels overlap on the GPU race. Its kernels report
+ * a bounded wait that ran out through gtb_device_status(), like every other kernel.
  * No counterpart in the reference: it is an addition of this engine. */
 #define GTB_DECODE_NOALLOC_SCRATCH_BYTES (40u << 20)
 GTB_API int gtb_decode_q8_0_noalloc(const void *q, int q_dtype, const void *k_q8, const void *v_q8,
@@ -165,9 +167,19 @@ GTB_API int gtb_attn_merge(float *o_acc, float *lse_acc, const void *o_part, con
 GTB_API const char *gtb_last_error(void);
 GTB_API void gtb_clear_error(void);
 
-/* Synchronises the current device and returns (then clears) its kernel status word: 0 = fine,
- * otherwise a code that a kernel wrote when one of its bounded waits ran out. */
+/* Synchronises the current device and returns (then clears) its kernel status words: 0 = fine,
+ * otherwise the code a kernel wrote when one of its bounded waits ran out or a check failed (the
+ * first nonzero of the main word and of the fixed word of gtb_decode_q8_0_noalloc). Allocates
+ * nothing. Replaces nothing in the reference, which runs no device kernels; its errors follow
+ * gt_last_error (csrc/gt_core.cpp:7-23). */
 GTB_API int gtb_device_status(void);
+
+/* Failure-detection self-test: launches on `stream` a one-warp kernel that waits on an mbarrier
+ * nothing ever arrives at, with the same bounded wait every kernel of this library uses but a limit
+ * of `limit_cycles` SM cycles (1000 .. 2^31) instead of about a second. The wait gives up, the
+ * kernel records status 90 and returns: gtb_device_status() then reports 90 once, and the device
+ * stays usable. No counterpart in the reference, which has no device code. */
+GTB_API int gtb_selftest_wait_timeout(int64_t limit_cycles, void *stream);
 
 /* Build-time facts: number of sm_100a kernels compiled in, and a version string. */
 GTB_API const char *gtb_version(void);
