@@ -31,6 +31,7 @@ p_i64 = ctypes.POINTER(c_int64)
 
 # gt_dtype codes (reference csrc/gguf_train.h:22-36, gguf_train/_dtype.py:85)
 GT_F32, GT_F16, GT_BF16, GT_F64, GT_I8, GT_U8, GT_I16, GT_I32, GT_I64, GT_BOOL = 0, 1, 2, 3, 4, 5, 6, 7, 8, 9
+GTB_BWD_DETERMINISTIC = 1  # gtb_sdpa_bwd_ex flag (include/gtb_attn.h)
 GT_Q8_0 = 108
 GT_DEV_CPU, GT_DEV_CUDA = 0, 1
 
@@ -52,6 +53,8 @@ def _configure(lib: ctypes.CDLL) -> ctypes.CDLL:
     lib.gtb_sdpa_fwd_host.restype = c_int
     lib.gtb_sdpa_bwd.argtypes = [P4, P4, P4, P4, P4, P4, c_void_p, c_float, c_int, P4, P4, P4, c_void_p]
     lib.gtb_sdpa_bwd.restype = c_int
+    lib.gtb_sdpa_bwd_ex.argtypes = [P4, P4, P4, P4, P4, P4, c_void_p, c_float, c_int, P4, P4, P4, c_int, c_void_p]
+    lib.gtb_sdpa_bwd_ex.restype = c_int
     lib.gtb_q8_0_quantize.argtypes = [c_void_p, c_int, c_int64, c_int64, c_void_p, c_void_p]
     lib.gtb_q8_0_quantize.restype = c_int
     lib.gtb_q8_0_append.argtypes = [c_void_p, c_int, c_int64, c_int64, c_int64, c_int64, c_void_p, c_int64, c_void_p,

@@ -529,7 +529,17 @@ GTB_API int gtb_sdpa_fwd_host(const gtb_tensor4* q, const gtb_tensor4* k, const 
 GTB_API int gtb_sdpa_bwd(const gtb_tensor4* dout, const gtb_tensor4* q, const gtb_tensor4* k, const gtb_tensor4* v,
                          const gtb_tensor4* mask, const gtb_tensor4* out, const void* lse, float scale, int is_causal,
                          gtb_tensor4* dq, gtb_tensor4* dk, gtb_tensor4* dv, void* stream) {
+    return gtb_sdpa_bwd_ex(dout, q, k, v, mask, out, lse, scale, is_causal, dq, dk, dv, 0, stream);
+}
+
+GTB_API int gtb_sdpa_bwd_ex(const gtb_tensor4* dout, const gtb_tensor4* q, const gtb_tensor4* k, const gtb_tensor4* v,
+                            const gtb_tensor4* mask, const gtb_tensor4* out, const void* lse, float scale, int is_causal,
+                            gtb_tensor4* dq, gtb_tensor4* dk, gtb_tensor4* dv, int flags, void* stream) {
     const char* ctx = "flash_attention_backward";
+    if (flags & ~GTB_BWD_DETERMINISTIC) {
+        set_errorf("%s: unknown flags 0x%x", ctx, flags);
+        return -1;
+    }
     BwdArgs a;
     if (!check_attn(ctx, q, k, v, mask, a.sh)) return -1;
     if (!dout || !out || !lse || !dq || !dk || !dv) {
@@ -559,6 +569,7 @@ GTB_API int gtb_sdpa_bwd(const gtb_tensor4* dout, const gtb_tensor4* q, const gt
     a.scale = resolve_scale(scale, a.sh.D);
     a.causal = is_causal ? 1 : 0;
     a.lse = lse;
+    a.deterministic = (flags & GTB_BWD_DETERMINISTIC) != 0;
     cudaStream_t st = (cudaStream_t)stream;
     // GTB_BWD_SIMT=1 forces the SIMT kernels (used to cross-check the two implementations)
     static const int force_simt = env_int("GTB_BWD_SIMT", 0);

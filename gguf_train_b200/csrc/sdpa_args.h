@@ -33,6 +33,7 @@ struct BwdArgs {
     int causal;
     const void* lse;   // (B,H,L) contiguous, from the forward (double for f64 inputs)
     void* scratch;     // B*H*L accumulators (float or double) for rowsum(dout * out)
+    bool deterministic = false;  // the separate dQ kernel instead of f32 reductions in global memory
 };
 
 // SIMT kernels: any float dtype, any D/Dv <= 256, masks, any strides.

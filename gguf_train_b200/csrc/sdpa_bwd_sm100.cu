@@ -888,14 +888,15 @@ bool fast_view(const gtb_tensor4& t, int dtype) {
 int64_t lpad_of(int64_t L) { return (L + BT - 1) / BT * BT; }
 
 // dQ summed inside the dK/dV kernel (D = 128): f32 reductions in global memory, so the bits of dQ
-// may differ from run to run in the last place. GTB_BWD_SPLIT_DQ=1 selects the separate dQ kernel
-// instead (recomputes S and dP per query tile; deterministic).
+// may differ from run to run in the last place. A deterministic call (gtb_sdpa_bwd_ex with
+// GTB_BWD_DETERMINISTIC) or GTB_BWD_SPLIT_DQ=1 in the environment selects the separate dQ kernel
+// instead (recomputes S and dP per query tile; the same bits on every run).
 bool fused_dq(const BwdArgs& a) {
     static const bool split = [] {
         const char* e = getenv("GTB_BWD_SPLIT_DQ");
         return e && e[0] == '1';
     }();
-    return a.sh.D == 128 && !split;
+    return a.sh.D == 128 && !split && !a.deterministic;
 }
 
 // A non-blocking stream per device for the dQ kernel (created once, kept for the process).

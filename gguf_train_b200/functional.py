@@ -102,8 +102,14 @@ def sdpa_forward(q, k, v, mask=None, scale: float | None = None, is_causal: bool
     return out, lse
 
 
-def sdpa_backward(grad_out, q, k, v, mask, out, lse, scale: float, is_causal: bool):
-    """One call of the native backward: returns (dq, dk, dv)."""
+def sdpa_backward(grad_out, q, k, v, mask, out, lse, scale: float, is_causal: bool,
+                  deterministic: bool | None = None):
+    """One call of the native backward: returns (dq, dk, dv). With `deterministic` (default: whether
+    torch.use_deterministic_algorithms is on) dq comes from the separate dq kernel and has the same
+    bits on every run; otherwise, for head size 128, dq is summed with f32 reductions in global
+    memory inside the dK/dV kernel (faster; the last bit may vary from run to run)."""
+    if deterministic is None:
+        deterministic = torch.are_deterministic_algorithms_enabled()
     B, H, L, D = q.shape
     S = k.shape[2]
     dq = torch.empty_like(q, memory_format=torch.contiguous_format)
@@ -114,10 +120,11 @@ def sdpa_backward(grad_out, q, k, v, mask, out, lse, scale: float, is_causal: bo
     mt = _native_mask(mask, B, H, L, S) if mask is not None else None
     tg, tq, tk, tv, to = _t4(grad_out), _t4(q), _t4(k), _t4(v), _t4(out)
     tdq, tdk, tdv = _t4(dq), _t4(dk), _t4(dv)
-    rc = _C.lib.gtb_sdpa_bwd(ctypes.byref(tg), ctypes.byref(tq), ctypes.byref(tk), ctypes.byref(tv),
-                             ctypes.byref(mt) if mt is not None else None, ctypes.byref(to),
-                             lse.data_ptr() if lse.numel() else None, float(scale), 1 if is_causal else 0,
-                             ctypes.byref(tdq), ctypes.byref(tdk), ctypes.byref(tdv), _stream(q.device))
+    rc = _C.lib.gtb_sdpa_bwd_ex(ctypes.byref(tg), ctypes.byref(tq), ctypes.byref(tk), ctypes.byref(tv),
+                                ctypes.byref(mt) if mt is not None else None, ctypes.byref(to),
+                                lse.data_ptr() if lse.numel() else None, float(scale), 1 if is_causal else 0,
+                                ctypes.byref(tdq), ctypes.byref(tdk), ctypes.byref(tdv),
+                                _C.GTB_BWD_DETERMINISTIC if deterministic else 0, _stream(q.device))
     _C.check_rc(rc, "flash_attention_backward")
     return dq, dk, dv
 

@@ -77,6 +77,17 @@ GTB_API int gtb_sdpa_bwd(const gtb_tensor4 *dout, const gtb_tensor4 *q, const gt
                          const void *lse, float scale, int is_causal,
                          gtb_tensor4 *dq, gtb_tensor4 *dk, gtb_tensor4 *dv, void *stream);
 
+/* gtb_sdpa_bwd with flags. GTB_BWD_DETERMINISTIC: dq from the separate dq kernel, the same bits on
+ * every run (what the environment variable GTB_BWD_SPLIT_DQ=1 selects for every call); needed where a
+ * recomputed backward must repeat exactly, as under activation checkpointing (reference
+ * gguf_train/utils/checkpoint.py:159-222) or torch.use_deterministic_algorithms. flags = 0 is
+ * gtb_sdpa_bwd. Replaces the same reference function as gtb_sdpa_bwd. */
+#define GTB_BWD_DETERMINISTIC 1
+GTB_API int gtb_sdpa_bwd_ex(const gtb_tensor4 *dout, const gtb_tensor4 *q, const gtb_tensor4 *k,
+                            const gtb_tensor4 *v, const gtb_tensor4 *mask, const gtb_tensor4 *out,
+                            const void *lse, float scale, int is_causal,
+                            gtb_tensor4 *dq, gtb_tensor4 *dk, gtb_tensor4 *dv, int flags, void *stream);
+
 /* Q8_0 quantisation of n_rows rows of row_len values (row_len % 32 == 0) into GGUF Q8_0 blocks
  * (fp16 scale + 32 int8, 34 bytes per 32 values), bit-exact with ggml's reference quantiser.
  * Replaces gt_quantize(t, GT_Q_BASE + 8) (reference csrc/gt_ops_extra.cpp:2002, which goes

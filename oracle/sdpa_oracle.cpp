@@ -332,80 +332,105 @@ int orc_sdpa_bwd(const double* q, const double* k, const double* v, const double
                  double scale, int is_causal, double* dq, double* dk, double* dv, int nthreads) {
     if (Hkv <= 0 || H % Hkv != 0) return -1;
     const int64_t group = H / Hkv;
-    set_threads(nthreads);
+    const int threads = set_threads(nthreads);
     std::fill(dk, dk + B * Hkv * S * D, 0.0);
     std::fill(dv, dv + B * Hkv * S * Dv, 0.0);
     const int64_t RB = 64;
+    const int64_t nblk = (L + RB - 1) / RB;
+    // Tasks: (b, kv head, part), each part a share of the group's (query head, row block) pairs.
+    // With fewer groups than threads a group is split into parts with private dk/dv sums, added up
+    // after the loop; otherwise each group is one task writing its own dk/dv. dq rows are disjoint.
+    const int64_t groups = B * Hkv;
+    const int64_t parts = std::max<int64_t>(1, std::min<int64_t>(threads / std::max<int64_t>(groups, 1), group * nblk));
+    std::vector<double> priv(parts > 1 ? (size_t)(groups * parts * S * (D + Dv)) : 0);
+    // Without a mask, a causally masked score (s > l) gets -1e9 and its probability exp(-1e9 - max)
+    // is exactly 0 in double, since key 0 is always allowed and keeps the row maximum finite: those
+    // dot products are skipped. With a mask the full row is formed as the reference forms it.
+    const bool skip_causal = is_causal && !mask;
 
-    // parallel over (b, kv head): each task owns dk/dv of its kv head, no races
-#pragma omp parallel for collapse(2) schedule(dynamic, 1)
-    for (int64_t b = 0; b < B; ++b) {
-        for (int64_t hk = 0; hk < Hkv; ++hk) {
-            const double* kb = k + (b * Hkv + hk) * S * D;
-            const double* vb = v + (b * Hkv + hk) * S * Dv;
-            double* dkb = dk + (b * Hkv + hk) * S * D;
-            double* dvb = dv + (b * Hkv + hk) * S * Dv;
-            std::vector<double> P(RB * S), DP(RB * S);
-            for (int64_t h = hk * group; h < (hk + 1) * group; ++h) {
-                for (int64_t l0 = 0; l0 < L; l0 += RB) {
-                    const int64_t nr = std::min(RB, L - l0);
-                    for (int64_t r = 0; r < nr; ++r) {
-                        const int64_t l = l0 + r;
-                        const double* qr = q + ((b * H + h) * L + l) * D;
-                        const double* gr = dout + ((b * H + h) * L + l) * Dv;
-                        double* pr = P.data() + r * S;
-                        double* dpr = DP.data() + r * S;
-                        double mx = -std::numeric_limits<double>::infinity();
-                        for (int64_t s = 0; s < S; ++s) {
-                            double dot = 0.0;
-                            const double* kr = kb + s * D;
-                            for (int64_t d = 0; d < D; ++d) dot += qr[d] * kr[d];
-                            double x = dot * scale;
-                            if (is_causal && s > l) x += -1e9;
-                            if (mask) {
-                                double mv = mask[mask_index(mask_ndim, mask_shape, b, h, l, s)];
-                                if (mask_is_bool) { if (mv == 0.0) x = -1e9; }
-                                else x += mv;
-                            }
-                            pr[s] = x;
-                            if (x > mx) mx = x;
-                        }
-                        double se = 0.0;
-                        for (int64_t s = 0; s < S; ++s) { pr[s] = std::exp(pr[s] - mx); se += pr[s]; }
-                        for (int64_t s = 0; s < S; ++s) pr[s] /= se;
-                        double rs = 0.0;
-                        for (int64_t s = 0; s < S; ++s) {
-                            double dot = 0.0;
-                            const double* vr = vb + s * Dv;
-                            for (int64_t d = 0; d < Dv; ++d) dot += gr[d] * vr[d];
-                            dpr[s] = dot;
-                            rs += dot * pr[s];
-                        }
-                        double* dqr = dq + ((b * H + h) * L + l) * D;
-                        for (int64_t d = 0; d < D; ++d) dqr[d] = 0.0;
-                        for (int64_t s = 0; s < S; ++s) {
-                            const double ds = pr[s] * (dpr[s] - rs);
-                            dpr[s] = ds;
-                            const double* kr = kb + s * D;
-                            for (int64_t d = 0; d < D; ++d) dqr[d] += ds * kr[d];
-                        }
-                        for (int64_t d = 0; d < D; ++d) dqr[d] *= scale;
+#pragma omp parallel for schedule(dynamic, 1)
+    for (int64_t task = 0; task < groups * parts; ++task) {
+        const int64_t gi = task / parts, part = task % parts;
+        const int64_t b = gi / Hkv, hk = gi % Hkv;
+        const double* kb = k + (b * Hkv + hk) * S * D;
+        const double* vb = v + (b * Hkv + hk) * S * Dv;
+        double* dkb = parts > 1 ? priv.data() + (size_t)task * S * (D + Dv) : dk + (b * Hkv + hk) * S * D;
+        double* dvb = parts > 1 ? dkb + S * D : dv + (b * Hkv + hk) * S * Dv;
+        std::vector<double> P(RB * S), DP(RB * S);
+        for (int64_t w = part; w < group * nblk; w += parts) {
+            const int64_t h = hk * group + w / nblk;
+            const int64_t l0 = (w % nblk) * RB;
+            const int64_t nr = std::min(RB, L - l0);
+            for (int64_t r = 0; r < nr; ++r) {
+                const int64_t l = l0 + r;
+                const double* qr = q + ((b * H + h) * L + l) * D;
+                const double* gr = dout + ((b * H + h) * L + l) * Dv;
+                double* pr = P.data() + r * S;
+                double* dpr = DP.data() + r * S;
+                const int64_t s_end = skip_causal ? std::min(S, l + 1) : S;
+                double mx = -std::numeric_limits<double>::infinity();
+                for (int64_t s = 0; s < s_end; ++s) {
+                    double dot = 0.0;
+                    const double* kr = kb + s * D;
+                    for (int64_t d = 0; d < D; ++d) dot += qr[d] * kr[d];
+                    double x = dot * scale;
+                    if (is_causal && s > l) x += -1e9;
+                    if (mask) {
+                        double mv = mask[mask_index(mask_ndim, mask_shape, b, h, l, s)];
+                        if (mask_is_bool) { if (mv == 0.0) x = -1e9; }
+                        else x += mv;
                     }
-                    // dv += P^T dO, dk += dS^T q * scale for this row block
-                    for (int64_t s = 0; s < S; ++s) {
-                        double* dvr = dvb + s * Dv;
-                        double* dkr = dkb + s * D;
-                        for (int64_t r = 0; r < nr; ++r) {
-                            const int64_t l = l0 + r;
-                            const double p = P[r * S + s];
-                            const double ds = DP[r * S + s] * scale;
-                            const double* gr = dout + ((b * H + h) * L + l) * Dv;
-                            const double* qr = q + ((b * H + h) * L + l) * D;
-                            if (p != 0.0) for (int64_t d = 0; d < Dv; ++d) dvr[d] += p * gr[d];
-                            if (ds != 0.0) for (int64_t d = 0; d < D; ++d) dkr[d] += ds * qr[d];
-                        }
-                    }
+                    pr[s] = x;
+                    if (x > mx) mx = x;
                 }
+                double se = 0.0;
+                for (int64_t s = 0; s < s_end; ++s) { pr[s] = std::exp(pr[s] - mx); se += pr[s]; }
+                for (int64_t s = 0; s < s_end; ++s) pr[s] /= se;
+                for (int64_t s = s_end; s < S; ++s) pr[s] = 0.0;
+                double rs = 0.0;
+                for (int64_t s = 0; s < s_end; ++s) {
+                    double dot = 0.0;
+                    const double* vr = vb + s * Dv;
+                    for (int64_t d = 0; d < Dv; ++d) dot += gr[d] * vr[d];
+                    dpr[s] = dot;
+                    rs += dot * pr[s];
+                }
+                for (int64_t s = s_end; s < S; ++s) dpr[s] = 0.0;
+                double* dqr = dq + ((b * H + h) * L + l) * D;
+                for (int64_t d = 0; d < D; ++d) dqr[d] = 0.0;
+                for (int64_t s = 0; s < s_end; ++s) {
+                    const double ds = pr[s] * (dpr[s] - rs);
+                    dpr[s] = ds;
+                    const double* kr = kb + s * D;
+                    for (int64_t d = 0; d < D; ++d) dqr[d] += ds * kr[d];
+                }
+                for (int64_t d = 0; d < D; ++d) dqr[d] *= scale;
+            }
+            // dv += P^T dO, dk += dS^T q * scale for this row block
+            for (int64_t s = 0; s < S; ++s) {
+                double* dvr = dvb + s * Dv;
+                double* dkr = dkb + s * D;
+                for (int64_t r = 0; r < nr; ++r) {
+                    const int64_t l = l0 + r;
+                    const double p = P[r * S + s];
+                    const double ds = DP[r * S + s] * scale;
+                    const double* gr = dout + ((b * H + h) * L + l) * Dv;
+                    const double* qr = q + ((b * H + h) * L + l) * D;
+                    if (p != 0.0) for (int64_t d = 0; d < Dv; ++d) dvr[d] += p * gr[d];
+                    if (ds != 0.0) for (int64_t d = 0; d < D; ++d) dkr[d] += ds * qr[d];
+                }
+            }
+        }
+    }
+    if (parts > 1) {
+#pragma omp parallel for
+        for (int64_t gi = 0; gi < groups; ++gi) {
+            double* dkg = dk + gi * S * D;
+            double* dvg = dv + gi * S * Dv;
+            for (int64_t part = 0; part < parts; ++part) {
+                const double* src = priv.data() + (size_t)(gi * parts + part) * S * (D + Dv);
+                for (int64_t i = 0; i < S * D; ++i) dkg[i] += src[i];
+                for (int64_t i = 0; i < S * Dv; ++i) dvg[i] += src[S * D + i];
             }
         }
     }
