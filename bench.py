@@ -6,9 +6,12 @@ Workload (one "step"): one causal GQA attention forward over a batch of B=8 sequ
 Hq=32, Hkv=8, L=S=4096, D=128, bf16, inputs N(0,1)*0.5 (seeded, generated on the device),
 scale 1/sqrt(128). Work per step: 4*B*Hq*(L(L+1)/2)*D = 1.0998e12 FLOP.
 
-Multi-GPU: one process per GPU (torchrun); batch x kv-head units are independent, so each rank
-runs its own full batch with no collective on the data path (weak scaling: per-GPU work fixed).
-The process group is used only for barriers and the max-over-ranks of the timed region.
+Multi-GPU: one process per GPU (torchrun). The (batch, kv head) units are independent, so a global
+batch is partitioned over the ranks by gguf_train_b200.sharding.ShardedAttention (contiguous unit
+ranges, no collective on the data path). The default line is weak scaling: a global batch of
+N x 8 sequences, each rank getting config 3's 64 units. `extra` adds strong-scaling lines (the fixed
+config-3 / config-4 batches and config 5a's 64 sequences split over the N ranks). The process
+group is used only for barriers and the max-over-ranks of the timed regions.
 
 Reported on one JSON line by rank 0:
   value        whole-job TFLOP/s with inputs resident in HBM (CUDA events on the launching
@@ -258,50 +261,67 @@ def run_decode(args, rank: int, world: int, dev, max_over_ranks=lambda x: x) -> 
 TRAIN = dict(B=4, H=32, Hkv=8, L=8192, D=128)
 
 
-def run_train(args, rank: int, world: int, dev, max_over_ranks=lambda x: x) -> dict:
+def run_train(args, rank: int, world: int, dev, max_over_ranks=lambda x: x, strong: bool = False) -> dict:
     """Config 4: causal GQA attention forward + backward, bf16, B=4 Hq=32 Hkv=8 L=S=8192 D=128,
     q/k/v N(0,1)*0.5 and upstream gradient N(0,1). Work per step: forward 4*B*Hq*L(L+1)/2*D FLOP and
-    backward twice that (the 4-GEMM convention; the kernels recompute S and dP, which is not credited)."""
+    backward twice that (the 4-GEMM convention; the kernels recompute S and dP, which is not credited).
+    The (batch, kv head) units are partitioned by sharding.ShardedAttention: weak scaling (a global
+    batch of N x 4, each rank config 4's 32 units) or, with `strong`, config 4's batch of 4 split over
+    the N ranks."""
     import torch
 
     from gguf_train_b200 import _C
-    from gguf_train_b200 import functional as Fn
+    from gguf_train_b200.sharding import ShardedAttention
 
     B, H, Hkv, L, D = TRAIN["B"], TRAIN["H"], TRAIN["Hkv"], TRAIN["L"], TRAIN["D"]
+    B_glob = B if strong else B * world
+    sa = ShardedAttention(B_glob, H, Hkv, world, rank)
+    b_lo, b_hi = sa.batch_span()
+    nb = b_hi - b_lo
     g = torch.Generator(device=dev)
-    g.manual_seed(4321 + rank)
-    q = (torch.randn((B, H, L, D), generator=g, device=dev) * 0.5).to(torch.bfloat16)
-    k = (torch.randn((B, Hkv, L, D), generator=g, device=dev) * 0.5).to(torch.bfloat16)
-    v = (torch.randn((B, Hkv, L, D), generator=g, device=dev) * 0.5).to(torch.bfloat16)
-    gd = torch.randn((B, H, L, D), generator=g, device=dev).to(torch.bfloat16)
+    g.manual_seed(4321 if strong else 4321 + rank)
+    if strong:  # the same global batch on every rank; each keeps the batches its units touch
+        sl = lambda t: t[b_lo:b_hi].contiguous()  # noqa: E731
+    else:
+        sl = lambda t: t  # noqa: E731
+    nq = B if strong else nb
+    q = sl((torch.randn((nq, H, L, D), generator=g, device=dev) * 0.5).to(torch.bfloat16))
+    k = sl((torch.randn((nq, Hkv, L, D), generator=g, device=dev) * 0.5).to(torch.bfloat16))
+    v = sl((torch.randn((nq, Hkv, L, D), generator=g, device=dev) * 0.5).to(torch.bfloat16))
+    gd = sl(torch.randn((nq, H, L, D), generator=g, device=dev).to(torch.bfloat16))
+    out = torch.empty_like(q)
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
     scale = 1.0 / math.sqrt(D)
-    fwd = fwd_flops(B, H, L, D)
+    fwd = fwd_flops(B, H, L, D)  # config 4's batch: one rank's share (weak) or the whole split batch (strong)
     stream = torch.cuda.current_stream(dev)
     for _ in range(max(args.warmup, 3)):
-        out, lse = Fn.sdpa_forward(q, k, v, None, scale, True)
-        Fn.sdpa_backward(gd, q, k, v, None, out, lse, scale, True)
+        lse = sa.forward(q, k, v, out, scale, True, base=b_lo)
+        sa.backward(gd, q, k, v, out, lse, dq, dk, dv, scale, True, base=b_lo)
     torch.cuda.synchronize(dev)
     steps = max(3, min(args.steps, 20))
     ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(steps)]
     for i in range(steps):
         ev[i][0].record(stream)
-        out, lse = Fn.sdpa_forward(q, k, v, None, scale, True)
+        lse = sa.forward(q, k, v, out, scale, True, base=b_lo)
         ev[i][1].record(stream)
-        Fn.sdpa_backward(gd, q, k, v, None, out, lse, scale, True)
+        sa.backward(gd, q, k, v, out, lse, dq, dk, dv, scale, True, base=b_lo)
         ev[i][2].record(stream)
     torch.cuda.synchronize(dev)
     f_ms = max_over_ranks(statistics.mean(e[0].elapsed_time(e[1]) for e in ev))
     b_ms = max_over_ranks(statistics.mean(e[1].elapsed_time(e[2]) for e in ev))
     peaks = load_peaks()
-    tf = 3 * fwd / ((f_ms + b_ms) * 1e-3) / 1e12
+    tf = 3 * fwd / ((f_ms + b_ms) * 1e-3) / 1e12  # strong: the whole batch's rate; weak: one rank's
+    per_gpu = tf / world if strong else tf
     line = {
-        "workload": "config 4: causal GQA forward+backward, bf16, B=4 Hq=32 Hkv=8 L=S=8192 D=128",
-        "value": tf * world, "unit": "TFLOP/s", "ms_per_step": f_ms + b_ms, "fwd_ms": f_ms, "bwd_ms": b_ms,
+        "workload": ("config 4 fixed batch (B=4, 32 units) split over the ranks" if strong else
+                     "config 4: causal GQA forward+backward, bf16, B=4 Hq=32 Hkv=8 L=S=8192 D=128"),
+        "value": tf if strong else tf * world, "unit": "TFLOP/s", "ms_per_step": f_ms + b_ms, "fwd_ms": f_ms,
+        "bwd_ms": b_ms, "scaling": "strong" if strong else "weak", "units_this_rank": sa.units,
         "flops_per_step": 3 * fwd,
         # the timed region is `steps` forward+backward pairs of a few ms each (well under a second of
         # back-to-back work), so the burst peak is the denominator
-        "roofline": {"bound": "tensor", "achieved": tf, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
-                     "frac": tf / peaks["bf16_tflops"],
+        "roofline": {"bound": "tensor", "achieved": per_gpu, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s per GPU",
+                     "frac": per_gpu / peaks["bf16_tflops"],
                      "peak_source": peaks["source"] + " bf16 dense (burst)",
                      "timed_ms": steps * (f_ms + b_ms),
                      "backward_tflops": 2 * fwd / (b_ms * 1e-3) / 1e12, "forward_tflops": fwd / (f_ms * 1e-3) / 1e12,
@@ -311,9 +331,202 @@ def run_train(args, rank: int, world: int, dev, max_over_ranks=lambda x: x) -> d
     }
     line["roofline"]["traffic_bwd_dkdv"] = profile_traffic("bwd_sm100_config4", "dkdv")
     line["roofline"]["traffic_bwd_dq_convert"] = profile_traffic("bwd_sm100_config4", "dq_convert")
-    del q, k, v, gd, out, lse
+    del q, k, v, gd, out, lse, dq, dk, dv
     torch.cuda.empty_cache()
     return line
+
+
+# ------------------------------------------------------------------ strong scaling and masked workloads
+
+def _time_events(stream, fn, steps: int) -> float:
+    """Mean ms of fn() over `steps` launches, CUDA events on `stream` around each."""
+    import torch
+
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for s, e in ev:
+        s.record(stream)
+        fn()
+        e.record(stream)
+    torch.cuda.synchronize()
+    return statistics.mean(s.elapsed_time(e) for s, e in ev)
+
+
+def run_prefill_strong(args, rank: int, world: int, dev, max_over_ranks=lambda x: x) -> dict:
+    """Config 3's fixed batch (B=8, 64 (batch, kv head) units) split over the ranks by
+    sharding.ShardedAttention: each rank runs 64/N units; TFLOP/s of the whole batch over the
+    slowest rank's time (strong scaling)."""
+    import torch
+
+    from gguf_train_b200.sharding import ShardedAttention
+
+    B, H, Hkv, L, D = CFG["B"], CFG["H"], CFG["Hkv"], CFG["L"], CFG["D"]
+    sa = ShardedAttention(B, H, Hkv, world, rank)
+    b_lo, b_hi = sa.batch_span()
+    g = torch.Generator(device=dev)
+    g.manual_seed(555)  # the same global batch on every rank; each keeps the batches its units touch
+    q = (torch.randn((B, H, L, D), generator=g, device=dev) * 0.5).to(torch.bfloat16)[b_lo:b_hi].contiguous()
+    k = (torch.randn((B, Hkv, L, D), generator=g, device=dev) * 0.5).to(torch.bfloat16)[b_lo:b_hi].contiguous()
+    v = (torch.randn((B, Hkv, L, D), generator=g, device=dev) * 0.5).to(torch.bfloat16)[b_lo:b_hi].contiguous()
+    out = torch.empty_like(q)
+    scale = 1.0 / math.sqrt(D)
+    step = lambda: sa.forward(q, k, v, out, scale, True, base=b_lo)  # noqa: E731
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize(dev)
+    steps = max(3, min(args.steps, 20))
+    ms = max_over_ranks(_time_events(torch.cuda.current_stream(dev), step, steps))
+    flops = fwd_flops(B, H, L, D)
+    return {"workload": "config 3 fixed batch (B=8, 64 units) split over the ranks", "value": flops / (ms * 1e-3) / 1e12,
+            "unit": "TFLOP/s", "ms_per_step": ms, "steps": steps, "scaling": "strong",
+            "units_this_rank": sa.units, "segments_rank0": [list(x) for x in sa.segs] if rank == 0 else None}
+
+
+def run_prefill_key_padding(args, rank: int, world: int, dev, max_over_ranks=lambda x: x) -> dict:
+    """Config 3 with a key-padding mask, the mask nn.TransformerEncoderLayer passes for padded batches:
+    a bool (B, 1, 1, S) mask in which sequence b may not attend its last n_b ~ U{0..64} keys, on the
+    tcgen05 kernel (the mask's 128 x 128 blocks classified first; only blocks holding padded keys
+    are read entry by entry). Reported against the unmasked forward on the same inputs."""
+    import torch
+
+    from gguf_train_b200 import _C
+    from gguf_train_b200 import functional as Fn
+
+    B, H, Hkv, L, D = CFG["B"], CFG["H"], CFG["Hkv"], CFG["L"], CFG["D"]
+    g = torch.Generator(device=dev)
+    g.manual_seed(99 + rank)
+    q = (torch.randn((B, H, L, D), generator=g, device=dev) * 0.5).to(torch.bfloat16)
+    k = (torch.randn((B, Hkv, L, D), generator=g, device=dev) * 0.5).to(torch.bfloat16)
+    v = (torch.randn((B, Hkv, L, D), generator=g, device=dev) * 0.5).to(torch.bfloat16)
+    pad = torch.randint(0, 65, (B,), generator=g, device=dev)
+    mask = (torch.arange(L, device=dev)[None, :] < (L - pad)[:, None]).view(B, 1, 1, L)
+    out = torch.empty_like(q)
+    scale = 1.0 / math.sqrt(D)
+    masked = lambda: Fn.sdpa_forward(q, k, v, mask, scale, True, need_lse=False, out=out)  # noqa: E731
+    plain = lambda: Fn.sdpa_forward(q, k, v, None, scale, True, need_lse=False, out=out)  # noqa: E731
+    for _ in range(max(args.warmup, 3)):
+        masked()
+        plain()
+    torch.cuda.synchronize(dev)
+    steps = max(3, min(args.steps, 20))
+    stream = torch.cuda.current_stream(dev)
+    ms_m = max_over_ranks(_time_events(stream, masked, steps))
+    path = _C.last_path()
+    ms_p = max_over_ranks(_time_events(stream, plain, steps))
+    flops = fwd_flops(B, H, L, D)
+    peaks = load_peaks()
+    tf = flops / (ms_m * 1e-3) / 1e12
+    return {"workload": "config 3 + key-padding mask (B,1,1,S) bool, last U{0..64} keys of each sequence masked",
+            "value": tf * world, "unit": "TFLOP/s", "ms_per_step": ms_m, "steps": steps, "kernel": path,
+            "unmasked_ms": ms_p, "fraction_of_unmasked": ms_p / ms_m,
+            "roofline": {"bound": "tensor", "achieved": tf, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                         "frac": tf / peaks["bf16_tflops"], "peak_source": peaks["source"] + " bf16 dense (burst)"},
+            "status": _C.device_status()}
+
+
+MHA = dict(B=16, E=512, H=8, L=512)
+
+
+def run_mha(args, rank: int, world: int, dev, max_over_ranks=lambda x: x) -> dict:
+    """Config 2: nn.MultiheadAttention, fp32, E=512, 8 heads, batch_first, B=16, L=512, an additive
+    float attn_mask with -inf at ~10% of the positions plus a key_padding_mask of the last U{0..64}
+    tokens, need_weights=False; forward + backward of the module (projections and attention) per
+    step. The attention itself (the engine's fp32 path: the SIMT kernels; a single-pass tf32
+    tensor-core product misses the 1e-3 tolerance) is also timed alone on the module's q, k, v and
+    merged mask. FLOPs: attention 4*B*H*L*S*D forward, twice that backward; projections 2*B*L*E*E per
+    linear, 4 linears forward, twice that backward."""
+    import torch
+
+    import gguf_train_b200 as gtb
+    from gguf_train_b200 import _C
+    from gguf_train_b200 import functional as Fn
+
+    B, E, H, L = MHA["B"], MHA["E"], MHA["H"], MHA["L"]
+    D = E // H
+    torch.manual_seed(2 + rank)
+    m = gtb.MultiheadAttention(E, H, batch_first=True, device=dev)
+    x = torch.randn((B, L, E), device=dev, requires_grad=True)
+    am = torch.where(torch.rand((L, L), device=dev) < 0.1, float("-inf"), 0.0)
+    am[:, 0] = 0.0
+    n_pad = torch.randint(0, 65, (B,), device=dev)
+    kpm = torch.arange(L, device=dev)[None, :] >= (L - n_pad)[:, None]
+    gy = torch.randn((B, L, E), device=dev)
+
+    def module_step():
+        y, _ = m(x, x, x, key_padding_mask=kpm, need_weights=False, attn_mask=am)
+        y.backward(gy)
+
+    with torch.no_grad():
+        qkv = torch.nn.functional.linear(x, m.in_proj_weight, m.in_proj_bias)
+        q, k, v = qkv.view(B, L, 3, H, D).permute(2, 0, 3, 1, 4).unbind(0)
+        bias = m._score_bias(am, kpm, B, L, L, q.dtype)
+    go = torch.randn_like(q)
+
+    def attention_step():
+        o, lse = Fn.sdpa_forward(q, k, v, bias, D ** -0.5, False)
+        Fn.sdpa_backward(go, q, k, v, bias, o, lse, D ** -0.5, False)
+
+    for _ in range(max(args.warmup, 3)):
+        module_step()
+        attention_step()
+    torch.cuda.synchronize(dev)
+    steps = max(3, min(args.steps, 20))
+    stream = torch.cuda.current_stream(dev)
+    ms_mod = max_over_ranks(_time_events(stream, module_step, steps))
+    ms_att = max_over_ranks(_time_events(stream, attention_step, steps))
+    path = _C.last_path()
+    att_flops = 3 * 4.0 * B * H * L * L * D
+    proj_flops = 3 * 4 * 2.0 * B * L * E * E
+    return {"workload": "config 2: nn.MultiheadAttention fp32 E=512 H=8 B=16 L=512, float mask (-inf ~10%) + "
+                        "key_padding_mask, forward + backward",
+            "value": (att_flops + proj_flops) * world / (ms_mod * 1e-3) / 1e12, "unit": "TFLOP/s",
+            "ms_per_step": ms_mod, "steps": steps,
+            "attention_ms": ms_att, "attention_tflops": att_flops / (ms_att * 1e-3) / 1e12, "attention_kernel": path,
+            "flops_per_step": {"attention": att_flops, "projections": proj_flops}, "dtype": "f32",
+            "status": _C.device_status()}
+
+
+def run_decode_strong(args, rank: int, world: int, dev, max_over_ranks=lambda x: x) -> dict:
+    """Config 5a's 64 sequences split over the ranks by sharding.balance_sequences (by cached length,
+    longest first); GB/s of the whole step's cache bytes over the slowest rank (strong scaling)."""
+    import torch
+
+    import gguf_train_b200 as gtb
+    from gguf_train_b200.sharding import balance_sequences
+
+    B, H, Hkv, D, Smax = DEC["B"], DEC["H"], DEC["Hkv"], DEC["D"], DEC["Smax"]
+    g = torch.Generator(device=dev)
+    g.manual_seed(77)  # the same lengths on every rank
+    lens_all = torch.randint(DEC["Lmin"], Smax + 1, (B,), generator=g, device=dev).to(torch.int32)
+    mine = balance_sequences(lens_all.cpu().tolist(), world)[rank]
+    lens = lens_all[mine].contiguous()
+    Smax_r = int(lens.max().item()) if mine else 1
+    Smax_r += Smax_r % 2  # even cache length: the tensor-core path's 16-byte row pairs
+    row = D // 32 * 34
+    n = len(mine)
+    kq = torch.empty((n, Hkv, Smax_r, row), dtype=torch.uint8, device=dev)
+    vq = torch.empty_like(kq)
+    gr = torch.Generator(device=dev)
+    gr.manual_seed(1000 + rank)
+    for i in range(n):
+        kq[i] = gtb.quantize_q8_0(torch.randn((Hkv, Smax_r, D), generator=gr, device=dev))
+        vq[i] = gtb.quantize_q8_0(torch.randn((Hkv, Smax_r, D), generator=gr, device=dev))
+    q = torch.randn((n, H, 1, D), generator=gr, device=dev).to(torch.float16)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    for _ in range(max(args.warmup, 3)):
+        gtb.decode_q8_0(q, kq, vq, lens)
+    torch.cuda.synchronize(dev)
+    stream = torch.cuda.current_stream(dev)
+    times = []
+    for _ in range(max(3, min(args.steps, 20))):
+        flush.zero_()
+        times.append(_time_events(stream, lambda: gtb.decode_q8_0(q, kq, vq, lens), 1))
+    ms = max_over_ranks(statistics.mean(times))
+    total = int(lens_all.sum().item()) * Hkv * 2 * row + B * H * D * 2 * 2
+    del kq, vq, flush
+    torch.cuda.empty_cache()
+    return {"workload": "config 5a's 64 sequences split over the ranks by cached length", "value": total / (ms * 1e-3) / 1e9,
+            "unit": "GB/s", "ms_per_step": ms, "scaling": "strong", "sequences_this_rank": n,
+            "tokens_this_rank": int(lens.sum().item())}
 
 
 # ------------------------------------------------------------------ long-context workload (config 5b)
@@ -393,9 +606,13 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--decode-batch", type=int, default=None,
                     help="sequences of the decode workload (default: config 5a's 64; smaller for profiling)")
-    ap.add_argument("--workload", default="prefill", choices=["prefill", "decode", "train", "ring"],
+    ap.add_argument("--workload", default="prefill",
+                    choices=["prefill", "decode", "train", "ring", "key_padding", "mha", "prefill_strong", "train_strong",
+                             "decode_strong"],
                     help="prefill: config 3 (the default line); train: config 4 fwd+bwd; decode: config 5a; "
-                         "ring: config 5b (one long sequence, K/V ring over the GPUs)")
+                         "ring: config 5b (one long sequence, K/V ring over the GPUs); key_padding: config 3 with a "
+                         "key-padding mask; mha: config 2 (nn.MultiheadAttention fp32 fwd+bwd); *_strong: the fixed "
+                         "config-3 / config-4 / config-5a work split over the GPUs")
     ap.add_argument("--no-extra", action="store_true",
                     help="default line without the fwd+bwd (config 4) and decode (config 5a) measurements")
     args = ap.parse_args()
@@ -431,14 +648,17 @@ def main() -> None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    if args.workload in ("decode", "train", "ring"):
+    if args.workload != "prefill":
         barrier()
-        runner = {"decode": run_decode, "train": run_train, "ring": run_ring}[args.workload]
+        runner = {"decode": run_decode, "train": run_train, "ring": run_ring, "key_padding": run_prefill_key_padding,
+                  "mha": run_mha, "prefill_strong": run_prefill_strong, "decode_strong": run_decode_strong,
+                  "train_strong": lambda *a: run_train(*a, strong=True)}[args.workload]
         res = runner(args, rank, world, dev, max_over_ranks)
-        if args.workload in ("train", "ring"):
+        if args.workload != "decode":
             scaling = res.pop("scaling", "weak")
             res = dict(metric=METRIC, n_gpus=world, steps=res.pop("steps", max(3, min(args.steps, 20))),
-                       warmup=max(args.warmup, 3), higher_is_better=True, scaling=scaling, vs_baseline=None, dtype="bf16",
+                       warmup=max(args.warmup, 3), higher_is_better=True, scaling=scaling, vs_baseline=None,
+                       dtype=res.pop("dtype", "bf16"),
                        data="synthetic: seeded normal inputs generated on the device",
                        config={"workload": res.pop("workload")}, **res)
         if world > 1:
@@ -448,18 +668,25 @@ def main() -> None:
             print(json.dumps(res), flush=True)
         return
 
+    from gguf_train_b200.sharding import ShardedAttention
+
     B, H, Hkv, L, D = CFG["B"], CFG["H"], CFG["Hkv"], CFG["L"], CFG["D"]
+    # weak scaling: a global batch of world x B sequences; this rank's share of its units is config 3
+    sa = ShardedAttention(B * world, H, Hkv, world, rank)
+    b_lo, b_hi = sa.batch_span()
+    assert sa.units == B * Hkv and b_hi - b_lo == B
     g = torch.Generator(device=dev)
     g.manual_seed(1234 + rank)
     q = (torch.randn((B, H, L, D), generator=g, device=dev) * 0.5).to(torch.bfloat16)
     k = (torch.randn((B, Hkv, L, D), generator=g, device=dev) * 0.5).to(torch.bfloat16)
     v = (torch.randn((B, Hkv, L, D), generator=g, device=dev) * 0.5).to(torch.bfloat16)
+    out = torch.empty_like(q)
     scale = 1.0 / math.sqrt(D)
     flops = fwd_flops(B, H, L, D)
     stream = torch.cuda.current_stream(dev)
 
     def step():
-        out, _ = gtb.functional.sdpa_forward(q, k, v, None, scale, True, need_lse=False)
+        sa.forward(q, k, v, out, scale, True, base=b_lo)  # one native call per segment (here one)
         return out
 
     for _ in range(max(args.warmup, 3)):
@@ -527,7 +754,9 @@ def main() -> None:
         "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic: seeded N(0,1)*0.5 generated on the device (the configuration's shapes and distribution)",
         "config": {"workload": WORKLOAD, "global_batch": B * world, "seq_len": L, "heads": H, "kv_heads": Hkv,
-                   "head_dim": D, "parallelism": f"batch x kv-head units, {world} replica(s), no collective",
+                   "head_dim": D,
+                   "parallelism": f"sharding.ShardedAttention: {B * Hkv} (batch, kv head) units per rank of a "
+                                  f"global batch of {B * world}, no collective",
                    "l2": "inputs larger than L2 (q+k+v = 402 MB per GPU)", "kernel": "fwd_sm100 (tcgen05/TMA)"},
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
                      "frac": achieved / peaks["bf16_tflops"],
@@ -551,6 +780,17 @@ def main() -> None:
         line["extra"]["decode_q8_0"] = run_decode(args, rank, world, dev, max_over_ranks)
         barrier()
         line["extra"]["long_context_ring"] = run_ring(args, rank, world, dev, max_over_ranks)
+        barrier()
+        line["extra"]["prefill_key_padding"] = run_prefill_key_padding(args, rank, world, dev, max_over_ranks)
+        barrier()
+        line["extra"]["mha_config2"] = run_mha(args, rank, world, dev, max_over_ranks)
+        if world > 1:  # strong scaling: the fixed batches split over the ranks
+            barrier()
+            line["extra"]["prefill_strong"] = run_prefill_strong(args, rank, world, dev, max_over_ranks)
+            barrier()
+            line["extra"]["fwd_bwd_strong"] = run_train(args, rank, world, dev, max_over_ranks, strong=True)
+            barrier()
+            line["extra"]["decode_strong"] = run_decode_strong(args, rank, world, dev, max_over_ranks)
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
         cv, threads, desc = cpu_sample(2)
         line["cpu_baseline"] = {"value": cv, "unit": "TFLOP/s", "cores": threads, "kind": "port", "sample": desc}

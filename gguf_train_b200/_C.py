@@ -86,6 +86,8 @@ def _configure(lib: ctypes.CDLL) -> ctypes.CDLL:
     lib.gtb_selftest_wait_timeout.restype = c_int
     lib.gtb_version.argtypes = []
     lib.gtb_version.restype = c_char_p
+    lib.gtb_last_path.argtypes = []
+    lib.gtb_last_path.restype = c_char_p
 
     # handle ABI (gguf_train_attn.h), argtypes as the reference binds them
     lib.gt_last_error.argtypes = []
@@ -220,3 +222,8 @@ def check_rc(rc: int, ctx: str = "") -> None:
 def device_status() -> int:
     """Synchronise and read (then clear) the device's kernel status word (0 = no timeout)."""
     return lib.gtb_device_status()
+
+
+def last_path() -> str:
+    """Kernel family ("tcgen05" or "simt") of this thread's last native attention forward/backward."""
+    return lib.gtb_last_path().decode()

@@ -25,6 +25,7 @@ constexpr long long WAIT_LIMIT_HOST = sm100::WAIT_LIMIT;
 
 namespace {
 thread_local std::string g_err;
+thread_local const char* g_last_path = "";  // kernel family of the calling thread's last attention call
 std::mutex g_status_mtx;
 int* g_status[64] = {};
 constexpr int MAX_EXTRA_WORDS = 4;
@@ -331,6 +332,8 @@ extern "C" {
 GTB_API const char* gtb_last_error(void) { return gtb::last_error(); }
 GTB_API void gtb_clear_error(void) { gtb::clear_error(); }
 
+GTB_API const char* gtb_last_path(void) { return g_last_path; }
+
 GTB_API const char* gtb_version(void) { return "gguf_train_b200 attention engine 0.1 (sm_100a)"; }
 
 GTB_API int gtb_device_status(void) {
@@ -396,7 +399,11 @@ GTB_API int gtb_sdpa_fwd(const gtb_tensor4* q, const gtb_tensor4* k, const gtb_t
     cudaStream_t st = (cudaStream_t)stream;
     // GTB_FWD_SIMT=1 forces the SIMT kernel (used to cross-check the two kernels)
     static const int force_simt = env_int("GTB_FWD_SIMT", 0);
-    if (!force_simt && fwd_sm100_supported(a)) return launch_fwd_sm100(a, st);
+    if (!force_simt && fwd_sm100_supported(a)) {
+        g_last_path = "tcgen05";
+        return launch_fwd_sm100(a, st);
+    }
+    g_last_path = "simt";
     return launch_fwd_simt(a, st);
 }
 
@@ -574,6 +581,7 @@ GTB_API int gtb_sdpa_bwd_ex(const gtb_tensor4* dout, const gtb_tensor4* q, const
     // GTB_BWD_SIMT=1 forces the SIMT kernels (used to cross-check the two implementations)
     static const int force_simt = env_int("GTB_BWD_SIMT", 0);
     const bool fast = !force_simt && bwd_sm100_supported(a);
+    g_last_path = fast ? "tcgen05" : "simt";
     const size_t bytes = fast ? bwd_sm100_scratch_bytes(a) : bwd_simt_scratch_bytes(a);
     int dev = 0;
     cudaGetDevice(&dev);

@@ -48,6 +48,7 @@
 #include <type_traits>
 
 #include "gtb_common.cuh"
+#include "mask_tiles.cuh"
 #include "sdpa_args.h"
 #include "sm100_ptx.cuh"
 
@@ -200,6 +201,7 @@ struct KvP {
     const float* delta;
     float* dqacc;  // (B, H, Lpad, D) f32, zeroed: unscaled dQ sums (fused dQ only)
     int* status;
+    MaskView mk;   // attention mask (AMASK instances only)
 };
 
 // Shared memory of the dK/dV kernel: K, V, two stages of (Q, dO, lse2, delta), with the fused dQ
@@ -217,7 +219,7 @@ struct KvSmem {
     static constexpr int SLACK = ALLOC - USED;
 };
 
-template <int D, bool BF16, bool FUSE>
+template <int D, bool BF16, bool FUSE, bool AMASK>
 __global__ void __launch_bounds__(NTHREADS, 1)
 bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                 const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmG, const KvP p) {
@@ -465,6 +467,9 @@ bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
             const float* lse_s = (const float*)(smem + OFF_ST + st * ST_BYTES + 2 * C::TILE) + wg * HB;  // -lse2
             const float* dl_s = lse_s + 128;                                                                 // -delta
             const uint64_t sc2 = f2_pack(p.scale_log2, p.scale_log2);
+            // the attention mask's class for this query tile and key block, and the query head
+            const int hq_it = hk * p.group + it / nq;
+            const uint8_t mcls = AMASK ? p.mk.tile_class(b, hq_it, i_start + it % nq, jt) : (uint8_t)MASK_NONE;
             // masking only where the causal diagonal crosses the sub-item: one branch per sub-item
             auto chunks = [&](auto masked) {
                 constexpr bool MASK = decltype(masked)::value;
@@ -474,6 +479,14 @@ bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
                     tmem_ld32(tmem + lane_addr + 256 + HB * wg + c * 32, ra);
                     tmem_ld32(tmem + lane_addr + 384 + HB * wg + c * 32, rb);
                     tmem_ld_wait();
+                    if constexpr (AMASK) {  // scores of queries q0 + 32c .. for this thread's key
+                        if (mcls == MASK_MIXED) {
+                            mask_apply_col32((float*)ra, p.mk, b, hq_it, q0 + c * 32, p.L, min((int64_t)key, p.S - 1));
+                        } else if (mcls == MASK_ALL) {
+#pragma unroll
+                            for (int i = 0; i < 32; ++i) ra[i] = __float_as_uint(-INFINITY);
+                        }
+                    }
 #pragma unroll
                     for (int i = 0; i < 32; i += 2) {
                         // packed two-lane f32: a = S * scale - lse2, ds = p * (dP - delta)
@@ -582,9 +595,10 @@ struct DqP {
     const float* lse2;
     const float* delta;
     int* status;
+    MaskView mk;  // attention mask (AMASK instances only)
 };
 
-template <int D, bool BF16>
+template <int D, bool BF16, bool AMASK>
 __global__ void __launch_bounds__(NTHREADS, 1)
 bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
               const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmG, const DqP p) {
@@ -767,6 +781,8 @@ bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
         const uint64_t sc2 = f2_pack(p.scale_log2, p.scale_log2), nl2 = f2_pack(nlse2, nlse2), nd2 = f2_pack(ndl, ndl);
         const int lim_s = (int)min(p.S, (int64_t)INT32_MAX) - 1;
         const int lim = p.causal ? min(lim_s, row) : lim_s;  // last key this row may see
+        const unsigned char* mrow = nullptr;  // mask entries of this row (padding rows read row L-1)
+        if constexpr (AMASK) mrow = p.mk.row(b, h, min((int64_t)row, p.L - 1));
         // warpgroup 0 copies its row of Q, warpgroup 1 its row of dO, from the 128-byte-swizzled tile
         // into TMEM (16-byte chunk c of row r of a 64-column slab sits at chunk c ^ (r & 7))
         bool ok = warp_wait(qg_full, 0, p.status, 59);
@@ -791,6 +807,7 @@ bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
             if (!ok || __any_sync(0xffffffffu, *(volatile int*)abort_flag)) break;
             tc_fence_after();
             const int kv0 = j * BT + wg * HB;  // first key of the sub-item
+            const uint8_t mcls = AMASK ? p.mk.tile_class(b, h, tile, j) : (uint8_t)MASK_NONE;
             // masking only on ragged or diagonal blocks: one branch per sub-item
             auto chunks = [&](auto masked) {
                 constexpr bool MASK = decltype(masked)::value;
@@ -800,6 +817,14 @@ bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
                     tmem_ld32(tmem + lane_addr + HB * wg + c * 32, ra);
                     tmem_ld32(tmem + lane_addr + 128 + HB * wg + c * 32, rb);
                     tmem_ld_wait();
+                    if constexpr (AMASK) {  // keys kv0 + 32c .. of this thread's query row
+                        if (mcls == MASK_MIXED) {
+                            mask_apply32((float*)ra, p.mk, mrow, kv0 + c * 32, p.S);
+                        } else if (mcls == MASK_ALL) {
+#pragma unroll
+                            for (int i = 0; i < 32; ++i) ra[i] = __float_as_uint(-INFINITY);
+                        }
+                    }
 #pragma unroll
                     for (int i = 0; i < 32; i += 2) {
                         // packed two-lane f32: a = S * scale - lse2, ds = p * (dP - delta)
@@ -911,8 +936,8 @@ cudaStream_t side_stream(int dev) {
     return streams[dev];
 }
 
-template <int D, bool BF16, bool FUSE>
-int run_bwd(const BwdArgs& a, cudaStream_t st) {
+template <int D, bool BF16, bool FUSE, bool AMASK>
+int run_bwd(const BwdArgs& a, const MaskView& mview, cudaStream_t st) {
     using C = BCfg<D>;
     const int64_t B = a.sh.B, H = a.sh.H, L = a.sh.L, S = a.sh.S, Lpad = lpad_of(L);
     float* lse2 = (float*)a.scratch;
@@ -945,22 +970,24 @@ int run_bwd(const BwdArgs& a, cudaStream_t st) {
     constexpr int SMEM_KV = KvSmem<D, FUSE>::ALLOC;
     constexpr int SMEM_DQ = 6 * C::TILE + 32 * 8 + 1024;  // + barriers, TMEM slot, flag
     if (!attr_set) {
-        if (cuda_failed(cudaFuncSetAttribute(bwd_dkdv_kernel<D, BF16, FUSE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             SMEM_KV), "cudaFuncSetAttribute(bwd dkdv)") ||
-            (!FUSE && cuda_failed(cudaFuncSetAttribute(bwd_dq_kernel<D, BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                       SMEM_DQ), "cudaFuncSetAttribute(bwd dq)")))
+        if (cuda_failed(cudaFuncSetAttribute(bwd_dkdv_kernel<D, BF16, FUSE, AMASK>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_KV),
+                        "cudaFuncSetAttribute(bwd dkdv)") ||
+            (!FUSE && cuda_failed(cudaFuncSetAttribute(bwd_dq_kernel<D, BF16, AMASK>,
+                                                       cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_DQ),
+                                  "cudaFuncSetAttribute(bwd dq)")))
             return -1;
         attr_set = true;
     }
     float* dqacc = FUSE ? delta + B * H * Lpad : nullptr;
     KvP kp{H, a.sh.Hkv, L, S, Lpad, group, n_qt, n_kvt, scale_log2, a.scale, a.causal,
            a.dk.data, a.dk.stride[0], a.dk.stride[1], a.dk.stride[2],
-           a.dv.data, a.dv.stride[0], a.dv.stride[1], a.dv.stride[2], lse2, delta, dqacc, status};
+           a.dv.data, a.dv.stride[0], a.dv.stride[1], a.dv.stride[2], lse2, delta, dqacc, status, mview};
     if constexpr (FUSE) {
         if (cuda_failed(cudaMemsetAsync(dqacc, 0, sizeof(float) * (size_t)(B * H * Lpad * D), st),
                         "flash_attention_backward: dQ sums reset"))
             return -1;
-        bwd_dkdv_kernel<D, BF16, true><<<dim3((unsigned)n_kvt, (unsigned)a.sh.Hkv, (unsigned)B), NTHREADS, SMEM_KV, st>>>(
+        bwd_dkdv_kernel<D, BF16, true, AMASK><<<dim3((unsigned)n_kvt, (unsigned)a.sh.Hkv, (unsigned)B), NTHREADS, SMEM_KV, st>>>(
             mq, mk, mv, mg, kp);
         if (cuda_failed(cudaGetLastError(), "flash_attention_backward: dK/dV/dQ launch")) return -1;
         const int64_t n = B * H * L * 16;
@@ -969,7 +996,7 @@ int run_bwd(const BwdArgs& a, cudaStream_t st) {
         return cuda_failed(cudaGetLastError(), "flash_attention_backward: dQ conversion launch") ? -1 : 0;
     }
     DqP dp{H, a.sh.Hkv, L, S, Lpad, group, n_qt, n_kvt, scale_log2, a.scale, a.causal,
-           a.dq.data, a.dq.stride[0], a.dq.stride[1], a.dq.stride[2], lse2, delta, status};
+           a.dq.data, a.dq.stride[0], a.dq.stride[1], a.dq.stride[2], lse2, delta, status, mview};
     // dK/dV and dQ only share the preprocess output: dQ runs on a side stream, forked after the
     // preprocess and joined before returning, so that each kernel's last partial wave of CTAs leaves
     // no SM idle while the other still has work
@@ -980,11 +1007,11 @@ int run_bwd(const BwdArgs& a, cudaStream_t st) {
                      cudaEventRecord(fork, st) == cudaSuccess && cudaStreamWaitEvent(side, fork, 0) == cudaSuccess;
     cudaGetLastError();  // a failed fork falls back to one stream
     cudaStream_t dq_st = two ? side : st;
-    bwd_dkdv_kernel<D, BF16, false><<<dim3((unsigned)n_kvt, (unsigned)a.sh.Hkv, (unsigned)B), NTHREADS, SMEM_KV, st>>>(
+    bwd_dkdv_kernel<D, BF16, false, AMASK><<<dim3((unsigned)n_kvt, (unsigned)a.sh.Hkv, (unsigned)B), NTHREADS, SMEM_KV, st>>>(
         mq, mk, mv, mg, kp);
     bool bad = cuda_failed(cudaGetLastError(), "flash_attention_backward: dK/dV launch");
     if (!bad) {
-        bwd_dq_kernel<D, BF16><<<dim3((unsigned)n_qt, (unsigned)H, (unsigned)B), NTHREADS, SMEM_DQ, dq_st>>>(mq, mk, mv, mg, dp);
+        bwd_dq_kernel<D, BF16, AMASK><<<dim3((unsigned)n_qt, (unsigned)H, (unsigned)B), NTHREADS, SMEM_DQ, dq_st>>>(mq, mk, mv, mg, dp);
         bad = cuda_failed(cudaGetLastError(), "flash_attention_backward: dQ launch");
     }
     if (two) {
@@ -1001,7 +1028,7 @@ int run_bwd(const BwdArgs& a, cudaStream_t st) {
 }  // namespace
 
 bool bwd_sm100_supported(const BwdArgs& a) {
-    if (a.has_mask) return false;
+    if (a.has_mask && !mask_supported(a.mask)) return false;
     const int dt = a.q.dtype;
     if (dt != BF16 && dt != F16) return false;
     if (a.sh.D != a.sh.Dv || (a.sh.D != 64 && a.sh.D != 128)) return false;
@@ -1018,13 +1045,25 @@ size_t bwd_sm100_scratch_bytes(const BwdArgs& a) {
     return sizeof(float) * rows * (2 + (fused_dq(a) ? (size_t)a.sh.D : 0));  // lse2, delta (+ dQ sums)
 }
 
-int launch_bwd_sm100(const BwdArgs& a, cudaStream_t st) {
+template <bool AMASK>
+int launch_bwd_masked(const BwdArgs& a, const MaskView& mview, cudaStream_t st) {
     const bool bf16 = a.q.dtype == BF16;
     if (a.sh.D == 128) {
-        if (fused_dq(a)) return bf16 ? run_bwd<128, true, true>(a, st) : run_bwd<128, false, true>(a, st);
-        return bf16 ? run_bwd<128, true, false>(a, st) : run_bwd<128, false, false>(a, st);
+        if (fused_dq(a))
+            return bf16 ? run_bwd<128, true, true, AMASK>(a, mview, st) : run_bwd<128, false, true, AMASK>(a, mview, st);
+        return bf16 ? run_bwd<128, true, false, AMASK>(a, mview, st) : run_bwd<128, false, false, AMASK>(a, mview, st);
     }
-    return bf16 ? run_bwd<64, true, false>(a, st) : run_bwd<64, false, false>(a, st);
+    return bf16 ? run_bwd<64, true, false, AMASK>(a, mview, st) : run_bwd<64, false, false, AMASK>(a, mview, st);
+}
+
+int launch_bwd_sm100(const BwdArgs& a, cudaStream_t st) {
+    if (!a.has_mask) return launch_bwd_masked<false>(a, MaskView{}, st);
+    MaskView mview;
+    void* table = nullptr;
+    if (build_mask_view(a.mask, a.sh.B, a.sh.H, a.sh.L, a.sh.S, a.scale, mview, &table, st) != 0) return -1;
+    const int rc = launch_bwd_masked<true>(a, mview, st);
+    if (table) cudaFreeAsync(table, st);  // after the kernels: the dq kernel's side stream is joined into st
+    return rc;
 }
 
 }  // namespace gtb

@@ -38,6 +38,7 @@
 #include <cudaTypedefs.h>
 
 #include "gtb_common.cuh"
+#include "mask_tiles.cuh"
 #include "sdpa_args.h"
 #include "sm100_ptx.cuh"
 
@@ -131,6 +132,7 @@ struct Params {
     int64_t os0, os1, os2;  // output strides of b, h, l (elements); d stride is 1
     float* lse;
     int* status;
+    MaskView mk;  // attention mask (MASK instances only)
 };
 
 // keys a row of tile t may see: [0, n_kv*BN) minus causal / ragged masking
@@ -149,7 +151,7 @@ __device__ __forceinline__ void mask_chunk(float* x, int kv0, int lim) {
         if (kv0 + i > lim) x[i] = -INFINITY;
 }
 
-template <int D, bool BF16, int EMU, bool PERSIST>
+template <int D, bool BF16, int EMU, bool PERSIST, bool MASK>
 __global__ void __launch_bounds__(NTHREADS, 1)
 fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                  const __grid_constant__ CUtensorMap tmV, const Params p) {
@@ -420,6 +422,9 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
             const int row0t = it.row0[t];
             const int grow = row0t + r;                   // query index
             const int lim = p.causal ? min(lim_s, grow) : lim_s;  // last key this row may see
+            // mask entries of this row (padding rows past L read row L-1; their results are dropped)
+            const unsigned char* mrow = nullptr;
+            if constexpr (MASK) mrow = p.mk.row(b, h, min((int64_t)grow, p.L - 1));
             float m_used = -INFINITY, lsum = 0.0f;
             for (int j = 0; j < nb; ++j) {
                 ok = warp_wait(&s_full[t], (u + j) & 1, p.status, 31);
@@ -427,6 +432,18 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
                 tc_fence_after();
                 const int kv0 = j * BN;
                 const bool need_mask = (kv0 + BN > p.S) || (p.causal && kv0 + BN - 1 > row0t);
+                // the attention mask's class for this tile and key block (the same for every row)
+                const uint8_t mcls = MASK ? p.mk.tile_class(b, h, row0t / BM, j) : (uint8_t)MASK_NONE;
+                auto attn_mask = [&](float* x, int s0) {
+                    if constexpr (MASK) {
+                        if (mcls == MASK_MIXED) {
+                            mask_apply32(x, p.mk, mrow, s0, p.S);
+                        } else if (mcls == MASK_ALL) {
+#pragma unroll
+                            for (int i = 0; i < 32; ++i) x[i] = -INFINITY;
+                        }
+                    }
+                };
                 // pass 1: row maximum, 64 columns at a time; columns 64..127 stay in registers for pass 2
                 uint32_t ra[32], rb[32];
                 float* xa = (float*)ra;
@@ -435,6 +452,8 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
                 tmem_ld32(s_tmem + 0, ra);
                 tmem_ld32(s_tmem + 32, rb);
                 tmem_ld_wait();
+                attn_mask(xa, kv0);
+                attn_mask(xb, kv0 + 32);
                 if (need_mask) { mask_chunk(xa, kv0, lim); mask_chunk(xb, kv0 + 32, lim); }
 #pragma unroll
                 for (int u = 0; u < 8; ++u) pm[u] = fmaxf(xa[u], xb[u]);
@@ -443,6 +462,8 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
                 tmem_ld32(s_tmem + 64, ra);
                 tmem_ld32(s_tmem + 96, rb);
                 tmem_ld_wait();
+                attn_mask(xa, kv0 + 64);
+                attn_mask(xb, kv0 + 96);
                 if (need_mask) { mask_chunk(xa, kv0 + 64, lim); mask_chunk(xb, kv0 + 96, lim); }
 #pragma unroll
                 for (int i = 0; i < 32; ++i) pm[i & 7] = fmax3(pm[i & 7], xa[i], xb[i]);
@@ -498,6 +519,8 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
                 tmem_ld32(s_tmem + 0, ra);
                 tmem_ld32(s_tmem + 32, rb);
                 tmem_ld_wait();
+                attn_mask(xa, kv0);
+                attn_mask(xb, kv0 + 32);
                 if (need_mask) { mask_chunk(xa, kv0, lim); mask_chunk(xb, kv0 + 32, lim); }
                 emit(xa, 0);
                 emit(xb, 1);
@@ -614,11 +637,12 @@ namespace {
 
 bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
 
-template <int D, bool BF16, int EMU>
-int run(const FwdArgs& a, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, cudaStream_t st) {
+template <int D, bool BF16, int EMU, bool MASK>
+int run(const FwdArgs& a, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const MaskView& mview,
+        cudaStream_t st) {
     using C = Cfg<D>;
-    auto kern_p = fwd_sm100_kernel<D, BF16, EMU, true>;
-    auto kern_1 = fwd_sm100_kernel<D, BF16, EMU, false>;
+    auto kern_p = fwd_sm100_kernel<D, BF16, EMU, true, MASK>;
+    auto kern_1 = fwd_sm100_kernel<D, BF16, EMU, false, MASK>;
     static bool attr_set = false;  // benign race: setting the same attribute twice is harmless
     if (!attr_set) {
         if (cuda_failed(cudaFuncSetAttribute(kern_p, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM),
@@ -637,6 +661,7 @@ int run(const FwdArgs& a, const CUtensorMap& mq, const CUtensorMap& mk, const CU
     p.o = a.o.data;
     p.os0 = a.o.stride[0]; p.os1 = a.o.stride[1]; p.os2 = a.o.stride[2];
     p.lse = (float*)a.lse;
+    p.mk = mview;
     int dev = 0;
     cudaGetDevice(&dev);
     p.status = device_status_word(dev);
@@ -683,18 +708,20 @@ int emu_setting() {
 }
 
 template <int D, bool BF16>
-int run_emu(const FwdArgs& a, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, cudaStream_t st) {
+int run_emu(const FwdArgs& a, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const MaskView& mview,
+            cudaStream_t st) {
+    if (mview.data) return run<D, BF16, 0, true>(a, mq, mk, mv, mview, st);  // masked: MUFU exponentials only
     switch (emu_setting()) {
-        case 4: return run<D, BF16, 4>(a, mq, mk, mv, st);
-        case 2: return run<D, BF16, 2>(a, mq, mk, mv, st);
-        default: return run<D, BF16, 0>(a, mq, mk, mv, st);
+        case 4: return run<D, BF16, 4, false>(a, mq, mk, mv, mview, st);
+        case 2: return run<D, BF16, 2, false>(a, mq, mk, mv, mview, st);
+        default: return run<D, BF16, 0, false>(a, mq, mk, mv, mview, st);
     }
 }
 
 }  // namespace
 
 bool fwd_sm100_supported(const FwdArgs& a) {
-    if (a.has_mask) return false;
+    if (a.has_mask && !mask_supported(a.mask)) return false;
     if (a.q.dtype != BF16 && a.q.dtype != F16) return false;
     if (a.k.dtype != a.q.dtype || a.v.dtype != a.q.dtype || a.o.dtype != a.q.dtype) return false;
     if (a.sh.D != a.sh.Dv || (a.sh.D != 64 && a.sh.D != 128)) return false;
@@ -717,8 +744,16 @@ int launch_fwd_sm100(const FwdArgs& a, cudaStream_t st) {
     if (!make_tma_map_4d(&mq, a.q, a.sh.D, bf16, BM) || !make_tma_map_4d(&mk, a.k, a.sh.D, bf16, BN) ||
         !make_tma_map_4d(&mv, a.v, a.sh.Dv, bf16, BN))
         return -1;
-    if (a.sh.D == 128) return bf16 ? run_emu<128, true>(a, mq, mk, mv, st) : run_emu<128, false>(a, mq, mk, mv, st);
-    return bf16 ? run_emu<64, true>(a, mq, mk, mv, st) : run_emu<64, false>(a, mq, mk, mv, st);
+    MaskView mview;
+    void* table = nullptr;
+    if (a.has_mask && build_mask_view(a.mask, a.sh.B, a.sh.H, a.sh.L, a.sh.S, a.scale, mview, &table, st) != 0) return -1;
+    int rc;
+    if (a.sh.D == 128)
+        rc = bf16 ? run_emu<128, true>(a, mq, mk, mv, mview, st) : run_emu<128, false>(a, mq, mk, mv, mview, st);
+    else
+        rc = bf16 ? run_emu<64, true>(a, mq, mk, mv, mview, st) : run_emu<64, false>(a, mq, mk, mv, mview, st);
+    if (table) cudaFreeAsync(table, st);  // after the kernel on the same stream
+    return rc;
 }
 
 }  // namespace gtb

@@ -12,7 +12,7 @@ Differences from the reference, by design:
   every key is masked, the forward gives 0 (as the reference) and the backward gives zero
   gradients; the reference's op-by-op backward would instead differentiate a softmax over
   -1e9 scores there.
-* The dropout path (dropout_p > 0) is the reference's composite of basic ops, run in torch.
+* The dropout path (dropout_p > 0) is a composite of torch ops with the reference's semantics.
 """
 
 from __future__ import annotations
@@ -80,16 +80,19 @@ def _native_mask(mask: torch.Tensor, B: int, H: int, L: int, S: int) -> _C.Tenso
     return _t4(mask, shape, stride)
 
 
-def sdpa_forward(q, k, v, mask=None, scale: float | None = None, is_causal: bool = False, need_lse: bool = True):
+def sdpa_forward(q, k, v, mask=None, scale: float | None = None, is_causal: bool = False, need_lse: bool = True,
+                 out: torch.Tensor | None = None):
     """One call of the native forward: returns (out, lse). lse is (B, H, L), float64 for float64
-    inputs and float32 otherwise, or None."""
+    inputs and float32 otherwise, or None. `out`, if given, is a (B, H, L, Dv) tensor or view of q's
+    dtype on q's device that receives the result (any strides; it is returned)."""
     _require_cuda("flash_attention", q, k, v, mask)
     if q.ndim != 4 or k.ndim != 4 or v.ndim != 4:
         raise RuntimeError("flash_attention expects 4D q, k, v tensors (B, H, L, D)")
     B, H, L, D = q.shape
     S, Dv = k.shape[2], v.shape[3]
     sc = (1.0 / math.sqrt(D)) if scale is None else float(scale)
-    out = torch.empty((B, H, L, Dv), dtype=q.dtype, device=q.device)
+    if out is None:
+        out = torch.empty((B, H, L, Dv), dtype=q.dtype, device=q.device)
     lse_dt = torch.float64 if q.dtype == torch.float64 else torch.float32
     lse = torch.empty((B, H, L), dtype=lse_dt, device=q.device) if need_lse else None
     mt = _native_mask(mask, B, H, L, S) if mask is not None else None
@@ -103,18 +106,22 @@ def sdpa_forward(q, k, v, mask=None, scale: float | None = None, is_causal: bool
 
 
 def sdpa_backward(grad_out, q, k, v, mask, out, lse, scale: float, is_causal: bool,
-                  deterministic: bool | None = None):
+                  deterministic: bool | None = None, grads=None):
     """One call of the native backward: returns (dq, dk, dv). With `deterministic` (default: whether
     torch.use_deterministic_algorithms is on) dq comes from the separate dq kernel and has the same
     bits on every run; otherwise, for head size 128, dq is summed with f32 reductions in global
-    memory inside the dK/dV kernel (faster; the last bit may vary from run to run)."""
+    memory inside the dK/dV kernel (faster; the last bit may vary from run to run). `grads`, if given,
+    is a (dq, dk, dv) triple of tensors or views shaped like q, k, v that receive the result."""
     if deterministic is None:
         deterministic = torch.are_deterministic_algorithms_enabled()
     B, H, L, D = q.shape
     S = k.shape[2]
-    dq = torch.empty_like(q, memory_format=torch.contiguous_format)
-    dk = torch.empty_like(k, memory_format=torch.contiguous_format)
-    dv = torch.empty_like(v, memory_format=torch.contiguous_format)
+    if grads is None:
+        dq = torch.empty_like(q, memory_format=torch.contiguous_format)
+        dk = torch.empty_like(k, memory_format=torch.contiguous_format)
+        dv = torch.empty_like(v, memory_format=torch.contiguous_format)
+    else:
+        dq, dk, dv = grads
     if grad_out.dtype != q.dtype:
         grad_out = grad_out.to(q.dtype)
     mt = _native_mask(mask, B, H, L, S) if mask is not None else None
@@ -133,13 +140,17 @@ class FlashAttentionFn(torch.autograd.Function):
     """The autograd Function behind scaled_dot_product_attention (reference _functions.py:1922).
 
     apply(q, k, v, mask, scale, is_causal): q (B,H,L,D), k (B,Hkv,S,D), v (B,Hkv,S,Dv), mask None,
-    (L,S) or 4-D, bool (True = may attend) or float (added); scale None -> 1/sqrt(D)."""
+    (L,S) or 4-D, bool (True = may attend) or float (added); scale None -> 1/sqrt(D).
+
+    The forward keeps what the backward needs to skip recomputing the softmax normaliser: the output
+    and the per-row log-sum-exp (the reference keeps only the inputs and rebuilds the probabilities
+    with separate ops, _functions.py:1934-1965)."""
 
     @staticmethod
     def forward(ctx, q, k, v, mask, scale, is_causal):
-        ctx.scale = float(scale) if scale is not None else (1.0 / math.sqrt(q.shape[-1]))
-        ctx.is_causal = bool(is_causal)
-        out, lse = sdpa_forward(q, k, v, mask, ctx.scale, ctx.is_causal, need_lse=True)
+        opts = (1.0 / math.sqrt(q.shape[-1]) if scale is None else float(scale), bool(is_causal))
+        out, lse = sdpa_forward(q, k, v, mask, *opts, need_lse=True)
+        ctx.opts = opts
         ctx.save_for_backward(q, k, v, mask, out, lse)
         return out
 
@@ -148,7 +159,7 @@ class FlashAttentionFn(torch.autograd.Function):
         if grad_out is None:
             return (None,) * 6
         q, k, v, mask, out, lse = ctx.saved_tensors
-        dq, dk, dv = sdpa_backward(grad_out, q, k, v, mask, out, lse, ctx.scale, ctx.is_causal)
+        dq, dk, dv = sdpa_backward(grad_out, q, k, v, mask, out, lse, *ctx.opts)
         return dq, dk, dv, None, None, None
 
 
@@ -159,6 +170,23 @@ def _autocast_lower(*ts):
         return ts, False
     dt = torch.get_autocast_dtype("cuda")
     return tuple(t.to(dt) if (t is not None and t.is_floating_point()) else t for t in ts), True
+
+
+def _as_4d_mask(mask: torch.Tensor, query: torch.Tensor, key: torch.Tensor) -> torch.Tensor:
+    """A mask of rank <= 4 lined up against the attention weights (B, H, L, S) from the right; each
+    of its dimensions must be 1 or the full size (the reference's rule, nn/functional.py:735-746).
+    Returns it as a 4-D view."""
+    if query.ndim != 4 or key.ndim != 4:
+        return mask  # the native call reports the shape error
+    target = (query.shape[0], query.shape[1], query.shape[2], key.shape[2])
+    lead = 4 - mask.ndim
+    padded = (1,) * max(lead, 0) + tuple(mask.shape)
+    if lead < 0 or any(size not in (1, full) for size, full in zip(padded, target)):
+        raise RuntimeError(
+            f"scaled_dot_product_attention: attn_mask of shape {list(mask.shape)} cannot be broadcast "
+            f"to the attention weights {list(target)}"
+        )
+    return mask if lead == 0 else mask.reshape(padded)  # leading size-1 dimensions: a view
 
 
 def scaled_dot_product_attention(
@@ -174,26 +202,19 @@ def scaled_dot_product_attention(
     """torch.nn.functional.scaled_dot_product_attention, as gguf_train defines it
     (nn/functional.py:724-767): a bool mask marks keys that MAY be attended, a float mask is added,
     masks broadcast from the right against (B, H, L, S), GQA applies whenever H % Hkv == 0
-    (`enable_gqa` is accepted and ignored), causal masking is top-left aligned."""
-    (enable_gqa,)
-    (query, key, value, attn_mask), cast = _autocast_lower(query, key, value, attn_mask)
+    (`enable_gqa` changes nothing), causal masking is top-left aligned. Without dropout the call is
+    FlashAttentionFn on the sm_100a kernels; with dropout it is the composite of
+    _attention_with_dropout."""
+    del enable_gqa
+    lowered, cast = _autocast_lower(query, key, value, attn_mask)
     if cast:
         with torch.autocast("cuda", enabled=False):
-            return scaled_dot_product_attention(query, key, value, attn_mask, dropout_p, is_causal, scale)
-    sc = (1.0 / math.sqrt(query.shape[-1])) if scale is None else float(scale)
-    if attn_mask is not None:
-        if query.ndim == 4 and key.ndim == 4:
-            want = (query.shape[0], query.shape[1], query.shape[2], key.shape[2])
-            if attn_mask.ndim > 4 or any(m != 1 and m != w for m, w in zip(reversed(attn_mask.shape), reversed(want))):
-                raise RuntimeError(
-                    f"scaled_dot_product_attention: attn_mask of shape {list(attn_mask.shape)} cannot be broadcast "
-                    f"to the attention weights {list(want)}"
-                )
-            if attn_mask.ndim != 4:
-                attn_mask = attn_mask.reshape((1,) * (4 - attn_mask.ndim) + tuple(attn_mask.shape))
-    if dropout_p == 0.0:
-        return FlashAttentionFn.apply(query, key, value, attn_mask, sc, is_causal)
-    return _sdpa_dropout(query, key, value, attn_mask, dropout_p, is_causal, sc)
+            return scaled_dot_product_attention(*lowered, dropout_p, is_causal, scale)
+    sc = 1.0 / math.sqrt(query.shape[-1]) if scale is None else float(scale)
+    mask = None if attn_mask is None else _as_4d_mask(attn_mask, query, key)
+    if dropout_p != 0.0:
+        return _attention_with_dropout(query, key, value, mask, float(dropout_p), bool(is_causal), sc)
+    return FlashAttentionFn.apply(query, key, value, mask, sc, is_causal)
 
 
 def sdpa_from_host(query: torch.Tensor, key: torch.Tensor, value: torch.Tensor, out: torch.Tensor | None = None,
@@ -243,26 +264,24 @@ def sdpa_from_host(query: torch.Tensor, key: torch.Tensor, value: torch.Tensor, 
     return out
 
 
-def _sdpa_dropout(query, key, value, attn_mask, dropout_p, is_causal, sc):
-    """The reference's dropout path (nn/functional.py:750-767): a composite of basic ops with -1e9
-    masking, run in torch (the engine has no fused dropout kernel)."""
-    B, H, L, D = query.shape
-    H_kv = key.shape[1]
-    k_u = key if H == H_kv else key.repeat_interleave(H // H_kv, dim=1)
-    v_u = value if H == H_kv else value.repeat_interleave(H // H_kv, dim=1)
-    scores = query.matmul(k_u.transpose(-2, -1)) * sc
+def _attention_with_dropout(q, k, v, mask, dropout_p: float, is_causal: bool, scale: float):
+    """Attention with dropout on the probabilities, the reference's dropout path
+    (nn/functional.py:750-767): masked entries (causal s > l, bool False) get -1e9 added or set, a
+    float mask is added, softmax over keys, dropout, then the weighted sum of v. Composed of torch
+    ops (the engine has no fused dropout kernel). Each kv head's query heads are stacked along the
+    rows, so k and v are used as they are instead of being repeated per query head."""
+    B, H, L, D = q.shape
+    Hkv, S, Dv = k.shape[1], k.shape[2], v.shape[3]
+    per_kv = H // Hkv
+    stacked = q.reshape(B, Hkv, per_kv * L, D)
+    logits = torch.matmul(stacked, k.transpose(-1, -2)).view(B, H, L, S) * scale
     if is_causal:
-        S = key.shape[-2]
-        cm = torch.ones((L, S), dtype=query.dtype, device=query.device).triu(diagonal=1) * (-1e9)
-        scores = scores + cm
-    if attn_mask is not None:
-        if attn_mask.dtype == torch.bool:
-            scores = scores.masked_fill(~attn_mask, -1e9)
-        else:
-            scores = scores + attn_mask
-    probs = torch.softmax(scores, dim=-1)
-    probs = torch.nn.functional.dropout(probs, p=dropout_p, training=True)
-    return probs.matmul(v_u)
+        above = torch.ones((L, S), dtype=torch.bool, device=q.device).triu(1)
+        logits = logits + above.to(logits.dtype) * -1e9
+    if mask is not None:
+        logits = logits.masked_fill(mask.logical_not(), -1e9) if mask.dtype == torch.bool else logits + mask
+    probs = torch.nn.functional.dropout(torch.softmax(logits, dim=-1), p=dropout_p, training=True)
+    return torch.matmul(probs.reshape(B, Hkv, per_kv * L, S), v).view(B, H, L, Dv)
 
 
 # ------------------------------------------------------------------ Q8_0 KV cache

@@ -1,11 +1,22 @@
 """nn.MultiheadAttention of gguf_train over the engine's attention.
 
-Same constructor, forward signature, layouts (batch_first, unbatched), mask rules and error
-messages as the reference (gguf_train/nn/modules/transformer.py:21-191). With need_weights=False
-attention runs through this package's scaled_dot_product_attention (the sm_100a path); with the
-default need_weights=True the reference materialises the weights with explicit matmul + softmax
-(:153-166), and so does this module, in torch. The in/out projections are plain torch linear
-layers (library GEMMs).
+Interface (kept so that the module is a drop-in): the constructor's arguments and the parameter
+names and shapes (in_proj_weight or q/k/v_proj_weight, in_proj_bias, out_proj), Xavier-uniform
+initialisation in that order, the forward's arguments and return value, the (L, E) / (L, B, E) /
+(B, L, E) layouts, the mask conventions (True in a bool attn_mask or key_padding_mask = NOT attended,
+turned into -1e9; float masks added) and the error messages of the reference
+(gguf_train/nn/modules/transformer.py:21-191).
+
+How it runs here:
+* self-attention with packed weights projects q, k and v with ONE GEMM over in_proj_weight and takes
+  the heads as strided views of its output (no copies); the attention kernels read those views
+  directly;
+* attn_mask and key_padding_mask are merged into one additive mask, which the tensor-core kernels
+  apply per 128 x 128 block (a key-padding mask costs almost nothing: only the blocks holding padded
+  keys are read entry by entry);
+* need_weights=False: scaled_dot_product_attention (the sm_100a path, forward and backward);
+  need_weights=True: the probabilities are formed explicitly (they are returned), as the reference
+  does, with torch ops.
 """
 
 from __future__ import annotations
@@ -21,134 +32,148 @@ class MultiheadAttention(nn.Module):
                  add_bias_kv: bool = False, add_zero_attn: bool = False, kdim: int | None = None,
                  vdim: int | None = None, batch_first: bool = False, device=None, dtype=None) -> None:
         super().__init__()
-        self.embed_dim = int(embed_dim)
-        self.num_heads = int(num_heads)
-        self.head_dim = self.embed_dim // self.num_heads
-        assert self.head_dim * self.num_heads == self.embed_dim, "embed_dim must be divisible by num_heads"
+        E, heads = int(embed_dim), int(num_heads)
+        self.embed_dim, self.num_heads = E, heads
+        self.head_dim = E // heads
+        assert self.head_dim * heads == E, "embed_dim must be divisible by num_heads"
         self.dropout = float(dropout)
         self.batch_first = bool(batch_first)
-        self.kdim = self.embed_dim if kdim is None else int(kdim)
-        self.vdim = self.embed_dim if vdim is None else int(vdim)
-        dt = dtype or torch.get_default_dtype()
-        self._qkv_same = self.kdim == self.embed_dim and self.vdim == self.embed_dim
-        if self._qkv_same:
-            self.in_proj_weight = nn.Parameter(torch.empty((3 * self.embed_dim, self.embed_dim), dtype=dt, device=device))
-            self.register_parameter("q_proj_weight", None)
-            self.register_parameter("k_proj_weight", None)
-            self.register_parameter("v_proj_weight", None)
-            nn.init.xavier_uniform_(self.in_proj_weight)
-        else:
-            self.register_parameter("in_proj_weight", None)
-            self.q_proj_weight = nn.Parameter(torch.empty((self.embed_dim, self.embed_dim), dtype=dt, device=device))
-            self.k_proj_weight = nn.Parameter(torch.empty((self.embed_dim, self.kdim), dtype=dt, device=device))
-            self.v_proj_weight = nn.Parameter(torch.empty((self.embed_dim, self.vdim), dtype=dt, device=device))
-            nn.init.xavier_uniform_(self.q_proj_weight)
-            nn.init.xavier_uniform_(self.k_proj_weight)
-            nn.init.xavier_uniform_(self.v_proj_weight)
-        if bias:
-            self.in_proj_bias = nn.Parameter(torch.zeros((3 * self.embed_dim,), dtype=dt, device=device))
-        else:
-            self.register_parameter("in_proj_bias", None)
-        self.out_proj = nn.Linear(self.embed_dim, self.embed_dim, bias=bias, device=device, dtype=dt)
+        self.kdim = E if kdim is None else int(kdim)
+        self.vdim = E if vdim is None else int(vdim)
+        self._qkv_same = self.kdim == E and self.vdim == E
+        make = dict(device=device, dtype=dtype or torch.get_default_dtype())
+        shapes = ({"in_proj_weight": (3 * E, E)} if self._qkv_same else
+                  {"q_proj_weight": (E, E), "k_proj_weight": (E, self.kdim), "v_proj_weight": (E, self.vdim)})
+        # registration (and so initialisation) order: in_proj_weight, q, k, v
+        for name in ("in_proj_weight", "q_proj_weight", "k_proj_weight", "v_proj_weight"):
+            if name in shapes:
+                self.register_parameter(name, nn.Parameter(nn.init.xavier_uniform_(torch.empty(shapes[name], **make))))
+            else:
+                self.register_parameter(name, None)
+        self.register_parameter("in_proj_bias", nn.Parameter(torch.zeros(3 * E, **make)) if bias else None)
+        self.out_proj = nn.Linear(E, E, bias=bias, **make)
+
+    # ---------------------------------------------------------------- forward
 
     def forward(self, query, key, value, key_padding_mask=None, need_weights: bool = True, attn_mask=None,
                 average_attn_weights: bool = True, is_causal: bool = False):
-        is_batched = query.ndim == 3
-        if not is_batched:
-            if query.ndim != 2 or key.ndim != 2 or value.ndim != 2:
-                raise RuntimeError(
-                    "MultiheadAttention: query, key and value must all be 3-D (batched) or all 2-D (unbatched), "
-                    f"got {query.ndim}-D, {key.ndim}-D and {value.ndim}-D"
-                )
-            batch_dim = 0 if self.batch_first else 1
-            query, key, value = query.unsqueeze(batch_dim), key.unsqueeze(batch_dim), value.unsqueeze(batch_dim)
+        self_attention = query is key and key is value
+        xq, xk, xv, kpm, unbatched = self._batch_major(query, key, value, key_padding_mask)
+        B, L, S = xq.shape[0], xq.shape[1], xk.shape[1]
+        q, k, v = self._heads(xq, xk, xv, self_attention)
+        bias = self._score_bias(attn_mask, kpm, B, L, S, q.dtype)
+        scale = self.head_dim ** -0.5
+        p_drop = self.dropout if self.training else 0.0
+        if need_weights:
+            ctx, weights = _attend_with_weights(q, k, v, bias, is_causal, scale, p_drop, average_attn_weights)
+        else:
+            ctx = F.scaled_dot_product_attention(q, k, v, attn_mask=bias, dropout_p=p_drop, is_causal=is_causal,
+                                                 scale=scale)
+            weights = None
+        y = self.out_proj(ctx.transpose(1, 2).reshape(B, L, self.embed_dim))
+        if not self.batch_first:
+            y = y.transpose(0, 1)
+        if unbatched:
+            y = y.squeeze(0 if self.batch_first else 1)
+            weights = None if weights is None else weights.squeeze(0)
+        return y, weights
+
+    def _batch_major(self, query, key, value, key_padding_mask):
+        """(B, L, E) views of the inputs whatever their layout, the key-padding mask as (B, S), and
+        whether the call was unbatched."""
+        ranks = (query.ndim, key.ndim, value.ndim)
+        unbatched = query.ndim == 2
+        if ranks not in ((3, 3, 3), (2, 2, 2)):
+            raise RuntimeError(
+                "MultiheadAttention: query, key and value must all be 3-D (batched) or all 2-D (unbatched), "
+                f"got {query.ndim}-D, {key.ndim}-D and {value.ndim}-D"
+            )
+        if unbatched:
             if key_padding_mask is not None:
                 if key_padding_mask.ndim != 1:
                     raise RuntimeError(
                         "MultiheadAttention: key_padding_mask of an unbatched input must be 1-D (S), "
                         f"got {list(key_padding_mask.shape)}"
                     )
-                key_padding_mask = key_padding_mask.unsqueeze(0)
-        elif key.ndim != 3 or value.ndim != 3:
-            raise RuntimeError(
-                "MultiheadAttention: query, key and value must all be 3-D (batched) or all 2-D (unbatched), "
-                f"got {query.ndim}-D, {key.ndim}-D and {value.ndim}-D"
-            )
-        if not self.batch_first:
-            query, key, value = query.transpose(0, 1), key.transpose(0, 1), value.transpose(0, 1)
-        B, L, E = query.shape
-        S = key.shape[1]
-        if self._qkv_same:
-            wq, wk, wv = self.in_proj_weight.chunk(3, dim=0)
+                key_padding_mask = key_padding_mask[None]
+            xs = [t[None] for t in (query, key, value)]
+        elif self.batch_first:
+            xs = [query, key, value]
         else:
-            wq, wk, wv = self.q_proj_weight, self.k_proj_weight, self.v_proj_weight
-        if self.in_proj_bias is not None:
-            bq, bk, bv = self.in_proj_bias.chunk(3, dim=0)
-        else:
-            bq = bk = bv = None
-        q = torch.nn.functional.linear(query, wq, bq).reshape((B, L, self.num_heads, self.head_dim)).transpose(1, 2)
-        k = torch.nn.functional.linear(key, wk, bk).reshape((B, S, self.num_heads, self.head_dim)).transpose(1, 2)
-        v = torch.nn.functional.linear(value, wv, bv).reshape((B, S, self.num_heads, self.head_dim)).transpose(1, 2)
+            xs = [t.transpose(0, 1) for t in (query, key, value)]
+        return xs[0], xs[1], xs[2], key_padding_mask, unbatched
 
-        mask = None
+    def _heads(self, xq, xk, xv, self_attention: bool):
+        """Per-head q, k, v of shape (B, heads, len, head_dim). Self-attention with packed weights
+        takes one GEMM over in_proj_weight; the heads are views of its (B, L, 3, heads, head_dim) output."""
+        B, heads, hd = xq.shape[0], self.num_heads, self.head_dim
+        if self_attention and self._qkv_same:
+            qkv = torch.nn.functional.linear(xq, self.in_proj_weight, self.in_proj_bias)
+            q, k, v = qkv.reshape(B, xq.shape[1], 3, heads, hd).permute(2, 0, 3, 1, 4).unbind(0)
+            return q, k, v
+        if self._qkv_same:
+            weights = self.in_proj_weight.chunk(3)
+        else:
+            weights = (self.q_proj_weight, self.k_proj_weight, self.v_proj_weight)
+        biases = (None,) * 3 if self.in_proj_bias is None else self.in_proj_bias.chunk(3)
+        return tuple(torch.nn.functional.linear(x, w, bb).reshape(B, x.shape[1], heads, hd).transpose(1, 2)
+                     for x, w, bb in zip((xq, xk, xv), weights, biases))
+
+    def _score_bias(self, attn_mask, kpm, B: int, L: int, S: int, dtype):
+        """attn_mask ((L, S) or (B*heads, L, S)) and key_padding_mask ((B, S)) as one additive mask
+        that broadcasts against the scores (B, heads, L, S), or None."""
+        bias = None
         if attn_mask is not None:
             if attn_mask.ndim == 2:
                 if tuple(attn_mask.shape) != (L, S):
-                    raise RuntimeError(f"MultiheadAttention: the 2D attn_mask has shape {list(attn_mask.shape)}, expected {[L, S]}")
-                mask = self._additive_mask(attn_mask, q.dtype, "attn_mask").reshape((1, 1, L, S))
-            elif attn_mask.ndim == 3:
-                if tuple(attn_mask.shape) != (B * self.num_heads, L, S):
                     raise RuntimeError(
-                        f"MultiheadAttention: the 3D attn_mask has shape {list(attn_mask.shape)}, "
-                        f"expected {[B * self.num_heads, L, S]}"
-                    )
-                mask = self._additive_mask(attn_mask, q.dtype, "attn_mask").reshape((B, self.num_heads, L, S))
+                        f"MultiheadAttention: the 2D attn_mask has shape {list(attn_mask.shape)}, expected {[L, S]}")
+                bias = _additive(attn_mask, dtype, "attn_mask").reshape(1, 1, L, S)
+            elif attn_mask.ndim == 3:
+                want = [B * self.num_heads, L, S]
+                if list(attn_mask.shape) != want:
+                    raise RuntimeError(
+                        f"MultiheadAttention: the 3D attn_mask has shape {list(attn_mask.shape)}, expected {want}")
+                bias = _additive(attn_mask, dtype, "attn_mask").reshape(B, self.num_heads, L, S)
             else:
                 raise RuntimeError(f"MultiheadAttention: attn_mask must be 2D or 3D, got {attn_mask.ndim}D")
-        if key_padding_mask is not None:
-            if tuple(key_padding_mask.shape) != (B, S):
+        if kpm is not None:
+            if tuple(kpm.shape) != (B, S):
                 raise RuntimeError(
-                    f"MultiheadAttention: key_padding_mask has shape {list(key_padding_mask.shape)}, expected {[B, S]}"
-                )
-            km = self._additive_mask(key_padding_mask, q.dtype, "key_padding_mask").reshape((B, 1, 1, S))
-            mask = km if mask is None else (mask + km)
-
-        scale = 1.0 / (self.head_dim ** 0.5)
-        if not need_weights:
-            attn_out = F.scaled_dot_product_attention(
-                q, k, v, attn_mask=mask, dropout_p=self.dropout if self.training else 0.0, is_causal=is_causal,
-                scale=scale,
-            )
-            attn_weights = None
-        else:
-            scores = q.matmul(k.transpose(-2, -1)) * scale
-            if is_causal:
-                cm = torch.ones((L, S), dtype=q.dtype, device=q.device).triu(diagonal=1) * (-1e9)
-                scores = scores + cm
-            if mask is not None:
-                scores = scores + mask
-            attn_weights = torch.softmax(scores, dim=-1)
-            if self.dropout > 0.0 and self.training:
-                attn_weights = torch.nn.functional.dropout(attn_weights, p=self.dropout, training=True)
-            attn_out = attn_weights.matmul(v)
-            if average_attn_weights:
-                attn_weights = attn_weights.mean(dim=1)
-        out = attn_out.transpose(1, 2).reshape((B, L, E))
-        out = self.out_proj(out)
-        if not self.batch_first:
-            out = out.transpose(0, 1)
-        if not is_batched:
-            out = out.squeeze(1 if not self.batch_first else 0)
-            if attn_weights is not None:
-                attn_weights = attn_weights.squeeze(0)
-        return out, attn_weights
+                    f"MultiheadAttention: key_padding_mask has shape {list(kpm.shape)}, expected {[B, S]}")
+            pad = _additive(kpm, dtype, "key_padding_mask").reshape(B, 1, 1, S)
+            bias = pad if bias is None else bias + pad
+        return bias
 
     @staticmethod
     def _additive_mask(mask, dtype, name: str):
-        """torch.nn convention (transformer.py:179-191): True in a bool attn_mask or key_padding_mask
-        marks a position that must NOT be attended; it becomes -1e9. A float mask is added as is."""
-        if mask.dtype == torch.bool:
-            return torch.zeros(mask.shape, dtype=dtype, device=mask.device).masked_fill(mask, -1e9)
-        if not mask.is_floating_point():
-            raise RuntimeError(f"MultiheadAttention: {name} must be a boolean or floating point tensor, got {mask.dtype}")
-        return mask if mask.dtype == dtype else mask.to(dtype)
+        """The reference's helper under its name (transformer.py:179-191): a mask as an additive one."""
+        return _additive(mask, dtype, name)
+
+
+def _additive(mask: torch.Tensor, dtype, name: str) -> torch.Tensor:
+    """torch.nn convention: True in a bool mask = the position must NOT be attended, which becomes
+    -1e9 (as the reference writes it); a float mask is added as it is, in the scores' dtype."""
+    if mask.dtype == torch.bool:
+        return torch.where(mask, -1e9, 0.0).to(dtype)
+    if not mask.is_floating_point():
+        raise RuntimeError(f"MultiheadAttention: {name} must be a boolean or floating point tensor, got {mask.dtype}")
+    return mask.to(dtype)
+
+
+def _attend_with_weights(q, k, v, bias, is_causal: bool, scale: float, p_drop: float, average: bool):
+    """Attention that also returns its probabilities (MultiheadAttention's need_weights=True,
+    reference transformer.py:153-166): -1e9 is added above the diagonal when causal, then the mask;
+    softmax over keys; dropout (training only) applies to the returned probabilities too; the
+    weights are averaged over heads when `average`."""
+    L, S = q.shape[2], k.shape[2]
+    logits = torch.matmul(q, k.transpose(2, 3)) * scale
+    if is_causal:
+        logits = logits + torch.full((L, S), -1e9, dtype=logits.dtype, device=logits.device).triu(1)
+    if bias is not None:
+        logits = logits + bias
+    probs = torch.softmax(logits, dim=3)
+    if p_drop > 0.0:
+        probs = torch.nn.functional.dropout(probs, p=p_drop, training=True)
+    ctx = torch.matmul(probs, v)
+    return ctx, (probs.mean(dim=1) if average else probs)

@@ -41,8 +41,11 @@ typedef struct gtb_tensor4 {
  *   lse: NULL or a (B,H,L) contiguous buffer that receives the natural-log sum of exp(scores)
  *   per row (-inf for a row with no allowed key, whose output is 0): float64 for f64 inputs,
  *   float32 otherwise.
- * Kernel choice: bf16/f16 with D == Dv in {64,128}, unit inner stride and no mask runs the
- * tcgen05/TMA kernel; everything else runs the SIMT kernel (f32/f64 accumulate as the input).
+ * Kernel choice: bf16/f16 with D == Dv in {64,128}, unit inner stride, and no mask or a bool / f32 /
+ * f16 / bf16 mask, runs the tcgen05/TMA kernel; everything else runs the SIMT kernel (f32/f64
+ * accumulate as the input). With a mask, a pre-pass classifies each 128-row x 128-key block of it
+ * (every key allowed with nothing added / none allowed / mixed) into a small table from the
+ * stream-ordered allocator, and only mixed blocks read the mask entry by entry.
  * For L <= 8192 the tcgen05 kernel runs persistent CTAs that claim work from a 4-byte counter taken
  * from the stream-ordered allocator and zeroed on the stream. */
 GTB_API int gtb_sdpa_fwd(const gtb_tensor4 *q, const gtb_tensor4 *k, const gtb_tensor4 *v,
@@ -173,6 +176,10 @@ GTB_API int gtb_decode_q8_0_noalloc(const void *q, int q_dtype, const void *k_q8
 GTB_API int gtb_attn_merge(float *o_acc, float *lse_acc, const void *o_part, const float *lse_part,
                            int part_dtype, int64_t groups, int64_t rows, int64_t D, int64_t part_gstride,
                            int64_t lse_gstride, void *stream);
+
+/* Kernel family of the calling thread's last gtb_sdpa_fwd / gtb_sdpa_bwd call: "tcgen05" (tensor
+ * cores, TMA) or "simt" ("" before the first). Lets a caller or a test see which path a call took. */
+GTB_API const char *gtb_last_path(void);
 
 /* Thread-local message of the last failure ("" if none). */
 GTB_API const char *gtb_last_error(void);
