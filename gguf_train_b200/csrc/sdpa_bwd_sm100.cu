@@ -460,6 +460,10 @@ bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
         for (int it = 0; it < nit; ++it) {
             const int st = it & 1;
             const int q0 = (i_start + it % nq) * BT + wg * HB;  // first query of the sub-item
+            // the attention mask's class for this query tile and key block, and the query head (the
+            // class byte is read before the waits so that the load completes during them)
+            const int hq_it = hk * p.group + it / nq;
+            const uint8_t mcls = AMASK ? p.mk.tile_class(b, hq_it, i_start + it % nq, jt) : (uint8_t)MASK_NONE;
             ok = warp_wait(&st_full[st], (it >> 1) & 1, p.status, 45);  // lse2 / delta of this tile
             if (ok) ok = warp_wait(&s_full[wg], it & 1, p.status, 46);
             if (!ok || __any_sync(0xffffffffu, *(volatile int*)abort_flag)) break;
@@ -467,9 +471,6 @@ bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
             const float* lse_s = (const float*)(smem + OFF_ST + st * ST_BYTES + 2 * C::TILE) + wg * HB;  // -lse2
             const float* dl_s = lse_s + 128;                                                                 // -delta
             const uint64_t sc2 = f2_pack(p.scale_log2, p.scale_log2);
-            // the attention mask's class for this query tile and key block, and the query head
-            const int hq_it = hk * p.group + it / nq;
-            const uint8_t mcls = AMASK ? p.mk.tile_class(b, hq_it, i_start + it % nq, jt) : (uint8_t)MASK_NONE;
             // masking only where the causal diagonal crosses the sub-item: one branch per sub-item
             auto chunks = [&](auto masked) {
                 constexpr bool MASK = decltype(masked)::value;
@@ -803,11 +804,12 @@ bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
             mbar_arrive(qt_full);
         }
         for (int j = 0; j < nblk && ok; ++j) {
+            // the attention mask's class of this key block, read before the wait
+            const uint8_t mcls = AMASK ? p.mk.tile_class(b, h, tile, j) : (uint8_t)MASK_NONE;
             ok = warp_wait(&s_full[wg], j & 1, p.status, 57);
             if (!ok || __any_sync(0xffffffffu, *(volatile int*)abort_flag)) break;
             tc_fence_after();
             const int kv0 = j * BT + wg * HB;  // first key of the sub-item
-            const uint8_t mcls = AMASK ? p.mk.tile_class(b, h, tile, j) : (uint8_t)MASK_NONE;
             // masking only on ragged or diagonal blocks: one branch per sub-item
             auto chunks = [&](auto masked) {
                 constexpr bool MASK = decltype(masked)::value;

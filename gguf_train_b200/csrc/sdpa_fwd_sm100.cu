@@ -427,13 +427,14 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
             if constexpr (MASK) mrow = p.mk.row(b, h, min((int64_t)grow, p.L - 1));
             float m_used = -INFINITY, lsum = 0.0f;
             for (int j = 0; j < nb; ++j) {
+                // the attention mask's class for this tile and key block (the same for every row), read
+                // before the wait for the block's scores so that the load completes during the wait
+                const uint8_t mcls = MASK ? p.mk.tile_class(b, h, row0t / BM, j) : (uint8_t)MASK_NONE;
                 ok = warp_wait(&s_full[t], (u + j) & 1, p.status, 31);
                 if (!ok || __any_sync(0xffffffffu, *(volatile int*)abort_flag)) break;
                 tc_fence_after();
                 const int kv0 = j * BN;
                 const bool need_mask = (kv0 + BN > p.S) || (p.causal && kv0 + BN - 1 > row0t);
-                // the attention mask's class for this tile and key block (the same for every row)
-                const uint8_t mcls = MASK ? p.mk.tile_class(b, h, row0t / BM, j) : (uint8_t)MASK_NONE;
                 auto attn_mask = [&](float* x, int s0) {
                     if constexpr (MASK) {
                         if (mcls == MASK_MIXED) {
