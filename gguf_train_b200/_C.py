@@ -45,15 +45,25 @@ class Tensor4(ctypes.Structure):
 P4 = ctypes.POINTER(Tensor4)
 
 
+class SdpaOpts(ctypes.Structure):
+    """gtb_sdpa_opts (include/gtb_attn.h): flags, dropout probability, dropout seed."""
+    _fields_ = [("flags", ctypes.c_int32), ("dropout_p", ctypes.c_float), ("dropout_seed", ctypes.c_uint64)]
+
+
+POPTS = ctypes.POINTER(SdpaOpts)
+
+
 def _configure(lib: ctypes.CDLL) -> ctypes.CDLL:
     # raw-pointer ABI (gtb_attn.h)
     lib.gtb_sdpa_fwd.argtypes = [P4, P4, P4, P4, c_float, c_int, P4, c_void_p, c_void_p]
+    lib.gtb_sdpa_fwd_ex.argtypes = [P4, P4, P4, P4, c_float, c_int, P4, c_void_p, POPTS, c_void_p]
+    lib.gtb_sdpa_fwd_ex.restype = c_int
     lib.gtb_sdpa_fwd.restype = c_int
     lib.gtb_sdpa_fwd_host.argtypes = [P4, P4, P4, c_float, c_int, P4, c_int, c_void_p]
     lib.gtb_sdpa_fwd_host.restype = c_int
     lib.gtb_sdpa_bwd.argtypes = [P4, P4, P4, P4, P4, P4, c_void_p, c_float, c_int, P4, P4, P4, c_void_p]
     lib.gtb_sdpa_bwd.restype = c_int
-    lib.gtb_sdpa_bwd_ex.argtypes = [P4, P4, P4, P4, P4, P4, c_void_p, c_float, c_int, P4, P4, P4, c_int, c_void_p]
+    lib.gtb_sdpa_bwd_ex.argtypes = [P4, P4, P4, P4, P4, P4, c_void_p, c_float, c_int, P4, P4, P4, POPTS, c_void_p]
     lib.gtb_sdpa_bwd_ex.restype = c_int
     lib.gtb_q8_0_quantize.argtypes = [c_void_p, c_int, c_int64, c_int64, c_void_p, c_void_p]
     lib.gtb_q8_0_quantize.restype = c_int

@@ -13,6 +13,7 @@
 #include <string>
 #include <vector>
 
+#include "dropout.cuh"
 #include "gtb_common.cuh"
 #include "q8_0_internal.h"
 #include "rope.cuh"
@@ -373,8 +374,23 @@ GTB_API int gtb_selftest_wait_timeout(int64_t limit_cycles, void* stream) {
 
 GTB_API int gtb_sdpa_fwd(const gtb_tensor4* q, const gtb_tensor4* k, const gtb_tensor4* v, const gtb_tensor4* mask,
                          float scale, int is_causal, gtb_tensor4* out, void* lse, void* stream) {
+    return gtb_sdpa_fwd_ex(q, k, v, mask, scale, is_causal, out, lse, nullptr, stream);
+}
+
+GTB_API int gtb_sdpa_fwd_ex(const gtb_tensor4* q, const gtb_tensor4* k, const gtb_tensor4* v, const gtb_tensor4* mask,
+                            float scale, int is_causal, gtb_tensor4* out, void* lse, const gtb_sdpa_opts* opts,
+                            void* stream) {
     const char* ctx = "flash_attention";
     FwdArgs a;
+    if (opts && !(opts->dropout_p >= 0.0f && opts->dropout_p < 1.0f)) {
+        set_errorf("%s: dropout probability has to be between 0 and 1, but got %g", ctx, (double)opts->dropout_p);
+        return -1;
+    }
+    if (opts) {
+        a.drop_p = opts->dropout_p;
+        a.drop_thr = drop_threshold(opts->dropout_p);
+        a.drop_seed = opts->dropout_seed;
+    }
     if (!check_attn(ctx, q, k, v, mask, a.sh)) return -1;
     if (!out) {
         set_errorf("%s: out is NULL", ctx);
@@ -536,15 +552,20 @@ GTB_API int gtb_sdpa_fwd_host(const gtb_tensor4* q, const gtb_tensor4* k, const 
 GTB_API int gtb_sdpa_bwd(const gtb_tensor4* dout, const gtb_tensor4* q, const gtb_tensor4* k, const gtb_tensor4* v,
                          const gtb_tensor4* mask, const gtb_tensor4* out, const void* lse, float scale, int is_causal,
                          gtb_tensor4* dq, gtb_tensor4* dk, gtb_tensor4* dv, void* stream) {
-    return gtb_sdpa_bwd_ex(dout, q, k, v, mask, out, lse, scale, is_causal, dq, dk, dv, 0, stream);
+    return gtb_sdpa_bwd_ex(dout, q, k, v, mask, out, lse, scale, is_causal, dq, dk, dv, nullptr, stream);
 }
 
 GTB_API int gtb_sdpa_bwd_ex(const gtb_tensor4* dout, const gtb_tensor4* q, const gtb_tensor4* k, const gtb_tensor4* v,
                             const gtb_tensor4* mask, const gtb_tensor4* out, const void* lse, float scale, int is_causal,
-                            gtb_tensor4* dq, gtb_tensor4* dk, gtb_tensor4* dv, int flags, void* stream) {
+                            gtb_tensor4* dq, gtb_tensor4* dk, gtb_tensor4* dv, const gtb_sdpa_opts* opts, void* stream) {
     const char* ctx = "flash_attention_backward";
+    const int flags = opts ? opts->flags : 0;
     if (flags & ~GTB_BWD_DETERMINISTIC) {
         set_errorf("%s: unknown flags 0x%x", ctx, flags);
+        return -1;
+    }
+    if (opts && !(opts->dropout_p >= 0.0f && opts->dropout_p < 1.0f)) {
+        set_errorf("%s: dropout probability has to be between 0 and 1, but got %g", ctx, (double)opts->dropout_p);
         return -1;
     }
     BwdArgs a;
@@ -577,6 +598,11 @@ GTB_API int gtb_sdpa_bwd_ex(const gtb_tensor4* dout, const gtb_tensor4* q, const
     a.causal = is_causal ? 1 : 0;
     a.lse = lse;
     a.deterministic = (flags & GTB_BWD_DETERMINISTIC) != 0;
+    if (opts) {
+        a.drop_p = opts->dropout_p;
+        a.drop_thr = drop_threshold(opts->dropout_p);
+        a.drop_seed = opts->dropout_seed;
+    }
     cudaStream_t st = (cudaStream_t)stream;
     // GTB_BWD_SIMT=1 forces the SIMT kernels (used to cross-check the two implementations)
     static const int force_simt = env_int("GTB_BWD_SIMT", 0);

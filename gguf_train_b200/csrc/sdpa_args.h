@@ -22,6 +22,9 @@ struct FwdArgs {
     float scale;       // already resolved (> 0)
     int causal;
     void* lse;         // nullable, (B,H,L) contiguous; double for f64 inputs, else float
+    float drop_p = 0.0f;         // dropout probability of the attention weights (0: none)
+    uint32_t drop_thr = 0;       // keep threshold of dropout.cuh
+    uint64_t drop_seed = 0;
 };
 
 struct BwdArgs {
@@ -34,6 +37,9 @@ struct BwdArgs {
     const void* lse;   // (B,H,L) contiguous, from the forward (double for f64 inputs)
     void* scratch;     // B*H*L accumulators (float or double) for rowsum(dout * out)
     bool deterministic = false;  // the separate dQ kernel instead of f32 reductions in global memory
+    float drop_p = 0.0f;         // dropout of the forward this backward belongs to (same seed)
+    uint32_t drop_thr = 0;
+    uint64_t drop_seed = 0;
 };
 
 // SIMT kernels: any float dtype, any D/Dv <= 256, masks, any strides.

@@ -47,6 +47,7 @@
 #include <mutex>
 #include <type_traits>
 
+#include "dropout.cuh"
 #include "gtb_common.cuh"
 #include "mask_tiles.cuh"
 #include "sdpa_args.h"
@@ -202,6 +203,9 @@ struct KvP {
     float* dqacc;  // (B, H, Lpad, D) f32, zeroed: unscaled dQ sums (fused dQ only)
     int* status;
     MaskView mk;   // attention mask (AMASK instances only)
+    uint32_t drop_thr;  // dropout of the forward (DROP instances only): keep threshold, seed, 1 / (1 - p)
+    uint64_t drop_seed;
+    float inv_keep;
 };
 
 // Shared memory of the dK/dV kernel: K, V, two stages of (Q, dO, lse2, delta), with the fused dQ
@@ -219,7 +223,7 @@ struct KvSmem {
     static constexpr int SLACK = ALLOC - USED;
 };
 
-template <int D, bool BF16, bool FUSE, bool AMASK>
+template <int D, bool BF16, bool FUSE, bool AMASK, bool DROP>
 __global__ void __launch_bounds__(NTHREADS, 1)
 bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                 const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmG, const KvP p) {
@@ -464,6 +468,7 @@ bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
             // class byte is read before the waits so that the load completes during them)
             const int hq_it = hk * p.group + it / nq;
             const uint8_t mcls = AMASK ? p.mk.tile_class(b, hq_it, i_start + it % nq, jt) : (uint8_t)MASK_NONE;
+            const uint32_t hkey = DROP ? drop_head_key(p.drop_seed, (uint32_t)(b * p.H + hq_it)) : 0u;
             ok = warp_wait(&st_full[st], (it >> 1) & 1, p.status, 45);  // lse2 / delta of this tile
             if (ok) ok = warp_wait(&s_full[wg], it & 1, p.status, 46);
             if (!ok || __any_sync(0xffffffffu, *(volatile int*)abort_flag)) break;
@@ -488,6 +493,18 @@ bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
                             for (int i = 0; i < 32; ++i) ra[i] = __float_as_uint(-INFINITY);
                         }
                     }
+                    uint32_t kbits = 0xffffffffu;  // dropout: which of the 32 queries keep this key
+                    if constexpr (DROP) {
+                        // lane i holds the row key of query q0 + 32c + i; every thread tests its own key
+                        const uint32_t rk_lane = drop_row_key(hkey, (uint32_t)(q0 + c * 32 + lane));
+                        kbits = 0;
+#pragma unroll
+                        for (int i = 0; i < 32; ++i)
+                            kbits |= (drop_keep(__shfl_sync(0xffffffffu, rk_lane, i), (uint32_t)key, p.drop_thr) ? 1u : 0u) << i;
+#pragma unroll
+                        for (int i = 0; i < 32; ++i)  // dP of a dropped element contributes nothing; kept ones / (1 - p)
+                            rb[i] = ((kbits >> i) & 1u) ? __float_as_uint(__uint_as_float(rb[i]) * p.inv_keep) : 0u;
+                    }
 #pragma unroll
                     for (int i = 0; i < 32; i += 2) {
                         // packed two-lane f32: a = S * scale - lse2, ds = p * (dP - delta)
@@ -503,6 +520,10 @@ bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
                         float d0, d1;
                         f2_unpack(f2_mul(f2_pack(p0, p1), f2_add(f2_pack(__uint_as_float(rb[i]), __uint_as_float(rb[i + 1])),
                                                                  *(const uint64_t*)(dl_s + qc))), d0, d1);
+                        if constexpr (DROP) {  // dV takes the kept probabilities (scaled at the store)
+                            if (!((kbits >> i) & 1u)) p0 = 0.0f;
+                            if (!((kbits >> (i + 1)) & 1u)) p1 = 0.0f;
+                        }
                         pk[i / 2] = pack2<BF16>(p0, p1);
                         dk[i / 2] = pack2<BF16>(d0, d1);
                     }
@@ -557,7 +578,7 @@ bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
                     uint32_t v[32];
                     tmem_ld32(tmem + lane_addr + c * 32, v);
                     tmem_ld_wait();
-                    if (key < p.S) store_row32<BF16>(dvrow + c * 32, v, 1.0f);
+                    if (key < p.S) store_row32<BF16>(dvrow + c * 32, v, DROP ? p.inv_keep : 1.0f);
                     tmem_ld32(tmem + lane_addr + 128 + c * 32, v);
                     tmem_ld_wait();
                     if (key < p.S) store_row32<BF16>(dkrow + c * 32, v, p.scale);
@@ -597,9 +618,12 @@ struct DqP {
     const float* delta;
     int* status;
     MaskView mk;  // attention mask (AMASK instances only)
+    uint32_t drop_thr;
+    uint64_t drop_seed;
+    float inv_keep;
 };
 
-template <int D, bool BF16, bool AMASK>
+template <int D, bool BF16, bool AMASK, bool DROP>
 __global__ void __launch_bounds__(NTHREADS, 1)
 bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
               const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmG, const DqP p) {
@@ -784,6 +808,7 @@ bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
         const int lim = p.causal ? min(lim_s, row) : lim_s;  // last key this row may see
         const unsigned char* mrow = nullptr;  // mask entries of this row (padding rows read row L-1)
         if constexpr (AMASK) mrow = p.mk.row(b, h, min((int64_t)row, p.L - 1));
+        const uint32_t rkey = DROP ? drop_row_key(drop_head_key(p.drop_seed, (uint32_t)(b * p.H + h)), (uint32_t)row) : 0u;
         // warpgroup 0 copies its row of Q, warpgroup 1 its row of dO, from the 128-byte-swizzled tile
         // into TMEM (16-byte chunk c of row r of a 64-column slab sits at chunk c ^ (r & 7))
         bool ok = warp_wait(qg_full, 0, p.status, 59);
@@ -826,6 +851,12 @@ bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
 #pragma unroll
                             for (int i = 0; i < 32; ++i) ra[i] = __float_as_uint(-INFINITY);
                         }
+                    }
+                    if constexpr (DROP) {  // dP of a dropped element contributes nothing; kept ones / (1 - p)
+#pragma unroll
+                        for (int i = 0; i < 32; ++i)
+                            rb[i] = drop_keep(rkey, (uint32_t)(kv0 + c * 32 + i), p.drop_thr)
+                                        ? __float_as_uint(__uint_as_float(rb[i]) * p.inv_keep) : 0u;
                     }
 #pragma unroll
                     for (int i = 0; i < 32; i += 2) {
@@ -938,7 +969,7 @@ cudaStream_t side_stream(int dev) {
     return streams[dev];
 }
 
-template <int D, bool BF16, bool FUSE, bool AMASK>
+template <int D, bool BF16, bool FUSE, bool AMASK, bool DROP>
 int run_bwd(const BwdArgs& a, const MaskView& mview, cudaStream_t st) {
     using C = BCfg<D>;
     const int64_t B = a.sh.B, H = a.sh.H, L = a.sh.L, S = a.sh.S, Lpad = lpad_of(L);
@@ -972,10 +1003,10 @@ int run_bwd(const BwdArgs& a, const MaskView& mview, cudaStream_t st) {
     constexpr int SMEM_KV = KvSmem<D, FUSE>::ALLOC;
     constexpr int SMEM_DQ = 6 * C::TILE + 32 * 8 + 1024;  // + barriers, TMEM slot, flag
     if (!attr_set) {
-        if (cuda_failed(cudaFuncSetAttribute(bwd_dkdv_kernel<D, BF16, FUSE, AMASK>,
+        if (cuda_failed(cudaFuncSetAttribute(bwd_dkdv_kernel<D, BF16, FUSE, AMASK, DROP>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_KV),
                         "cudaFuncSetAttribute(bwd dkdv)") ||
-            (!FUSE && cuda_failed(cudaFuncSetAttribute(bwd_dq_kernel<D, BF16, AMASK>,
+            (!FUSE && cuda_failed(cudaFuncSetAttribute(bwd_dq_kernel<D, BF16, AMASK, DROP>,
                                                        cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_DQ),
                                   "cudaFuncSetAttribute(bwd dq)")))
             return -1;
@@ -984,12 +1015,13 @@ int run_bwd(const BwdArgs& a, const MaskView& mview, cudaStream_t st) {
     float* dqacc = FUSE ? delta + B * H * Lpad : nullptr;
     KvP kp{H, a.sh.Hkv, L, S, Lpad, group, n_qt, n_kvt, scale_log2, a.scale, a.causal,
            a.dk.data, a.dk.stride[0], a.dk.stride[1], a.dk.stride[2],
-           a.dv.data, a.dv.stride[0], a.dv.stride[1], a.dv.stride[2], lse2, delta, dqacc, status, mview};
+           a.dv.data, a.dv.stride[0], a.dv.stride[1], a.dv.stride[2], lse2, delta, dqacc, status, mview,
+           a.drop_thr, a.drop_seed, 1.0f / (1.0f - a.drop_p)};
     if constexpr (FUSE) {
         if (cuda_failed(cudaMemsetAsync(dqacc, 0, sizeof(float) * (size_t)(B * H * Lpad * D), st),
                         "flash_attention_backward: dQ sums reset"))
             return -1;
-        bwd_dkdv_kernel<D, BF16, true, AMASK><<<dim3((unsigned)n_kvt, (unsigned)a.sh.Hkv, (unsigned)B), NTHREADS, SMEM_KV, st>>>(
+        bwd_dkdv_kernel<D, BF16, true, AMASK, DROP><<<dim3((unsigned)n_kvt, (unsigned)a.sh.Hkv, (unsigned)B), NTHREADS, SMEM_KV, st>>>(
             mq, mk, mv, mg, kp);
         if (cuda_failed(cudaGetLastError(), "flash_attention_backward: dK/dV/dQ launch")) return -1;
         const int64_t n = B * H * L * 16;
@@ -998,7 +1030,8 @@ int run_bwd(const BwdArgs& a, const MaskView& mview, cudaStream_t st) {
         return cuda_failed(cudaGetLastError(), "flash_attention_backward: dQ conversion launch") ? -1 : 0;
     }
     DqP dp{H, a.sh.Hkv, L, S, Lpad, group, n_qt, n_kvt, scale_log2, a.scale, a.causal,
-           a.dq.data, a.dq.stride[0], a.dq.stride[1], a.dq.stride[2], lse2, delta, status, mview};
+           a.dq.data, a.dq.stride[0], a.dq.stride[1], a.dq.stride[2], lse2, delta, status, mview,
+           a.drop_thr, a.drop_seed, 1.0f / (1.0f - a.drop_p)};
     // dK/dV and dQ only share the preprocess output: dQ runs on a side stream, forked after the
     // preprocess and joined before returning, so that each kernel's last partial wave of CTAs leaves
     // no SM idle while the other still has work
@@ -1009,11 +1042,11 @@ int run_bwd(const BwdArgs& a, const MaskView& mview, cudaStream_t st) {
                      cudaEventRecord(fork, st) == cudaSuccess && cudaStreamWaitEvent(side, fork, 0) == cudaSuccess;
     cudaGetLastError();  // a failed fork falls back to one stream
     cudaStream_t dq_st = two ? side : st;
-    bwd_dkdv_kernel<D, BF16, false, AMASK><<<dim3((unsigned)n_kvt, (unsigned)a.sh.Hkv, (unsigned)B), NTHREADS, SMEM_KV, st>>>(
+    bwd_dkdv_kernel<D, BF16, false, AMASK, DROP><<<dim3((unsigned)n_kvt, (unsigned)a.sh.Hkv, (unsigned)B), NTHREADS, SMEM_KV, st>>>(
         mq, mk, mv, mg, kp);
     bool bad = cuda_failed(cudaGetLastError(), "flash_attention_backward: dK/dV launch");
     if (!bad) {
-        bwd_dq_kernel<D, BF16, AMASK><<<dim3((unsigned)n_qt, (unsigned)H, (unsigned)B), NTHREADS, SMEM_DQ, dq_st>>>(mq, mk, mv, mg, dp);
+        bwd_dq_kernel<D, BF16, AMASK, DROP><<<dim3((unsigned)n_qt, (unsigned)H, (unsigned)B), NTHREADS, SMEM_DQ, dq_st>>>(mq, mk, mv, mg, dp);
         bad = cuda_failed(cudaGetLastError(), "flash_attention_backward: dQ launch");
     }
     if (two) {
@@ -1047,15 +1080,20 @@ size_t bwd_sm100_scratch_bytes(const BwdArgs& a) {
     return sizeof(float) * rows * (2 + (fused_dq(a) ? (size_t)a.sh.D : 0));  // lse2, delta (+ dQ sums)
 }
 
-template <bool AMASK>
-int launch_bwd_masked(const BwdArgs& a, const MaskView& mview, cudaStream_t st) {
+template <bool AMASK, bool DROP>
+int launch_bwd_variant(const BwdArgs& a, const MaskView& mview, cudaStream_t st) {
     const bool bf16 = a.q.dtype == BF16;
     if (a.sh.D == 128) {
         if (fused_dq(a))
-            return bf16 ? run_bwd<128, true, true, AMASK>(a, mview, st) : run_bwd<128, false, true, AMASK>(a, mview, st);
-        return bf16 ? run_bwd<128, true, false, AMASK>(a, mview, st) : run_bwd<128, false, false, AMASK>(a, mview, st);
+            return bf16 ? run_bwd<128, true, true, AMASK, DROP>(a, mview, st) : run_bwd<128, false, true, AMASK, DROP>(a, mview, st);
+        return bf16 ? run_bwd<128, true, false, AMASK, DROP>(a, mview, st) : run_bwd<128, false, false, AMASK, DROP>(a, mview, st);
     }
-    return bf16 ? run_bwd<64, true, false, AMASK>(a, mview, st) : run_bwd<64, false, false, AMASK>(a, mview, st);
+    return bf16 ? run_bwd<64, true, false, AMASK, DROP>(a, mview, st) : run_bwd<64, false, false, AMASK, DROP>(a, mview, st);
+}
+
+template <bool AMASK>
+int launch_bwd_masked(const BwdArgs& a, const MaskView& mview, cudaStream_t st) {
+    return a.drop_p > 0.0f ? launch_bwd_variant<AMASK, true>(a, mview, st) : launch_bwd_variant<AMASK, false>(a, mview, st);
 }
 
 int launch_bwd_sm100(const BwdArgs& a, cudaStream_t st) {

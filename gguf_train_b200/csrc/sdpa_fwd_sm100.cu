@@ -37,6 +37,7 @@
 
 #include <cudaTypedefs.h>
 
+#include "dropout.cuh"
 #include "gtb_common.cuh"
 #include "mask_tiles.cuh"
 #include "sdpa_args.h"
@@ -133,6 +134,9 @@ struct Params {
     float* lse;
     int* status;
     MaskView mk;  // attention mask (MASK instances only)
+    uint32_t drop_thr;   // dropout (DROP instances only): keep threshold, seed, 1 / (1 - p)
+    uint64_t drop_seed;
+    float inv_keep;
 };
 
 // keys a row of tile t may see: [0, n_kv*BN) minus causal / ragged masking
@@ -151,7 +155,7 @@ __device__ __forceinline__ void mask_chunk(float* x, int kv0, int lim) {
         if (kv0 + i > lim) x[i] = -INFINITY;
 }
 
-template <int D, bool BF16, int EMU, bool PERSIST, bool MASK>
+template <int D, bool BF16, int EMU, bool PERSIST, bool MASK, bool DROP>
 __global__ void __launch_bounds__(NTHREADS, 1)
 fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                  const __grid_constant__ CUtensorMap tmV, const Params p) {
@@ -425,6 +429,8 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
             // mask entries of this row (padding rows past L read row L-1; their results are dropped)
             const unsigned char* mrow = nullptr;
             if constexpr (MASK) mrow = p.mk.row(b, h, min((int64_t)grow, p.L - 1));
+            // dropout: this row's key of the counter-based keep decisions (dropout.cuh)
+            const uint32_t rkey = DROP ? drop_row_key(drop_head_key(p.drop_seed, (uint32_t)(b * p.H + h)), (uint32_t)grow) : 0u;
             float m_used = -INFINITY, lsum = 0.0f;
             for (int j = 0; j < nb; ++j) {
                 // the attention mask's class for this tile and key block (the same for every row), read
@@ -495,6 +501,12 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
                 uint64_t ps2[2] = {0ull, 0ull};
                 auto emit = [&](const float* x, int c) {
                     uint32_t pk[16];
+                    uint32_t kbits = 0;  // dropout: keep decisions of keys kv0 + 32c .. kv0 + 32c + 31
+                    if constexpr (DROP) {
+#pragma unroll
+                        for (int i = 0; i < 32; ++i)
+                            kbits |= (drop_keep(rkey, (uint32_t)(kv0 + 32 * c + i), p.drop_thr) ? 1u : 0u) << i;
+                    }
 #pragma unroll
                     for (int i = 0; i < 32; i += 2) {
                         const uint64_t a2 = f2_fma(f2_pack(x[i], x[i + 1]), sc2, nm2);
@@ -506,9 +518,13 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
                             f2_unpack(a2, a0, a1);
                             p2 = f2_pack(ex2(a0), ex2(a1));
                         }
-                        ps2[(i >> 1) & 1] = f2_add(ps2[(i >> 1) & 1], p2);
+                        ps2[(i >> 1) & 1] = f2_add(ps2[(i >> 1) & 1], p2);  // the normaliser: undropped
                         float p0, p1;
                         f2_unpack(p2, p0, p1);
+                        if constexpr (DROP) {  // the PV product takes only the kept probabilities
+                            if (!((kbits >> i) & 1u)) p0 = 0.0f;
+                            if (!((kbits >> (i + 1)) & 1u)) p1 = 0.0f;
+                        }
                         pk[i / 2] = pack2<BF16>(p0, p1);
                     }
                     tmem_st16(s_tmem + P_OFF + c * 16, pk);
@@ -541,7 +557,7 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
                 ok = warp_wait(&o_final[t], nf & 1, p.status, 33);
                 if (ok) {
                     tc_fence_after();
-                    const float inv = lsum > 0.0f ? 1.0f / lsum : 0.0f;
+                    const float inv = lsum > 0.0f ? (DROP ? p.inv_keep : 1.0f) / lsum : 0.0f;
                     T* orow = (T*)p.o + (int64_t)b * p.os0 + (int64_t)h * p.os1 + (int64_t)grow * p.os2;
 #pragma unroll
                     for (int c = 0; c < D / 32; ++c) {
@@ -638,12 +654,12 @@ namespace {
 
 bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
 
-template <int D, bool BF16, int EMU, bool MASK>
+template <int D, bool BF16, int EMU, bool MASK, bool DROP>
 int run(const FwdArgs& a, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const MaskView& mview,
         cudaStream_t st) {
     using C = Cfg<D>;
-    auto kern_p = fwd_sm100_kernel<D, BF16, EMU, true, MASK>;
-    auto kern_1 = fwd_sm100_kernel<D, BF16, EMU, false, MASK>;
+    auto kern_p = fwd_sm100_kernel<D, BF16, EMU, true, MASK, DROP>;
+    auto kern_1 = fwd_sm100_kernel<D, BF16, EMU, false, MASK, DROP>;
     static bool attr_set = false;  // benign race: setting the same attribute twice is harmless
     if (!attr_set) {
         if (cuda_failed(cudaFuncSetAttribute(kern_p, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM),
@@ -663,6 +679,9 @@ int run(const FwdArgs& a, const CUtensorMap& mq, const CUtensorMap& mk, const CU
     p.os0 = a.o.stride[0]; p.os1 = a.o.stride[1]; p.os2 = a.o.stride[2];
     p.lse = (float*)a.lse;
     p.mk = mview;
+    p.drop_thr = a.drop_thr;
+    p.drop_seed = a.drop_seed;
+    p.inv_keep = 1.0f / (1.0f - a.drop_p);
     int dev = 0;
     cudaGetDevice(&dev);
     p.status = device_status_word(dev);
@@ -711,11 +730,15 @@ int emu_setting() {
 template <int D, bool BF16>
 int run_emu(const FwdArgs& a, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const MaskView& mview,
             cudaStream_t st) {
-    if (mview.data) return run<D, BF16, 0, true>(a, mq, mk, mv, mview, st);  // masked: MUFU exponentials only
+    // masked or dropout: MUFU exponentials only
+    if (a.drop_p > 0.0f)
+        return mview.data ? run<D, BF16, 0, true, true>(a, mq, mk, mv, mview, st)
+                          : run<D, BF16, 0, false, true>(a, mq, mk, mv, mview, st);
+    if (mview.data) return run<D, BF16, 0, true, false>(a, mq, mk, mv, mview, st);
     switch (emu_setting()) {
-        case 4: return run<D, BF16, 4, false>(a, mq, mk, mv, mview, st);
-        case 2: return run<D, BF16, 2, false>(a, mq, mk, mv, mview, st);
-        default: return run<D, BF16, 0, false>(a, mq, mk, mv, mview, st);
+        case 4: return run<D, BF16, 4, false, false>(a, mq, mk, mv, mview, st);
+        case 2: return run<D, BF16, 2, false, false>(a, mq, mk, mv, mview, st);
+        default: return run<D, BF16, 0, false, false>(a, mq, mk, mv, mview, st);
     }
 }
 

@@ -15,6 +15,7 @@
 #include <cfloat>
 #include <cmath>
 
+#include "dropout.cuh"
 #include "gtb_common.cuh"
 #include "sdpa_args.h"
 
@@ -60,6 +61,10 @@ struct FwdP {
     float scale;
     int causal;
     void* lse;  // Acc[B*H*L]
+    int drop;   // dropout of the attention probabilities (dropout.cuh)
+    uint32_t drop_thr;
+    uint64_t drop_seed;
+    float inv_keep;  // 1 / (1 - p)
 };
 
 struct BwdP {
@@ -70,6 +75,10 @@ struct BwdP {
     int causal;
     const void* lse;  // Acc[B*H*L]
     void* rowsum;     // Acc[B*H*L]
+    int drop;
+    uint32_t drop_thr;
+    uint64_t drop_seed;
+    float inv_keep;
 };
 
 // score modifier: returns false if (b,h,l,s) may not be attended, else adds a float mask value
@@ -104,6 +113,7 @@ __global__ void __launch_bounds__(ROWS * 32) fwd_simt_kernel(FwdP p) {
     }
     int64_t s_end = p.S;
     if (p.causal) s_end = min(p.S, min(l0 + ROWS, p.L));  // keys 0 .. last row of the CTA
+    const uint32_t rkey = p.drop ? drop_row_key(drop_head_key(p.drop_seed, (uint32_t)(b * p.H + h)), (uint32_t)l) : 0u;
     Acc m = neg_inf<Acc>(), lsum = 0;
     Acc o[MAXI];
 #pragma unroll
@@ -135,11 +145,12 @@ __global__ void __launch_bounds__(ROWS * 32) fwd_simt_kernel(FwdP p) {
         if (m_new == neg_inf<Acc>()) continue;  // nothing allowed so far in this row
         const Acc alpha = (m == neg_inf<Acc>()) ? (Acc)0 : acc_exp(m - m_new);
         const Acc pj = (sc == neg_inf<Acc>()) ? (Acc)0 : acc_exp(sc - m_new);
-        lsum = lsum * alpha + warp_sum(pj);
+        lsum = lsum * alpha + warp_sum(pj);  // the normaliser sums the undropped probabilities
+        const Acc pv = (p.drop && !drop_keep(rkey, (uint32_t)s, p.drop_thr)) ? (Acc)0 : pj;
 #pragma unroll
         for (int i = 0; i < MAXI; ++i) o[i] *= alpha;
         for (int j = 0; j < KT; ++j) {
-            const Acc pb = __shfl_sync(0xffffffffu, pj, j);
+            const Acc pb = __shfl_sync(0xffffffffu, pv, j);
             if (pb == (Acc)0) continue;
             const Acc* vr = v_s + j * p.Dv;
 #pragma unroll
@@ -151,7 +162,7 @@ __global__ void __launch_bounds__(ROWS * 32) fwd_simt_kernel(FwdP p) {
         m = m_new;
     }
     if (!row_ok) return;
-    const Acc inv = lsum > (Acc)0 ? (Acc)1 / lsum : (Acc)0;
+    const Acc inv = lsum > (Acc)0 ? (p.drop ? (Acc)p.inv_keep : (Acc)1) / lsum : (Acc)0;
     T* og = (T*)p.o.p;
 #pragma unroll
     for (int i = 0; i < MAXI; ++i) {
@@ -210,6 +221,7 @@ __global__ void __launch_bounds__(ROWS * 32) bwd_dq_kernel(BwdP p) {
     const Acc di = row_ok ? ((const Acc*)p.rowsum)[row] : (Acc)0;
     int64_t s_end = p.S;
     if (p.causal) s_end = min(p.S, min(l0 + ROWS, p.L));
+    const uint32_t rkey = p.drop ? drop_row_key(drop_head_key(p.drop_seed, (uint32_t)(b * p.H + h)), (uint32_t)l) : 0u;
     Acc dq[MAXI];
 #pragma unroll
     for (int i = 0; i < MAXI; ++i) dq[i] = 0;
@@ -240,6 +252,7 @@ __global__ void __launch_bounds__(ROWS * 32) bwd_dq_kernel(BwdP p) {
                 const Acc* gr = g_s + warp * p.Dv;
                 const Acc* vr = v_s + lane * (p.Dv + 1);
                 for (int64_t d = 0; d < p.Dv; ++d) dp += gr[d] * vr[d];
+                if (p.drop) dp = drop_keep(rkey, (uint32_t)s, p.drop_thr) ? dp * (Acc)p.inv_keep : (Acc)0;
                 ds = pr * (dp - di);
             }
         }
@@ -328,7 +341,15 @@ __global__ void __launch_bounds__(ROWS * 32) bwd_dkdv_kernel(BwdP p) {
                     const Acc* gr = g_s + lane * (p.Dv + 1);
                     const Acc* vr = v_s + warp * p.Dv;
                     for (int64_t d = 0; d < p.Dv; ++d) dp += gr[d] * vr[d];
+                    Acc pv = pr;  // the probability the forward multiplied v by
+                    if (p.drop) {
+                        const bool kept = drop_keep(drop_row_key(drop_head_key(p.drop_seed, (uint32_t)(b * p.H + h)),
+                                                                 (uint32_t)l), (uint32_t)s, p.drop_thr);
+                        dp = kept ? dp * (Acc)p.inv_keep : (Acc)0;
+                        pv = kept ? pr * (Acc)p.inv_keep : (Acc)0;
+                    }
                     ds = pr * (dp - di_s[lane]);
+                    pr = pv;
                 }
             }
             for (int j = 0; j < KT; ++j) {
@@ -383,6 +404,8 @@ int run_fwd(const FwdArgs& a, cudaStream_t st) {
     p.H = a.sh.H; p.Hkv = a.sh.Hkv; p.L = a.sh.L; p.S = a.sh.S; p.D = a.sh.D; p.Dv = a.sh.Dv;
     p.group = a.sh.H / a.sh.Hkv;
     p.scale = a.scale; p.causal = a.causal; p.lse = a.lse;
+    p.drop = a.drop_p > 0.0f; p.drop_thr = a.drop_thr; p.drop_seed = a.drop_seed;
+    p.inv_keep = 1.0f / (1.0f - a.drop_p);
     const size_t smem = fwd_smem<Acc>(p.D, p.Dv);
     if (!set_smem(fwd_simt_kernel<T, Acc>, smem)) return -1;
     dim3 grid((unsigned)((p.L + ROWS - 1) / ROWS), (unsigned)p.H, (unsigned)a.sh.B);
@@ -400,6 +423,8 @@ int run_bwd(const BwdArgs& a, cudaStream_t st) {
     p.H = a.sh.H; p.Hkv = a.sh.Hkv; p.L = a.sh.L; p.S = a.sh.S; p.D = a.sh.D; p.Dv = a.sh.Dv;
     p.group = a.sh.H / a.sh.Hkv;
     p.scale = a.scale; p.causal = a.causal; p.lse = a.lse; p.rowsum = a.scratch;
+    p.drop = a.drop_p > 0.0f; p.drop_thr = a.drop_thr; p.drop_seed = a.drop_seed;
+    p.inv_keep = 1.0f / (1.0f - a.drop_p);
     const int64_t B = a.sh.B;
     const int64_t rows = B * p.H * p.L;
     if (rows > 0) {

@@ -12,7 +12,10 @@ Differences from the reference, by design:
   every key is masked, the forward gives 0 (as the reference) and the backward gives zero
   gradients; the reference's op-by-op backward would instead differentiate a softmax over
   -1e9 scores there.
-* The dropout path (dropout_p > 0) is a composite of torch ops with the reference's semantics.
+* Dropout (dropout_p > 0) runs inside the kernels: each keep/drop decision is a counter-based hash of
+  (seed, batch-head, query, key), so the backward recomputes the forward's mask without storing it;
+  the reference draws its mask from its sequential generator, so the masks differ, the semantics
+  (inverted dropout on the softmax probabilities) do not.
 """
 
 from __future__ import annotations
@@ -80,11 +83,24 @@ def _native_mask(mask: torch.Tensor, B: int, H: int, L: int, S: int) -> _C.Tenso
     return _t4(mask, shape, stride)
 
 
+def _opts(flags: int = 0, dropout_p: float = 0.0, seed: int = 0) -> _C.SdpaOpts:
+    o = _C.SdpaOpts()
+    o.flags, o.dropout_p, o.dropout_seed = int(flags), float(dropout_p), int(seed) & (2**64 - 1)
+    return o
+
+
+def dropout_seed() -> int:
+    """A dropout seed drawn from torch's default generator (so torch.manual_seed makes it repeat)."""
+    return int(torch.randint(0, 2**62, (), dtype=torch.int64).item())
+
+
 def sdpa_forward(q, k, v, mask=None, scale: float | None = None, is_causal: bool = False, need_lse: bool = True,
-                 out: torch.Tensor | None = None):
+                 out: torch.Tensor | None = None, dropout_p: float = 0.0, seed: int = 0):
     """One call of the native forward: returns (out, lse). lse is (B, H, L), float64 for float64
     inputs and float32 otherwise, or None. `out`, if given, is a (B, H, L, Dv) tensor or view of q's
-    dtype on q's device that receives the result (any strides; it is returned)."""
+    dtype on q's device that receives the result (any strides; it is returned). With dropout_p > 0 the
+    attention probabilities are dropped with that probability (kept ones scaled by 1/(1-p)) by the
+    counter-based decisions of `seed`; the lse is that of the undropped probabilities."""
     _require_cuda("flash_attention", q, k, v, mask)
     if q.ndim != 4 or k.ndim != 4 or v.ndim != 4:
         raise RuntimeError("flash_attention expects 4D q, k, v tensors (B, H, L, D)")
@@ -97,21 +113,23 @@ def sdpa_forward(q, k, v, mask=None, scale: float | None = None, is_causal: bool
     lse = torch.empty((B, H, L), dtype=lse_dt, device=q.device) if need_lse else None
     mt = _native_mask(mask, B, H, L, S) if mask is not None else None
     tq, tk, tv, to = _t4(q), _t4(k), _t4(v), _t4(out)
-    rc = _C.lib.gtb_sdpa_fwd(ctypes.byref(tq), ctypes.byref(tk), ctypes.byref(tv),
-                             ctypes.byref(mt) if mt is not None else None, sc, 1 if is_causal else 0,
-                             ctypes.byref(to), lse.data_ptr() if lse is not None and lse.numel() else None,
-                             _stream(q.device))
+    opts = _opts(0, dropout_p, seed)
+    rc = _C.lib.gtb_sdpa_fwd_ex(ctypes.byref(tq), ctypes.byref(tk), ctypes.byref(tv),
+                                ctypes.byref(mt) if mt is not None else None, sc, 1 if is_causal else 0,
+                                ctypes.byref(to), lse.data_ptr() if lse is not None and lse.numel() else None,
+                                ctypes.byref(opts), _stream(q.device))
     _C.check_rc(rc, "flash_attention")
     return out, lse
 
 
 def sdpa_backward(grad_out, q, k, v, mask, out, lse, scale: float, is_causal: bool,
-                  deterministic: bool | None = None, grads=None):
+                  deterministic: bool | None = None, grads=None, dropout_p: float = 0.0, seed: int = 0):
     """One call of the native backward: returns (dq, dk, dv). With `deterministic` (default: whether
     torch.use_deterministic_algorithms is on) dq comes from the separate dq kernel and has the same
     bits on every run; otherwise, for head size 128, dq is summed with f32 reductions in global
     memory inside the dK/dV kernel (faster; the last bit may vary from run to run). `grads`, if given,
-    is a (dq, dk, dv) triple of tensors or views shaped like q, k, v that receive the result."""
+    is a (dq, dk, dv) triple of tensors or views shaped like q, k, v that receive the result.
+    dropout_p and seed: those of the forward that produced `out` (its dropout mask is recomputed)."""
     if deterministic is None:
         deterministic = torch.are_deterministic_algorithms_enabled()
     B, H, L, D = q.shape
@@ -131,7 +149,8 @@ def sdpa_backward(grad_out, q, k, v, mask, out, lse, scale: float, is_causal: bo
                                 ctypes.byref(mt) if mt is not None else None, ctypes.byref(to),
                                 lse.data_ptr() if lse.numel() else None, float(scale), 1 if is_causal else 0,
                                 ctypes.byref(tdq), ctypes.byref(tdk), ctypes.byref(tdv),
-                                _C.GTB_BWD_DETERMINISTIC if deterministic else 0, _stream(q.device))
+                                ctypes.byref(_opts(_C.GTB_BWD_DETERMINISTIC if deterministic else 0, dropout_p, seed)),
+                                _stream(q.device))
     _C.check_rc(rc, "flash_attention_backward")
     return dq, dk, dv
 
@@ -139,28 +158,31 @@ def sdpa_backward(grad_out, q, k, v, mask, out, lse, scale: float, is_causal: bo
 class FlashAttentionFn(torch.autograd.Function):
     """The autograd Function behind scaled_dot_product_attention (reference _functions.py:1922).
 
-    apply(q, k, v, mask, scale, is_causal): q (B,H,L,D), k (B,Hkv,S,D), v (B,Hkv,S,Dv), mask None,
-    (L,S) or 4-D, bool (True = may attend) or float (added); scale None -> 1/sqrt(D).
+    apply(q, k, v, mask, scale, is_causal[, dropout_p]): q (B,H,L,D), k (B,Hkv,S,D), v (B,Hkv,S,Dv), mask
+    None, (L,S) or 4-D, bool (True = may attend) or float (added); scale None -> 1/sqrt(D). dropout_p > 0
+    (an addition of this engine) drops attention probabilities inside the kernels with a seed drawn
+    from torch's generator, kept for the backward.
 
     The forward keeps what the backward needs to skip recomputing the softmax normaliser: the output
     and the per-row log-sum-exp (the reference keeps only the inputs and rebuilds the probabilities
     with separate ops, _functions.py:1934-1965)."""
 
     @staticmethod
-    def forward(ctx, q, k, v, mask, scale, is_causal):
+    def forward(ctx, q, k, v, mask, scale, is_causal, dropout_p=0.0):
         opts = (1.0 / math.sqrt(q.shape[-1]) if scale is None else float(scale), bool(is_causal))
-        out, lse = sdpa_forward(q, k, v, mask, *opts, need_lse=True)
-        ctx.opts = opts
+        drop = (float(dropout_p), dropout_seed() if dropout_p else 0)
+        out, lse = sdpa_forward(q, k, v, mask, *opts, need_lse=True, dropout_p=drop[0], seed=drop[1])
+        ctx.opts, ctx.drop = opts, drop
         ctx.save_for_backward(q, k, v, mask, out, lse)
         return out
 
     @staticmethod
     def backward(ctx, grad_out):
         if grad_out is None:
-            return (None,) * 6
+            return (None,) * 7
         q, k, v, mask, out, lse = ctx.saved_tensors
-        dq, dk, dv = sdpa_backward(grad_out, q, k, v, mask, out, lse, *ctx.opts)
-        return dq, dk, dv, None, None, None
+        dq, dk, dv = sdpa_backward(grad_out, q, k, v, mask, out, lse, *ctx.opts, dropout_p=ctx.drop[0], seed=ctx.drop[1])
+        return dq, dk, dv, None, None, None, None
 
 
 def _autocast_lower(*ts):
@@ -202,9 +224,10 @@ def scaled_dot_product_attention(
     """torch.nn.functional.scaled_dot_product_attention, as gguf_train defines it
     (nn/functional.py:724-767): a bool mask marks keys that MAY be attended, a float mask is added,
     masks broadcast from the right against (B, H, L, S), GQA applies whenever H % Hkv == 0
-    (`enable_gqa` changes nothing), causal masking is top-left aligned. Without dropout the call is
-    FlashAttentionFn on the sm_100a kernels; with dropout it is the composite of
-    _attention_with_dropout."""
+    (`enable_gqa` changes nothing), causal masking is top-left aligned. The call is FlashAttentionFn on
+    the sm_100a kernels, dropout included (dropout_p > 0: the probabilities are dropped inside the
+    kernels, with the reference's semantics; the mask is drawn from a counter-based hash seeded from
+    torch's generator instead of the reference's sequential generator)."""
     del enable_gqa
     lowered, cast = _autocast_lower(query, key, value, attn_mask)
     if cast:
@@ -213,7 +236,7 @@ def scaled_dot_product_attention(
     sc = 1.0 / math.sqrt(query.shape[-1]) if scale is None else float(scale)
     mask = None if attn_mask is None else _as_4d_mask(attn_mask, query, key)
     if dropout_p != 0.0:
-        return _attention_with_dropout(query, key, value, mask, float(dropout_p), bool(is_causal), sc)
+        return FlashAttentionFn.apply(query, key, value, mask, sc, is_causal, float(dropout_p))
     return FlashAttentionFn.apply(query, key, value, mask, sc, is_causal)
 
 
@@ -262,26 +285,6 @@ def sdpa_from_host(query: torch.Tensor, key: torch.Tensor, value: torch.Tensor, 
                                       ctypes.byref(to), pieces, torch.cuda.current_stream(dev).cuda_stream)
     _C.check_rc(rc, "flash_attention")
     return out
-
-
-def _attention_with_dropout(q, k, v, mask, dropout_p: float, is_causal: bool, scale: float):
-    """Attention with dropout on the probabilities, the reference's dropout path
-    (nn/functional.py:750-767): masked entries (causal s > l, bool False) get -1e9 added or set, a
-    float mask is added, softmax over keys, dropout, then the weighted sum of v. Composed of torch
-    ops (the engine has no fused dropout kernel). Each kv head's query heads are stacked along the
-    rows, so k and v are used as they are instead of being repeated per query head."""
-    B, H, L, D = q.shape
-    Hkv, S, Dv = k.shape[1], k.shape[2], v.shape[3]
-    per_kv = H // Hkv
-    stacked = q.reshape(B, Hkv, per_kv * L, D)
-    logits = torch.matmul(stacked, k.transpose(-1, -2)).view(B, H, L, S) * scale
-    if is_causal:
-        above = torch.ones((L, S), dtype=torch.bool, device=q.device).triu(1)
-        logits = logits + above.to(logits.dtype) * -1e9
-    if mask is not None:
-        logits = logits.masked_fill(mask.logical_not(), -1e9) if mask.dtype == torch.bool else logits + mask
-    probs = torch.nn.functional.dropout(torch.softmax(logits, dim=-1), p=dropout_p, training=True)
-    return torch.matmul(probs.reshape(B, Hkv, per_kv * L, S), v).view(B, H, L, Dv)
 
 
 # ------------------------------------------------------------------ Q8_0 KV cache

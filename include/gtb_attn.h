@@ -80,16 +80,38 @@ GTB_API int gtb_sdpa_bwd(const gtb_tensor4 *dout, const gtb_tensor4 *q, const gt
                          const void *lse, float scale, int is_causal,
                          gtb_tensor4 *dq, gtb_tensor4 *dk, gtb_tensor4 *dv, void *stream);
 
-/* gtb_sdpa_bwd with flags. GTB_BWD_DETERMINISTIC: dq from the separate dq kernel, the same bits on
- * every run (what the environment variable GTB_BWD_SPLIT_DQ=1 selects for every call); needed where a
- * recomputed backward must repeat exactly, as under activation checkpointing (reference
- * gguf_train/utils/checkpoint.py:159-222) or torch.use_deterministic_algorithms. flags = 0 is
- * gtb_sdpa_bwd. Replaces the same reference function as gtb_sdpa_bwd. */
+/* Options of gtb_sdpa_fwd_ex / gtb_sdpa_bwd_ex (NULL = all zero).
+ *   flags: GTB_BWD_DETERMINISTIC (backward): dq from the separate dq kernel, the same bits on every
+ *     run (what the environment variable GTB_BWD_SPLIT_DQ=1 selects for every call); needed where a
+ *     recomputed backward must repeat exactly, as under activation checkpointing (reference
+ *     gguf_train/utils/checkpoint.py:159-222) or torch.use_deterministic_algorithms.
+ *   dropout_p in [0, 1): dropout on the attention probabilities, as the reference's
+ *     F.scaled_dot_product_attention(dropout_p > 0) (gguf_train/nn/functional.py:750-767): each
+ *     probability is dropped with probability dropout_p and the kept ones scaled by 1/(1 - dropout_p);
+ *     the softmax normaliser and the lse are those of the undropped probabilities.
+ *   dropout_seed: the keep / drop decision of element (b, h, l, s) is a pure function of the seed and
+ *     the indices (a counter-based hash, no generator state), so the backward given the forward's
+ *     seed reproduces the forward's mask exactly, on any kernel. */
+typedef struct gtb_sdpa_opts {
+    int32_t flags;
+    float dropout_p;
+    uint64_t dropout_seed;
+} gtb_sdpa_opts;
 #define GTB_BWD_DETERMINISTIC 1
+
+/* gtb_sdpa_fwd with options (dropout). Replaces the same reference function as gtb_sdpa_fwd, and the
+ * dropout branch of F.scaled_dot_product_attention (gguf_train/nn/functional.py:750-767). */
+GTB_API int gtb_sdpa_fwd_ex(const gtb_tensor4 *q, const gtb_tensor4 *k, const gtb_tensor4 *v,
+                            const gtb_tensor4 *mask, float scale, int is_causal,
+                            gtb_tensor4 *out, void *lse, const gtb_sdpa_opts *opts, void *stream);
+
+/* gtb_sdpa_bwd with options (determinism, dropout: pass the forward's dropout_p and seed).
+ * Replaces the same reference function as gtb_sdpa_bwd. */
 GTB_API int gtb_sdpa_bwd_ex(const gtb_tensor4 *dout, const gtb_tensor4 *q, const gtb_tensor4 *k,
                             const gtb_tensor4 *v, const gtb_tensor4 *mask, const gtb_tensor4 *out,
                             const void *lse, float scale, int is_causal,
-                            gtb_tensor4 *dq, gtb_tensor4 *dk, gtb_tensor4 *dv, int flags, void *stream);
+                            gtb_tensor4 *dq, gtb_tensor4 *dk, gtb_tensor4 *dv, const gtb_sdpa_opts *opts,
+                            void *stream);
 
 /* Q8_0 quantisation of n_rows rows of row_len values (row_len % 32 == 0) into GGUF Q8_0 blocks
  * (fp16 scale + 32 int8, 34 bytes per 32 values), bit-exact with ggml's reference quantiser.
