@@ -423,6 +423,45 @@ GTB_API int gtb_sdpa_fwd_ex(const gtb_tensor4* q, const gtb_tensor4* k, const gt
     return launch_fwd_simt(a, st);
 }
 
+GTB_API int gtb_attn_weights(const gtb_tensor4* q, const gtb_tensor4* k, const gtb_tensor4* mask, const void* lse,
+                             float scale, int is_causal, int average, const gtb_sdpa_opts* opts, gtb_tensor4* out,
+                             void* stream) {
+    const char* ctx = "attention_weights";
+    FwdArgs a;
+    if (!check_attn(ctx, q, k, k, mask, a.sh)) return -1;
+    a.sh.Dv = a.sh.D;
+    if (!out || !lse) {
+        set_errorf("%s: out and lse are required", ctx);
+        return -1;
+    }
+    const int64_t osh[4] = {a.sh.B, average ? 1 : a.sh.H, a.sh.L, a.sh.S};
+    if (!same_shape(*out, osh) || out->dtype != q->dtype || !row_major(*out)) {
+        set_errorf("%s: out must be a contiguous %s tensor in q's dtype", ctx, shape_str(osh, 4).c_str());
+        return -1;
+    }
+    if (opts && !(opts->dropout_p >= 0.0f && opts->dropout_p < 1.0f)) {
+        set_errorf("%s: dropout probability has to be between 0 and 1, but got %g", ctx, (double)opts->dropout_p);
+        return -1;
+    }
+    if (numel4(*out) == 0) return 0;
+    if (!check_device_ptr(q->data, ctx, "q") || !check_device_ptr(out->data, ctx, "out") ||
+        !check_device_ptr(lse, ctx, "lse"))
+        return -1;
+    if (a.sh.S > 0 && !check_device_ptr(k->data, ctx, "k")) return -1;
+    if (mask && !check_device_ptr(mask->data, ctx, "attn_mask")) return -1;
+    a.q = *q; a.k = *k; a.v = *k;
+    a.has_mask = mask != nullptr;
+    if (mask) a.mask = broadcast_mask(*mask);
+    a.scale = resolve_scale(scale, a.sh.D);
+    a.causal = is_causal ? 1 : 0;
+    if (opts) {
+        a.drop_p = opts->dropout_p;
+        a.drop_thr = drop_threshold(opts->dropout_p);
+        a.drop_seed = opts->dropout_seed;
+    }
+    return launch_attn_weights(a, lse, out->data, average != 0, (cudaStream_t)stream);
+}
+
 GTB_API int gtb_sdpa_fwd_host(const gtb_tensor4* q, const gtb_tensor4* k, const gtb_tensor4* v, float scale, int is_causal,
                               gtb_tensor4* out, int pieces, void* stream) {
     const char* ctx = "flash_attention_host";

@@ -42,6 +42,10 @@ struct BwdArgs {
     uint64_t drop_seed = 0;
 };
 
+// Attention weights from a finished forward's lse (attn_weights.cu): out (B, L, S) when `average`
+// (mean over heads) else (B, H, L, S), contiguous, in q's dtype.
+int launch_attn_weights(const FwdArgs& a, const void* lse, void* out, bool average, cudaStream_t st);
+
 // SIMT kernels: any float dtype, any D/Dv <= 256, masks, any strides.
 int launch_fwd_simt(const FwdArgs& a, cudaStream_t st);
 int launch_bwd_simt(const BwdArgs& a, cudaStream_t st);

@@ -185,6 +185,107 @@ class FlashAttentionFn(torch.autograd.Function):
         return dq, dk, dv, None, None, None, None
 
 
+class FlashAttentionLseFn(torch.autograd.Function):
+    """FlashAttentionFn that also returns the per-row log-sum-exp (not differentiable) and takes the
+    dropout seed from the caller: apply(q, k, v, mask, scale, is_causal, dropout_p, seed) ->
+    (out, lse). MultiheadAttention uses it when it returns its attention weights, which are formed
+    from the same lse and the same dropout decisions."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, mask, scale, is_causal, dropout_p, seed):
+        opts = (1.0 / math.sqrt(q.shape[-1]) if scale is None else float(scale), bool(is_causal))
+        out, lse = sdpa_forward(q, k, v, mask, *opts, need_lse=True, dropout_p=float(dropout_p), seed=int(seed))
+        ctx.opts, ctx.drop = opts, (float(dropout_p), int(seed))
+        ctx.save_for_backward(q, k, v, mask, out, lse)
+        ctx.mark_non_differentiable(lse)
+        return out, lse
+
+    @staticmethod
+    def backward(ctx, grad_out, _grad_lse):
+        if grad_out is None:
+            return (None,) * 8
+        q, k, v, mask, out, lse = ctx.saved_tensors
+        dq, dk, dv = sdpa_backward(grad_out, q, k, v, mask, out, lse, *ctx.opts, dropout_p=ctx.drop[0], seed=ctx.drop[1])
+        return dq, dk, dv, None, None, None, None, None
+
+
+def attention_weights(q, k, lse, mask=None, scale: float | None = None, is_causal: bool = False,
+                      average: bool = True, dropout_p: float = 0.0, seed: int = 0) -> torch.Tensor:
+    """The attention probabilities of a forward that has run (its lse, mask, scale, causality and
+    dropout seed), on the device: (B, L, S) averaged over heads, or (B, H, L, S); q's dtype. The
+    need_weights=True output of MultiheadAttention (reference transformer.py:153-166), without the
+    (B, H, L, S) scores of the reference's matmul + softmax."""
+    _require_cuda("attention_weights", q, k, lse, mask)
+    B, H, L, D = q.shape
+    S = k.shape[2]
+    sc = (1.0 / math.sqrt(D)) if scale is None else float(scale)
+    out = torch.empty((B, 1 if average else H, L, S), dtype=q.dtype, device=q.device)
+    mt = _native_mask(mask, B, H, L, S) if mask is not None else None
+    tq, tk, to = _t4(q), _t4(k), _t4(out)
+    rc = _C.lib.gtb_attn_weights(ctypes.byref(tq), ctypes.byref(tk), ctypes.byref(mt) if mt is not None else None,
+                                 lse.data_ptr() if lse.numel() else None, sc, 1 if is_causal else 0,
+                                 1 if average else 0, ctypes.byref(_opts(0, dropout_p, seed)), ctypes.byref(to),
+                                 _stream(q.device))
+    _C.check_rc(rc, "attention_weights")
+    return out[:, 0] if average else out
+
+
+def _keep_mask_torch(seed: int, p: float, B: int, H: int, L: int, S: int, device) -> torch.Tensor:
+    """The kernels' dropout decisions (csrc/dropout.cuh: lowbias32 chained over seed, batch-head, row,
+    key) in torch integer ops, for the recomputing backward of attention_weights."""
+    M = 0xFFFFFFFF
+
+    def h32(x):
+        x = x ^ (x >> 16)
+        x = (x * 0x7FEB352D) & M
+        x = x ^ (x >> 15)
+        x = (x * 0x846CA68B) & M
+        return x ^ (x >> 16)
+
+    thr = min(int(float(torch.tensor(p, dtype=torch.float32)) * 4294967296.0), M)
+    bh = torch.arange(B * H, device=device, dtype=torch.int64)
+    head = h32(((seed >> 32) & M) ^ h32((seed & M) ^ bh))
+    row = h32(head[:, None] ^ torch.arange(L, device=device, dtype=torch.int64)[None])
+    x = h32((row[:, :, None] + torch.arange(S, device=device, dtype=torch.int64)[None, None]) & M)
+    return (x >= thr).view(B, H, L, S)
+
+
+class AttentionWeightsFn(torch.autograd.Function):
+    """attention_weights as an autograd Function: apply(q, k, lse, mask, scale, is_causal, average,
+    dropout_p, seed). The forward is the native kernel. Gradients reach q and k only when the caller
+    differentiates through the returned weights (rare: they are usually inspected); the backward then
+    recomputes the probabilities with torch ops (scores, softmax, the same dropout decisions) and
+    differentiates those."""
+
+    @staticmethod
+    def forward(ctx, q, k, lse, mask, scale, is_causal, average, dropout_p, seed):
+        ctx.args = (scale, bool(is_causal), bool(average), float(dropout_p), int(seed))
+        ctx.save_for_backward(q, k, mask)
+        return attention_weights(q, k, lse, mask, scale, is_causal, average, dropout_p, seed)
+
+    @staticmethod
+    def backward(ctx, grad_w):
+        q, k, mask = ctx.saved_tensors
+        scale, causal, average, p, seed = ctx.args
+        with torch.enable_grad():
+            qd, kd = q.detach().requires_grad_(), k.detach().requires_grad_()
+            B, H, L, D = q.shape
+            S, group = k.shape[2], H // k.shape[1]
+            sc = (1.0 / math.sqrt(D)) if scale is None else float(scale)
+            logits = torch.matmul(qd.float(), kd.float().repeat_interleave(group, dim=1).transpose(2, 3)) * sc
+            if causal:
+                logits = logits.masked_fill(torch.ones((L, S), dtype=torch.bool, device=q.device).triu(1), float("-inf"))
+            if mask is not None:
+                logits = logits.masked_fill(mask.logical_not(), float("-inf")) if mask.dtype == torch.bool \
+                    else logits + mask.float()
+            probs = torch.softmax(logits, dim=3)
+            if p > 0.0:
+                probs = probs * _keep_mask_torch(seed, p, B, H, L, S, q.device) / (1.0 - p)
+            w = probs.mean(dim=1) if average else probs
+            dq, dk = torch.autograd.grad(w, (qd, kd), grad_w.float())
+        return dq.to(q.dtype), dk.to(k.dtype), None, None, None, None, None, None, None
+
+
 def _autocast_lower(*ts):
     """Inside torch.autocast, floating arguments are cast to the autocast dtype, as the reference's
     _autocast_op(_AUTOCAST_LOWER) does for SDPA (gguf_train/_tensor.py:261-282)."""

@@ -15,8 +15,10 @@ How it runs here:
   apply per 128 x 128 block (a key-padding mask costs almost nothing: only the blocks holding padded
   keys are read entry by entry);
 * need_weights=False: scaled_dot_product_attention (the sm_100a path, forward and backward);
-  need_weights=True: the probabilities are formed explicitly (they are returned), as the reference
-  does, with torch ops.
+  need_weights=True: the output comes from the same fused kernels (which also return each row's
+  log-sum-exp) and the returned weights from a kernel that turns the lse back into probabilities,
+  with the same dropout decisions (functional.attention_weights); the reference instead forms the
+  (B, heads, L, S) scores with matmul + softmax.
 """
 
 from __future__ import annotations
@@ -65,7 +67,11 @@ class MultiheadAttention(nn.Module):
         scale = self.head_dim ** -0.5
         p_drop = self.dropout if self.training else 0.0
         if need_weights:
-            ctx, weights = _attend_with_weights(q, k, v, bias, is_causal, scale, p_drop, average_attn_weights)
+            # the output through the fused kernels, then the weights from the same lse and the same
+            # dropout decisions by the weights kernel (no (B, heads, L, S) scores are formed)
+            seed = F.dropout_seed() if p_drop else 0
+            ctx, lse = F.FlashAttentionLseFn.apply(q, k, v, bias, scale, is_causal, p_drop, seed)
+            weights = F.AttentionWeightsFn.apply(q, k, lse, bias, scale, is_causal, average_attn_weights, p_drop, seed)
         else:
             ctx = F.scaled_dot_product_attention(q, k, v, attn_mask=bias, dropout_p=p_drop, is_causal=is_causal,
                                                  scale=scale)
@@ -159,21 +165,3 @@ def _additive(mask: torch.Tensor, dtype, name: str) -> torch.Tensor:
     if not mask.is_floating_point():
         raise RuntimeError(f"MultiheadAttention: {name} must be a boolean or floating point tensor, got {mask.dtype}")
     return mask.to(dtype)
-
-
-def _attend_with_weights(q, k, v, bias, is_causal: bool, scale: float, p_drop: float, average: bool):
-    """Attention that also returns its probabilities (MultiheadAttention's need_weights=True,
-    reference transformer.py:153-166): -1e9 is added above the diagonal when causal, then the mask;
-    softmax over keys; dropout (training only) applies to the returned probabilities too; the
-    weights are averaged over heads when `average`."""
-    L, S = q.shape[2], k.shape[2]
-    logits = torch.matmul(q, k.transpose(2, 3)) * scale
-    if is_causal:
-        logits = logits + torch.full((L, S), -1e9, dtype=logits.dtype, device=logits.device).triu(1)
-    if bias is not None:
-        logits = logits + bias
-    probs = torch.softmax(logits, dim=3)
-    if p_drop > 0.0:
-        probs = torch.nn.functional.dropout(probs, p=p_drop, training=True)
-    ctx = torch.matmul(probs, v)
-    return ctx, (probs.mean(dim=1) if average else probs)

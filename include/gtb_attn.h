@@ -113,6 +113,17 @@ GTB_API int gtb_sdpa_bwd_ex(const gtb_tensor4 *dout, const gtb_tensor4 *q, const
                             gtb_tensor4 *dq, gtb_tensor4 *dk, gtb_tensor4 *dv, const gtb_sdpa_opts *opts,
                             void *stream);
 
+/* Attention weights (probabilities) of a forward that has run, from its lse: the need_weights=True
+ * output of MultiheadAttention (reference gguf_train/nn/modules/transformer.py:153-166, which forms
+ * them with matmul + softmax). P[b,h,l,s] = exp(scale * q.k + mask - lse[b,h,l]), 0 where masked or
+ * (causal) s > l; with opts->dropout_p > 0 and the forward's seed, times keep / (1 - p) with the
+ * forward's decisions (the weights the output was formed with). q, k, mask, scale, is_causal as in
+ * gtb_sdpa_fwd; lse as gtb_sdpa_fwd wrote it. out: contiguous in q's dtype, (B, 1, L, S) with
+ * average != 0 (mean over the H heads) or (B, H, L, S). Any head size up to 256. */
+GTB_API int gtb_attn_weights(const gtb_tensor4 *q, const gtb_tensor4 *k, const gtb_tensor4 *mask, const void *lse,
+                             float scale, int is_causal, int average, const gtb_sdpa_opts *opts, gtb_tensor4 *out,
+                             void *stream);
+
 /* Q8_0 quantisation of n_rows rows of row_len values (row_len % 32 == 0) into GGUF Q8_0 blocks
  * (fp16 scale + 32 int8, 34 bytes per 32 values), bit-exact with ggml's reference quantiser.
  * Replaces gt_quantize(t, GT_Q_BASE + 8) (reference csrc/gt_ops_extra.cpp:2002, which goes

@@ -57,17 +57,16 @@ def test_mha_parameters_follow_the_reference():
     assert m.head_dim == 64
 
 
-def test_mha_need_weights_path_runs_on_cpu():
-    """need_weights=True materialises the weights with matmul + softmax, as the reference does
-    (transformer.py:153-166), so it needs no attention kernel."""
+def test_mha_need_weights_path_refuses_cpu_tensors():
+    """need_weights=True runs on the engine's kernels too (the output from the fused forward, the
+    weights from its lse), so a CPU input is refused like every other attention call."""
     import gguf_train_b200 as gtb
 
     torch.manual_seed(0)
     m = gtb.MultiheadAttention(8, 2, batch_first=True).eval()
     x = torch.randn(2, 4, 8)
-    out, w = m(x, x, x)
-    assert out.shape == (2, 4, 8) and w.shape == (2, 4, 4)
-    assert torch.allclose(w.sum(-1), torch.ones(2, 4))
+    with pytest.raises(RuntimeError, match="CUDA tensors only"):
+        m(x, x, x)
 
 
 def test_q8_0_python_checks():
