@@ -324,8 +324,10 @@ def run_train(args, rank: int, world: int, dev, max_over_ranks=lambda x: x, stro
                      "frac": per_gpu / peaks["bf16_tflops"],
                      "peak_source": peaks["source"] + " bf16 dense (burst)",
                      "timed_ms": steps * (f_ms + b_ms),
-                     "backward_tflops": 2 * fwd / (b_ms * 1e-3) / 1e12, "forward_tflops": fwd / (f_ms * 1e-3) / 1e12,
-                     "backward_frac": 2 * fwd / (b_ms * 1e-3) / 1e12 / peaks["bf16_tflops"]},
+                     # per GPU: a strong-scaling rank ran 1/N of the batch's FLOPs in these times
+                     "backward_tflops": 2 * fwd / (b_ms * 1e-3) / 1e12 / (world if strong else 1),
+                     "forward_tflops": fwd / (f_ms * 1e-3) / 1e12 / (world if strong else 1),
+                     "backward_frac": 2 * fwd / (b_ms * 1e-3) / 1e12 / (world if strong else 1) / peaks["bf16_tflops"]},
         "launches_per_step": "forward 1, backward 3 (preprocess, dK/dV with the dQ sums, dQ conversion)",
         "gpu_launches": 4 * steps, "status": _C.device_status(),
     }
