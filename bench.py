@@ -487,6 +487,45 @@ def run_mha(args, rank: int, world: int, dev, max_over_ranks=lambda x: x) -> dic
             "status": _C.device_status()}
 
 
+def run_linear(args, rank: int, world: int, dev, max_over_ranks=lambda x: x) -> dict:
+    """The tensor-core linear layer (gtb_linear: c = a b^T + bias, bf16, f32 accumulation) on
+    MultiheadAttention's bf16 in-projection at config 2's token count (M = 16 x 512 tokens, N = 3 x 512,
+    K = 512) and on a large square product (8192^3); torch.matmul (cuBLAS) on the same operands is timed
+    beside it for reference. FLOPs 2 M N K per call."""
+    import torch
+
+    from gguf_train_b200 import functional as Fn
+
+    peaks = load_peaks()
+    res = {"workload": "tcgen05 linear (gtb_linear), bf16", "unit": "TFLOP/s", "shapes": []}
+    g = torch.Generator(device=dev)
+    g.manual_seed(5 + rank)
+    for M, N, K in ((8192, 1536, 512), (8192, 8192, 8192)):
+        a = torch.randn((M, K), generator=g, device=dev).to(torch.bfloat16)
+        b = (torch.randn((N, K), generator=g, device=dev) / K ** 0.5).to(torch.bfloat16)
+        bias = torch.randn((N,), generator=g, device=dev).to(torch.bfloat16)
+        ours = lambda: Fn._linear_2d(a, b, bias)  # noqa: E731
+        lib = lambda: torch.addmm(bias, a, b.t())  # noqa: E731
+        for _ in range(max(args.warmup, 3)):
+            ours()
+            lib()
+        torch.cuda.synchronize(dev)
+        steps = max(3, min(args.steps, 20))
+        stream = torch.cuda.current_stream(dev)
+        ms = max_over_ranks(_time_events(stream, ours, steps))
+        ms_lib = max_over_ranks(_time_events(stream, lib, steps))
+        tf = 2.0 * M * N * K / (ms * 1e-3) / 1e12
+        res["shapes"].append({"M": M, "N": N, "K": K, "ms": ms, "tflops": tf, "frac": tf / peaks["bf16_tflops"],
+                              "cublas_ms": ms_lib, "cublas_tflops": 2.0 * M * N * K / (ms_lib * 1e-3) / 1e12})
+        del a, b, bias
+    res["value"] = res["shapes"][-1]["tflops"] * world
+    res["roofline"] = {"bound": "tensor", "achieved": res["shapes"][-1]["tflops"], "peak": peaks["bf16_tflops"],
+                       "unit": "TFLOP/s", "frac": res["shapes"][-1]["frac"],
+                       "peak_source": peaks["source"] + " bf16 dense (burst)"}
+    torch.cuda.empty_cache()
+    return res
+
+
 def run_decode_strong(args, rank: int, world: int, dev, max_over_ranks=lambda x: x) -> dict:
     """Config 5a's 64 sequences split over the ranks by sharding.balance_sequences (by cached length,
     longest first); GB/s of the whole step's cache bytes over the slowest rank (strong scaling)."""
@@ -609,8 +648,8 @@ def main() -> None:
     ap.add_argument("--decode-batch", type=int, default=None,
                     help="sequences of the decode workload (default: config 5a's 64; smaller for profiling)")
     ap.add_argument("--workload", default="prefill",
-                    choices=["prefill", "decode", "train", "ring", "key_padding", "mha", "prefill_strong", "train_strong",
-                             "decode_strong"],
+                    choices=["prefill", "decode", "train", "ring", "key_padding", "mha", "linear", "prefill_strong",
+                             "train_strong", "decode_strong"],
                     help="prefill: config 3 (the default line); train: config 4 fwd+bwd; decode: config 5a; "
                          "ring: config 5b (one long sequence, K/V ring over the GPUs); key_padding: config 3 with a "
                          "key-padding mask; mha: config 2 (nn.MultiheadAttention fp32 fwd+bwd); *_strong: the fixed "
@@ -653,7 +692,7 @@ def main() -> None:
     if args.workload != "prefill":
         barrier()
         runner = {"decode": run_decode, "train": run_train, "ring": run_ring, "key_padding": run_prefill_key_padding,
-                  "mha": run_mha, "prefill_strong": run_prefill_strong, "decode_strong": run_decode_strong,
+                  "mha": run_mha, "linear": run_linear, "prefill_strong": run_prefill_strong, "decode_strong": run_decode_strong,
                   "train_strong": lambda *a: run_train(*a, strong=True)}[args.workload]
         res = runner(args, rank, world, dev, max_over_ranks)
         if args.workload != "decode":
@@ -786,6 +825,8 @@ def main() -> None:
         line["extra"]["prefill_key_padding"] = run_prefill_key_padding(args, rank, world, dev, max_over_ranks)
         barrier()
         line["extra"]["mha_config2"] = run_mha(args, rank, world, dev, max_over_ranks)
+        barrier()
+        line["extra"]["linear_bf16"] = run_linear(args, rank, world, dev, max_over_ranks)
         if world > 1:  # strong scaling: the fixed batches split over the ranks
             barrier()
             line["extra"]["prefill_strong"] = run_prefill_strong(args, rank, world, dev, max_over_ranks)

@@ -60,6 +60,9 @@ def _configure(lib: ctypes.CDLL) -> ctypes.CDLL:
     lib.gtb_sdpa_fwd_ex.restype = c_int
     lib.gtb_attn_weights.argtypes = [P4, P4, P4, c_void_p, c_float, c_int, c_int, POPTS, P4, c_void_p]
     lib.gtb_attn_weights.restype = c_int
+    lib.gtb_linear.argtypes = [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_int64,
+                               c_int64, c_int, c_void_p]
+    lib.gtb_linear.restype = c_int
     lib.gtb_sdpa_fwd.restype = c_int
     lib.gtb_sdpa_fwd_host.argtypes = [P4, P4, P4, c_float, c_int, P4, c_int, c_void_p]
     lib.gtb_sdpa_fwd_host.restype = c_int

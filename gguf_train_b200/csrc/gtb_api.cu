@@ -423,6 +423,36 @@ GTB_API int gtb_sdpa_fwd_ex(const gtb_tensor4* q, const gtb_tensor4* k, const gt
     return launch_fwd_simt(a, st);
 }
 
+GTB_API int gtb_linear(const void* a, const void* b, const void* bias, void* c, int64_t M, int64_t N, int64_t K,
+                       int64_t lda, int64_t ldb, int64_t ldc, int dtype, void* stream) {
+    const char* ctx = "linear";
+    if (M < 0 || N < 0 || K <= 0) {
+        set_errorf("%s: sizes must be M, N >= 0 and K > 0 (got %lld, %lld, %lld)", ctx, (long long)M, (long long)N,
+                   (long long)K);
+        return -1;
+    }
+    if (dtype != BF16 && dtype != F16) {
+        set_errorf("%s: the tensor-core linear takes bf16 or f16 operands", ctx);
+        return -1;
+    }
+    if (lda < K || ldb < K || ldc < N || lda % 8 || ldb % 8 || ldc % 8) {
+        set_errorf("%s: leading dimensions must cover the rows and be multiples of 8 elements", ctx);
+        return -1;
+    }
+    if (M >= (1ll << 31) || N >= (1ll << 31) || K >= (1ll << 31)) {
+        set_errorf("%s: sizes out of range", ctx);
+        return -1;
+    }
+    if (M == 0 || N == 0) return 0;
+    if (!check_device_ptr(a, ctx, "a") || !check_device_ptr(b, ctx, "b") || !check_device_ptr(c, ctx, "c")) return -1;
+    if (bias && !check_device_ptr(bias, ctx, "bias")) return -1;
+    if (((uintptr_t)a | (uintptr_t)b | (uintptr_t)c) & 15) {
+        set_errorf("%s: a, b and c must be 16-byte aligned", ctx);
+        return -1;
+    }
+    return launch_linear_sm100(a, b, bias, c, M, N, K, lda, ldb, ldc, dtype, (cudaStream_t)stream);
+}
+
 GTB_API int gtb_attn_weights(const gtb_tensor4* q, const gtb_tensor4* k, const gtb_tensor4* mask, const void* lse,
                              float scale, int is_causal, int average, const gtb_sdpa_opts* opts, gtb_tensor4* out,
                              void* stream) {

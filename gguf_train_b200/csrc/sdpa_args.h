@@ -42,9 +42,20 @@ struct BwdArgs {
     uint64_t drop_seed = 0;
 };
 
+// C (M, N) = A (M, K) B (N, K)^T (+ bias) on the tensor cores (linear_sm100.cu): bf16/f16, row-major
+// with leading dimensions lda, ldb, ldc (elements), 16-byte aligned rows, K > 0.
+int launch_linear_sm100(const void* a, const void* b, const void* bias, void* c, int64_t M, int64_t N, int64_t K,
+                        int64_t lda, int64_t ldb, int64_t ldc, int dtype, cudaStream_t st);
+
 // Attention weights from a finished forward's lse (attn_weights.cu): out (B, L, S) when `average`
 // (mean over heads) else (B, H, L, S), contiguous, in q's dtype.
 int launch_attn_weights(const FwdArgs& a, const void* lse, void* out, bool average, cudaStream_t st);
+
+// fp32 kernels register-blocked on 64 x 64 tiles (sdpa_f32_tiled.cu): f32 with D = Dv = 64, masks,
+// dropout, any strides. The backward takes rowsum(dout * out) per row in `delta` (B, H, L).
+bool f32_tiled_supported(const AttnShape& sh, int dtype);
+int launch_fwd_f32_tiled(const FwdArgs& a, cudaStream_t st);
+int launch_bwd_f32_tiled(const BwdArgs& a, const float* delta, cudaStream_t st);
 
 // SIMT kernels: any float dtype, any D/Dv <= 256, masks, any strides.
 int launch_fwd_simt(const FwdArgs& a, cudaStream_t st);

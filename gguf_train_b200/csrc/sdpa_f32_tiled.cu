@@ -1,0 +1,449 @@
+// fp32 attention on the CUDA cores, register-blocked: the path of f32 inputs with head size 64 (the
+// tensor-core kernels take 16-bit inputs; a single-pass tf32 product would miss the 1e-3 tolerance of
+// fp32 attention). Other fp32 head sizes run on the one-warp-per-row kernels of sdpa_simt.cu.
+//
+// Every kernel works on 64 x 64 tiles with 256 threads: thread t owns a 4 x 4 block (rows 4*(t/16)..,
+// columns 4*(t%16)..), so the 16 threads of one half-warp hold one row group and a row's reductions are
+// four shuffles. Operands sit in shared memory transposed where a thread reads four consecutive rows
+// or columns at once (float4): the inner loops issue two 16-byte shared loads per 16 FMAs.
+//
+//   forward     one CTA per 64 query rows of one (batch, head), key tiles of 64: S = Q K^T, online
+//               softmax (running max and sum per row), P to shared memory, O += P V; out = O / sum,
+//               lse = max + log(sum).
+//   dq          one CTA per 64 query rows: S and dP = dO V^T recomputed per key tile, P = exp(S - lse),
+//               dS = P (dP - delta), dQ += dS K.
+//   dk / dv     one CTA per 64 keys of one (batch, kv head), looping over the query tiles of every query
+//               head of the kv head: S^T = K Q^T, dP^T = V dO^T, P^T, dS^T; dV += P^T dO, dK += dS^T Q.
+//
+// Semantics are those of the SIMT kernels (sdpa_simt.cu) and of gt_flash_attention (reference
+// csrc/gt_ops_nn.cpp:2423-2525): top-left causal, bool mask 0 = masked, float mask added to the scaled
+// score, GQA head map h / (H/Hkv), a row with no allowed key gives 0 (and zero gradients), dropout with
+// the decisions of dropout.cuh. delta = rowsum(dO * O) comes from the SIMT rowsum kernel.
+
+#include <cmath>
+
+#include "dropout.cuh"
+#include "gtb_common.cuh"
+#include "sdpa_args.h"
+
+namespace gtb {
+namespace {
+
+constexpr int T = 64;          // rows and columns of a tile
+constexpr int NT = 256;        // threads per CTA
+constexpr int PAD = 4;         // float padding of transposed tiles (keeps 16-byte alignment)
+
+struct V4 {
+    const float* p;
+    int64_t s0, s1, s2, s3;
+};
+
+struct TiledP {
+    V4 q, k, v, o, g, dq, dk, dv, m;
+    int mask_dtype;  // -1: none
+    int64_t B, H, Hkv, L, S, group;
+    float scale;
+    int causal;
+    float* lse;            // (B, H, L) forward output / backward input
+    const float* delta;    // (B, H, L) rowsum(dO * O), backward
+    int drop;
+    uint32_t drop_thr;
+    uint64_t drop_seed;
+    float inv_keep;
+};
+
+__device__ __forceinline__ float half_warp_max(float v) {
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+__device__ __forceinline__ float half_warp_sum(float v) {
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// mask adjustment of one scaled score: false if (b, h, l, s) may not be attended, else adds a float
+// mask entry
+__device__ __forceinline__ bool mask_score(const TiledP& p, int64_t b, int64_t h, int64_t l, int64_t s, float& x) {
+    if (p.mask_dtype < 0) return true;
+    const int64_t idx = b * p.m.s0 + h * p.m.s1 + l * p.m.s2 + s * p.m.s3;
+    if (p.mask_dtype == BOOL) return ((const uint8_t*)p.m.p)[idx] != 0;
+    x += load_any<float>(p.m.p, idx, p.mask_dtype);
+    return true;
+}
+
+// Load a 64 x D tile of a (B, heads, rows, D) tensor transposed into sm[d][r] (row stride T + PAD);
+// rows at or past `rows` read 0.
+template <int D>
+__device__ __forceinline__ void load_t(float* sm, const V4& t, int64_t b, int64_t h, int64_t r0, int64_t rows) {
+    for (int i = threadIdx.x; i < T * D; i += NT) {
+        const int r = i / D, d = i % D;
+        const int64_t row = r0 + r;
+        sm[d * (T + PAD) + r] = row < rows ? t.p[b * t.s0 + h * t.s1 + row * t.s2 + d * t.s3] : 0.0f;
+    }
+}
+// The same tile row-major: sm[r][d] (row stride D + PAD)
+template <int D>
+__device__ __forceinline__ void load_r(float* sm, const V4& t, int64_t b, int64_t h, int64_t r0, int64_t rows) {
+    for (int i = threadIdx.x; i < T * D; i += NT) {
+        const int r = i / D, d = i % D;
+        const int64_t row = r0 + r;
+        sm[r * (D + PAD) + d] = row < rows ? t.p[b * t.s0 + h * t.s1 + row * t.s2 + d * t.s3] : 0.0f;
+    }
+}
+
+// acc[i][j] += sum_d A[d][ra + i] * B[d][cb + j] over d < D (A, B transposed tiles)
+template <int D>
+__device__ __forceinline__ void block_dot(float (&acc)[4][4], const float* A, const float* B, int ra, int cb) {
+#pragma unroll 8
+    for (int d = 0; d < D; ++d) {
+        const float4 a = *(const float4*)(A + d * (T + PAD) + ra);
+        const float4 c = *(const float4*)(B + d * (T + PAD) + cb);
+        const float av[4] = {a.x, a.y, a.z, a.w}, cv[4] = {c.x, c.y, c.z, c.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], cv[j], acc[i][j]);
+    }
+}
+
+// out[i][j] += sum_s P[s][ra + i] * V[s][cb + j] over the 64 rows s of P (transposed) and V (row-major)
+template <int D>
+__device__ __forceinline__ void block_pv(float (&out)[4][D / 16], const float* P, const float* V, int ra, int cb) {
+#pragma unroll 4
+    for (int s = 0; s < T; ++s) {
+        const float4 a = *(const float4*)(P + s * (T + PAD) + ra);
+        const float av[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+        for (int q = 0; q < D / 64; ++q) {
+            const float4 c = *(const float4*)(V + s * (D + PAD) + cb + 64 * q);
+            const float cv[4] = {c.x, c.y, c.z, c.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) out[i][4 * q + j] = fmaf(av[i], cv[j], out[i][4 * q + j]);
+        }
+    }
+}
+
+// ------------------------------------------------------------------ forward
+
+template <int D>
+__global__ void __launch_bounds__(NT, 2) fwd_f32_tiled_kernel(TiledP p) {
+    extern __shared__ __align__(16) float smem[];
+    float* Qs = smem;                        // [D][T + PAD]
+    float* Ks = Qs + D * (T + PAD);          // [D][T + PAD]
+    float* Vs = Ks + D * (T + PAD);          // [T][D + PAD]
+    float* Ps = Vs + T * (D + PAD);          // [T keys][T + PAD rows]
+    const int tid = threadIdx.x, rg = tid / 16, cg = tid % 16;
+    const int ra = 4 * rg, cb = 4 * cg;
+    const int64_t b = blockIdx.z, h = blockIdx.y, hk = h / p.group, l0 = (int64_t)blockIdx.x * T;
+    load_t<D>(Qs, p.q, b, h, l0, p.L);
+    float m[4], lsum[4], o[4][D / 16];
+    uint32_t rkey[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        m[i] = -INFINITY;
+        lsum[i] = 0.0f;
+        rkey[i] = p.drop ? drop_row_key(drop_head_key(p.drop_seed, (uint32_t)(b * p.H + h)), (uint32_t)(l0 + ra + i)) : 0u;
+#pragma unroll
+        for (int j = 0; j < D / 16; ++j) o[i][j] = 0.0f;
+    }
+    int64_t s_end = p.S;
+    if (p.causal) s_end = min(p.S, min(l0 + T, p.L));
+    for (int64_t s0 = 0; s0 < s_end; s0 += T) {
+        __syncthreads();
+        load_t<D>(Ks, p.k, b, hk, s0, p.S);
+        load_r<D>(Vs, p.v, b, hk, s0, p.S);
+        __syncthreads();
+        float x[4][4] = {};
+        block_dot<D>(x, Qs, Ks, ra, cb);
+        float pv[4][4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int64_t l = l0 + ra + i;
+            float rmax = -INFINITY;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int64_t s = s0 + cb + j;
+                float v = x[i][j] * p.scale;
+                const bool ok = l < p.L && s < p.S && !(p.causal && s > l) && mask_score(p, b, h, l, s, v);
+                x[i][j] = ok ? v : -INFINITY;
+                rmax = fmaxf(rmax, x[i][j]);
+            }
+            const float m_new = fmaxf(m[i], half_warp_max(rmax));
+            const float alpha = m_new == -INFINITY ? 1.0f : __expf(m[i] - m_new);
+            float rs = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float e = x[i][j] == -INFINITY ? 0.0f : __expf(x[i][j] - m_new);
+                rs += e;
+                pv[i][j] = (p.drop && !drop_keep(rkey[i], (uint32_t)(s0 + cb + j), p.drop_thr)) ? 0.0f : e;
+            }
+            lsum[i] = lsum[i] * alpha + half_warp_sum(rs);
+#pragma unroll
+            for (int j = 0; j < D / 16; ++j) o[i][j] *= alpha;
+            m[i] = m_new;
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+            *(float4*)(Ps + (cb + j) * (T + PAD) + ra) = make_float4(pv[0][j], pv[1][j], pv[2][j], pv[3][j]);
+        __syncthreads();
+        block_pv<D>(o, Ps, Vs, ra, cb);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int64_t l = l0 + ra + i;
+        if (l >= p.L) continue;
+        const float inv = lsum[i] > 0.0f ? (p.drop ? p.inv_keep : 1.0f) / lsum[i] : 0.0f;
+        float* orow = (float*)p.o.p + b * p.o.s0 + h * p.o.s1 + l * p.o.s2;
+#pragma unroll
+        for (int q = 0; q < D / 64; ++q)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) orow[(cb + 64 * q + j) * p.o.s3] = o[i][4 * q + j] * inv;
+        if (p.lse && cg == 0) p.lse[(b * p.H + h) * p.L + l] = lsum[i] > 0.0f ? m[i] + __logf(lsum[i]) : -INFINITY;
+    }
+}
+
+// ------------------------------------------------------------------ dq
+
+template <int D>
+__global__ void __launch_bounds__(NT, 2) bwd_dq_f32_tiled_kernel(TiledP p) {
+    extern __shared__ __align__(16) float smem[];
+    float* Qs = smem;                        // [D][T + PAD]
+    float* Gs = Qs + D * (T + PAD);          // dO [D][T + PAD]
+    float* Ks = Gs + D * (T + PAD);          // [D][T + PAD]  (K transposed, for S)
+    float* Vs = Ks + D * (T + PAD);          // [D][T + PAD]  (V transposed, for dP)
+    float* Kr = Vs + D * (T + PAD);          // [T][D + PAD]  (K row-major, for dQ += dS K)
+    float* Ds = Kr + T * (D + PAD);          // dS [T keys][T + PAD rows]
+    const int tid = threadIdx.x, rg = tid / 16, cg = tid % 16;
+    const int ra = 4 * rg, cb = 4 * cg;
+    const int64_t b = blockIdx.z, h = blockIdx.y, hk = h / p.group, l0 = (int64_t)blockIdx.x * T;
+    load_t<D>(Qs, p.q, b, h, l0, p.L);
+    load_t<D>(Gs, p.g, b, h, l0, p.L);
+    float lse[4], dl[4], dq[4][D / 16];
+    uint32_t rkey[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int64_t l = l0 + ra + i;
+        lse[i] = l < p.L ? p.lse[(b * p.H + h) * p.L + l] : -INFINITY;
+        dl[i] = l < p.L ? p.delta[(b * p.H + h) * p.L + l] : 0.0f;
+        rkey[i] = p.drop ? drop_row_key(drop_head_key(p.drop_seed, (uint32_t)(b * p.H + h)), (uint32_t)l) : 0u;
+#pragma unroll
+        for (int j = 0; j < D / 16; ++j) dq[i][j] = 0.0f;
+    }
+    int64_t s_end = p.S;
+    if (p.causal) s_end = min(p.S, min(l0 + T, p.L));
+    for (int64_t s0 = 0; s0 < s_end; s0 += T) {
+        __syncthreads();
+        load_t<D>(Ks, p.k, b, hk, s0, p.S);
+        load_t<D>(Vs, p.v, b, hk, s0, p.S);
+        load_r<D>(Kr, p.k, b, hk, s0, p.S);
+        __syncthreads();
+        float x[4][4] = {}, dp[4][4] = {};
+        block_dot<D>(x, Qs, Ks, ra, cb);
+        block_dot<D>(dp, Gs, Vs, ra, cb);
+        float ds[4][4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int64_t l = l0 + ra + i;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int64_t s = s0 + cb + j;
+                float v = x[i][j] * p.scale;
+                const bool ok = l < p.L && s < p.S && !(p.causal && s > l) && lse[i] != -INFINITY &&
+                                mask_score(p, b, h, l, s, v) && v != -INFINITY;
+                const float pr = ok ? __expf(v - lse[i]) : 0.0f;
+                float d = dp[i][j];
+                if (p.drop) d = drop_keep(rkey[i], (uint32_t)s, p.drop_thr) ? d * p.inv_keep : 0.0f;
+                ds[i][j] = pr * (d - dl[i]);
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+            *(float4*)(Ds + (cb + j) * (T + PAD) + ra) = make_float4(ds[0][j], ds[1][j], ds[2][j], ds[3][j]);
+        __syncthreads();
+        block_pv<D>(dq, Ds, Kr, ra, cb);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int64_t l = l0 + ra + i;
+        if (l >= p.L) continue;
+        float* row = (float*)p.dq.p + b * p.dq.s0 + h * p.dq.s1 + l * p.dq.s2;
+#pragma unroll
+        for (int q = 0; q < D / 64; ++q)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) row[(cb + 64 * q + j) * p.dq.s3] = dq[i][4 * q + j] * p.scale;
+    }
+}
+
+// ------------------------------------------------------------------ dk / dv
+
+template <int D>
+__global__ void __launch_bounds__(NT, 2) bwd_dkdv_f32_tiled_kernel(TiledP p) {
+    extern __shared__ __align__(16) float smem[];
+    float* Ks = smem;                        // K^T [D][T + PAD]  (rows = this CTA's keys)
+    float* Vs = Ks + D * (T + PAD);          // V^T [D][T + PAD]
+    float* Qs = Vs + D * (T + PAD);          // Q^T [D][T + PAD]  (a query tile)
+    float* Gs = Qs + D * (T + PAD);          // dO^T [D][T + PAD]
+    float* Qr = Gs + D * (T + PAD);          // Q row-major [T][D + PAD]
+    float* Gr = Qr + T * (D + PAD);          // dO row-major [T][D + PAD]
+    float* Ps = Gr + T * (D + PAD);          // P^T as [query][key + PAD] (for dV += P^T dO)
+    float* Ds = Ps + T * (T + PAD);          // dS^T as [query][key + PAD]
+    float* LD = Ds + T * (T + PAD);          // lse[T], delta[T] of the query tile
+    const int tid = threadIdx.x, rg = tid / 16, cg = tid % 16;
+    const int ra = 4 * rg, cb = 4 * cg;      // ra: this thread's keys, cb: queries (S^T) or dims (dK/dV)
+    const int64_t b = blockIdx.z, hk = blockIdx.y, s0 = (int64_t)blockIdx.x * T;
+    load_t<D>(Ks, p.k, b, hk, s0, p.S);
+    load_t<D>(Vs, p.v, b, hk, s0, p.S);
+    float dk[4][D / 16], dv[4][D / 16];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < D / 16; ++j) { dk[i][j] = 0.0f; dv[i][j] = 0.0f; }
+    // causal: keys s0.. are seen by queries l >= s0
+    const int64_t l_begin = p.causal ? (s0 / T) * T : 0;
+    for (int64_t h = hk * p.group; h < (hk + 1) * p.group; ++h) {
+        const uint32_t hkey = p.drop ? drop_head_key(p.drop_seed, (uint32_t)(b * p.H + h)) : 0u;
+        for (int64_t l0 = l_begin; l0 < p.L; l0 += T) {
+            __syncthreads();
+            load_t<D>(Qs, p.q, b, h, l0, p.L);
+            load_t<D>(Gs, p.g, b, h, l0, p.L);
+            load_r<D>(Qr, p.q, b, h, l0, p.L);
+            load_r<D>(Gr, p.g, b, h, l0, p.L);
+            for (int i = tid; i < T; i += NT) {
+                const int64_t l = l0 + i;
+                LD[i] = l < p.L ? p.lse[(b * p.H + h) * p.L + l] : -INFINITY;
+                LD[T + i] = l < p.L ? p.delta[(b * p.H + h) * p.L + l] : 0.0f;
+            }
+            __syncthreads();
+            float x[4][4] = {}, dp[4][4] = {};
+            block_dot<D>(x, Ks, Qs, ra, cb);  // S^T[key][query]
+            block_dot<D>(dp, Vs, Gs, ra, cb); // dP^T
+            float pt[4][4], dst[4][4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int64_t s = s0 + ra + i;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int64_t l = l0 + cb + j;
+                    const float lse = LD[cb + j];
+                    float v = x[i][j] * p.scale;
+                    const bool ok = l < p.L && s < p.S && !(p.causal && s > l) && lse != -INFINITY &&
+                                    mask_score(p, b, h, l, s, v) && v != -INFINITY;
+                    const float pr = ok ? __expf(v - lse) : 0.0f;
+                    float d = dp[i][j], pk = pr;
+                    if (p.drop) {
+                        const bool kept = drop_keep(drop_row_key(hkey, (uint32_t)l), (uint32_t)s, p.drop_thr);
+                        d = kept ? d * p.inv_keep : 0.0f;
+                        pk = kept ? pr * p.inv_keep : 0.0f;
+                    }
+                    pt[i][j] = pk;
+                    dst[i][j] = pr * (d - LD[T + cb + j]);
+                }
+            }
+            // P^T, dS^T stored [query][key]: rows of the "A" operand of block_pv are queries
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                *(float4*)(Ps + (cb + j) * (T + PAD) + ra) = make_float4(pt[0][j], pt[1][j], pt[2][j], pt[3][j]);
+                *(float4*)(Ds + (cb + j) * (T + PAD) + ra) = make_float4(dst[0][j], dst[1][j], dst[2][j], dst[3][j]);
+            }
+            __syncthreads();
+            block_pv<D>(dv, Ps, Gr, ra, cb);   // dV[key][d] += sum_l P^T[key][l] dO[l][d]
+            block_pv<D>(dk, Ds, Qr, ra, cb);   // dK[key][d] += sum_l dS^T[key][l] Q[l][d]
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int64_t s = s0 + ra + i;
+        if (s >= p.S) continue;
+        float* krow = (float*)p.dk.p + b * p.dk.s0 + hk * p.dk.s1 + s * p.dk.s2;
+        float* vrow = (float*)p.dv.p + b * p.dv.s0 + hk * p.dv.s1 + s * p.dv.s2;
+#pragma unroll
+        for (int q = 0; q < D / 64; ++q)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                krow[(cb + 64 * q + j) * p.dk.s3] = dk[i][4 * q + j] * p.scale;
+                vrow[(cb + 64 * q + j) * p.dv.s3] = dv[i][4 * q + j];
+            }
+    }
+}
+
+template <typename K>
+bool smem_attr(K kern, size_t bytes) {
+    return !cuda_failed(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes),
+                        "fp32 tiled attention: shared memory");
+}
+
+V4 v4(const gtb_tensor4& t) { return V4{(const float*)t.data, t.stride[0], t.stride[1], t.stride[2], t.stride[3]}; }
+
+template <int D>
+int fwd_d(const TiledP& p, cudaStream_t st) {
+    const size_t smem = sizeof(float) * (3 * D * (T + PAD) + T * (D + PAD) + T * (T + PAD));
+    if (!smem_attr(fwd_f32_tiled_kernel<D>, smem)) return -1;
+    dim3 grid((unsigned)((p.L + T - 1) / T), (unsigned)p.H, (unsigned)p.B);
+    fwd_f32_tiled_kernel<D><<<grid, NT, smem, st>>>(p);
+    return cuda_failed(cudaGetLastError(), "fp32 tiled attention forward launch") ? -1 : 0;
+}
+
+template <int D>
+int bwd_d(const TiledP& p, cudaStream_t st) {
+    const size_t s_dq = sizeof(float) * (4 * D * (T + PAD) + T * (D + PAD) + T * (T + PAD));
+    const size_t s_kv = sizeof(float) * (4 * D * (T + PAD) + 2 * T * (D + PAD) + 2 * T * (T + PAD) + 2 * T);
+    if (!smem_attr(bwd_dq_f32_tiled_kernel<D>, s_dq) || !smem_attr(bwd_dkdv_f32_tiled_kernel<D>, s_kv)) return -1;
+    if (p.L > 0) {
+        bwd_dq_f32_tiled_kernel<D><<<dim3((unsigned)((p.L + T - 1) / T), (unsigned)p.H, (unsigned)p.B), NT, s_dq, st>>>(p);
+        if (cuda_failed(cudaGetLastError(), "fp32 tiled attention dq launch")) return -1;
+    }
+    if (p.S > 0) {
+        bwd_dkdv_f32_tiled_kernel<D><<<dim3((unsigned)((p.S + T - 1) / T), (unsigned)p.Hkv, (unsigned)p.B), NT, s_kv, st>>>(p);
+        if (cuda_failed(cudaGetLastError(), "fp32 tiled attention dk/dv launch")) return -1;
+    }
+    return 0;
+}
+
+TiledP common(const gtb_tensor4& q, const gtb_tensor4& k, const gtb_tensor4& v, bool has_mask, const gtb_tensor4& mask,
+              const AttnShape& sh, float scale, int causal, float drop_p, uint32_t drop_thr, uint64_t drop_seed) {
+    TiledP p{};
+    p.q = v4(q); p.k = v4(k); p.v = v4(v);
+    p.m = has_mask ? V4{(const float*)mask.data, mask.stride[0], mask.stride[1], mask.stride[2], mask.stride[3]}
+                   : V4{nullptr, 0, 0, 0, 0};
+    p.mask_dtype = has_mask ? mask.dtype : -1;
+    p.B = sh.B; p.H = sh.H; p.Hkv = sh.Hkv; p.L = sh.L; p.S = sh.S; p.group = sh.H / sh.Hkv;
+    p.scale = scale;
+    p.causal = causal;
+    p.drop = drop_p > 0.0f;
+    p.drop_thr = drop_thr;
+    p.drop_seed = drop_seed;
+    p.inv_keep = 1.0f / (1.0f - drop_p);
+    return p;
+}
+
+}  // namespace
+
+bool f32_tiled_supported(const AttnShape& sh, int dtype) {
+    return dtype == F32 && sh.D == 64 && sh.Dv == 64 && sh.B <= 65535 && sh.H <= 65535 && sh.L < (1ll << 31) &&
+           sh.S < (1ll << 31);
+}
+
+int launch_fwd_f32_tiled(const FwdArgs& a, cudaStream_t st) {
+    TiledP p = common(a.q, a.k, a.v, a.has_mask, a.mask, a.sh, a.scale, a.causal, a.drop_p, a.drop_thr, a.drop_seed);
+    p.o = v4(a.o);
+    p.lse = (float*)a.lse;
+    return fwd_d<64>(p, st);
+}
+
+int launch_bwd_f32_tiled(const BwdArgs& a, const float* delta, cudaStream_t st) {
+    TiledP p = common(a.q, a.k, a.v, a.has_mask, a.mask, a.sh, a.scale, a.causal, a.drop_p, a.drop_thr, a.drop_seed);
+    p.o = v4(a.o);
+    p.g = v4(a.dout);
+    p.dq = v4(a.dq);
+    p.dk = v4(a.dk);
+    p.dv = v4(a.dv);
+    p.lse = (float*)a.lse;
+    p.delta = delta;
+    return bwd_d<64>(p, st);
+}
+
+}  // namespace gtb

@@ -14,6 +14,7 @@
 
 #include <cfloat>
 #include <cmath>
+#include <type_traits>
 
 #include "dropout.cuh"
 #include "gtb_common.cuh"
@@ -430,6 +431,10 @@ int run_bwd(const BwdArgs& a, cudaStream_t st) {
     if (rows > 0) {
         bwd_rowsum_kernel<T, Acc><<<(unsigned)((rows + ROWS - 1) / ROWS), ROWS * 32, 0, st>>>(p, B);
         if (cuda_failed(cudaGetLastError(), "sdpa backward rowsum launch")) return -1;
+    }
+    if (std::is_same<T, float>::value && f32_tiled_supported(a.sh, a.q.dtype))  // fp32, D = 64: blocked kernels
+        return launch_bwd_f32_tiled(a, (const float*)a.scratch, st);
+    if (rows > 0) {
         const size_t s1 = dq_smem<Acc>(p.D, p.Dv);
         if (!set_smem(bwd_dq_kernel<T, Acc>, s1)) return -1;
         dim3 g1((unsigned)((p.L + ROWS - 1) / ROWS), (unsigned)p.H, (unsigned)B);
@@ -454,6 +459,7 @@ int launch_fwd_simt(const FwdArgs& a, cudaStream_t st) {
                    (long long)a.sh.D, (long long)a.sh.Dv);
         return -1;
     }
+    if (f32_tiled_supported(a.sh, a.q.dtype)) return launch_fwd_f32_tiled(a, st);
     switch (a.q.dtype) {
         case F32: return run_fwd<float, float>(a, st);
         case F64: return run_fwd<double, double>(a, st);

@@ -388,6 +388,60 @@ def sdpa_from_host(query: torch.Tensor, key: torch.Tensor, value: torch.Tensor, 
     return out
 
 
+# ------------------------------------------------------------------ linear layers (MHA projections)
+
+def _linear_2d(a: torch.Tensor, b: torch.Tensor, bias: torch.Tensor | None) -> torch.Tensor:
+    """c = a b^T (+ bias) on the tensor-core GEMM: a (M, K), b (N, K) contiguous 16-bit CUDA tensors."""
+    M, K = a.shape
+    N = b.shape[0]
+    c = torch.empty((M, N), dtype=a.dtype, device=a.device)
+    rc = _C.lib.gtb_linear(a.data_ptr(), b.data_ptr(), bias.data_ptr() if bias is not None else None, c.data_ptr(),
+                           M, N, K, K, K, N, _code(a), _stream(a.device))
+    _C.check_rc(rc, "linear")
+    return c
+
+
+class LinearFn(torch.autograd.Function):
+    """F.linear(x, weight, bias) for bf16/f16 on the repo's tcgen05 GEMM (gtb_linear), the role of
+    gt_linear (reference csrc/gt_ops_nn.cpp:256-335). Backward: dx = dy W and dW = dy^T x are the same
+    kernel on transposed copies (both operands K-major), db = the column sums of dy."""
+
+    @staticmethod
+    def forward(ctx, x, weight, bias):
+        lead = x.shape[:-1]
+        x2 = x.reshape(-1, x.shape[-1]).contiguous()
+        w = weight.contiguous()
+        y = _linear_2d(x2, w, bias.contiguous() if bias is not None else None)
+        ctx.save_for_backward(x2, w)
+        ctx.has_bias = bias is not None
+        return y.view(*lead, w.shape[0])
+
+    @staticmethod
+    def backward(ctx, gy):
+        x2, w = ctx.saved_tensors
+        g2 = gy.reshape(-1, w.shape[0]).contiguous()
+        dx = dw = db = None
+        if ctx.needs_input_grad[0]:
+            dx = _linear_2d(g2, w.t().contiguous(), None).view(*gy.shape[:-1], w.shape[1])
+        if ctx.needs_input_grad[1]:
+            dw = _linear_2d(g2.t().contiguous(), x2.t().contiguous(), None)
+        if ctx.has_bias and ctx.needs_input_grad[2]:
+            db = g2.float().sum(0).to(g2.dtype)
+        return dx, dw, db
+
+
+def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None) -> torch.Tensor:
+    """F.linear on the engine: bf16/f16 on the tensor-core GEMM (LinearFn); other dtypes (fp32: there
+    is no repo fp32 GEMM to beat cuBLAS's on the CUDA cores) and leading sizes that are not multiples
+    of 8 through torch.nn.functional.linear."""
+    _require_cuda("linear", x, weight, bias)
+    K, N = x.shape[-1], weight.shape[0]
+    if x.dtype in (torch.bfloat16, torch.float16) and weight.dtype == x.dtype and \
+            (bias is None or bias.dtype == x.dtype) and K % 8 == 0 and N % 8 == 0 and K > 0 and x.numel() > 0:
+        return LinearFn.apply(x, weight, bias)
+    return torch.nn.functional.linear(x, weight, bias)
+
+
 # ------------------------------------------------------------------ Q8_0 KV cache
 
 def quantize_q8_0(x: torch.Tensor) -> torch.Tensor:

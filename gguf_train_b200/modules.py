@@ -8,9 +8,10 @@ turned into -1e9; float masks added) and the error messages of the reference
 (gguf_train/nn/modules/transformer.py:21-191).
 
 How it runs here:
-* self-attention with packed weights projects q, k and v with ONE GEMM over in_proj_weight and takes
-  the heads as strided views of its output (no copies); the attention kernels read those views
-  directly;
+* the in/out projections run on the repo's tcgen05 GEMM for bf16/f16 (functional.linear; fp32 on
+  cuBLAS); self-attention with packed weights projects q, k and v with ONE GEMM over
+  in_proj_weight and takes the heads as strided views of its output (no copies); the attention
+  kernels read those views directly;
 * attn_mask and key_padding_mask are merged into one additive mask, which the tensor-core kernels
   apply per 128 x 128 block (a key-padding mask costs almost nothing: only the blocks holding padded
   keys are read entry by entry);
@@ -62,8 +63,8 @@ class MultiheadAttention(nn.Module):
         self_attention = query is key and key is value
         xq, xk, xv, kpm, unbatched = self._batch_major(query, key, value, key_padding_mask)
         B, L, S = xq.shape[0], xq.shape[1], xk.shape[1]
+        bias = self._score_bias(attn_mask, kpm, B, L, S, xq.dtype)  # argument errors before any device work
         q, k, v = self._heads(xq, xk, xv, self_attention)
-        bias = self._score_bias(attn_mask, kpm, B, L, S, q.dtype)
         scale = self.head_dim ** -0.5
         p_drop = self.dropout if self.training else 0.0
         if need_weights:
@@ -76,7 +77,7 @@ class MultiheadAttention(nn.Module):
             ctx = F.scaled_dot_product_attention(q, k, v, attn_mask=bias, dropout_p=p_drop, is_causal=is_causal,
                                                  scale=scale)
             weights = None
-        y = self.out_proj(ctx.transpose(1, 2).reshape(B, L, self.embed_dim))
+        y = F.linear(ctx.transpose(1, 2).reshape(B, L, self.embed_dim), self.out_proj.weight, self.out_proj.bias)
         if not self.batch_first:
             y = y.transpose(0, 1)
         if unbatched:
@@ -114,7 +115,7 @@ class MultiheadAttention(nn.Module):
         takes one GEMM over in_proj_weight; the heads are views of its (B, L, 3, heads, head_dim) output."""
         B, heads, hd = xq.shape[0], self.num_heads, self.head_dim
         if self_attention and self._qkv_same:
-            qkv = torch.nn.functional.linear(xq, self.in_proj_weight, self.in_proj_bias)
+            qkv = F.linear(xq, self.in_proj_weight, self.in_proj_bias)
             q, k, v = qkv.reshape(B, xq.shape[1], 3, heads, hd).permute(2, 0, 3, 1, 4).unbind(0)
             return q, k, v
         if self._qkv_same:
@@ -122,7 +123,7 @@ class MultiheadAttention(nn.Module):
         else:
             weights = (self.q_proj_weight, self.k_proj_weight, self.v_proj_weight)
         biases = (None,) * 3 if self.in_proj_bias is None else self.in_proj_bias.chunk(3)
-        return tuple(torch.nn.functional.linear(x, w, bb).reshape(B, x.shape[1], heads, hd).transpose(1, 2)
+        return tuple(F.linear(x, w, bb).reshape(B, x.shape[1], heads, hd).transpose(1, 2)
                      for x, w, bb in zip((xq, xk, xv), weights, biases))
 
     def _score_bias(self, attn_mask, kpm, B: int, L: int, S: int, dtype):

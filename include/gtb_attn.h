@@ -124,6 +124,14 @@ GTB_API int gtb_attn_weights(const gtb_tensor4 *q, const gtb_tensor4 *k, const g
                              float scale, int is_causal, int average, const gtb_sdpa_opts *opts, gtb_tensor4 *out,
                              void *stream);
 
+/* Linear layer on the tensor cores: c (M, N) = a (M, K) b (N, K)^T (+ bias (N)), i.e. F.linear(a, b, bias)
+ * for row-major a and b. Replaces gt_linear (reference csrc/gt_ops_nn.cpp:256-335, a ggml_mul_mat graph)
+ * for 16-bit operands: dtype bf16 or f16 for a, b, bias (nullable) and c; f32 accumulation.
+ * lda, ldb, ldc: elements between consecutive rows, multiples of 8 (16-byte rows); pointers 16-byte
+ * aligned; K > 0. MultiheadAttention's projections and their backward products use it. */
+GTB_API int gtb_linear(const void *a, const void *b, const void *bias, void *c, int64_t M, int64_t N, int64_t K,
+                       int64_t lda, int64_t ldb, int64_t ldc, int dtype, void *stream);
+
 /* Q8_0 quantisation of n_rows rows of row_len values (row_len % 32 == 0) into GGUF Q8_0 blocks
  * (fp16 scale + 32 int8, 34 bytes per 32 values), bit-exact with ggml's reference quantiser.
  * Replaces gt_quantize(t, GT_Q_BASE + 8) (reference csrc/gt_ops_extra.cpp:2002, which goes
