@@ -118,3 +118,73 @@ def test_errors(tmp_path):
     gguf_io.save_gguf(tmp_path / "z.gguf", {"q": gguf_io.Q8_0(torch.zeros(1, 34, dtype=torch.uint8))})
     with pytest.raises(RuntimeError, match="dequantize runs on the GPU"):
         gguf_io.load_gguf(tmp_path / "z.gguf", dequantize=True)
+
+
+def test_shapes_and_types_gguf_cannot_hold_round_trip(tmp_path):
+    """More than four dimensions, scalars, leading ones, empty tensors, uint8, bool and complex: stored
+    in a form GGUF holds (at most four dimensions, int8/f32/f64 carriers) with the real shape and type
+    under the reserved keys, as the reference writes them (csrc/gt_ops_extra.cpp:1497-1516); gguf-py
+    still reads the file, and the reserved keys stay out of the metadata."""
+    from gguf import GGUFReader
+
+    from gguf_train_b200 import gguf_io
+
+    rs = np.random.RandomState(5)
+    k = rs.randn(2, 1, 3, 2, 4, 32).astype(np.float32)
+    src = {
+        "five": torch.from_numpy(rs.randn(2, 3, 1, 4, 5).astype(np.float32)),
+        "scalar": torch.tensor(3.5, dtype=torch.float64),
+        "lead": torch.from_numpy(rs.randn(1, 5).astype(np.float32)),
+        "empty": torch.zeros(0, 4, dtype=torch.float16),
+        "u8": torch.arange(250, 256, dtype=torch.uint8).reshape(2, 3),
+        "mask": torch.tensor([[True, False, True], [False, False, True]]),
+        "c64": torch.randn(3, 2, dtype=torch.complex64),
+        "c128": torch.tensor(1 - 2j, dtype=torch.complex128),
+        "q6": gguf_io.Q8_0(_blocks(k)),
+        "plain": torch.from_numpy(rs.randn(2, 3, 4, 5).astype(np.float32)),
+    }
+    path = tmp_path / "odd.gguf"
+    gguf_io.save_gguf(path, src, {"general.name": "odd"})
+
+    r = GGUFReader(path)
+    assert all(len(t.shape) <= 4 for t in r.tensors)
+    keys = set(r.fields)
+    assert "gguf_train.shape.five" in keys and "gguf_train.dtype.u8" in keys
+    assert "gguf_train.shape.plain" not in keys and "gguf_train.dtype.plain" not in keys
+
+    gf = gguf_io.load_gguf(path)
+    assert not any(k.startswith("gguf_train.") for k in gf.metadata)
+    for name, t in src.items():
+        got = gf[name]
+        if isinstance(t, gguf_io.Q8_0):
+            assert got.blocks.shape == t.blocks.shape and torch.equal(got.blocks, t.blocks)
+        else:
+            assert got.dtype == t.dtype and got.shape == t.shape, name
+            assert torch.equal(got, t), name
+
+    with pytest.raises(ValueError, match="is reserved"):
+        gguf_io.save_gguf(tmp_path / "r.gguf", {}, {"gguf_train.shape.x": [1]})
+
+
+def test_reserved_keys_written_by_another_writer_are_applied(tmp_path):
+    """A file laid out as the reference writes a 5-D uint8 tensor (int8 bytes, the outer dimensions
+    folded, real shape and type under the reserved keys), produced here with gguf-py, loads with its
+    real shape and type."""
+    from gguf import GGMLQuantizationType, GGUFWriter
+
+    from gguf_train_b200 import gguf_io
+
+    real = (2, 2, 3, 1, 4)
+    vals = np.arange(48, dtype=np.uint8) * 5
+    path = tmp_path / "ref_like.gguf"
+    w = GGUFWriter(path, arch="llama")
+    w.add_array("gguf_train.shape.t", list(real))
+    w.add_string("gguf_train.dtype.t", "uint8")
+    w.add_tensor("t", vals.view(np.int8).reshape(4, 3, 1, 4), raw_dtype=GGMLQuantizationType.I8)
+    w.write_header_to_file()
+    w.write_kv_data_to_file()
+    w.write_tensors_to_file()
+    w.close()
+    gf = gguf_io.load_gguf(path)
+    assert gf["t"].dtype == torch.uint8 and tuple(gf["t"].shape) == real
+    assert torch.equal(gf["t"].flatten(), torch.from_numpy(vals))
