@@ -11,11 +11,12 @@
 //                warpgroup works on its S the tensor core runs the other tile's MMAs;
 //   warps 2-3    idle;
 //   warps 4-7    softmax + epilogue of tile 0, warps 8-11 of tile 1: one query row per thread (TMEM
-//                lane = row). Two passes over S in TMEM (row maximum, then exponentials) so a row never
-//                has to sit in registers whole; online softmax in the log2 domain with lazy rescaling
-//                (O and the running sum are rescaled only when the maximum grows by more than 2^8);
-//                P (bf16/f16) is written into the upper half of the tile's S columns, where the PV MMA
-//                reads it as its A operand.
+//                lane = row). One pass over S in TMEM, 32 keys at a time, exponentiating against the
+//                running maximum (online softmax in the log2 domain with lazy rescaling: the offset is
+//                raised only when a chunk's maximum exceeds it by more than 2^8, and then the block's
+//                earlier probabilities are rescaled; O and the running sum are rescaled once per block);
+//                P (bf16/f16) of each 32-key chunk is written over the first 16 of the chunk's S
+//                columns, where the PV MMA reads it as its A operand.
 // TMEM columns: S_0 [0,128), S_1 [128,256), O_0 [256,256+D), O_1 [384,384+D).
 //
 // Semantics are those of gt_flash_attention (reference csrc/gt_ops_nn.cpp:2423-2525): causal is
@@ -70,7 +71,6 @@ struct Cfg {
 
 __device__ __forceinline__ uint32_t s_col(int t) { return (uint32_t)t * 128u; }
 __device__ __forceinline__ uint32_t o_col(int t) { return 256u + (uint32_t)t * 128u; }
-constexpr uint32_t P_OFF = 64;  // P_t lives in S_t's columns [64, 128)
 
 // 2^x on the FMA/ALU pipes, to take part of the softmax's exponentials off the MUFU unit, for a
 // packed pair of floats. Range reduction x = n + f with n = round(x) (adding 1.5 * 2^23 rounds to an
@@ -105,6 +105,21 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
     if constexpr (BF16) asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
     else asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
     return r;
+}
+
+// both 16-bit values of a packed pair times a (f32 product, rounded back to nearest even)
+template <bool BF16>
+__device__ __forceinline__ uint32_t scale_pair(uint32_t w, float a) {
+    float lo, hi;
+    if constexpr (BF16) {
+        lo = __uint_as_float(w << 16);
+        hi = __uint_as_float(w & 0xffff0000u);
+    } else {
+        const __half2 h = *reinterpret_cast<const __half2*>(&w);
+        lo = __low2float(h);
+        hi = __high2float(h);
+    }
+    return pack2<BF16>(lo * a, hi * a);
 }
 
 // max of three (one instruction on sm_100)
@@ -341,11 +356,13 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
                 if (!mbar_wait(&v_full[vs], (jg / C::VS) & 1, p.status, 24)) return false;
                 tc_fence_after();
                 const uint64_t vb = vs ? vd1 : vd0;
-                const uint32_t dst = tmem + o_col(t), pa = tmem + s_col(t) + P_OFF;
+                const uint32_t dst = tmem + o_col(t), pa = tmem + s_col(t);
 #pragma unroll
                 for (int kk = 0; kk < BN / 16; ++kk) {
-                    // A = P_t(j): 16-bit values packed two per TMEM column, 8 columns per K step
-                    mma_ts(dst, pa + kk * 8, desc_advance(vb, kk * 2048), IDESC_PV, (!first || kk > 0) ? 1u : 0u);
+                    // A = P_t(j): 16-bit values packed two per TMEM column; keys 32c..32c+31 sit in
+                    // columns 32c..32c+15, 8 columns per K step
+                    mma_ts(dst, pa + 32 * (kk >> 1) + 8 * (kk & 1), desc_advance(vb, kk * 2048), IDESC_PV,
+                           (!first || kk > 0) ? 1u : 0u);
                 }
                 return true;
             };
@@ -451,55 +468,19 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
                         }
                     }
                 };
-                // pass 1: row maximum, 64 columns at a time; columns 64..127 stay in registers for pass 2
-                uint32_t ra[32], rb[32];
-                float* xa = (float*)ra;
-                float* xb = (float*)rb;
-                float pm[8];
-                tmem_ld32(s_tmem + 0, ra);
-                tmem_ld32(s_tmem + 32, rb);
-                tmem_ld_wait();
-                attn_mask(xa, kv0);
-                attn_mask(xb, kv0 + 32);
-                if (need_mask) { mask_chunk(xa, kv0, lim); mask_chunk(xb, kv0 + 32, lim); }
-#pragma unroll
-                for (int u = 0; u < 8; ++u) pm[u] = fmaxf(xa[u], xb[u]);
-#pragma unroll
-                for (int i = 8; i < 32; ++i) pm[i & 7] = fmax3(pm[i & 7], xa[i], xb[i]);
-                tmem_ld32(s_tmem + 64, ra);
-                tmem_ld32(s_tmem + 96, rb);
-                tmem_ld_wait();
-                attn_mask(xa, kv0 + 64);
-                attn_mask(xb, kv0 + 96);
-                if (need_mask) { mask_chunk(xa, kv0 + 64, lim); mask_chunk(xb, kv0 + 96, lim); }
-#pragma unroll
-                for (int i = 0; i < 32; ++i) pm[i & 7] = fmax3(pm[i & 7], xa[i], xb[i]);
-                const float mx = fmax3(fmax3(pm[0], pm[1], pm[2]), fmax3(pm[3], pm[4], pm[5]), fmaxf(pm[6], pm[7]));
-                const float m_new = fmaxf(m_used, mx * p.scale_log2);
-                const bool rescale = m_new > m_used + 8.0f;  // false while the row has no finite score
-                if (__any_sync(0xffffffffu, rescale && j > 0)) {
-                    // PV_t(j-1) is complete: it was issued before S_t(j), whose completion we just saw
-                    const float alpha = rescale ? ex2(m_used - m_new) : 1.0f;
-#pragma unroll
-                    for (int c = 0; c < D / 32; ++c) {
-                        uint32_t ov[32];
-                        tmem_ld32(o_tmem + c * 32, ov);
-                        tmem_ld_wait();
-#pragma unroll
-                        for (int i = 0; i < 32; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
-                        tmem_st32(o_tmem + c * 32, ov);
-                    }
-                }
-                if (rescale) {
-                    lsum *= ex2(m_used - m_new);
-                    m_used = m_new;
-                }
-                const float neg_m = (m_used == -INFINITY) ? 0.0f : -m_used;
-                // pass 2: exponentials, 32 columns at a time, P into S's columns [64, 128); the scale-and-
-                // subtract and the row sum run as packed two-lane f32 operations
-                const uint64_t sc2 = f2_pack(p.scale_log2, p.scale_log2), nm2 = f2_pack(neg_m, neg_m);
+                // One pass over S, 32 columns (keys) at a time, with the running maximum m_used as the
+                // exponent's offset: a chunk whose maximum exceeds m_used by more than 2^8 first raises
+                // m_used for its rows and rescales the probabilities this block already wrote and their
+                // partial sum (rare once a row has seen a few keys); O and the running sum are rescaled
+                // once at the end of the block. P of chunk c (keys 32c..32c+31) is written over S's
+                // columns 32c..32c+15, which the chunk has just read, as packed 16-bit pairs (the PV
+                // MMA's A operand). The scale-and-subtract and the sums run as packed two-lane f32.
+                const float m_start = m_used;
+                const uint64_t sc2 = f2_pack(p.scale_log2, p.scale_log2);
                 uint64_t ps2[2] = {0ull, 0ull};
                 auto emit = [&](const float* x, int c) {
+                    const float neg_m = (m_used == -INFINITY) ? 0.0f : -m_used;
+                    const uint64_t nm2 = f2_pack(neg_m, neg_m);
                     uint32_t pk[16];
                     uint32_t kbits = 0;  // dropout: keep decisions of keys kv0 + 32c .. kv0 + 32c + 31
                     if constexpr (DROP) {
@@ -527,25 +508,79 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
                         }
                         pk[i / 2] = pack2<BF16>(p0, p1);
                     }
-                    tmem_st16(s_tmem + P_OFF + c * 16, pk);
+                    tmem_st16(s_tmem + 32 * c, pk);
                 };
-                // P chunk c (keys 32c..32c+31) goes to columns 64+16c. Chunks 2, 3 come from the registers
-                // first (their P lands on columns already read), then columns 0..63 are read again.
-                emit(xa, 2);
-                emit(xb, 3);
-                tmem_ld32(s_tmem + 0, ra);
-                tmem_ld32(s_tmem + 32, rb);
-                tmem_ld_wait();
-                attn_mask(xa, kv0);
-                attn_mask(xb, kv0 + 32);
-                if (need_mask) { mask_chunk(xa, kv0, lim); mask_chunk(xb, kv0 + 32, lim); }
-                emit(xa, 0);
-                emit(xb, 1);
+                // keys 64h..64h+63 (chunks 2h, 2h+1 in xa, xb): one maximum, one decision, then both chunks
+                auto step = [&](float* xa, float* xb, int h) {
+                    attn_mask(xa, kv0 + 64 * h);
+                    attn_mask(xb, kv0 + 64 * h + 32);
+                    if (need_mask) {
+                        mask_chunk(xa, kv0 + 64 * h, lim);
+                        mask_chunk(xb, kv0 + 64 * h + 32, lim);
+                    }
+                    float pm[8];
+#pragma unroll
+                    for (int u = 0; u < 8; ++u) pm[u] = fmaxf(xa[u], xb[u]);
+#pragma unroll
+                    for (int i = 8; i < 32; ++i) pm[i & 7] = fmax3(pm[i & 7], xa[i], xb[i]);
+                    const float cm =
+                        fmax3(fmax3(pm[0], pm[1], pm[2]), fmax3(pm[3], pm[4], pm[5]), fmaxf(pm[6], pm[7])) * p.scale_log2;
+                    const float m_new = fmaxf(m_used, cm);
+                    const bool raise = m_new > m_used + 8.0f;  // false while the row has no finite score
+                    if (__any_sync(0xffffffffu, raise)) {
+                        const float alpha = raise ? ex2(m_used - m_new) : 1.0f;
+                        if (h > 0) {  // rescale the first half's probabilities, written as chunks 0 and 1
+                            tmem_st_wait();
+#pragma unroll
+                            for (int c2 = 0; c2 < 2; ++c2) {
+                                uint32_t w[16];
+                                tmem_ldx<16>(s_tmem + 32 * c2, w);
+                                tmem_ld_wait();
+#pragma unroll
+                                for (int i = 0; i < 16; ++i) w[i] = scale_pair<BF16>(w[i], alpha);
+                                tmem_st16(s_tmem + 32 * c2, w);
+                            }
+                        }
+                        if (raise) {
+                            const uint64_t al2 = f2_pack(alpha, alpha);
+                            ps2[0] = f2_mul(ps2[0], al2);
+                            ps2[1] = f2_mul(ps2[1], al2);
+                            m_used = m_new;
+                        }
+                    }
+                    emit(xa, 2 * h);
+                    emit(xb, 2 * h + 1);
+                };
+                {
+                    uint32_t ra[32], rb[32];
+                    tmem_ld32(s_tmem + 0, ra);
+                    tmem_ld32(s_tmem + 32, rb);
+                    tmem_ld_wait();
+                    step((float*)ra, (float*)rb, 0);
+                    tmem_ld32(s_tmem + 64, ra);
+                    tmem_ld32(s_tmem + 96, rb);
+                    tmem_ld_wait();
+                    step((float*)ra, (float*)rb, 1);
+                }
+                const bool grew = m_used != m_start;
+                if (__any_sync(0xffffffffu, grew && j > 0)) {
+                    // PV_t(j-1) is complete: it was issued before S_t(j), whose completion we have seen
+                    const float alpha = grew ? ex2(m_start - m_used) : 1.0f;
+#pragma unroll
+                    for (int c = 0; c < D / 32; ++c) {
+                        uint32_t ov[32];
+                        tmem_ld32(o_tmem + c * 32, ov);
+                        tmem_ld_wait();
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
+                        tmem_st32(o_tmem + c * 32, ov);
+                    }
+                }
                 {
                     float s0, s1, s2, s3;
                     f2_unpack(ps2[0], s0, s1);
                     f2_unpack(ps2[1], s2, s3);
-                    lsum += (s0 + s1) + (s2 + s3);
+                    lsum = (grew ? lsum * ex2(m_start - m_used) : lsum) + ((s0 + s1) + (s2 + s3));
                 }
                 tmem_st_wait();
                 tc_fence_before();

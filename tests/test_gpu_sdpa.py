@@ -12,7 +12,7 @@ import numpy as np
 import pytest
 
 from oracle import oracle as O
-from tests._util import assert_close, seeded, to_dev
+from tests._util import DT, assert_close, seeded, to_dev
 
 pytestmark = pytest.mark.gpu
 
@@ -88,6 +88,37 @@ def test_forward_matches_oracle(dtype, B, H, Hkv, L, S, D, Dv, causal, mask):
     assert _C.device_status() == 0
     atol, rtol = TOL[dtype]
     assert_close(got, want, atol, rtol, f"forward {dtype} {(B, H, Hkv, L, S, D)} causal={causal} mask={mask}")
+
+
+@pytest.mark.parametrize("dtype,causal", [("bf16", False), ("f16", False), ("bf16", True)])
+def test_forward_rescales_when_the_maximum_jumps_inside_a_block(dtype, causal):
+    """Scores that climb along the keys (q . k = A_l * 0.3 s in the first head dimension): rows with
+    A_l = 8 see their maximum grow by ~9.8 (log2 units) every 32 keys, so the forward raises its
+    exponent offset inside every key block and rescales the probabilities already written; rows with
+    A_l in {0, 2, -8} in the same warps never do. Output and lse against the oracle."""
+    import gguf_train_b200 as gtb
+    from gguf_train_b200 import functional as F
+    from gguf_train_b200 import _C
+
+    B, H, Hkv, L, S, D = 1, 2, 1, 256, 384, 128
+    O.manual_seed(4242)
+    q = O.randn(B, H, L, D) * 0.05
+    k = O.randn(B, Hkv, S, D) * 0.05
+    v = seeded((B, Hkv, S, D), dtype, 0.5)
+    amp = np.array([0.0, 2.0, 8.0, -8.0])[np.arange(L) % 4]
+    q[..., 0] = amp
+    k[..., 0] = 0.3 * np.arange(S)
+    q, k = O.round_to(q, DT[dtype]), O.round_to(k, DT[dtype])
+    want = O.sdpa_fwd(q, k, v, None, False, scale=0.0, is_causal=causal)
+    sc = np.einsum("bhld,bsd->bhls", q, k[:, 0]) / np.sqrt(D)
+    if causal:
+        sc = np.where(np.arange(S)[None, :] > np.arange(L)[:, None], -np.inf, sc)
+    mx = sc.max(-1, keepdims=True)
+    want_lse = (mx + np.log(np.exp(sc - mx).sum(-1, keepdims=True)))[..., 0]
+    out, lse = F.sdpa_forward(to_dev(q, dtype), to_dev(k, dtype), to_dev(v, dtype), None, None, causal)
+    assert _C.device_status() == 0
+    assert_close(out, want, 2e-2, 1e-2, f"forward {dtype} causal={causal} with climbing scores")
+    assert_close(lse, want_lse, 2e-3, 1e-4, "lse with climbing scores")
 
 
 BWD_CASES = [
