@@ -41,6 +41,7 @@ struct V4 {
 struct TiledP {
     V4 q, k, v, o, g, dq, dk, dv, m;
     int mask_dtype;  // -1: none
+    int vec;         // q, k, v, dO rows contiguous and 16-byte aligned: 16-byte row-major tile loads
     int64_t B, H, Hkv, L, S, group;
     float scale;
     int causal;
@@ -83,9 +84,19 @@ __device__ __forceinline__ void load_t(float* sm, const V4& t, int64_t b, int64_
         sm[d * (T + PAD) + r] = row < rows ? t.p[b * t.s0 + h * t.s1 + row * t.s2 + d * t.s3] : 0.0f;
     }
 }
-// The same tile row-major: sm[r][d] (row stride D + PAD)
+// The same tile row-major: sm[r][d] (row stride D + PAD); 16-byte loads and stores when the rows are
+// contiguous and 16-byte aligned (vec)
 template <int D>
-__device__ __forceinline__ void load_r(float* sm, const V4& t, int64_t b, int64_t h, int64_t r0, int64_t rows) {
+__device__ __forceinline__ void load_r(float* sm, const V4& t, int64_t b, int64_t h, int64_t r0, int64_t rows, bool vec) {
+    if (vec) {
+        for (int i = threadIdx.x; i < T * D / 4; i += NT) {
+            const int r = i / (D / 4), d = 4 * (i % (D / 4));
+            const int64_t row = r0 + r;
+            *(float4*)(sm + r * (D + PAD) + d) =
+                row < rows ? *(const float4*)(t.p + b * t.s0 + h * t.s1 + row * t.s2 + d) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        return;
+    }
     for (int i = threadIdx.x; i < T * D; i += NT) {
         const int r = i / D, d = i % D;
         const int64_t row = r0 + r;
@@ -155,7 +166,7 @@ __global__ void __launch_bounds__(NT, 2) fwd_f32_tiled_kernel(TiledP p) {
     for (int64_t s0 = 0; s0 < s_end; s0 += T) {
         __syncthreads();
         load_t<D>(Ks, p.k, b, hk, s0, p.S);
-        load_r<D>(Vs, p.v, b, hk, s0, p.S);
+        load_r<D>(Vs, p.v, b, hk, s0, p.S, p.vec);
         __syncthreads();
         float x[4][4] = {};
         block_dot<D>(x, Qs, Ks, ra, cb);
@@ -239,7 +250,7 @@ __global__ void __launch_bounds__(NT, 2) bwd_dq_f32_tiled_kernel(TiledP p) {
         __syncthreads();
         load_t<D>(Ks, p.k, b, hk, s0, p.S);
         load_t<D>(Vs, p.v, b, hk, s0, p.S);
-        load_r<D>(Kr, p.k, b, hk, s0, p.S);
+        load_r<D>(Kr, p.k, b, hk, s0, p.S, p.vec);
         __syncthreads();
         float x[4][4] = {}, dp[4][4] = {};
         block_dot<D>(x, Qs, Ks, ra, cb);
@@ -289,9 +300,12 @@ __global__ void __launch_bounds__(NT, 2) bwd_dkdv_f32_tiled_kernel(TiledP p) {
     float* Gs = Qs + D * (T + PAD);          // dO^T [D][T + PAD]
     float* Qr = Gs + D * (T + PAD);          // Q row-major [T][D + PAD]
     float* Gr = Qr + T * (D + PAD);          // dO row-major [T][D + PAD]
-    float* Ps = Gr + T * (D + PAD);          // P^T as [query][key + PAD] (for dV += P^T dO)
-    float* Ds = Ps + T * (T + PAD);          // dS^T as [query][key + PAD]
-    float* LD = Ds + T * (T + PAD);          // lse[T], delta[T] of the query tile
+    // P^T and dS^T as [query][key + PAD] (for dV += P^T dO, dK += dS^T Q) reuse the transposed Q and
+    // dO tiles, which are dead once S^T and dP^T are formed: 102.5 KB in all, two CTAs per SM
+    static_assert(D == T, "P^T / dS^T take the place of the transposed Q / dO tiles");
+    float* Ps = Qs;
+    float* Ds = Gs;
+    float* LD = Gr + T * (D + PAD);          // lse[T], delta[T] of the query tile
     const int tid = threadIdx.x, rg = tid / 16, cg = tid % 16;
     const int ra = 4 * rg, cb = 4 * cg;      // ra: this thread's keys, cb: queries (S^T) or dims (dK/dV)
     const int64_t b = blockIdx.z, hk = blockIdx.y, s0 = (int64_t)blockIdx.x * T;
@@ -310,8 +324,8 @@ __global__ void __launch_bounds__(NT, 2) bwd_dkdv_f32_tiled_kernel(TiledP p) {
             __syncthreads();
             load_t<D>(Qs, p.q, b, h, l0, p.L);
             load_t<D>(Gs, p.g, b, h, l0, p.L);
-            load_r<D>(Qr, p.q, b, h, l0, p.L);
-            load_r<D>(Gr, p.g, b, h, l0, p.L);
+            load_r<D>(Qr, p.q, b, h, l0, p.L, p.vec);
+            load_r<D>(Gr, p.g, b, h, l0, p.L, p.vec);
             for (int i = tid; i < T; i += NT) {
                 const int64_t l = l0 + i;
                 LD[i] = l < p.L ? p.lse[(b * p.H + h) * p.L + l] : -INFINITY;
@@ -343,6 +357,7 @@ __global__ void __launch_bounds__(NT, 2) bwd_dkdv_f32_tiled_kernel(TiledP p) {
                     dst[i][j] = pr * (d - LD[T + cb + j]);
                 }
             }
+            __syncthreads();  // every thread has read the transposed Q / dO tiles that P^T / dS^T replace
             // P^T, dS^T stored [query][key]: rows of the "A" operand of block_pv are queries
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
@@ -378,6 +393,14 @@ bool smem_attr(K kern, size_t bytes) {
 
 V4 v4(const gtb_tensor4& t) { return V4{(const float*)t.data, t.stride[0], t.stride[1], t.stride[2], t.stride[3]}; }
 
+// rows of 16-byte-aligned, contiguous floats: the tile loads may use 16-byte accesses
+bool rows16(const gtb_tensor4& t) {
+    if (((uintptr_t)t.data & 15) != 0 || t.stride[3] != 1) return false;
+    for (int i = 0; i < 3; ++i)
+        if (t.shape[i] > 1 && t.stride[i] % 4 != 0) return false;
+    return true;
+}
+
 template <int D>
 int fwd_d(const TiledP& p, cudaStream_t st) {
     const size_t smem = sizeof(float) * (3 * D * (T + PAD) + T * (D + PAD) + T * (T + PAD));
@@ -390,7 +413,7 @@ int fwd_d(const TiledP& p, cudaStream_t st) {
 template <int D>
 int bwd_d(const TiledP& p, cudaStream_t st) {
     const size_t s_dq = sizeof(float) * (4 * D * (T + PAD) + T * (D + PAD) + T * (T + PAD));
-    const size_t s_kv = sizeof(float) * (4 * D * (T + PAD) + 2 * T * (D + PAD) + 2 * T * (T + PAD) + 2 * T);
+    const size_t s_kv = sizeof(float) * (4 * D * (T + PAD) + 2 * T * (D + PAD) + 2 * T);
     if (!smem_attr(bwd_dq_f32_tiled_kernel<D>, s_dq) || !smem_attr(bwd_dkdv_f32_tiled_kernel<D>, s_kv)) return -1;
     if (p.L > 0) {
         bwd_dq_f32_tiled_kernel<D><<<dim3((unsigned)((p.L + T - 1) / T), (unsigned)p.H, (unsigned)p.B), NT, s_dq, st>>>(p);
@@ -410,6 +433,7 @@ TiledP common(const gtb_tensor4& q, const gtb_tensor4& k, const gtb_tensor4& v, 
     p.m = has_mask ? V4{(const float*)mask.data, mask.stride[0], mask.stride[1], mask.stride[2], mask.stride[3]}
                    : V4{nullptr, 0, 0, 0, 0};
     p.mask_dtype = has_mask ? mask.dtype : -1;
+    p.vec = rows16(q) && rows16(k) && rows16(v);
     p.B = sh.B; p.H = sh.H; p.Hkv = sh.Hkv; p.L = sh.L; p.S = sh.S; p.group = sh.H / sh.Hkv;
     p.scale = scale;
     p.causal = causal;
@@ -438,6 +462,7 @@ int launch_bwd_f32_tiled(const BwdArgs& a, const float* delta, cudaStream_t st) 
     TiledP p = common(a.q, a.k, a.v, a.has_mask, a.mask, a.sh, a.scale, a.causal, a.drop_p, a.drop_thr, a.drop_seed);
     p.o = v4(a.o);
     p.g = v4(a.dout);
+    p.vec = p.vec && rows16(a.dout);
     p.dq = v4(a.dq);
     p.dk = v4(a.dk);
     p.dv = v4(a.dv);
