@@ -75,9 +75,38 @@ __device__ __forceinline__ bool mask_score(const TiledP& p, int64_t b, int64_t h
 }
 
 // Load a 64 x D tile of a (B, heads, rows, D) tensor transposed into sm[d][r] (row stride T + PAD);
-// rows at or past `rows` read 0.
+// rows at or past `rows` read 0. With 16-byte rows (vec) a thread reads four consecutive d of one row
+// and consecutive threads take consecutive rows, so that a warp's four scalar stores per load each
+// cover 32 consecutive words of sm (no bank conflict); all of a thread's loads are issued first.
 template <int D>
-__device__ __forceinline__ void load_t(float* sm, const V4& t, int64_t b, int64_t h, int64_t r0, int64_t rows) {
+__device__ __forceinline__ void load_t(float* sm, const V4& t, int64_t b, int64_t h, int64_t r0, int64_t rows,
+                                       bool vec = false) {
+    if (vec) {
+        constexpr int PER = T * D / 4 / NT;  // float4 loads per thread
+        constexpr int G = 1;                 // loads in flight per thread
+#pragma unroll
+        for (int u0 = 0; u0 < PER; u0 += G) {
+            float4 v[G];
+#pragma unroll
+            for (int u = 0; u < G; ++u) {
+                const int i = threadIdx.x + (u0 + u) * NT;
+                const int r = i % T, d = 4 * (i / T);
+                const int64_t row = r0 + r;
+                v[u] = row < rows ? *(const float4*)(t.p + b * t.s0 + h * t.s1 + row * t.s2 + d)
+                                  : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int u = 0; u < G; ++u) {
+                const int i = threadIdx.x + (u0 + u) * NT;
+                const int r = i % T, d = 4 * (i / T);
+                sm[(d + 0) * (T + PAD) + r] = v[u].x;
+                sm[(d + 1) * (T + PAD) + r] = v[u].y;
+                sm[(d + 2) * (T + PAD) + r] = v[u].z;
+                sm[(d + 3) * (T + PAD) + r] = v[u].w;
+            }
+        }
+        return;
+    }
     for (int i = threadIdx.x; i < T * D; i += NT) {
         const int r = i / D, d = i % D;
         const int64_t row = r0 + r;
@@ -150,7 +179,7 @@ __global__ void __launch_bounds__(NT, 2) fwd_f32_tiled_kernel(TiledP p) {
     const int tid = threadIdx.x, rg = tid / 16, cg = tid % 16;
     const int ra = 4 * rg, cb = 4 * cg;
     const int64_t b = blockIdx.z, h = blockIdx.y, hk = h / p.group, l0 = (int64_t)blockIdx.x * T;
-    load_t<D>(Qs, p.q, b, h, l0, p.L);
+    load_t<D>(Qs, p.q, b, h, l0, p.L, p.vec);
     float m[4], lsum[4], o[4][D / 16];
     uint32_t rkey[4];
 #pragma unroll
@@ -165,7 +194,7 @@ __global__ void __launch_bounds__(NT, 2) fwd_f32_tiled_kernel(TiledP p) {
     if (p.causal) s_end = min(p.S, min(l0 + T, p.L));
     for (int64_t s0 = 0; s0 < s_end; s0 += T) {
         __syncthreads();
-        load_t<D>(Ks, p.k, b, hk, s0, p.S);
+        load_t<D>(Ks, p.k, b, hk, s0, p.S);  // scalar: keeps this loop within 128 registers
         load_r<D>(Vs, p.v, b, hk, s0, p.S, p.vec);
         __syncthreads();
         float x[4][4] = {};
@@ -231,8 +260,8 @@ __global__ void __launch_bounds__(NT, 2) bwd_dq_f32_tiled_kernel(TiledP p) {
     const int tid = threadIdx.x, rg = tid / 16, cg = tid % 16;
     const int ra = 4 * rg, cb = 4 * cg;
     const int64_t b = blockIdx.z, h = blockIdx.y, hk = h / p.group, l0 = (int64_t)blockIdx.x * T;
-    load_t<D>(Qs, p.q, b, h, l0, p.L);
-    load_t<D>(Gs, p.g, b, h, l0, p.L);
+    load_t<D>(Qs, p.q, b, h, l0, p.L, p.vec);
+    load_t<D>(Gs, p.g, b, h, l0, p.L, p.vec);
     float lse[4], dl[4], dq[4][D / 16];
     uint32_t rkey[4];
 #pragma unroll
@@ -248,7 +277,7 @@ __global__ void __launch_bounds__(NT, 2) bwd_dq_f32_tiled_kernel(TiledP p) {
     if (p.causal) s_end = min(p.S, min(l0 + T, p.L));
     for (int64_t s0 = 0; s0 < s_end; s0 += T) {
         __syncthreads();
-        load_t<D>(Ks, p.k, b, hk, s0, p.S);
+        load_t<D>(Ks, p.k, b, hk, s0, p.S);  // the scalar loads keep this loop within 128 registers
         load_t<D>(Vs, p.v, b, hk, s0, p.S);
         load_r<D>(Kr, p.k, b, hk, s0, p.S, p.vec);
         __syncthreads();
@@ -309,8 +338,8 @@ __global__ void __launch_bounds__(NT, 2) bwd_dkdv_f32_tiled_kernel(TiledP p) {
     const int tid = threadIdx.x, rg = tid / 16, cg = tid % 16;
     const int ra = 4 * rg, cb = 4 * cg;      // ra: this thread's keys, cb: queries (S^T) or dims (dK/dV)
     const int64_t b = blockIdx.z, hk = blockIdx.y, s0 = (int64_t)blockIdx.x * T;
-    load_t<D>(Ks, p.k, b, hk, s0, p.S);
-    load_t<D>(Vs, p.v, b, hk, s0, p.S);
+    load_t<D>(Ks, p.k, b, hk, s0, p.S, p.vec);
+    load_t<D>(Vs, p.v, b, hk, s0, p.S, p.vec);
     float dk[4][D / 16], dv[4][D / 16];
 #pragma unroll
     for (int i = 0; i < 4; ++i)
@@ -322,7 +351,7 @@ __global__ void __launch_bounds__(NT, 2) bwd_dkdv_f32_tiled_kernel(TiledP p) {
         const uint32_t hkey = p.drop ? drop_head_key(p.drop_seed, (uint32_t)(b * p.H + h)) : 0u;
         for (int64_t l0 = l_begin; l0 < p.L; l0 += T) {
             __syncthreads();
-            load_t<D>(Qs, p.q, b, h, l0, p.L);
+            load_t<D>(Qs, p.q, b, h, l0, p.L);  // the scalar loads keep this loop within 128 registers
             load_t<D>(Gs, p.g, b, h, l0, p.L);
             load_r<D>(Qr, p.q, b, h, l0, p.L, p.vec);
             load_r<D>(Gr, p.g, b, h, l0, p.L, p.vec);
