@@ -11,12 +11,12 @@
 //                warpgroup works on its S the tensor core runs the other tile's MMAs;
 //   warps 2-3    idle;
 //   warps 4-7    softmax + epilogue of tile 0, warps 8-11 of tile 1: one query row per thread (TMEM
-//                lane = row). One pass over S in TMEM, 32 keys at a time, exponentiating against the
-//                running maximum (online softmax in the log2 domain with lazy rescaling: the offset is
-//                raised only when a chunk's maximum exceeds it by more than 2^8, and then the block's
-//                earlier probabilities are rescaled; O and the running sum are rescaled once per block);
-//                P (bf16/f16) of each 32-key chunk is written over the first 16 of the chunk's S
-//                columns, where the PV MMA reads it as its A operand.
+//                lane = row). A whole 128-key block of S is read from TMEM into registers at once (the
+//                softmax warpgroups run with 200 registers a thread, taken from warpgroup 0 with
+//                setmaxnreg); online softmax in the log2 domain with lazy rescaling (the exponent
+//                offset is raised only when the block's maximum exceeds it by more than 2^8, and O and
+//                the running sum are rescaled then); P (bf16/f16) of each 32-key chunk is written over
+//                the first 16 of the chunk's S columns, where the PV MMA reads it as its A operand.
 // TMEM columns: S_0 [0,128), S_1 [128,256), O_0 [256,256+D), O_1 [384,384+D).
 //
 // Semantics are those of gt_flash_attention (reference csrc/gt_ops_nn.cpp:2423-2525): causal is
@@ -52,6 +52,8 @@ using namespace sm100;
 constexpr int BM = 128;          // rows per query tile
 constexpr int BN = 128;          // keys per K/V tile
 constexpr int NTHREADS = 384;
+constexpr int REG_LO = 104;      // registers per thread of warpgroup 0 (TMA, MMA) after the split
+constexpr int REG_HI = 200;      // ... of the softmax warpgroups
 constexpr uint32_t TMEM_COLS = 512;
 
 template <int D>
@@ -105,21 +107,6 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
     if constexpr (BF16) asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
     else asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
     return r;
-}
-
-// both 16-bit values of a packed pair times a (f32 product, rounded back to nearest even)
-template <bool BF16>
-__device__ __forceinline__ uint32_t scale_pair(uint32_t w, float a) {
-    float lo, hi;
-    if constexpr (BF16) {
-        lo = __uint_as_float(w << 16);
-        hi = __uint_as_float(w & 0xffff0000u);
-    } else {
-        const __half2 h = *reinterpret_cast<const __half2*>(&w);
-        lo = __low2float(h);
-        hi = __high2float(h);
-    }
-    return pack2<BF16>(lo * a, hi * a);
 }
 
 // max of three (one instruction on sm_100)
@@ -251,168 +238,178 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    // Registers: warpgroup 0 (TMA, MMA, two idle warps) hands registers to the two softmax warpgroups,
+    // which hold a whole 128-key block of scores. Every thread executes its warpgroup's setmaxnreg at
+    // the top of its role's branch below, converged (the instruction is .sync.aligned and
+    // warpgroup-wide; the compiler allocates the code a setmaxnreg dominates within its count):
+    // 128 x REG_LO + 256 x REG_HI stays within the 384 x 168 registers the block is launched with.
+    static_assert(128 * REG_LO + 256 * REG_HI <= NTHREADS * 168, "register split above the launch's registers");
 
-    if (warp == 0) {
-        // ------------------------------------------------------------ TMA producer
-        if (lane == 0) {
-            prefetch_tmap(&tmQ);
-            prefetch_tmap(&tmK);
-            prefetch_tmap(&tmV);
-            int J = 0, nitem = 0;  // K/V blocks and items started so far
-            int nk = 0, nv = 0, nql = 0;  // K, V and Q loads issued
-            bool ok = true;
-            // claims run one item ahead (the atomic's latency is hidden); one item per CTA otherwise
-            int next = PERSIST ? atomicAdd(p.claim, 1) : (int)blockIdx.x;
-            for (;; ++nitem) {
-                const int i = next;
-                if constexpr (PERSIST) {
-                    const int slot = nitem & 1;
-                    if (nitem >= 2) ok = mbar_wait(&item_empty[slot], ((nitem >> 1) - 1) & 1, p.status, 14);
-                    if (!ok || *(volatile int*)abort_flag) { ok = false; break; }
-                    item_slot[slot] = i < p.n_items ? i : -1;
-                    mbar_arrive(&item_full[slot]);
-                }
-                if (i >= p.n_items) break;
-                next = PERSIST ? atomicAdd(p.claim, 1) : p.n_items;
-                const Item it = item_of(i);
-                const int nq = it.nblk[1] > 0 ? 2 : 1;
-                auto load_q = [&]() {
-                    mbar_expect_tx(q_full, nq * C::TILE);
-                    for (int t = 0; t < nq; ++t)
-                        for (int a = 0; a < C::ATOMS; ++a)
-                            tma_load_4d(smem + C::OFF_Q + t * C::TILE + a * C::ATOM_BYTES, &tmQ, a * 64, it.row0[t], it.h,
-                                        it.b, q_full);
-                    ++nql;
-                };
-                if (nitem == 0) load_q();  // the CTA's first item: nothing to wait for, Q first
-                for (int j = 0; j < it.n && ok; ++j, ++J) {
-                    const int ks = J % C::KS;
-                    if (J >= C::KS) ok = mbar_wait(&k_empty[ks], ((J / C::KS) - 1) & 1, p.status, 11);
-                    if (!ok || *(volatile int*)abort_flag) { ok = false; break; }
-                    mbar_expect_tx(&k_full[ks], C::TILE);
-                    for (int a = 0; a < C::ATOMS; ++a)
-                        tma_load_4d(smem + C::OFF_K + ks * C::TILE + a * C::ATOM_BYTES, &tmK, a * 64, j * BN, it.hk, it.b,
-                                    &k_full[ks]);
-                    ++nk;
-                    const int vs = J % C::VS;
-                    if (J >= C::VS) ok = mbar_wait(&v_empty[vs], ((J / C::VS) - 1) & 1, p.status, 12);
-                    if (!ok || *(volatile int*)abort_flag) { ok = false; break; }
-                    mbar_expect_tx(&v_full[vs], C::TILE);
-                    for (int a = 0; a < C::ATOMS; ++a)
-                        tma_load_4d(smem + C::OFF_V + vs * C::TILE + a * C::ATOM_BYTES, &tmV, a * 64, j * BN, it.hk, it.b,
-                                    &v_full[vs]);
-                    ++nv;
-                    if (j == 0 && nitem > 0) {
-                        // Q of a later item, once the previous item's S MMAs have read theirs (after this
-                        // item's first K/V block, whose slots may free up earlier)
-                        ok = mbar_wait(q_empty, (nitem - 1) & 1, p.status, 13);
+    if (warp < 4) {
+        setmaxnreg_dec<REG_LO>();
+        if (warp == 0) {
+            // ------------------------------------------------------------ TMA producer
+            if (lane == 0) {
+                prefetch_tmap(&tmQ);
+                prefetch_tmap(&tmK);
+                prefetch_tmap(&tmV);
+                int J = 0, nitem = 0;  // K/V blocks and items started so far
+                int nk = 0, nv = 0, nql = 0;  // K, V and Q loads issued
+                bool ok = true;
+                // claims run one item ahead (the atomic's latency is hidden); one item per CTA otherwise
+                int next = PERSIST ? atomicAdd(p.claim, 1) : (int)blockIdx.x;
+                for (;; ++nitem) {
+                    const int i = next;
+                    if constexpr (PERSIST) {
+                        const int slot = nitem & 1;
+                        if (nitem >= 2) ok = mbar_wait(&item_empty[slot], ((nitem >> 1) - 1) & 1, p.status, 14);
                         if (!ok || *(volatile int*)abort_flag) { ok = false; break; }
-                        load_q();
+                        item_slot[slot] = i < p.n_items ? i : -1;
+                        mbar_arrive(&item_full[slot]);
+                    }
+                    if (i >= p.n_items) break;
+                    next = PERSIST ? atomicAdd(p.claim, 1) : p.n_items;
+                    const Item it = item_of(i);
+                    const int nq = it.nblk[1] > 0 ? 2 : 1;
+                    auto load_q = [&]() {
+                        mbar_expect_tx(q_full, nq * C::TILE);
+                        for (int t = 0; t < nq; ++t)
+                            for (int a = 0; a < C::ATOMS; ++a)
+                                tma_load_4d(smem + C::OFF_Q + t * C::TILE + a * C::ATOM_BYTES, &tmQ, a * 64, it.row0[t], it.h,
+                                            it.b, q_full);
+                        ++nql;
+                    };
+                    if (nitem == 0) load_q();  // the CTA's first item: nothing to wait for, Q first
+                    for (int j = 0; j < it.n && ok; ++j, ++J) {
+                        const int ks = J % C::KS;
+                        if (J >= C::KS) ok = mbar_wait(&k_empty[ks], ((J / C::KS) - 1) & 1, p.status, 11);
+                        if (!ok || *(volatile int*)abort_flag) { ok = false; break; }
+                        mbar_expect_tx(&k_full[ks], C::TILE);
+                        for (int a = 0; a < C::ATOMS; ++a)
+                            tma_load_4d(smem + C::OFF_K + ks * C::TILE + a * C::ATOM_BYTES, &tmK, a * 64, j * BN, it.hk, it.b,
+                                        &k_full[ks]);
+                        ++nk;
+                        const int vs = J % C::VS;
+                        if (J >= C::VS) ok = mbar_wait(&v_empty[vs], ((J / C::VS) - 1) & 1, p.status, 12);
+                        if (!ok || *(volatile int*)abort_flag) { ok = false; break; }
+                        mbar_expect_tx(&v_full[vs], C::TILE);
+                        for (int a = 0; a < C::ATOMS; ++a)
+                            tma_load_4d(smem + C::OFF_V + vs * C::TILE + a * C::ATOM_BYTES, &tmV, a * 64, j * BN, it.hk, it.b,
+                                        &v_full[vs]);
+                        ++nv;
+                        if (j == 0 && nitem > 0) {
+                            // Q of a later item, once the previous item's S MMAs have read theirs (after this
+                            // item's first K/V block, whose slots may free up earlier)
+                            ok = mbar_wait(q_empty, (nitem - 1) & 1, p.status, 13);
+                            if (!ok || *(volatile int*)abort_flag) { ok = false; break; }
+                            load_q();
+                        }
                     }
                 }
-            }
-            if (!ok) *(volatile int*)abort_flag = 1;
-            if (*(volatile int*)abort_flag) {
-                // drain our own copies before the CTA exits (bounded): the last Q and the last K/V blocks
-                if (nql > 0) mbar_wait(q_full, (nql - 1) & 1, nullptr, 0);
-                for (int jj = max(0, nk - C::KS); jj < nk; ++jj) mbar_wait(&k_full[jj % C::KS], (jj / C::KS) & 1, nullptr, 0);
-                for (int jj = max(0, nv - C::VS); jj < nv; ++jj) mbar_wait(&v_full[jj % C::VS], (jj / C::VS) & 1, nullptr, 0);
-            }
-        }
-    } else if (warp == 1) {
-        // ------------------------------------------------------------ MMA issuer
-        if (lane == 0) {
-            constexpr uint32_t IDESC_S = idesc_f16(BM, BN, BF16, false);
-            constexpr uint32_t IDESC_PV = idesc_f16(BM, D, BF16, true);
-            // operand descriptors of every buffer, built once: per MMA only a constant is added to the
-            // start address
-            static_assert(C::KS == 2 && C::VS == 2, "descriptor selection below assumes two K and two V stages");
-            const uint64_t qd0 = desc_sw128(smem_u32(smem + C::OFF_Q), 16, 1024);
-            const uint64_t qd1 = desc_sw128(smem_u32(smem + C::OFF_Q + C::TILE), 16, 1024);
-            const uint64_t kd0 = desc_sw128(smem_u32(smem + C::OFF_K), 16, 1024);
-            const uint64_t kd1 = desc_sw128(smem_u32(smem + C::OFF_K + C::TILE), 16, 1024);
-            const uint64_t vd0 = desc_sw128(smem_u32(smem + C::OFF_V), C::ATOM_BYTES, 1024);
-            const uint64_t vd1 = desc_sw128(smem_u32(smem + C::OFF_V + C::TILE), C::ATOM_BYTES, 1024);
-            // J: K/V block of the ring (over all items); u[t]: blocks of tile t so far (s_full / p_full
-            // phases); nf[t]: items with a tile t so far (o_final / o_empty phases)
-            int J = 0, u[2] = {0, 0}, nf[2] = {0, 0}, nitem = 0;
-            auto issue_s = [&](int t, int jg) -> bool {  // S_t of ring block jg
-                const int ks = jg % C::KS;
-                if (!mbar_wait(&k_full[ks], (jg / C::KS) & 1, p.status, 22)) return false;
-                tc_fence_after();
-                const uint64_t qb = t ? qd1 : qd0, kb = ks ? kd1 : kd0;
-                const uint32_t dst = tmem + s_col(t);
-#pragma unroll
-                for (int kk = 0; kk < D / 16; ++kk) {
-                    const uint32_t off = (uint32_t)((kk / 4) * C::ATOM_BYTES + (kk % 4) * 32);
-                    mma_ss(dst, desc_advance(qb, off), desc_advance(kb, off), IDESC_S, kk > 0 ? 1u : 0u);
+                if (!ok) *(volatile int*)abort_flag = 1;
+                if (*(volatile int*)abort_flag) {
+                    // drain our own copies before the CTA exits (bounded): the last Q and the last K/V blocks
+                    if (nql > 0) mbar_wait(q_full, (nql - 1) & 1, nullptr, 0);
+                    for (int jj = max(0, nk - C::KS); jj < nk; ++jj) mbar_wait(&k_full[jj % C::KS], (jj / C::KS) & 1, nullptr, 0);
+                    for (int jj = max(0, nv - C::VS); jj < nv; ++jj) mbar_wait(&v_full[jj % C::VS], (jj / C::VS) & 1, nullptr, 0);
                 }
-                mma_commit(&s_full[t]);
-                return true;
-            };
-            auto issue_pv = [&](int t, int jg, int ut, bool first) -> bool {  // PV_t of ring block jg
-                if (!mbar_wait(&p_full[t], ut & 1, p.status, 23)) return false;
-                const int vs = jg % C::VS;
-                if (!mbar_wait(&v_full[vs], (jg / C::VS) & 1, p.status, 24)) return false;
-                tc_fence_after();
-                const uint64_t vb = vs ? vd1 : vd0;
-                const uint32_t dst = tmem + o_col(t), pa = tmem + s_col(t);
-#pragma unroll
-                for (int kk = 0; kk < BN / 16; ++kk) {
-                    // A = P_t(j): 16-bit values packed two per TMEM column; keys 32c..32c+31 sit in
-                    // columns 32c..32c+15, 8 columns per K step
-                    mma_ts(dst, pa + 32 * (kk >> 1) + 8 * (kk & 1), desc_advance(vb, kk * 2048), IDESC_PV,
-                           (!first || kk > 0) ? 1u : 0u);
-                }
-                return true;
-            };
-            bool ok = true;
-            for (;; ++nitem) {
-                int i;
-                if constexpr (PERSIST) {
-                    const int slot = nitem & 1;
-                    ok = mbar_wait(&item_full[slot], (nitem >> 1) & 1, p.status, 27);
+            }
+        } else if (warp == 1) {
+            // ------------------------------------------------------------ MMA issuer
+            if (lane == 0) {
+                constexpr uint32_t IDESC_S = idesc_f16(BM, BN, BF16, false);
+                constexpr uint32_t IDESC_PV = idesc_f16(BM, D, BF16, true);
+                // operand descriptors of every buffer, built once: per MMA only a constant is added to the
+                // start address
+                static_assert(C::KS == 2 && C::VS == 2, "descriptor selection below assumes two K and two V stages");
+                const uint64_t qd0 = desc_sw128(smem_u32(smem + C::OFF_Q), 16, 1024);
+                const uint64_t qd1 = desc_sw128(smem_u32(smem + C::OFF_Q + C::TILE), 16, 1024);
+                const uint64_t kd0 = desc_sw128(smem_u32(smem + C::OFF_K), 16, 1024);
+                const uint64_t kd1 = desc_sw128(smem_u32(smem + C::OFF_K + C::TILE), 16, 1024);
+                const uint64_t vd0 = desc_sw128(smem_u32(smem + C::OFF_V), C::ATOM_BYTES, 1024);
+                const uint64_t vd1 = desc_sw128(smem_u32(smem + C::OFF_V + C::TILE), C::ATOM_BYTES, 1024);
+                // J: K/V block of the ring (over all items); u[t]: blocks of tile t so far (s_full / p_full
+                // phases); nf[t]: items with a tile t so far (o_final / o_empty phases)
+                int J = 0, u[2] = {0, 0}, nf[2] = {0, 0}, nitem = 0;
+                auto issue_s = [&](int t, int jg) -> bool {  // S_t of ring block jg
+                    const int ks = jg % C::KS;
+                    if (!mbar_wait(&k_full[ks], (jg / C::KS) & 1, p.status, 22)) return false;
+                    tc_fence_after();
+                    const uint64_t qb = t ? qd1 : qd0, kb = ks ? kd1 : kd0;
+                    const uint32_t dst = tmem + s_col(t);
+    #pragma unroll
+                    for (int kk = 0; kk < D / 16; ++kk) {
+                        const uint32_t off = (uint32_t)((kk / 4) * C::ATOM_BYTES + (kk % 4) * 32);
+                        mma_ss(dst, desc_advance(qb, off), desc_advance(kb, off), IDESC_S, kk > 0 ? 1u : 0u);
+                    }
+                    mma_commit(&s_full[t]);
+                    return true;
+                };
+                auto issue_pv = [&](int t, int jg, int ut, bool first) -> bool {  // PV_t of ring block jg
+                    if (!mbar_wait(&p_full[t], ut & 1, p.status, 23)) return false;
+                    const int vs = jg % C::VS;
+                    if (!mbar_wait(&v_full[vs], (jg / C::VS) & 1, p.status, 24)) return false;
+                    tc_fence_after();
+                    const uint64_t vb = vs ? vd1 : vd0;
+                    const uint32_t dst = tmem + o_col(t), pa = tmem + s_col(t);
+    #pragma unroll
+                    for (int kk = 0; kk < BN / 16; ++kk) {
+                        // A = P_t(j): 16-bit values packed two per TMEM column; keys 32c..32c+31 sit in
+                        // columns 32c..32c+15, 8 columns per K step
+                        mma_ts(dst, pa + 32 * (kk >> 1) + 8 * (kk & 1), desc_advance(vb, kk * 2048), IDESC_PV,
+                               (!first || kk > 0) ? 1u : 0u);
+                    }
+                    return true;
+                };
+                bool ok = true;
+                for (;; ++nitem) {
+                    int i;
+                    if constexpr (PERSIST) {
+                        const int slot = nitem & 1;
+                        ok = mbar_wait(&item_full[slot], (nitem >> 1) & 1, p.status, 27);
+                        if (!ok) break;
+                        i = item_slot[slot];
+                        mbar_arrive(&item_empty[slot]);
+                    } else {
+                        i = nitem == 0 ? (int)blockIdx.x : -1;
+                    }
+                    if (i < 0) break;
+                    const Item it = item_of(i);
+                    ok = mbar_wait(q_full, nitem & 1, p.status, 21);
+                    for (int t = 0; t < 2 && ok; ++t)
+                        if (it.nblk[t] > 0) ok = issue_s(t, J);
                     if (!ok) break;
-                    i = item_slot[slot];
-                    mbar_arrive(&item_empty[slot]);
-                } else {
-                    i = nitem == 0 ? (int)blockIdx.x : -1;
-                }
-                if (i < 0) break;
-                const Item it = item_of(i);
-                ok = mbar_wait(q_full, nitem & 1, p.status, 21);
-                for (int t = 0; t < 2 && ok; ++t)
-                    if (it.nblk[t] > 0) ok = issue_s(t, J);
-                if (!ok) break;
-                mma_commit(&k_empty[J % C::KS]);
-                if (it.n == 1) mma_commit(q_empty);  // every S of the item issued
-                for (int j = 0; j < it.n && ok; ++j) {
-                    for (int t = 0; t < 2 && ok; ++t) {
-                        if (j >= it.nblk[t]) continue;
-                        // the first PV of an item overwrites O_t: the previous item's epilogue must have read it
-                        if (j == 0 && nf[t] > 0) ok = mbar_wait(&o_empty[t], (nf[t] - 1) & 1, p.status, 26);
-                        if (ok) ok = issue_pv(t, J + j, u[t] + j, j == 0);
-                        if (ok && j + 1 < it.nblk[t]) ok = issue_s(t, J + j + 1);
-                        if (ok && j + 1 == it.nblk[t]) mma_commit(&o_final[t]);
+                    mma_commit(&k_empty[J % C::KS]);
+                    if (it.n == 1) mma_commit(q_empty);  // every S of the item issued
+                    for (int j = 0; j < it.n && ok; ++j) {
+                        for (int t = 0; t < 2 && ok; ++t) {
+                            if (j >= it.nblk[t]) continue;
+                            // the first PV of an item overwrites O_t: the previous item's epilogue must have read it
+                            if (j == 0 && nf[t] > 0) ok = mbar_wait(&o_empty[t], (nf[t] - 1) & 1, p.status, 26);
+                            if (ok) ok = issue_pv(t, J + j, u[t] + j, j == 0);
+                            if (ok && j + 1 < it.nblk[t]) ok = issue_s(t, J + j + 1);
+                            if (ok && j + 1 == it.nblk[t]) mma_commit(&o_final[t]);
+                        }
+                        if (!ok || *(volatile int*)abort_flag) { ok = false; break; }
+                        mma_commit(&v_empty[(J + j) % C::VS]);
+                        if (j + 1 < it.n) mma_commit(&k_empty[(J + j + 1) % C::KS]);
+                        if (j + 2 == it.n) mma_commit(q_empty);  // the item's last S MMAs were issued at this j
                     }
-                    if (!ok || *(volatile int*)abort_flag) { ok = false; break; }
-                    mma_commit(&v_empty[(J + j) % C::VS]);
-                    if (j + 1 < it.n) mma_commit(&k_empty[(J + j + 1) % C::KS]);
-                    if (j + 2 == it.n) mma_commit(q_empty);  // the item's last S MMAs were issued at this j
+                    J += it.n;
+                    for (int t = 0; t < 2; ++t) {
+                        u[t] += it.nblk[t];
+                        nf[t] += it.nblk[t] > 0 ? 1 : 0;
+                    }
                 }
-                J += it.n;
-                for (int t = 0; t < 2; ++t) {
-                    u[t] += it.nblk[t];
-                    nf[t] += it.nblk[t] > 0 ? 1 : 0;
+                if (!ok) *(volatile int*)abort_flag = 1;
+                if (*(volatile int*)abort_flag) {
+                    mma_commit(drain);  // wait (bounded) for every MMA we issued before TMEM is freed
+                    mbar_wait(drain, 0, nullptr, 0);
                 }
-            }
-            if (!ok) *(volatile int*)abort_flag = 1;
-            if (*(volatile int*)abort_flag) {
-                mma_commit(drain);  // wait (bounded) for every MMA we issued before TMEM is freed
-                mbar_wait(drain, 0, nullptr, 0);
             }
         }
-    } else if (warp >= 4) {
+    } else {
+        setmaxnreg_inc<REG_HI>();
         // ------------------------------------------------------------ softmax + epilogue of tile t
         const int t = (warp - 4) >> 2;
         const int quad = warp & 3;                    // TMEM lanes this warp may access
@@ -468,13 +465,11 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
                         }
                     }
                 };
-                // One pass over S, 32 columns (keys) at a time, with the running maximum m_used as the
-                // exponent's offset: a chunk whose maximum exceeds m_used by more than 2^8 first raises
-                // m_used for its rows and rescales the probabilities this block already wrote and their
-                // partial sum (rare once a row has seen a few keys); O and the running sum are rescaled
-                // once at the end of the block. P of chunk c (keys 32c..32c+31) is written over S's
-                // columns 32c..32c+15, which the chunk has just read, as packed 16-bit pairs (the PV
-                // MMA's A operand). The scale-and-subtract and the sums run as packed two-lane f32.
+                // The block's scores in registers, the running maximum m_used as the exponent's offset
+                // (raised when the block's maximum exceeds it by more than 2^8; O and the running sum
+                // are rescaled at the end of the block when it moved). P of chunk c (keys 32c..32c+31)
+                // is written over S's columns 32c..32c+15, already read, as packed 16-bit pairs (the
+                // PV MMA's A operand). The scale-and-subtract and the sums run as packed two-lane f32.
                 const float m_start = m_used;
                 const uint64_t sc2 = f2_pack(p.scale_log2, p.scale_log2);
                 uint64_t ps2[2] = {0ull, 0ull};
@@ -510,57 +505,48 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
                     }
                     tmem_st16(s_tmem + 32 * c, pk);
                 };
-                // keys 64h..64h+63 (chunks 2h, 2h+1 in xa, xb): one maximum, one decision, then both chunks
-                auto step = [&](float* xa, float* xb, int h) {
-                    attn_mask(xa, kv0 + 64 * h);
-                    attn_mask(xb, kv0 + 64 * h + 32);
+                {
+                    // the block's 128 scores in registers: one maximum, one decision per row (nothing of
+                    // this block is written before it), then the four chunks' probabilities
+                    uint32_t ra[32], rb[32], rc[32], rd[32];
+                    tmem_ld32(s_tmem + 0, ra);
+                    tmem_ld32(s_tmem + 32, rb);
+                    tmem_ld32(s_tmem + 64, rc);
+                    tmem_ld32(s_tmem + 96, rd);
+                    tmem_ld_wait();
+                    float* xa = (float*)ra;
+                    float* xb = (float*)rb;
+                    float* xc = (float*)rc;
+                    float* xd = (float*)rd;
+                    attn_mask(xa, kv0);
+                    attn_mask(xb, kv0 + 32);
+                    attn_mask(xc, kv0 + 64);
+                    attn_mask(xd, kv0 + 96);
                     if (need_mask) {
-                        mask_chunk(xa, kv0 + 64 * h, lim);
-                        mask_chunk(xb, kv0 + 64 * h + 32, lim);
+                        mask_chunk(xa, kv0, lim);
+                        mask_chunk(xb, kv0 + 32, lim);
+                        mask_chunk(xc, kv0 + 64, lim);
+                        mask_chunk(xd, kv0 + 96, lim);
                     }
                     float pm[8];
 #pragma unroll
-                    for (int u = 0; u < 8; ++u) pm[u] = fmaxf(xa[u], xb[u]);
+                    for (int u = 0; u < 8; ++u) pm[u] = fmax3(xa[u], xb[u], xc[u]);
 #pragma unroll
-                    for (int i = 8; i < 32; ++i) pm[i & 7] = fmax3(pm[i & 7], xa[i], xb[i]);
+                    for (int u = 0; u < 8; ++u) pm[u] = fmax3(pm[u], xd[u], xa[u + 8]);
+#pragma unroll
+                    for (int i = 8; i < 32; ++i) pm[i & 7] = fmax3(pm[i & 7], xb[i], xc[i]);
+#pragma unroll
+                    for (int i = 8; i < 32; ++i) pm[i & 7] = fmaxf(pm[i & 7], xd[i]);
+#pragma unroll
+                    for (int i = 16; i < 32; i += 2) pm[i & 7] = fmax3(pm[i & 7], xa[i], xa[i + 1]);
                     const float cm =
                         fmax3(fmax3(pm[0], pm[1], pm[2]), fmax3(pm[3], pm[4], pm[5]), fmaxf(pm[6], pm[7])) * p.scale_log2;
                     const float m_new = fmaxf(m_used, cm);
-                    const bool raise = m_new > m_used + 8.0f;  // false while the row has no finite score
-                    if (__any_sync(0xffffffffu, raise)) {
-                        const float alpha = raise ? ex2(m_used - m_new) : 1.0f;
-                        if (h > 0) {  // rescale the first half's probabilities, written as chunks 0 and 1
-                            tmem_st_wait();
-#pragma unroll
-                            for (int c2 = 0; c2 < 2; ++c2) {
-                                uint32_t w[16];
-                                tmem_ldx<16>(s_tmem + 32 * c2, w);
-                                tmem_ld_wait();
-#pragma unroll
-                                for (int i = 0; i < 16; ++i) w[i] = scale_pair<BF16>(w[i], alpha);
-                                tmem_st16(s_tmem + 32 * c2, w);
-                            }
-                        }
-                        if (raise) {
-                            const uint64_t al2 = f2_pack(alpha, alpha);
-                            ps2[0] = f2_mul(ps2[0], al2);
-                            ps2[1] = f2_mul(ps2[1], al2);
-                            m_used = m_new;
-                        }
-                    }
-                    emit(xa, 2 * h);
-                    emit(xb, 2 * h + 1);
-                };
-                {
-                    uint32_t ra[32], rb[32];
-                    tmem_ld32(s_tmem + 0, ra);
-                    tmem_ld32(s_tmem + 32, rb);
-                    tmem_ld_wait();
-                    step((float*)ra, (float*)rb, 0);
-                    tmem_ld32(s_tmem + 64, ra);
-                    tmem_ld32(s_tmem + 96, rb);
-                    tmem_ld_wait();
-                    step((float*)ra, (float*)rb, 1);
+                    if (m_new > m_used + 8.0f) m_used = m_new;  // false while the row has no finite score
+                    emit(xa, 0);
+                    emit(xb, 1);
+                    emit(xc, 2);
+                    emit(xd, 3);
                 }
                 const bool grew = m_used != m_start;
                 if (__any_sync(0xffffffffu, grew && j > 0)) {
