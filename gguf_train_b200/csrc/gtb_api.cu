@@ -419,7 +419,7 @@ GTB_API int gtb_sdpa_fwd_ex(const gtb_tensor4* q, const gtb_tensor4* k, const gt
         g_last_path = "tcgen05";
         return launch_fwd_sm100(a, st);
     }
-    g_last_path = "simt";
+    g_last_path = f32_tiled_supported(a.sh, a.q.dtype) ? "f32_tiled" : "simt";
     return launch_fwd_simt(a, st);
 }
 
@@ -676,7 +676,7 @@ GTB_API int gtb_sdpa_bwd_ex(const gtb_tensor4* dout, const gtb_tensor4* q, const
     // GTB_BWD_SIMT=1 forces the SIMT kernels (used to cross-check the two implementations)
     static const int force_simt = env_int("GTB_BWD_SIMT", 0);
     const bool fast = !force_simt && bwd_sm100_supported(a);
-    g_last_path = fast ? "tcgen05" : "simt";
+    g_last_path = fast ? "tcgen05" : f32_tiled_supported(a.sh, a.q.dtype) ? "f32_tiled" : "simt";
     const size_t bytes = fast ? bwd_sm100_scratch_bytes(a) : bwd_simt_scratch_bytes(a);
     int dev = 0;
     cudaGetDevice(&dev);

@@ -219,7 +219,8 @@ GTB_API int gtb_attn_merge(float *o_acc, float *lse_acc, const void *o_part, con
                            int64_t lse_gstride, void *stream);
 
 /* Kernel family of the calling thread's last gtb_sdpa_fwd / gtb_sdpa_bwd call: "tcgen05" (tensor
- * cores, TMA) or "simt" ("" before the first). Lets a caller or a test see which path a call took. */
+ * cores, TMA), "f32_tiled" (fp32 with head size 64, register-blocked on the CUDA cores) or "simt"
+ * (one warp per row; "" before the first). Lets a caller or a test see which path a call took. */
 GTB_API const char *gtb_last_path(void);
 
 /* Thread-local message of the last failure ("" if none). */
