@@ -419,3 +419,21 @@ def test_sdpa_from_host_matches_the_device_call(dtype, B, H, Hkv, L, S, D, causa
     torch.cuda.current_stream().synchronize()
     assert got.device.type == "cpu" and got.is_pinned()
     assert torch.equal(got, want.cpu())
+
+
+def test_path_reports_the_kernel_family():
+    """gtb_last_path names the kernels a call took: tcgen05 for 16-bit head size 128, the
+    register-blocked fp32 kernels for fp32 head size 64, the one-warp-per-row kernels otherwise."""
+    import torch
+
+    import gguf_train_b200 as gtb
+    from gguf_train_b200 import _C
+
+    for dtype, D, want in ((torch.bfloat16, 128, "tcgen05"), (torch.float32, 64, "f32_tiled"),
+                           (torch.float32, 32, "simt")):
+        q, k, v = (torch.randn(1, 2, 70, D, device="cuda", dtype=dtype, requires_grad=True) for _ in range(3))
+        out = gtb.scaled_dot_product_attention(q, k, v, is_causal=True)
+        assert _C.last_path() == want, (dtype, D, _C.last_path())
+        out.sum().backward()
+        assert _C.last_path() == want, (dtype, D, "backward", _C.last_path())
+    assert _C.device_status() == 0
