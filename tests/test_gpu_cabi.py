@@ -103,3 +103,52 @@ def test_handle_rope_matches_oracle():
     assert _C.device_status() == 0
     assert_close(got, O.rope(x, pos.astype(np.int64), 64, 2), 2e-5, 1e-5, "gt_rope")
     assert_close(back, O.rope(x, pos.astype(np.int64), 64, 2, backward=True), 2e-5, 1e-5, "gt_rope_backward")
+
+
+def test_reference_shaped_function_over_handles():
+    """FlashAttentionFn as the reference's autograd engine runs it (gguf_train/_functions.py:1922-1965:
+    forward(ctx, q, k, v, mask, scale, is_causal), backward(ctx, grad_out) -> six gradients), rewired to
+    the engine as INTEGRATION.md shows: the forward saves the output and the log-sum-exp, the backward
+    is one native call. Everything crosses the handle ABI (gt_tensor *), no torch tensor is involved;
+    a bool (B, 1, L, S) key-padding mask, GQA and a causal mask, bf16."""
+    import math
+
+    from gguf_train_b200 import _C
+    from gguf_train_b200 import handles as H
+
+    class Context:  # what of the reference's Context the Function uses
+        def save_for_backward(self, *tensors):
+            self.saved_tensors = tensors
+
+    class FlashAttentionFn:
+        @staticmethod
+        def forward(ctx, q, k, v, mask, scale, is_causal):
+            ctx.scale = float(scale) if scale is not None else 1.0 / math.sqrt(q.shape[-1])
+            ctx.is_causal = bool(is_causal)
+            out, lse = H.flash_attention_fwd_lse(q, k, v, mask, ctx.scale, ctx.is_causal)
+            ctx.save_for_backward(q, k, v, mask, out, lse)
+            return out
+
+        @staticmethod
+        def backward(ctx, grad_out):
+            q, k, v, mask, out, lse = ctx.saved_tensors
+            dq, dk, dv = H.flash_attention_backward(grad_out, q, k, v, mask, out, lse, ctx.scale, ctx.is_causal)
+            return dq, dk, dv, None, None, None
+
+    O.manual_seed(23)
+    B, Hq, Hkv, L, D = 2, 4, 2, 200, 128
+    q, k, v = (seeded(s, "bf16", 0.5) for s in ((B, Hq, L, D), (B, Hkv, L, D), (B, Hkv, L, D)))
+    g = seeded((B, Hq, L, D), "bf16")
+    keep = np.ones((B, 1, 1, L), dtype=bool)
+    keep[0, ..., 170:] = False  # the last 30 keys of sequence 0 are padding
+    mh = H.Handle.from_numpy(keep.astype(np.uint8), _C.GT_BOOL)
+    ctx = Context()
+    out = FlashAttentionFn.forward(ctx, _h(q, "bf16"), _h(k, "bf16"), _h(v, "bf16"), mh, None, True)
+    grads = FlashAttentionFn.backward(ctx, _h(g, "bf16"))
+    assert grads[3:] == (None, None, None)
+    m = np.broadcast_to(keep, (B, 1, L, L)).astype(np.float64)
+    assert_close(_back(out, "bf16"), O.sdpa_fwd(q, k, v, m, True, is_causal=True), 2e-2, 1e-2, "forward")
+    want = O.sdpa_bwd(q, k, v, g, m, True, is_causal=True)
+    for name, got, w in zip(("dq", "dk", "dv"), grads[:3], want):
+        assert_close(_back(got, "bf16"), w, 2e-2, 1e-2, name)
+    assert _C.device_status() == 0
