@@ -688,6 +688,17 @@ int run(const FwdArgs& a, const CUtensorMap& mq, const CUtensorMap& mk, const CU
             cuda_failed(cudaFuncSetAttribute(kern_1, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM),
                         "cudaFuncSetAttribute(fwd_sm100)"))
             return -1;
+        // setmaxnreg.inc waits until the block's registers cover the split: refuse to launch a build
+        // whose kernels were compiled with fewer registers a thread than the split assumes
+        for (auto kern : {kern_p, kern_1}) {
+            cudaFuncAttributes fa;
+            if (cuda_failed(cudaFuncGetAttributes(&fa, kern), "cudaFuncGetAttributes(fwd_sm100)")) return -1;
+            if ((int64_t)fa.numRegs * NTHREADS < 128 * REG_LO + 256 * REG_HI) {
+                set_errorf("flash_attention (sm100): kernel built with %d registers a thread, below the %d the "
+                           "register split needs", fa.numRegs, (128 * REG_LO + 256 * REG_HI + NTHREADS - 1) / NTHREADS);
+                return -1;
+            }
+        }
         attr_set = true;
     }
     Params p;
