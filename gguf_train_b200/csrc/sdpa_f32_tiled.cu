@@ -42,6 +42,7 @@ struct TiledP {
     V4 q, k, v, o, g, dq, dk, dv, m;
     int mask_dtype;  // -1: none
     int vec;         // q, k, v, dO rows contiguous and 16-byte aligned: 16-byte row-major tile loads
+    int mvec;        // f32 or bool mask with contiguous, aligned key rows and S % 4 == 0: mask_row4
     int64_t B, H, Hkv, L, S, group;
     float scale;
     int causal;
@@ -72,6 +73,18 @@ __device__ __forceinline__ bool mask_score(const TiledP& p, int64_t b, int64_t h
     if (p.mask_dtype == BOOL) return ((const uint8_t*)p.m.p)[idx] != 0;
     x += load_any<float>(p.m.p, idx, p.mask_dtype);
     return true;
+}
+
+// The mask's additive values for keys s .. s+3 of row (b, h, l) in one load (p.mvec; s % 4 == 0 and
+// s < S): an f32 mask's entries (16 bytes), or 0 / -inf for a bool mask's allowed / masked keys (4 bytes)
+__device__ __forceinline__ float4 mask_row4(const TiledP& p, int64_t b, int64_t h, int64_t l, int64_t s) {
+    const int64_t idx = b * p.m.s0 + h * p.m.s1 + l * p.m.s2 + s;
+    if (p.mask_dtype == BOOL) {
+        const uint32_t w = *(const uint32_t*)((const uint8_t*)p.m.p + idx);
+        return make_float4((w & 0xffu) ? 0.0f : -INFINITY, (w & 0xff00u) ? 0.0f : -INFINITY,
+                           (w & 0xff0000u) ? 0.0f : -INFINITY, (w >> 24) ? 0.0f : -INFINITY);
+    }
+    return *(const float4*)(p.m.p + idx);
 }
 
 // Load a 64 x D tile of a (B, heads, rows, D) tensor transposed into sm[d][r] (row stride T + PAD);
@@ -204,11 +217,13 @@ __global__ void __launch_bounds__(NT, 2) fwd_f32_tiled_kernel(TiledP p) {
         for (int i = 0; i < 4; ++i) {
             const int64_t l = l0 + ra + i;
             float rmax = -INFINITY;
+            const float4 mv4 = p.mvec && l < p.L && s0 + cb < p.S ? mask_row4(p, b, h, l, s0 + cb) : make_float4(0.f, 0.f, 0.f, 0.f);
+            const float mv[4] = {mv4.x, mv4.y, mv4.z, mv4.w};
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
                 const int64_t s = s0 + cb + j;
-                float v = x[i][j] * p.scale;
-                const bool ok = l < p.L && s < p.S && !(p.causal && s > l) && mask_score(p, b, h, l, s, v);
+                float v = x[i][j] * p.scale + mv[j];
+                const bool ok = l < p.L && s < p.S && !(p.causal && s > l) && (p.mvec || mask_score(p, b, h, l, s, v));
                 x[i][j] = ok ? v : -INFINITY;
                 rmax = fmaxf(rmax, x[i][j]);
             }
@@ -288,12 +303,14 @@ __global__ void __launch_bounds__(NT, 2) bwd_dq_f32_tiled_kernel(TiledP p) {
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             const int64_t l = l0 + ra + i;
+            const float4 mv4 = p.mvec && l < p.L && s0 + cb < p.S ? mask_row4(p, b, h, l, s0 + cb) : make_float4(0.f, 0.f, 0.f, 0.f);
+            const float mv[4] = {mv4.x, mv4.y, mv4.z, mv4.w};
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
                 const int64_t s = s0 + cb + j;
-                float v = x[i][j] * p.scale;
+                float v = x[i][j] * p.scale + mv[j];
                 const bool ok = l < p.L && s < p.S && !(p.causal && s > l) && lse[i] != -INFINITY &&
-                                mask_score(p, b, h, l, s, v) && v != -INFINITY;
+                                (p.mvec || mask_score(p, b, h, l, s, v)) && v != -INFINITY;
                 const float pr = ok ? __expf(v - lse[i]) : 0.0f;
                 float d = dp[i][j];
                 if (p.drop) d = drop_keep(rkey[i], (uint32_t)s, p.drop_thr) ? d * p.inv_keep : 0.0f;
@@ -365,16 +382,20 @@ __global__ void __launch_bounds__(NT, 2) bwd_dkdv_f32_tiled_kernel(TiledP p) {
             block_dot<D>(x, Ks, Qs, ra, cb);  // S^T[key][query]
             block_dot<D>(dp, Vs, Gs, ra, cb); // dP^T
             float pt[4][4], dst[4][4];
+            // queries outer: the mask entries of query l for this thread's four keys are one load
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const int64_t s = s0 + ra + i;
+            for (int j = 0; j < 4; ++j) {
+                const int64_t l = l0 + cb + j;
+                const float lse = LD[cb + j];
+                const float4 mv4 =
+                    p.mvec && l < p.L && s0 + ra < p.S ? mask_row4(p, b, h, l, s0 + ra) : make_float4(0.f, 0.f, 0.f, 0.f);
+                const float mv[4] = {mv4.x, mv4.y, mv4.z, mv4.w};
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const int64_t l = l0 + cb + j;
-                    const float lse = LD[cb + j];
-                    float v = x[i][j] * p.scale;
+                for (int i = 0; i < 4; ++i) {
+                    const int64_t s = s0 + ra + i;
+                    float v = x[i][j] * p.scale + mv[i];
                     const bool ok = l < p.L && s < p.S && !(p.causal && s > l) && lse != -INFINITY &&
-                                    mask_score(p, b, h, l, s, v) && v != -INFINITY;
+                                    (p.mvec || mask_score(p, b, h, l, s, v)) && v != -INFINITY;
                     const float pr = ok ? __expf(v - lse) : 0.0f;
                     float d = dp[i][j], pk = pr;
                     if (p.drop) {
@@ -463,6 +484,14 @@ TiledP common(const gtb_tensor4& q, const gtb_tensor4& k, const gtb_tensor4& v, 
                    : V4{nullptr, 0, 0, 0, 0};
     p.mask_dtype = has_mask ? mask.dtype : -1;
     p.vec = rows16(q) && rows16(k) && rows16(v);
+    // the mask's key rows read four entries at a time: f32 or bool, contiguous along the keys, every
+    // stride a multiple of four entries and S a multiple of four (a 4-key group never straddles S)
+    p.mvec = 0;
+    if (has_mask && (mask.dtype == F32 || mask.dtype == BOOL) && mask.stride[3] == 1 && sh.S % 4 == 0) {
+        bool ok = ((uintptr_t)mask.data & (mask.dtype == F32 ? 15 : 3)) == 0;
+        for (int i = 0; i < 3; ++i) ok = ok && mask.stride[i] % 4 == 0;
+        p.mvec = ok ? 1 : 0;
+    }
     p.B = sh.B; p.H = sh.H; p.Hkv = sh.Hkv; p.L = sh.L; p.S = sh.S; p.group = sh.H / sh.Hkv;
     p.scale = scale;
     p.causal = causal;

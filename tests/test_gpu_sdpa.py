@@ -55,6 +55,8 @@ FWD_CASES = [
     ("f32", 2, 3, 3, 4, 5, 6, 6, False, "bool"),        # reference test shape (test_pooling_and_attention.py:349)
     ("f32", 2, 3, 3, 4, 5, 6, 6, False, "float"),
     ("f64", 1, 2, 2, 4, 4, 8, 8, True, None),           # gradcheck shape (test_autograd.py:136)
+    ("f32", 2, 4, 2, 96, 128, 64, 64, False, "float"),  # fp32 tiled kernels, mask rows read 4 keys at a time
+    ("f32", 1, 2, 2, 100, 132, 64, 64, True, "bool"),
     ("bf16", 1, 4, 2, 300, 300, 128, 128, True, None),  # tcgen05 path, ragged last tile, GQA
     ("bf16", 2, 4, 1, 200, 333, 128, 128, False, None), # tcgen05 path, L != S
     ("bf16", 1, 2, 2, 257, 130, 128, 128, True, None),  # causal with L > S (top-left)
@@ -126,6 +128,8 @@ BWD_CASES = [
     ("f32", 2, 3, 3, 4, 5, 6, 6, False, "bool"),
     ("f32", 1, 4, 2, 33, 47, 16, 24, False, "float"),
     ("f64", 1, 2, 2, 4, 4, 8, 8, True, None),
+    ("f32", 2, 4, 2, 96, 128, 64, 64, False, "float"),  # fp32 tiled kernels, mask rows read 4 keys at a time
+    ("f32", 1, 2, 2, 100, 132, 64, 64, True, "bool"),
     ("bf16", 1, 4, 2, 200, 200, 128, 128, True, None),
     ("f16", 1, 2, 2, 130, 70, 64, 64, False, None),
     ("bf16", 1, 4, 1, 384, 384, 128, 128, True, None),   # tcgen05 backward: GQA group of 4, 3 tiles
