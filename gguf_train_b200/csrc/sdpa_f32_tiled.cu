@@ -146,6 +146,23 @@ __device__ __forceinline__ void load_r(float* sm, const V4& t, int64_t b, int64_
     }
 }
 
+// The same row-major tile with asynchronous 16-byte copies (cp.async, rows past `rows` zero-filled), for
+// 16-byte rows (vec): the copies run while the kernel computes with other tiles; cp_async_wait() and a
+// barrier before the tile is read.
+template <int D>
+__device__ __forceinline__ void load_r_async(float* sm, const V4& t, int64_t b, int64_t h, int64_t r0, int64_t rows) {
+    for (int i = threadIdx.x; i < T * D / 4; i += NT) {
+        const int r = i / (D / 4), d = 4 * (i % (D / 4));
+        const int64_t row = r0 + r;
+        const bool in = row < rows;
+        const float* src = t.p + b * t.s0 + h * t.s1 + (in ? row : r0) * t.s2 + d;  // a valid address either way
+        const uint32_t dst = (uint32_t)__cvta_generic_to_shared(sm + r * (D + PAD) + d);
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(in ? 16 : 0) : "memory");
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
 // acc[i][j] += sum_d A[d][ra + i] * B[d][cb + j] over d < D (A, B transposed tiles)
 template <int D>
 __device__ __forceinline__ void block_dot(float (&acc)[4][4], const float* A, const float* B, int ra, int cb) {
@@ -207,8 +224,9 @@ __global__ void __launch_bounds__(NT, 2) fwd_f32_tiled_kernel(TiledP p) {
     if (p.causal) s_end = min(p.S, min(l0 + T, p.L));
     for (int64_t s0 = 0; s0 < s_end; s0 += T) {
         __syncthreads();
+        if (p.vec) load_r_async<D>(Vs, p.v, b, hk, s0, p.S);  // lands while S and the softmax are computed
+        else load_r<D>(Vs, p.v, b, hk, s0, p.S, false);
         load_t<D>(Ks, p.k, b, hk, s0, p.S);  // scalar: keeps this loop within 128 registers
-        load_r<D>(Vs, p.v, b, hk, s0, p.S, p.vec);
         __syncthreads();
         float x[4][4] = {};
         block_dot<D>(x, Qs, Ks, ra, cb);
@@ -244,6 +262,7 @@ __global__ void __launch_bounds__(NT, 2) fwd_f32_tiled_kernel(TiledP p) {
 #pragma unroll
         for (int j = 0; j < 4; ++j)
             *(float4*)(Ps + (cb + j) * (T + PAD) + ra) = make_float4(pv[0][j], pv[1][j], pv[2][j], pv[3][j]);
+        if (p.vec) cp_async_wait();
         __syncthreads();
         block_pv<D>(o, Ps, Vs, ra, cb);
     }
@@ -292,9 +311,10 @@ __global__ void __launch_bounds__(NT, 2) bwd_dq_f32_tiled_kernel(TiledP p) {
     if (p.causal) s_end = min(p.S, min(l0 + T, p.L));
     for (int64_t s0 = 0; s0 < s_end; s0 += T) {
         __syncthreads();
+        if (p.vec) load_r_async<D>(Kr, p.k, b, hk, s0, p.S);  // lands while S, dP and dS are computed
+        else load_r<D>(Kr, p.k, b, hk, s0, p.S, false);
         load_t<D>(Ks, p.k, b, hk, s0, p.S);  // the scalar loads keep this loop within 128 registers
         load_t<D>(Vs, p.v, b, hk, s0, p.S);
-        load_r<D>(Kr, p.k, b, hk, s0, p.S, p.vec);
         __syncthreads();
         float x[4][4] = {}, dp[4][4] = {};
         block_dot<D>(x, Qs, Ks, ra, cb);
@@ -320,6 +340,7 @@ __global__ void __launch_bounds__(NT, 2) bwd_dq_f32_tiled_kernel(TiledP p) {
 #pragma unroll
         for (int j = 0; j < 4; ++j)
             *(float4*)(Ds + (cb + j) * (T + PAD) + ra) = make_float4(ds[0][j], ds[1][j], ds[2][j], ds[3][j]);
+        if (p.vec) cp_async_wait();
         __syncthreads();
         block_pv<D>(dq, Ds, Kr, ra, cb);
     }
@@ -368,10 +389,15 @@ __global__ void __launch_bounds__(NT, 2) bwd_dkdv_f32_tiled_kernel(TiledP p) {
         const uint32_t hkey = p.drop ? drop_head_key(p.drop_seed, (uint32_t)(b * p.H + h)) : 0u;
         for (int64_t l0 = l_begin; l0 < p.L; l0 += T) {
             __syncthreads();
+            if (p.vec) {  // these land while S^T, dP^T, P^T and dS^T are computed
+                load_r_async<D>(Qr, p.q, b, h, l0, p.L);
+                load_r_async<D>(Gr, p.g, b, h, l0, p.L);
+            } else {
+                load_r<D>(Qr, p.q, b, h, l0, p.L, false);
+                load_r<D>(Gr, p.g, b, h, l0, p.L, false);
+            }
             load_t<D>(Qs, p.q, b, h, l0, p.L);  // the scalar loads keep this loop within 128 registers
             load_t<D>(Gs, p.g, b, h, l0, p.L);
-            load_r<D>(Qr, p.q, b, h, l0, p.L, p.vec);
-            load_r<D>(Gr, p.g, b, h, l0, p.L, p.vec);
             for (int i = tid; i < T; i += NT) {
                 const int64_t l = l0 + i;
                 LD[i] = l < p.L ? p.lse[(b * p.H + h) * p.L + l] : -INFINITY;
@@ -414,6 +440,7 @@ __global__ void __launch_bounds__(NT, 2) bwd_dkdv_f32_tiled_kernel(TiledP p) {
                 *(float4*)(Ps + (cb + j) * (T + PAD) + ra) = make_float4(pt[0][j], pt[1][j], pt[2][j], pt[3][j]);
                 *(float4*)(Ds + (cb + j) * (T + PAD) + ra) = make_float4(dst[0][j], dst[1][j], dst[2][j], dst[3][j]);
             }
+            if (p.vec) cp_async_wait();
             __syncthreads();
             block_pv<D>(dv, Ps, Gr, ra, cb);   // dV[key][d] += sum_l P^T[key][l] dO[l][d]
             block_pv<D>(dk, Ds, Qr, ra, cb);   // dK[key][d] += sum_l dS^T[key][l] Q[l][d]
