@@ -162,6 +162,50 @@ __device__ __forceinline__ void load_r_async(float* sm, const V4& t, int64_t b, 
     asm volatile("cp.async.commit_group;" ::: "memory");
 }
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+
+// A 64 x D tile row-major without padding, its 16-byte chunks XOR-swizzled by (row / 4) % 8 (chunk c
+// of row r at r * D + 4 * (c ^ ((r >> 2) & 7))), loaded with cp.async (16-byte rows; rows past `rows`
+// zero-filled; the caller commits): block_dot_rb reads it as the transposed operand without bank
+// conflicts, so no transposing store is needed and the copy can run behind other work.
+template <int D>
+__device__ __forceinline__ void load_swz_async(float* sm, const V4& t, int64_t b, int64_t h, int64_t r0, int64_t rows) {
+    static_assert(D / 4 >= 8, "the swizzle spans eight 16-byte chunks");
+    for (int i = threadIdx.x; i < T * D / 4; i += NT) {
+        const int r = i / (D / 4), c = i % (D / 4);
+        const int64_t row = r0 + r;
+        const bool in = row < rows;
+        const float* src = t.p + b * t.s0 + h * t.s1 + (in ? row : r0) * t.s2 + 4 * c;
+        const uint32_t dst = (uint32_t)__cvta_generic_to_shared(sm + r * D + 4 * (c ^ ((r >> 2) & 7)));
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(in ? 16 : 0) : "memory");
+    }
+}
+
+// acc[i][j] += sum_d A[d][ra + i] * Br[cb + j][d] over d < D: A transposed (as block_dot), Br a
+// swizzled row-major tile (load_swz_async). Rows cb..cb+3 share one swizzle (cb is a multiple of 4), and
+// the eight threads of a quarter warp (cb/4 = 0..7 or 8..15) read eight different bank groups.
+template <int D>
+__device__ __forceinline__ void block_dot_rb(float (&acc)[4][4], const float* A, const float* Br, int ra, int cb) {
+    const int sw = (cb >> 2) & 7;
+#pragma unroll 2
+    for (int c = 0; c < D / 4; ++c) {
+        float bv[4][4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float4 t = *(const float4*)(Br + (cb + j) * D + 4 * (c ^ sw));
+            bv[j][0] = t.x; bv[j][1] = t.y; bv[j][2] = t.z; bv[j][3] = t.w;
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const float4 a = *(const float4*)(A + (4 * c + k) * (T + PAD) + ra);
+            const float av[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], bv[j][k], acc[i][j]);
+        }
+    }
+}
 
 // acc[i][j] += sum_d A[d][ra + i] * B[d][cb + j] over d < D (A, B transposed tiles)
 template <int D>
@@ -199,13 +243,16 @@ __device__ __forceinline__ void block_pv(float (&out)[4][D / 16], const float* P
 
 // ------------------------------------------------------------------ forward
 
-template <int D>
+// VEC (16-byte rows): K as a swizzled row-major tile and V row-major, both double-buffered and copied
+// with cp.async one key tile ahead, so that the loads run behind the products; otherwise K transposed
+// and V row-major, loaded synchronously per key tile.
+template <int D, bool VEC>
 __global__ void __launch_bounds__(NT, 2) fwd_f32_tiled_kernel(TiledP p) {
     extern __shared__ __align__(16) float smem[];
     float* Qs = smem;                        // [D][T + PAD]
-    float* Ks = Qs + D * (T + PAD);          // [D][T + PAD]
-    float* Vs = Ks + D * (T + PAD);          // [T][D + PAD]
-    float* Ps = Vs + T * (D + PAD);          // [T keys][T + PAD rows]
+    float* Ps = Qs + D * (T + PAD);          // [T keys][T + PAD rows]
+    float* Kb = Ps + T * (T + PAD);          // VEC: 2 x [T][D] swizzled; else [D][T + PAD]
+    float* Vb = Kb + (VEC ? 2 * T * D : D * (T + PAD));  // VEC: 2 x [T][D + PAD]; else [T][D + PAD]
     const int tid = threadIdx.x, rg = tid / 16, cg = tid % 16;
     const int ra = 4 * rg, cb = 4 * cg;
     const int64_t b = blockIdx.z, h = blockIdx.y, hk = h / p.group, l0 = (int64_t)blockIdx.x * T;
@@ -222,14 +269,32 @@ __global__ void __launch_bounds__(NT, 2) fwd_f32_tiled_kernel(TiledP p) {
     }
     int64_t s_end = p.S;
     if (p.causal) s_end = min(p.S, min(l0 + T, p.L));
-    for (int64_t s0 = 0; s0 < s_end; s0 += T) {
-        __syncthreads();
-        if (p.vec) load_r_async<D>(Vs, p.v, b, hk, s0, p.S);  // lands while S and the softmax are computed
-        else load_r<D>(Vs, p.v, b, hk, s0, p.S, false);
-        load_t<D>(Ks, p.k, b, hk, s0, p.S);  // scalar: keeps this loop within 128 registers
-        __syncthreads();
+    if constexpr (VEC) {
+        if (s_end > 0) {
+            load_swz_async<D>(Kb, p.k, b, hk, 0, p.S);
+            load_r_async<D>(Vb, p.v, b, hk, 0, p.S);  // commits the group
+        }
+    }
+    for (int64_t s0 = 0, it = 0; s0 < s_end; s0 += T, ++it) {
+        const int buf = VEC ? (int)(it & 1) : 0;
+        float* Ks = Kb + buf * T * D;
+        float* Vs = Vb + buf * T * (D + PAD);
+        if constexpr (VEC) {
+            cp_async_wait();  // this tile's K and V
+            __syncthreads();  // ... visible to all; the other buffers are free (the last tile is done)
+            if (s0 + T < s_end) {
+                load_swz_async<D>(Kb + (buf ^ 1) * T * D, p.k, b, hk, s0 + T, p.S);
+                load_r_async<D>(Vb + (buf ^ 1) * T * (D + PAD), p.v, b, hk, s0 + T, p.S);
+            }
+        } else {
+            __syncthreads();
+            load_r<D>(Vs, p.v, b, hk, s0, p.S, false);
+            load_t<D>(Ks, p.k, b, hk, s0, p.S);
+            __syncthreads();
+        }
         float x[4][4] = {};
-        block_dot<D>(x, Qs, Ks, ra, cb);
+        if constexpr (VEC) block_dot_rb<D>(x, Qs, Ks, ra, cb);
+        else block_dot<D>(x, Qs, Ks, ra, cb);
         float pv[4][4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
@@ -262,7 +327,6 @@ __global__ void __launch_bounds__(NT, 2) fwd_f32_tiled_kernel(TiledP p) {
 #pragma unroll
         for (int j = 0; j < 4; ++j)
             *(float4*)(Ps + (cb + j) * (T + PAD) + ra) = make_float4(pv[0][j], pv[1][j], pv[2][j], pv[3][j]);
-        if (p.vec) cp_async_wait();
         __syncthreads();
         block_pv<D>(o, Ps, Vs, ra, cb);
     }
@@ -478,13 +542,19 @@ bool rows16(const gtb_tensor4& t) {
     return true;
 }
 
+template <int D, bool VEC>
+int fwd_dv(const TiledP& p, cudaStream_t st) {
+    const size_t smem = sizeof(float) * (D * (T + PAD) + T * (T + PAD) +
+                                         (VEC ? 2 * T * D + 2 * T * (D + PAD) : D * (T + PAD) + T * (D + PAD)));
+    if (!smem_attr(fwd_f32_tiled_kernel<D, VEC>, smem)) return -1;
+    dim3 grid((unsigned)((p.L + T - 1) / T), (unsigned)p.H, (unsigned)p.B);
+    fwd_f32_tiled_kernel<D, VEC><<<grid, NT, smem, st>>>(p);
+    return cuda_failed(cudaGetLastError(), "fp32 tiled attention forward launch") ? -1 : 0;
+}
+
 template <int D>
 int fwd_d(const TiledP& p, cudaStream_t st) {
-    const size_t smem = sizeof(float) * (3 * D * (T + PAD) + T * (D + PAD) + T * (T + PAD));
-    if (!smem_attr(fwd_f32_tiled_kernel<D>, smem)) return -1;
-    dim3 grid((unsigned)((p.L + T - 1) / T), (unsigned)p.H, (unsigned)p.B);
-    fwd_f32_tiled_kernel<D><<<grid, NT, smem, st>>>(p);
-    return cuda_failed(cudaGetLastError(), "fp32 tiled attention forward launch") ? -1 : 0;
+    return p.vec ? fwd_dv<D, true>(p, st) : fwd_dv<D, false>(p, st);
 }
 
 template <int D>
