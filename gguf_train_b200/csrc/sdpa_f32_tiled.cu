@@ -241,6 +241,27 @@ __device__ __forceinline__ void block_pv(float (&out)[4][D / 16], const float* P
     }
 }
 
+// The same with V a swizzled row-major tile (load_swz_async): row s, chunk c at 4 * (c ^ ((s >> 2) & 7)).
+// The threads of a quarter warp read one row s at eight different chunks: no bank conflict.
+template <int D>
+__device__ __forceinline__ void block_pv_swz(float (&out)[4][D / 16], const float* P, const float* Vz, int ra, int cb) {
+#pragma unroll 4
+    for (int s = 0; s < T; ++s) {
+        const float4 a = *(const float4*)(P + s * (T + PAD) + ra);
+        const float av[4] = {a.x, a.y, a.z, a.w};
+        const int sw = (s >> 2) & 7;
+#pragma unroll
+        for (int q = 0; q < D / 64; ++q) {
+            const float4 c = *(const float4*)(Vz + s * D + 4 * (((cb >> 2) + 16 * q) ^ sw));
+            const float cv[4] = {c.x, c.y, c.z, c.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) out[i][4 * q + j] = fmaf(av[i], cv[j], out[i][4 * q + j]);
+        }
+    }
+}
+
 // ------------------------------------------------------------------ forward
 
 // VEC (16-byte rows): K as a swizzled row-major tile and V row-major, both double-buffered and copied
@@ -422,17 +443,21 @@ __global__ void __launch_bounds__(NT, 2) bwd_dq_f32_tiled_kernel(TiledP p) {
 
 // ------------------------------------------------------------------ dk / dv
 
-template <int D>
+// VEC (16-byte rows): each query tile's Q and dO are copied once (cp.async) as swizzled row-major tiles
+// that serve both as the operand of S^T = K Q^T / dP^T = V dO^T and as the row-major operand of
+// dK += dS^T Q / dV += P^T dO. Otherwise Q and dO are loaded transposed and row-major, and P^T / dS^T
+// take the place of the transposed tiles once S^T and dP^T are formed. Either way 102.5 KB of shared
+// memory: two CTAs per SM.
+template <int D, bool VEC>
 __global__ void __launch_bounds__(NT, 2) bwd_dkdv_f32_tiled_kernel(TiledP p) {
     extern __shared__ __align__(16) float smem[];
     float* Ks = smem;                        // K^T [D][T + PAD]  (rows = this CTA's keys)
     float* Vs = Ks + D * (T + PAD);          // V^T [D][T + PAD]
-    float* Qs = Vs + D * (T + PAD);          // Q^T [D][T + PAD]  (a query tile)
-    float* Gs = Qs + D * (T + PAD);          // dO^T [D][T + PAD]
-    float* Qr = Gs + D * (T + PAD);          // Q row-major [T][D + PAD]
-    float* Gr = Qr + T * (D + PAD);          // dO row-major [T][D + PAD]
-    // P^T and dS^T as [query][key + PAD] (for dV += P^T dO, dK += dS^T Q) reuse the transposed Q and
-    // dO tiles, which are dead once S^T and dP^T are formed: 102.5 KB in all, two CTAs per SM
+    float* Qs = Vs + D * (T + PAD);          // Q^T [D][T + PAD] (VEC: P^T only)
+    float* Gs = Qs + D * (T + PAD);          // dO^T [D][T + PAD] (VEC: dS^T only)
+    float* Qr = Gs + D * (T + PAD);          // Q row-major [T][D + PAD] (VEC: swizzled [T][D])
+    float* Gr = Qr + T * (D + PAD);          // dO row-major [T][D + PAD] (VEC: swizzled [T][D])
+    // P^T and dS^T as [query][key + PAD] (for dV += P^T dO, dK += dS^T Q)
     static_assert(D == T, "P^T / dS^T take the place of the transposed Q / dO tiles");
     float* Ps = Qs;
     float* Ds = Gs;
@@ -453,24 +478,31 @@ __global__ void __launch_bounds__(NT, 2) bwd_dkdv_f32_tiled_kernel(TiledP p) {
         const uint32_t hkey = p.drop ? drop_head_key(p.drop_seed, (uint32_t)(b * p.H + h)) : 0u;
         for (int64_t l0 = l_begin; l0 < p.L; l0 += T) {
             __syncthreads();
-            if (p.vec) {  // these land while S^T, dP^T, P^T and dS^T are computed
-                load_r_async<D>(Qr, p.q, b, h, l0, p.L);
-                load_r_async<D>(Gr, p.g, b, h, l0, p.L);
+            if constexpr (VEC) {
+                load_swz_async<D>(Qr, p.q, b, h, l0, p.L);
+                load_swz_async<D>(Gr, p.g, b, h, l0, p.L);
+                cp_async_commit();
             } else {
                 load_r<D>(Qr, p.q, b, h, l0, p.L, false);
                 load_r<D>(Gr, p.g, b, h, l0, p.L, false);
+                load_t<D>(Qs, p.q, b, h, l0, p.L);  // the scalar loads keep this loop within 128 registers
+                load_t<D>(Gs, p.g, b, h, l0, p.L);
             }
-            load_t<D>(Qs, p.q, b, h, l0, p.L);  // the scalar loads keep this loop within 128 registers
-            load_t<D>(Gs, p.g, b, h, l0, p.L);
             for (int i = tid; i < T; i += NT) {
                 const int64_t l = l0 + i;
                 LD[i] = l < p.L ? p.lse[(b * p.H + h) * p.L + l] : -INFINITY;
                 LD[T + i] = l < p.L ? p.delta[(b * p.H + h) * p.L + l] : 0.0f;
             }
+            if constexpr (VEC) cp_async_wait();
             __syncthreads();
             float x[4][4] = {}, dp[4][4] = {};
-            block_dot<D>(x, Ks, Qs, ra, cb);  // S^T[key][query]
-            block_dot<D>(dp, Vs, Gs, ra, cb); // dP^T
+            if constexpr (VEC) {
+                block_dot_rb<D>(x, Ks, Qr, ra, cb);  // S^T[key][query]
+                block_dot_rb<D>(dp, Vs, Gr, ra, cb); // dP^T
+            } else {
+                block_dot<D>(x, Ks, Qs, ra, cb);
+                block_dot<D>(dp, Vs, Gs, ra, cb);
+            }
             float pt[4][4], dst[4][4];
             // queries outer: the mask entries of query l for this thread's four keys are one load
 #pragma unroll
@@ -504,10 +536,14 @@ __global__ void __launch_bounds__(NT, 2) bwd_dkdv_f32_tiled_kernel(TiledP p) {
                 *(float4*)(Ps + (cb + j) * (T + PAD) + ra) = make_float4(pt[0][j], pt[1][j], pt[2][j], pt[3][j]);
                 *(float4*)(Ds + (cb + j) * (T + PAD) + ra) = make_float4(dst[0][j], dst[1][j], dst[2][j], dst[3][j]);
             }
-            if (p.vec) cp_async_wait();
             __syncthreads();
-            block_pv<D>(dv, Ps, Gr, ra, cb);   // dV[key][d] += sum_l P^T[key][l] dO[l][d]
-            block_pv<D>(dk, Ds, Qr, ra, cb);   // dK[key][d] += sum_l dS^T[key][l] Q[l][d]
+            if constexpr (VEC) {
+                block_pv_swz<D>(dv, Ps, Gr, ra, cb);  // dV[key][d] += sum_l P^T[key][l] dO[l][d]
+                block_pv_swz<D>(dk, Ds, Qr, ra, cb);  // dK[key][d] += sum_l dS^T[key][l] Q[l][d]
+            } else {
+                block_pv<D>(dv, Ps, Gr, ra, cb);
+                block_pv<D>(dk, Ds, Qr, ra, cb);
+            }
         }
     }
 #pragma unroll
@@ -561,13 +597,14 @@ template <int D>
 int bwd_d(const TiledP& p, cudaStream_t st) {
     const size_t s_dq = sizeof(float) * (4 * D * (T + PAD) + T * (D + PAD) + T * (T + PAD));
     const size_t s_kv = sizeof(float) * (4 * D * (T + PAD) + 2 * T * (D + PAD) + 2 * T);
-    if (!smem_attr(bwd_dq_f32_tiled_kernel<D>, s_dq) || !smem_attr(bwd_dkdv_f32_tiled_kernel<D>, s_kv)) return -1;
+    auto kv_kern = p.vec ? bwd_dkdv_f32_tiled_kernel<D, true> : bwd_dkdv_f32_tiled_kernel<D, false>;
+    if (!smem_attr(bwd_dq_f32_tiled_kernel<D>, s_dq) || !smem_attr(kv_kern, s_kv)) return -1;
     if (p.L > 0) {
         bwd_dq_f32_tiled_kernel<D><<<dim3((unsigned)((p.L + T - 1) / T), (unsigned)p.H, (unsigned)p.B), NT, s_dq, st>>>(p);
         if (cuda_failed(cudaGetLastError(), "fp32 tiled attention dq launch")) return -1;
     }
     if (p.S > 0) {
-        bwd_dkdv_f32_tiled_kernel<D><<<dim3((unsigned)((p.S + T - 1) / T), (unsigned)p.Hkv, (unsigned)p.B), NT, s_kv, st>>>(p);
+        kv_kern<<<dim3((unsigned)((p.S + T - 1) / T), (unsigned)p.Hkv, (unsigned)p.B), NT, s_kv, st>>>(p);
         if (cuda_failed(cudaGetLastError(), "fp32 tiled attention dk/dv launch")) return -1;
     }
     return 0;
