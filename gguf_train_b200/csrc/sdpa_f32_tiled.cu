@@ -367,14 +367,17 @@ __global__ void __launch_bounds__(NT, 2) fwd_f32_tiled_kernel(TiledP p) {
 
 // ------------------------------------------------------------------ dq
 
-template <int D>
+// VEC (16-byte rows): per key tile one swizzled row-major copy of K (the operand of S = Q K^T and of
+// dQ += dS K) and of V (the operand of dP = dO V^T), copied with cp.async; the next tile's V is copied
+// while dQ += dS K runs. Otherwise K is loaded transposed and row-major and V transposed.
+template <int D, bool VEC>
 __global__ void __launch_bounds__(NT, 2) bwd_dq_f32_tiled_kernel(TiledP p) {
     extern __shared__ __align__(16) float smem[];
     float* Qs = smem;                        // [D][T + PAD]
     float* Gs = Qs + D * (T + PAD);          // dO [D][T + PAD]
-    float* Ks = Gs + D * (T + PAD);          // [D][T + PAD]  (K transposed, for S)
-    float* Vs = Ks + D * (T + PAD);          // [D][T + PAD]  (V transposed, for dP)
-    float* Kr = Vs + D * (T + PAD);          // [T][D + PAD]  (K row-major, for dQ += dS K)
+    float* Ks = Gs + D * (T + PAD);          // [D][T + PAD]  (K transposed, for S; VEC: K swizzled [T][D])
+    float* Vs = Ks + D * (T + PAD);          // [D][T + PAD]  (V transposed, for dP; VEC: V swizzled [T][D])
+    float* Kr = Vs + D * (T + PAD);          // [T][D + PAD]  (K row-major, for dQ += dS K; VEC: unused)
     float* Ds = Kr + T * (D + PAD);          // dS [T keys][T + PAD rows]
     const int tid = threadIdx.x, rg = tid / 16, cg = tid % 16;
     const int ra = 4 * rg, cb = 4 * cg;
@@ -394,16 +397,32 @@ __global__ void __launch_bounds__(NT, 2) bwd_dq_f32_tiled_kernel(TiledP p) {
     }
     int64_t s_end = p.S;
     if (p.causal) s_end = min(p.S, min(l0 + T, p.L));
+    if constexpr (VEC) {
+        if (s_end > 0) {
+            load_swz_async<D>(Vs, p.v, b, hk, 0, p.S);
+            cp_async_commit();
+        }
+    }
     for (int64_t s0 = 0; s0 < s_end; s0 += T) {
-        __syncthreads();
-        if (p.vec) load_r_async<D>(Kr, p.k, b, hk, s0, p.S);  // lands while S, dP and dS are computed
-        else load_r<D>(Kr, p.k, b, hk, s0, p.S, false);
-        load_t<D>(Ks, p.k, b, hk, s0, p.S);  // the scalar loads keep this loop within 128 registers
-        load_t<D>(Vs, p.v, b, hk, s0, p.S);
+        __syncthreads();  // the last tile's dQ += dS K is done with K and dS
+        if constexpr (VEC) {
+            load_swz_async<D>(Ks, p.k, b, hk, s0, p.S);
+            cp_async_commit();
+            cp_async_wait();  // this tile's K and V
+        } else {
+            load_r<D>(Kr, p.k, b, hk, s0, p.S, false);
+            load_t<D>(Ks, p.k, b, hk, s0, p.S);  // the scalar loads keep this loop within 128 registers
+            load_t<D>(Vs, p.v, b, hk, s0, p.S);
+        }
         __syncthreads();
         float x[4][4] = {}, dp[4][4] = {};
-        block_dot<D>(x, Qs, Ks, ra, cb);
-        block_dot<D>(dp, Gs, Vs, ra, cb);
+        if constexpr (VEC) {
+            block_dot_rb<D>(x, Qs, Ks, ra, cb);
+            block_dot_rb<D>(dp, Gs, Vs, ra, cb);
+        } else {
+            block_dot<D>(x, Qs, Ks, ra, cb);
+            block_dot<D>(dp, Gs, Vs, ra, cb);
+        }
         float ds[4][4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
@@ -425,9 +444,16 @@ __global__ void __launch_bounds__(NT, 2) bwd_dq_f32_tiled_kernel(TiledP p) {
 #pragma unroll
         for (int j = 0; j < 4; ++j)
             *(float4*)(Ds + (cb + j) * (T + PAD) + ra) = make_float4(ds[0][j], ds[1][j], ds[2][j], ds[3][j]);
-        if (p.vec) cp_async_wait();
-        __syncthreads();
-        block_pv<D>(dq, Ds, Kr, ra, cb);
+        __syncthreads();  // dS is written and every thread is done with V
+        if constexpr (VEC) {
+            if (s0 + T < s_end) {  // the next tile's V, behind dQ += dS K
+                load_swz_async<D>(Vs, p.v, b, hk, s0 + T, p.S);
+                cp_async_commit();
+            }
+            block_pv_swz<D>(dq, Ds, Ks, ra, cb);
+        } else {
+            block_pv<D>(dq, Ds, Kr, ra, cb);
+        }
     }
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -598,9 +624,10 @@ int bwd_d(const TiledP& p, cudaStream_t st) {
     const size_t s_dq = sizeof(float) * (4 * D * (T + PAD) + T * (D + PAD) + T * (T + PAD));
     const size_t s_kv = sizeof(float) * (4 * D * (T + PAD) + 2 * T * (D + PAD) + 2 * T);
     auto kv_kern = p.vec ? bwd_dkdv_f32_tiled_kernel<D, true> : bwd_dkdv_f32_tiled_kernel<D, false>;
-    if (!smem_attr(bwd_dq_f32_tiled_kernel<D>, s_dq) || !smem_attr(kv_kern, s_kv)) return -1;
+    auto dq_kern = p.vec ? bwd_dq_f32_tiled_kernel<D, true> : bwd_dq_f32_tiled_kernel<D, false>;
+    if (!smem_attr(dq_kern, s_dq) || !smem_attr(kv_kern, s_kv)) return -1;
     if (p.L > 0) {
-        bwd_dq_f32_tiled_kernel<D><<<dim3((unsigned)((p.L + T - 1) / T), (unsigned)p.H, (unsigned)p.B), NT, s_dq, st>>>(p);
+        dq_kern<<<dim3((unsigned)((p.L + T - 1) / T), (unsigned)p.H, (unsigned)p.B), NT, s_dq, st>>>(p);
         if (cuda_failed(cudaGetLastError(), "fp32 tiled attention dq launch")) return -1;
     }
     if (p.S > 0) {
