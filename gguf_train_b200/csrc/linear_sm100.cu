@@ -52,6 +52,7 @@ struct LinP {
     void* c;
     int64_t ldc;       // elements between rows of C
     int vec;           // 16-byte stores allowed (ldc % 8 == 0, aligned C)
+    int bias_vec;      // 16-byte bias loads allowed (aligned bias)
     int* status;
 };
 
@@ -179,9 +180,25 @@ linear_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
                 for (int i = 0; i < 32; ++i) x[i] = __uint_as_float(v[i]);
                 if (p.bias) {
                     const T* bb = (const T*)p.bias + col0;
+                    if (p.bias_vec && col0 + 32 <= p.N) {
+                        // the chunk's 32 bias values in four 16-byte loads (the same address across the
+                        // warp: one transaction each)
 #pragma unroll
-                    for (int i = 0; i < 32; ++i)
-                        if (col0 + i < p.N) x[i] += Elem<T>::load(bb + i);
+                        for (int q = 0; q < 4; ++q) {
+                            const uint4 w = ((const uint4*)bb)[q];
+                            const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) {
+                                const T* pair = (const T*)&ww[e];
+                                x[8 * q + 2 * e] += Elem<T>::load(pair);
+                                x[8 * q + 2 * e + 1] += Elem<T>::load(pair + 1);
+                            }
+                        }
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 32; ++i)
+                            if (col0 + i < p.N) x[i] += Elem<T>::load(bb + i);
+                    }
                 }
                 if (p.vec && col0 + 32 <= p.N) {
                     uint32_t w[16];
@@ -270,6 +287,7 @@ int launch_linear_sm100(const void* a, const void* b, const void* bias, void* c,
     p.c = c;
     p.ldc = ldc;
     p.vec = (ldc % 8 == 0) && (((uintptr_t)c & 15) == 0);
+    p.bias_vec = bias && (((uintptr_t)bias & 15) == 0);
     if (bn == 128) return bf16 ? run_linear<128, true>(ma, mb, p, st) : run_linear<128, false>(ma, mb, p, st);
     return bf16 ? run_linear<256, true>(ma, mb, p, st) : run_linear<256, false>(ma, mb, p, st);
 }
