@@ -39,7 +39,9 @@ struct LCfg {
     static constexpr int A_BYTES = BM * BK * 2;   // 16 KB
     static constexpr int B_BYTES = BN * BK * 2;
     static constexpr int STAGE = A_BYTES + B_BYTES;
-    static constexpr int OFF_BAR = STAGES * STAGE;
+    static constexpr int OFF_STG = STAGES * STAGE;  // per epilogue warp: 32 rows x 64 bytes (+16 padding)
+    static constexpr int STG_ROW = 80;
+    static constexpr int OFF_BAR = OFF_STG + 4 * 32 * STG_ROW;
     static constexpr int NBAR = 2 * STAGES + 4 + 1;
     static constexpr int SMEM = OFF_BAR + NBAR * 8 + 16 + 1024;
     static constexpr uint32_t TMEM_COLS = 2 * BN;  // 256 or 512
@@ -168,24 +170,29 @@ linear_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
             const int tm = tile / p.tiles_n, tn = tile % p.tiles_n;
             const int64_t row = (int64_t)tm * BM + r;
             T* crow = (T*)p.c + row * p.ldc;
+            unsigned char* stg = smem + C::OFF_STG + quad * 32 * C::STG_ROW;  // this warp's staging rows
 #pragma unroll 1
             for (int c = 0; c < BN / 32; ++c) {
+                const int64_t col0 = (int64_t)tn * BN + c * 32;
+                // the chunk's 32 bias values in four 16-byte loads (the same address across the warp: one
+                // transaction each), issued before the wait for the accumulator so the two overlap
+                const bool bvec = p.bias && p.bias_vec && col0 + 32 <= p.N;
+                uint4 bw[4];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) bw[q] = bvec ? ((const uint4*)((const T*)p.bias + col0))[q] : make_uint4(0, 0, 0, 0);
                 uint32_t v[32];
                 tmem_ld32(tmem + lane_addr + (uint32_t)(buf * BN + c * 32), v);
                 tmem_ld_wait();
-                const int64_t col0 = (int64_t)tn * BN + c * 32;
-                if (row >= p.M || col0 >= p.N) continue;
+                if (col0 >= p.N) continue;  // the same for the whole warp
                 float x[32];
 #pragma unroll
                 for (int i = 0; i < 32; ++i) x[i] = __uint_as_float(v[i]);
                 if (p.bias) {
                     const T* bb = (const T*)p.bias + col0;
-                    if (p.bias_vec && col0 + 32 <= p.N) {
-                        // the chunk's 32 bias values in four 16-byte loads (the same address across the
-                        // warp: one transaction each)
+                    if (bvec) {
 #pragma unroll
                         for (int q = 0; q < 4; ++q) {
-                            const uint4 w = ((const uint4*)bb)[q];
+                            const uint4 w = bw[q];
                             const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
                             for (int e = 0; e < 4; ++e) {
@@ -201,13 +208,25 @@ linear_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
                     }
                 }
                 if (p.vec && col0 + 32 <= p.N) {
+                    // through the warp's staging rows, so that each 16-byte store instruction writes 8 rows
+                    // x 64 contiguous bytes instead of 32 rows x 16 bytes (rows of 80 bytes: the writes of
+                    // a quarter warp hit eight different bank groups)
                     uint32_t w[16];
 #pragma unroll
                     for (int i = 0; i < 16; ++i) w[i] = pack2<BF16>(x[2 * i], x[2 * i + 1]);
-                    uint4* dst = (uint4*)(crow + col0);
 #pragma unroll
-                    for (int q = 0; q < 4; ++q) dst[q] = make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
-                } else {
+                    for (int q = 0; q < 4; ++q)
+                        *(uint4*)(stg + lane * C::STG_ROW + 16 * q) = make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+                    __syncwarp();
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        const int rr = lane / 4 + 8 * k, seg = lane % 4;  // row of the warp's 32, 16-byte segment
+                        const uint4 val = *(const uint4*)(stg + rr * C::STG_ROW + 16 * seg);
+                        const int64_t grow = (int64_t)tm * BM + quad * 32 + rr;
+                        if (grow < p.M) *(uint4*)((T*)p.c + grow * p.ldc + col0 + 8 * seg) = val;
+                    }
+                    __syncwarp();
+                } else if (row < p.M) {
 #pragma unroll
                     for (int i = 0; i < 32; ++i)
                         if (col0 + i < p.N) Elem<T>::store(crow + col0 + i, x[i]);
