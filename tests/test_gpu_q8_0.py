@@ -188,6 +188,9 @@ def test_append_past_the_cache_end_is_skipped_and_reported():
     ("f32", 1, 4, 33, 128, 128, 2, 500000.0, 1.0),   # NeoX, llama-3 base
     ("f32", 2, 2, 17, 96, 32, 0, 10000.0, 0.25),     # partial rotation, linear position scaling
     ("bf16", 2, 8, 64, 128, 128, 2, 10000.0, 1.0),
+    ("bf16", 2, 3, 70, 128, 128, 0, 10000.0, 1.0),   # 16-bit rows: normal mode, S not a multiple of 16
+    ("f16", 1, 4, 33, 128, 64, 2, 500000.0, 1.0),    # 16-bit rows: NeoX, partial rotation
+    ("f16", 2, 2, 17, 64, 32, 0, 10000.0, 0.25),
 ])
 def test_rope_matches_oracle(dtype, B, H, S, D, n_dims, mode, base, fscale):
     """rope (forward) and its backward through RoPEFn against the oracle's restatement of ggml's
@@ -211,6 +214,24 @@ def test_rope_matches_oracle(dtype, B, H, S, D, n_dims, mode, base, fscale):
     atol, rtol = (2e-5, 1e-5) if dtype == "f32" else (2e-2, 1e-2)
     assert_close(y, want, atol, rtol, "rope forward")
     assert_close(tx.grad, gwant, atol, rtol, "rope backward")
+
+
+@pytest.mark.parametrize("dtype,mode,n_dims", [("bf16", 0, 128), ("bf16", 2, 128), ("f16", 2, 64), ("f16", 0, 96)])
+def test_rope_16bit_rows_equal_the_f32_path_rounded(dtype, mode, n_dims):
+    """16-bit rows take the table-based kernel (angles computed once per position, 16-byte accesses);
+    f32 rows take the per-pair kernel. Both form the same f32 angles and products, so the 16-bit
+    result is bit for bit the f32 result on the same values rounded to the 16-bit type."""
+    import torch
+
+    import gguf_train_b200 as gtb
+
+    B, H, S, D = 2, 4, 300, 128
+    dt = torch.bfloat16 if dtype == "bf16" else torch.float16
+    x = torch.randn(B, H, S, D, device="cuda").to(dt)
+    pos = torch.tensor((np.arange(S) * 131 + 7) % 8000, dtype=torch.int32, device="cuda")
+    got = gtb.rope(x, pos, n_dims, mode, 0, 10000.0, 1.0)
+    ref = gtb.rope(x.float(), pos, n_dims, mode, 0, 10000.0, 1.0).to(dt)
+    assert torch.equal(got, ref)
 
 
 def test_append_with_rope_equals_rope_then_quantise():
