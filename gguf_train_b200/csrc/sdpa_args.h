@@ -55,6 +55,8 @@ int launch_attn_weights(const FwdArgs& a, const void* lse, void* out, bool avera
 // dropout, any strides. The backward takes rowsum(dout * out) per row in `delta` (B, H, L).
 bool f32_tiled_supported(const AttnShape& sh, int dtype);
 int launch_fwd_f32_tiled(const FwdArgs& a, cudaStream_t st);
+bool attn_weights_f32_tiled_supported(const FwdArgs& a, const void* out);
+int launch_attn_weights_f32_tiled(const FwdArgs& a, const void* lse, void* out, bool average, cudaStream_t st);
 int launch_bwd_f32_tiled(const BwdArgs& a, const float* delta, cudaStream_t st);
 
 // SIMT kernels: any float dtype, any D/Dv <= 256, masks, any strides.

@@ -52,6 +52,7 @@ struct TiledP {
     uint32_t drop_thr;
     uint64_t drop_seed;
     float inv_keep;
+    int average;           // attention weights: the mean over heads (B, L, S), else every head (B, H, L, S)
 };
 
 __device__ __forceinline__ float half_warp_max(float v) {
@@ -588,6 +589,121 @@ __global__ void __launch_bounds__(NT, 2) bwd_dkdv_f32_tiled_kernel(TiledP p) {
     }
 }
 
+// ------------------------------------------------------------------ attention weights
+
+// acc[i][j] += sum_d Ar[ra + i][d] * Br[cb + j][d]: both operands swizzled row-major tiles
+// (load_swz_async). Rows ra..ra+3 share one swizzle and the threads of a quarter warp share ra (one
+// broadcast address for A); for B they read eight different bank groups, as in block_dot_rb.
+template <int D>
+__device__ __forceinline__ void block_dot_rr(float (&acc)[4][4], const float* Ar, const float* Br, int ra, int cb) {
+    const int swa = (ra >> 2) & 7, swb = (cb >> 2) & 7;
+#pragma unroll 2
+    for (int c = 0; c < D / 4; ++c) {
+        float av[4][4], bv[4][4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float4 t = *(const float4*)(Ar + (ra + i) * D + 4 * (c ^ swa));
+            av[i][0] = t.x; av[i][1] = t.y; av[i][2] = t.z; av[i][3] = t.w;
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float4 t = *(const float4*)(Br + (cb + j) * D + 4 * (c ^ swb));
+            bv[j][0] = t.x; bv[j][1] = t.y; bv[j][2] = t.z; bv[j][3] = t.w;
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i][k], bv[j][k], acc[i][j]);
+    }
+}
+
+// MultiheadAttention's need_weights output for fp32 q/k with head size 64 and 16-byte rows, from the
+// forward's lse: P[b,h,l,s] = exp(q.k * scale + mask - lse[b,h,l]) (0 where masked or causal-masked;
+// under dropout times keep / (1 - p), the forward's decisions). One CTA per (batch, 64 rows, 64 keys):
+// per head, the Q rows and the K rows are copied with cp.async as swizzled row-major tiles, double-
+// buffered so that the next head's copies run behind this head's products; each thread forms a 4 x 4
+// block of scores, and the head mean accumulates in registers (or every head's weights are stored).
+template <int D>
+__global__ void __launch_bounds__(NT, 2) attn_weights_f32_tiled_kernel(TiledP p) {
+    extern __shared__ __align__(16) float smem[];  // 2 x (Q [T][D], K [T][D]) swizzled
+    const int tid = threadIdx.x, rg = tid / 16, cg = tid % 16;
+    const int ra = 4 * rg, cb = 4 * cg;  // rows ra.., keys cb.. of the tile
+    const int64_t b = blockIdx.z, l0 = (int64_t)blockIdx.y * T, s0 = (int64_t)blockIdx.x * T;
+    const bool dead = p.causal && s0 > l0 + T - 1;  // every key after every row of the tile
+    float acc[4][4] = {};
+    auto issue = [&](int64_t h, int buf) {
+        float* qb = smem + buf * 2 * T * D;
+        load_swz_async<D>(qb, p.q, b, h, l0, p.L);
+        load_swz_async<D>(qb + T * D, p.k, b, h / p.group, s0, p.S);
+        cp_async_commit();
+    };
+    if (!dead) issue(0, 0);
+    for (int64_t h = 0; h < p.H; ++h) {
+        const int buf = (int)(h & 1);
+        float w[4][4] = {};
+        if (!dead) {
+            cp_async_wait();  // this head's Q and K
+            __syncthreads();  // ... visible to all; the other buffer is free (the last head is done)
+            if (h + 1 < p.H) issue(h + 1, buf ^ 1);
+            const float* qb = smem + buf * 2 * T * D;
+            float x[4][4] = {};
+            block_dot_rr<D>(x, qb, qb + T * D, ra, cb);
+            const uint32_t hkey = p.drop ? drop_head_key(p.drop_seed, (uint32_t)(b * p.H + h)) : 0u;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int64_t l = l0 + ra + i;
+                if (l >= p.L) continue;
+                const float lse = p.lse[(b * p.H + h) * p.L + l];
+                const float4 mv4 = p.mvec && s0 + cb < p.S ? mask_row4(p, b, h, l, s0 + cb) : make_float4(0.f, 0.f, 0.f, 0.f);
+                const float mv[4] = {mv4.x, mv4.y, mv4.z, mv4.w};
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int64_t s = s0 + cb + j;
+                    float v = x[i][j] * p.scale + mv[j];
+                    const bool ok = s < p.S && !(p.causal && s > l) && lse != -INFINITY &&
+                                    (p.mvec || mask_score(p, b, h, l, s, v)) && v != -INFINITY;
+                    float e = ok ? __expf(v - lse) : 0.0f;
+                    if (p.drop && e != 0.0f)
+                        e = drop_keep(drop_row_key(hkey, (uint32_t)l), (uint32_t)s, p.drop_thr) ? e * p.inv_keep : 0.0f;
+                    w[i][j] = e;
+                }
+            }
+        }
+        if (p.average) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) acc[i][j] += w[i][j];
+        } else {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int64_t l = l0 + ra + i;
+                if (l >= p.L) continue;
+                float* o = (float*)p.o.p + ((b * p.H + h) * p.L + l) * p.S + s0 + cb;
+                if (s0 + cb + 3 < p.S && (p.S & 3) == 0) *(float4*)o = make_float4(w[i][0], w[i][1], w[i][2], w[i][3]);
+                else
+                    for (int j = 0; j < 4; ++j)
+                        if (s0 + cb + j < p.S) o[j] = w[i][j];
+            }
+        }
+    }
+    if (!p.average) return;
+    const float inv_h = 1.0f / (float)p.H;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int64_t l = l0 + ra + i;
+        if (l >= p.L) continue;
+        float* o = (float*)p.o.p + (b * p.L + l) * p.S + s0 + cb;
+        if (s0 + cb + 3 < p.S && (p.S & 3) == 0)
+            *(float4*)o = make_float4(acc[i][0] * inv_h, acc[i][1] * inv_h, acc[i][2] * inv_h, acc[i][3] * inv_h);
+        else
+            for (int j = 0; j < 4; ++j)
+                if (s0 + cb + j < p.S) o[j] = acc[i][j] * inv_h;
+    }
+}
+
 template <typename K>
 bool smem_attr(K kern, size_t bytes) {
     return !cuda_failed(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes),
@@ -668,6 +784,24 @@ TiledP common(const gtb_tensor4& q, const gtb_tensor4& k, const gtb_tensor4& v, 
 bool f32_tiled_supported(const AttnShape& sh, int dtype) {
     return dtype == F32 && sh.D == 64 && sh.Dv == 64 && sh.B <= 65535 && sh.H <= 65535 && sh.L < (1ll << 31) &&
            sh.S < (1ll << 31);
+}
+
+bool attn_weights_f32_tiled_supported(const FwdArgs& a, const void* out) {
+    return a.q.dtype == F32 && a.k.dtype == F32 && a.sh.D == 64 && a.sh.B <= 65535 && a.sh.L < (1ll << 31) &&
+           a.sh.S < (1ll << 31) && ((uintptr_t)out & 15) == 0 && rows16(a.q) && rows16(a.k);
+}
+
+int launch_attn_weights_f32_tiled(const FwdArgs& a, const void* lse, void* out, bool average, cudaStream_t st) {
+    TiledP p = common(a.q, a.k, a.v, a.has_mask, a.mask, a.sh, a.scale, a.causal, a.drop_p, a.drop_thr, a.drop_seed);
+    p.o = V4{(const float*)out, 0, 0, 0, 1};
+    p.lse = (float*)lse;
+    p.average = average ? 1 : 0;
+    constexpr int D = 64;
+    const size_t smem = sizeof(float) * 4 * T * D;
+    if (!smem_attr(attn_weights_f32_tiled_kernel<D>, smem)) return -1;
+    dim3 grid((unsigned)((a.sh.S + T - 1) / T), (unsigned)((a.sh.L + T - 1) / T), (unsigned)a.sh.B);
+    attn_weights_f32_tiled_kernel<D><<<grid, NT, smem, st>>>(p);
+    return cuda_failed(cudaGetLastError(), "attention weights (fp32 tiled) launch") ? -1 : 0;
 }
 
 int launch_fwd_f32_tiled(const FwdArgs& a, cudaStream_t st) {

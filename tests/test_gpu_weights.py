@@ -34,6 +34,8 @@ def _probs(q, k, mask, is_bool, scale, causal):
     ("bf16", 2, 4, 2, 200, 200, 128, True, None, True),
     ("bf16", 1, 4, 4, 130, 190, 64, False, "kpm", False),
     ("f32", 2, 8, 8, 64, 64, 64, False, "float", True),
+    ("f32", 2, 4, 2, 100, 130, 64, True, None, False),   # fp32 tiled kernel: causal, GQA, every head, S % 4 != 0
+    ("f32", 1, 4, 1, 97, 200, 64, False, "kpm", True),   # fp32 tiled kernel: bool mask read 4 keys per load
     ("f16", 1, 2, 1, 40, 70, 32, True, None, False),
     ("f64", 1, 2, 2, 17, 23, 8, False, "float", True),
 ])
