@@ -4,16 +4,23 @@
 //
 // Every kernel works on 64 x 64 tiles with 256 threads: thread t owns a 4 x 4 block (rows 4*(t/16)..,
 // columns 4*(t%16)..), so the 16 threads of one half-warp hold one row group and a row's reductions are
-// four shuffles. Operands sit in shared memory transposed where a thread reads four consecutive rows
-// or columns at once (float4): the inner loops issue two 16-byte shared loads per 16 FMAs.
+// four shuffles. The inner loops issue two 16-byte shared loads per 16 FMAs. With 16-byte rows (the
+// VEC instances) the tiles a kernel streams are copied with cp.async as row-major tiles whose 16-byte
+// chunks are XOR-swizzled by (row / 4) % 8, which the products read either as the transposed operand
+// (block_dot_rb, block_dot_rr) or row-major (block_pv_swz) without bank conflicts, so one copy serves
+// both roles and no transposing store is needed; otherwise tiles are loaded transposed and row-major.
+// An f32 or bool mask with contiguous, aligned key rows is read four keys per load.
 //
-//   forward     one CTA per 64 query rows of one (batch, head), key tiles of 64: S = Q K^T, online
-//               softmax (running max and sum per row), P to shared memory, O += P V; out = O / sum,
-//               lse = max + log(sum).
+//   forward     one CTA per 64 query rows of one (batch, head), key tiles of 64 (K and V double-
+//               buffered a tile ahead): S = Q K^T, online softmax (running max and sum per row), P to
+//               shared memory, O += P V; out = O / sum, lse = max + log(sum).
 //   dq          one CTA per 64 query rows: S and dP = dO V^T recomputed per key tile, P = exp(S - lse),
 //               dS = P (dP - delta), dQ += dS K.
 //   dk / dv     one CTA per 64 keys of one (batch, kv head), looping over the query tiles of every query
 //               head of the kv head: S^T = K Q^T, dP^T = V dO^T, P^T, dS^T; dV += P^T dO, dK += dS^T Q.
+//   weights     MultiheadAttention's need_weights output from the forward's lse: one CTA per (batch, 64
+//               rows, 64 keys), the heads' Q and K tiles double-buffered, exp(S - lse) averaged over
+//               heads in registers or stored per head.
 //
 // Semantics are those of the SIMT kernels (sdpa_simt.cu) and of gt_flash_attention (reference
 // csrc/gt_ops_nn.cpp:2423-2525): top-left causal, bool mask 0 = masked, float mask added to the scaled
