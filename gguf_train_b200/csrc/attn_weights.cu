@@ -160,6 +160,8 @@ int launch_attn_weights(const FwdArgs& a, const void* lse, void* out, bool avera
     p.drop_thr = a.drop_thr;
     p.drop_seed = a.drop_seed;
     p.inv_keep = 1.0f / (1.0f - a.drop_p);
+    // bf16/f16 with D in {64, 128}: the tensor-core kernel of attn_weights_sm100.cu
+    if (weights_sm100_supported(a, out)) return launch_weights_sm100(a, lse, out, average, st);
     // fp32, head size 64, 16-byte rows: the register-blocked kernel of sdpa_f32_tiled.cu
     if (attn_weights_f32_tiled_supported(a, out)) return launch_attn_weights_f32_tiled(a, lse, out, average, st);
     switch (a.q.dtype) {

@@ -50,6 +50,9 @@ int launch_linear_sm100(const void* a, const void* b, const void* bias, void* c,
 // Attention weights from a finished forward's lse (attn_weights.cu): out (B, L, S) when `average`
 // (mean over heads) else (B, H, L, S), contiguous, in q's dtype.
 int launch_attn_weights(const FwdArgs& a, const void* lse, void* out, bool average, cudaStream_t st);
+// ... on the tensor cores for bf16/f16 q/k with D in {64, 128} (attn_weights_sm100.cu)
+bool weights_sm100_supported(const FwdArgs& a, const void* out);
+int launch_weights_sm100(const FwdArgs& a, const void* lse, void* out, bool average, cudaStream_t st);
 
 // fp32 kernels register-blocked on 64 x 64 tiles (sdpa_f32_tiled.cu): f32 with D = Dv = 64, masks,
 // dropout, any strides. The backward takes rowsum(dout * out) per row in `delta` (B, H, L).

@@ -37,6 +37,8 @@ def _probs(q, k, mask, is_bool, scale, causal):
     ("f32", 2, 4, 2, 100, 130, 64, True, None, False),   # fp32 tiled kernel: causal, GQA, every head, S % 4 != 0
     ("f32", 1, 4, 1, 97, 200, 64, False, "kpm", True),   # fp32 tiled kernel: bool mask read 4 keys per load
     ("f16", 1, 2, 1, 40, 70, 32, True, None, False),
+    ("bf16", 2, 4, 1, 300, 256, 128, False, "float", True),  # tcgen05 kernel: float mask, 16-byte stores
+    ("f16", 1, 4, 2, 260, 264, 64, True, None, False),       # tcgen05 kernel: causal, every head
     ("f64", 1, 2, 2, 17, 23, 8, False, "float", True),
 ])
 def test_weights_match_the_explicit_softmax(dt, B, H, Hkv, L, S, D, causal, kind, average):
@@ -114,7 +116,8 @@ def test_mha_need_weights_matches_the_reference_module():
     torch.testing.assert_close(tx1.grad, tx2.grad, atol=1e-10, rtol=1e-10)
 
 
-def test_weights_under_dropout_are_those_the_output_used():
+@pytest.mark.parametrize("dt", ["f32", "bf16"])
+def test_weights_under_dropout_are_those_the_output_used(dt):
     """Under dropout the returned per-head weights are P * keep / (1 - p) with the forward's decisions:
     weights @ v reproduces the attention output exactly as the kernels formed it."""
     import torch
@@ -123,10 +126,11 @@ def test_weights_under_dropout_are_those_the_output_used():
 
     O.manual_seed(9)
     B, H, L, D, p, seed = 1, 2, 80, 64, 0.3, 4242
-    q, k, v = (seeded((B, H, L, D), "f32", 0.5) for _ in range(3))
-    tq, tk, tv = (to_dev(x, "f32") for x in (q, k, v))
+    q, k, v = (seeded((B, H, L, D), dt, 0.5) for _ in range(3))
+    tq, tk, tv = (to_dev(x, dt) for x in (q, k, v))
     out, lse = Fn.sdpa_forward(tq, tk, tv, None, None, True, dropout_p=p, seed=seed)
     w = Fn.attention_weights(tq, tk, lse, None, None, True, average=False, dropout_p=p, seed=seed)
-    torch.testing.assert_close(torch.matmul(w, tv), out, atol=1e-5, rtol=1e-5)
+    tol = 1e-5 if dt == "f32" else 2e-2  # 16-bit: the weights and the output are each rounded to bf16
+    torch.testing.assert_close(torch.matmul(w.float(), tv.float()), out.float(), atol=tol, rtol=tol)
     frac = float((w == 0)[0, :, -1].float().mean())  # the last row sees every key: ~30% dropped
     assert 0.15 < frac < 0.45
