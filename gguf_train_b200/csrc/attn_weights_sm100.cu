@@ -38,6 +38,8 @@ using namespace sm100;
 constexpr int WB = 128;            // rows and keys of a tile
 constexpr int WTHREADS = 384;
 constexpr uint32_t WTMEM = 256;    // two S buffers
+constexpr int WREG_LO = 104;       // registers a thread of warpgroup 0 (TMA, MMA) after the split
+constexpr int WREG_HI = 200;       // ... of the two compute warpgroups
 constexpr float WLOG2E = 1.4426950408889634f;
 
 template <int D>
@@ -84,7 +86,31 @@ __device__ __forceinline__ void store_row(T* row, int64_t s, int64_t S, const fl
             dst[q] = make_uint4(pack2w<BF16>(v[8 * q], v[8 * q + 1]), pack2w<BF16>(v[8 * q + 2], v[8 * q + 3]),
                                 pack2w<BF16>(v[8 * q + 4], v[8 * q + 5]), pack2w<BF16>(v[8 * q + 6], v[8 * q + 7]));
     } else {
-        for (int i = 0; i < N && s + i < S; ++i) Elem<T>::store(row + s + i, v[i]);
+#pragma unroll
+        for (int i = 0; i < N; ++i)  // unrolled with constant indices: v stays in registers
+            if (s + i < S) Elem<T>::store(row + s + i, v[i]);
+    }
+}
+
+// one 32-key chunk of a row (keys sc..sc+31): scores in x -> weights, in place
+template <bool MASK, bool DROP>
+__device__ __forceinline__ void weights_chunk(float* x, uint8_t mcls, const MaskView& mk, const unsigned char* mrow,
+                                              int sc, int64_t S, int lim, float scale_log2, float nl2,
+                                              uint32_t rkey, uint32_t drop_thr, float inv_keep) {
+    if constexpr (MASK) {
+        if (mcls == MASK_MIXED) {
+            mask_apply32(x, mk, mrow, sc, S);
+        } else if (mcls == MASK_ALL) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) x[i] = -INFINITY;
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+        const bool in = sc + i <= lim;
+        float e = in ? ex2(fmaf(x[i], scale_log2, nl2)) : 0.0f;  // ex2(-inf) = 0
+        if constexpr (DROP) e = drop_keep(rkey, (uint32_t)(sc + i), drop_thr) ? e * inv_keep : 0.0f;
+        x[i] = e;
     }
 }
 
@@ -126,6 +152,12 @@ weights_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_const
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
+    // Registers: warpgroup 0 (TMA, MMA, two idle warps) hands registers to the compute warpgroups, which
+    // hold 64 scores and 64 head-sum accumulators a thread. Every thread executes its warpgroup's
+    // setmaxnreg at the top of its role's branch, converged (.sync.aligned, warpgroup-wide).
+    static_assert(128 * WREG_LO + 256 * WREG_HI <= WTHREADS * 168, "register split above the launch's registers");
+    if (warp < 4) {
+    setmaxnreg_dec<WREG_LO>();
     if (warp == 0) {
         if (lane == 0 && nh > 0) {
             prefetch_tmap(&tmQ);
@@ -177,12 +209,14 @@ weights_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_const
                 mbar_wait(drain, 0, nullptr, 0);
             }
         }
-    } else if (warp >= 4) {
+    }
+    } else {
+        setmaxnreg_inc<WREG_HI>();
         const int wg = (warp - 4) >> 2;           // keys 64 wg .. of the tile
         const int quad = warp & 3;
         const int64_t l = l0 + quad * 32 + lane;  // this thread's query row
         const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(wg * 64);
-        const int64_t sk = s0 + wg * 64;          // first key of this thread's 64
+        const int sk = (int)s0 + wg * 64;         // first key of this thread's 64 (S < 2^30)
         const int lim = (int)(p.causal ? min(l, p.S - 1) : p.S - 1);  // last key the row may see
         T* const out = (T*)p.out;
         const bool vec = (p.S % 8) == 0;          // rows start 16-byte aligned
@@ -190,9 +224,12 @@ weights_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_const
 #pragma unroll
         for (int i = 0; i < 64; ++i) acc[i] = 0.0f;
         bool ok = true;
+        const float* lse_row = p.lse + b * p.H * p.L + min(l, p.L - 1);  // head h at lse_row[h * L]
+        float lse_next = nh > 0 ? lse_row[0] : 0.0f;                     // one head ahead of its use
         for (int64_t h = 0; h < nh && ok; ++h) {
             const int st = (int)(h & 1);
-            const float lse = l < p.L ? p.lse[(b * p.H + h) * p.L + l] : -INFINITY;
+            const float lse = l < p.L ? lse_next : -INFINITY;
+            if (h + 1 < nh) lse_next = lse_row[(h + 1) * p.L];
             const float nl2 = lse == -INFINITY ? -INFINITY : -lse * WLOG2E;
             const uint8_t mcls = MASK ? p.mk.tile_class(b, h, lt, kt) : (uint8_t)MASK_NONE;
             const unsigned char* mrow = nullptr;
@@ -208,31 +245,18 @@ weights_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_const
             tmem_ld_wait();
             tc_fence_before();
             mbar_arrive(&s_empty[st]);  // the buffer is free for the head after next
+            float* const xa = (float*)ra;  // scores, then (in place) the weights
+            float* const xb = (float*)rb;
+            weights_chunk<MASK, DROP>(xa, mcls, p.mk, mrow, sk, p.S, lim, p.scale_log2, nl2, rkey, p.drop_thr, p.inv_keep);
+            weights_chunk<MASK, DROP>(xb, mcls, p.mk, mrow, sk + 32, p.S, lim, p.scale_log2, nl2, rkey, p.drop_thr,
+                                      p.inv_keep);
+            if (p.average) {
 #pragma unroll
-            for (int c = 0; c < 2; ++c) {
-                float* x = c ? (float*)rb : (float*)ra;  // scores, then (in place) the weights
-                const int64_t sc = sk + 32 * c;
-                if constexpr (MASK) {
-                    if (mcls == MASK_MIXED) {
-                        mask_apply32(x, p.mk, mrow, (int)sc, p.S);
-                    } else if (mcls == MASK_ALL) {
-#pragma unroll
-                        for (int i = 0; i < 32; ++i) x[i] = -INFINITY;
-                    }
-                }
-#pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    const bool in = sc + i <= lim;
-                    float e = in ? ex2(fmaf(x[i], p.scale_log2, nl2)) : 0.0f;  // ex2(-inf) = 0
-                    if constexpr (DROP) e = drop_keep(rkey, (uint32_t)(sc + i), p.drop_thr) ? e * p.inv_keep : 0.0f;
-                    x[i] = e;
-                }
-                if (p.average) {
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) acc[32 * c + i] += x[i];
-                } else if (l < p.L) {
-                    store_row<32, BF16>(out + ((b * p.H + h) * p.L + l) * p.S, sc, p.S, x, vec);
-                }
+                for (int i = 0; i < 32; ++i) { acc[i] += xa[i]; acc[32 + i] += xb[i]; }
+            } else if (l < p.L) {
+                T* row = out + ((b * p.H + h) * p.L + l) * p.S;
+                store_row<32, BF16>(row, sk, p.S, xa, vec);
+                store_row<32, BF16>(row, sk + 32, p.S, xb, vec);
             }
         }
         if (!ok) {
@@ -267,6 +291,15 @@ int run_weights_sm100(const CUtensorMap& mq, const CUtensorMap& mk, const WParam
         if (cuda_failed(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM),
                         "attention weights (sm100): shared memory"))
             return -1;
+        // setmaxnreg.inc waits until the block's registers cover the split: refuse a build whose kernel
+        // was compiled with fewer registers a thread than the split assumes
+        cudaFuncAttributes fa;
+        if (cuda_failed(cudaFuncGetAttributes(&fa, kern), "cudaFuncGetAttributes(weights_sm100)")) return -1;
+        if ((int64_t)fa.numRegs * WTHREADS < 128 * WREG_LO + 256 * WREG_HI) {
+            set_errorf("attention weights (sm100): kernel built with %d registers a thread, below the %d the "
+                       "register split needs", fa.numRegs, (128 * WREG_LO + 256 * WREG_HI + WTHREADS - 1) / WTHREADS);
+            return -1;
+        }
         attr = true;
     }
     dim3 grid((unsigned)((S + WB - 1) / WB), (unsigned)((L + WB - 1) / WB), (unsigned)B);
