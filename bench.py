@@ -588,6 +588,53 @@ def run_linear(args, rank: int, world: int, dev, max_over_ranks=lambda x: x) -> 
     return res
 
 
+def run_weights(args, rank: int, world: int, dev, max_over_ranks=lambda x: x) -> dict:
+    """MultiheadAttention's need_weights output at config 3's shape (bf16, B=8, Hq=32, Hkv=8, L=4096,
+    D=128, causal): the head-averaged weights (B, L, S) formed by the tcgen05 weights kernel from the
+    forward's lse (functional.attention_weights). Per (head, query, key) of the causal triangle the
+    kernel does a 2*D-FLOP product on the tensor cores and one exponential on the MUFU unit (16 a clock
+    per SM); both rates are reported, the exponentials against the MUFU's nominal rate at the sampled
+    clock. The forward that produces lse runs once, outside the timed region; the output (268 MB) is
+    larger than L2 and rewritten by every launch."""
+    import torch
+
+    from gguf_train_b200 import _C
+    from gguf_train_b200 import functional as Fn
+
+    B, H, Hkv, L, D = CFG["B"], CFG["H"], CFG["Hkv"], CFG["L"], CFG["D"]
+    g = torch.Generator(device=dev)
+    g.manual_seed(77 + rank)
+    q = (torch.randn((B, H, L, D), generator=g, device=dev) * 0.5).to(torch.bfloat16)
+    k = (torch.randn((B, Hkv, L, D), generator=g, device=dev) * 0.5).to(torch.bfloat16)
+    v = (torch.randn((B, Hkv, L, D), generator=g, device=dev) * 0.5).to(torch.bfloat16)
+    scale = 1.0 / math.sqrt(D)
+    _, lse = Fn.sdpa_forward(q, k, v, None, scale, True)
+    step = lambda: Fn.attention_weights(q, k, lse, None, scale, True, True)  # noqa: E731
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize(dev)
+    steps = max(10, min(args.steps, 50))
+    with ClockSampler(torch.cuda.current_device()) as sampler:
+        ms = max_over_ranks(_time_events(torch.cuda.current_stream(dev), step, steps))
+    clocks = sampler.summary()
+    pairs = B * H * L * (L + 1) / 2  # (head, query, key) triples of the causal triangle
+    tf = 2.0 * D * pairs / (ms * 1e-3) / 1e12
+    peaks = load_peaks()
+    mhz = clocks.get("sm_mhz") or 1965.0
+    mufu_peak = 16 * 148 * mhz * 1e6  # exponentials a second
+    exps = pairs / (ms * 1e-3)
+    del q, k, v, lse
+    torch.cuda.empty_cache()
+    return {"workload": "need_weights at config 3's shape: head-averaged attention weights (B, L, S) from the "
+                        "forward's lse, bf16, causal", "value": tf * world, "unit": "TFLOP/s", "ms_per_step": ms,
+            "steps": steps, "scaling": "weak",
+            "roofline": {"bound": "tensor", "achieved": tf, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                         "frac": tf / peaks["bf16_tflops"], "peak_source": peaks["source"] + " bf16 dense (burst)"},
+            "mufu": {"exps_per_s": exps, "nominal_per_s": mufu_peak, "frac": exps / mufu_peak,
+                     "note": "16 exponentials a clock per SM x 148 SMs at the median sampled SM clock"},
+            "clocks": clocks, "status": _C.device_status()}
+
+
 def run_decode_strong(args, rank: int, world: int, dev, max_over_ranks=lambda x: x) -> dict:
     """Config 5a's 64 sequences split over the ranks by sharding.balance_sequences (by cached length,
     longest first); GB/s of the whole step's cache bytes over the slowest rank (strong scaling)."""
@@ -711,11 +758,12 @@ def main() -> None:
                     help="sequences of the decode workload (default: config 5a's 64; smaller for profiling)")
     ap.add_argument("--workload", default="prefill",
                     choices=["prefill", "decode", "train", "ring", "key_padding", "mha", "linear", "prefill_strong",
-                             "train_strong", "decode_strong"],
+                             "train_strong", "decode_strong", "weights"],
                     help="prefill: config 3 (the default line); train: config 4 fwd+bwd; decode: config 5a; "
                          "ring: config 5b (one long sequence, K/V ring over the GPUs); key_padding: config 3 with a "
                          "key-padding mask; mha: config 2 (nn.MultiheadAttention fp32 fwd+bwd); *_strong: the fixed "
-                         "config-3 / config-4 / config-5a work split over the GPUs")
+                         "config-3 / config-4 / config-5a work split over the GPUs; weights: MHA's need_weights output at "
+                         "config 3's shape")
     ap.add_argument("--no-extra", action="store_true",
                     help="default line without the fwd+bwd (config 4) and decode (config 5a) measurements")
     args = ap.parse_args()
@@ -755,7 +803,7 @@ def main() -> None:
         barrier()
         runner = {"decode": run_decode, "train": run_train, "ring": run_ring, "key_padding": run_prefill_key_padding,
                   "mha": run_mha, "linear": run_linear, "prefill_strong": run_prefill_strong, "decode_strong": run_decode_strong,
-                  "train_strong": lambda *a: run_train(*a, strong=True)}[args.workload]
+                  "train_strong": lambda *a: run_train(*a, strong=True), "weights": run_weights}[args.workload]
         res = runner(args, rank, world, dev, max_over_ranks)
         if args.workload != "decode":
             scaling = res.pop("scaling", "weak")
@@ -889,6 +937,8 @@ def main() -> None:
         line["extra"]["mha_config2"] = run_mha(args, rank, world, dev, max_over_ranks)
         barrier()
         line["extra"]["linear_bf16"] = run_linear(args, rank, world, dev, max_over_ranks)
+        barrier()
+        line["extra"]["need_weights"] = run_weights(args, rank, world, dev, max_over_ranks)
         if world > 1:  # strong scaling: the fixed batches split over the ranks
             barrier()
             line["extra"]["prefill_strong"] = run_prefill_strong(args, rank, world, dev, max_over_ranks)

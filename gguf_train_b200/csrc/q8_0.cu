@@ -88,7 +88,7 @@ __global__ void q8_0_append_kernel(const T* __restrict__ x, int64_t Hkv, int64_t
     } else {
         const T* xr = x + r * nb_row * QK;  // the whole row: a NeoX partner can sit in another block
         float v[QK];
-#pragma unroll 4
+#pragma unroll  // constant indices: v stays in registers
         for (int e = 0; e < QK; ++e) {
             const int c = (int)(j * QK) + e;
             float xc = (float)Elem<T>::load(xr + c);
