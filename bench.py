@@ -601,7 +601,8 @@ def run_weights(args, rank: int, world: int, dev, max_over_ranks=lambda x: x) ->
     from gguf_train_b200 import _C
     from gguf_train_b200 import functional as Fn
 
-    B, H, Hkv, L, D = CFG["B"], CFG["H"], CFG["Hkv"], CFG["L"], CFG["D"]
+    H, Hkv, L, D = CFG["H"], CFG["Hkv"], CFG["L"], CFG["D"]
+    B = args.weights_batch or CFG["B"]
     g = torch.Generator(device=dev)
     g.manual_seed(77 + rank)
     q = (torch.randn((B, H, L, D), generator=g, device=dev) * 0.5).to(torch.bfloat16)
@@ -625,8 +626,8 @@ def run_weights(args, rank: int, world: int, dev, max_over_ranks=lambda x: x) ->
     exps = pairs / (ms * 1e-3)
     del q, k, v, lse
     torch.cuda.empty_cache()
-    return {"workload": "need_weights at config 3's shape: head-averaged attention weights (B, L, S) from the "
-                        "forward's lse, bf16, causal", "value": tf * world, "unit": "TFLOP/s", "ms_per_step": ms,
+    return {"workload": f"need_weights at config 3's shape (B={B}): head-averaged attention weights (B, L, S) "
+                        "from the forward's lse, bf16, causal", "value": tf * world, "unit": "TFLOP/s", "ms_per_step": ms,
             "steps": steps, "scaling": "weak",
             "roofline": {"bound": "tensor", "achieved": tf, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
                          "frac": tf / peaks["bf16_tflops"], "peak_source": peaks["source"] + " bf16 dense (burst)"},
@@ -756,6 +757,8 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--decode-batch", type=int, default=None,
                     help="sequences of the decode workload (default: config 5a's 64; smaller for profiling)")
+    ap.add_argument("--weights-batch", type=int, default=None,
+                    help="sequences of the weights workload (default: config 3's 8; smaller for profiling)")
     ap.add_argument("--workload", default="prefill",
                     choices=["prefill", "decode", "train", "ring", "key_padding", "mha", "linear", "prefill_strong",
                              "train_strong", "decode_strong", "weights"],
