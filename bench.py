@@ -636,6 +636,60 @@ def run_weights(args, rank: int, world: int, dev, max_over_ranks=lambda x: x) ->
             "clocks": clocks, "status": _C.device_status()}
 
 
+def run_rope_prefill(args, rank: int, world: int, dev, max_over_ranks=lambda x: x) -> dict:
+    """Config 3 preceded by RoPE on q and k (n_dims = 128, normal pairs, freq_base 10^4, positions
+    0..L-1), the llama-style prefill: gtb_sdpa_fwd_rope (q rotated inside the tcgen05 kernel, k once
+    into k_rot) against rope() on q and k followed by the forward, on the same inputs. FLOPs: the
+    attention's (4 D per causal pair)."""
+    import torch
+
+    import gguf_train_b200 as gtb
+    from gguf_train_b200 import _C
+    from gguf_train_b200 import functional as Fn
+
+    B, H, Hkv, L, D = CFG["B"], CFG["H"], CFG["Hkv"], CFG["L"], CFG["D"]
+    g = torch.Generator(device=dev)
+    g.manual_seed(31 + rank)
+    q = (torch.randn((B, H, L, D), generator=g, device=dev) * 0.5).to(torch.bfloat16)
+    k = (torch.randn((B, Hkv, L, D), generator=g, device=dev) * 0.5).to(torch.bfloat16)
+    v = (torch.randn((B, Hkv, L, D), generator=g, device=dev) * 0.5).to(torch.bfloat16)
+    pos = torch.arange(L, dtype=torch.int32, device=dev)
+    scale = 1.0 / math.sqrt(D)
+    fused = lambda: Fn.sdpa_forward_rope(q, k, v, pos, D, 0, 10000.0, 1.0, scale=scale, is_causal=True,  # noqa: E731
+                                         need_lse=False)
+    in_kernel = lambda: Fn.sdpa_forward_rope(q, k, v, pos, D, 0, 10000.0, 1.0, scale=scale,  # noqa: E731
+                                             is_causal=True, need_lse=False, q_in_kernel=True)
+
+    def unfused():
+        qr = gtb.rope(q, pos, D, 0, 0, 10000.0, 1.0)
+        kr = gtb.rope(k, pos, D, 0, 0, 10000.0, 1.0)
+        return Fn.sdpa_forward(qr, kr, v, None, scale, True, need_lse=False)
+
+    for _ in range(max(args.warmup, 3)):
+        fused()
+        in_kernel()
+        unfused()
+    torch.cuda.synchronize(dev)
+    steps = max(3, min(args.steps, 20))
+    stream = torch.cuda.current_stream(dev)
+    ms_f = max_over_ranks(_time_events(stream, fused, steps))
+    path = _C.last_path()
+    ms_k = max_over_ranks(_time_events(stream, in_kernel, steps))
+    ms_u = max_over_ranks(_time_events(stream, unfused, steps))
+    flops = fwd_flops(B, H, L, D)
+    peaks = load_peaks()
+    tf = flops / (ms_f * 1e-3) / 1e12
+    del q, k, v
+    torch.cuda.empty_cache()
+    return {"workload": "config 3 with RoPE on q and k first (n_dims 128, normal pairs, positions 0..L-1): "
+                        "gtb_sdpa_fwd_rope", "value": tf * world, "unit": "TFLOP/s", "ms_per_step": ms_f,
+            "steps": steps, "kernel": path, "unfused_ms": ms_u, "speedup_over_unfused": ms_u / ms_f,
+            "q_in_kernel_ms": ms_k,
+            "roofline": {"bound": "tensor", "achieved": tf, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                         "frac": tf / peaks["bf16_tflops"], "peak_source": peaks["source"] + " bf16 dense (burst)"},
+            "status": _C.device_status()}
+
+
 def run_decode_strong(args, rank: int, world: int, dev, max_over_ranks=lambda x: x) -> dict:
     """Config 5a's 64 sequences split over the ranks by sharding.balance_sequences (by cached length,
     longest first); GB/s of the whole step's cache bytes over the slowest rank (strong scaling)."""
@@ -761,12 +815,12 @@ def main() -> None:
                     help="sequences of the weights workload (default: config 3's 8; smaller for profiling)")
     ap.add_argument("--workload", default="prefill",
                     choices=["prefill", "decode", "train", "ring", "key_padding", "mha", "linear", "prefill_strong",
-                             "train_strong", "decode_strong", "weights"],
+                             "train_strong", "decode_strong", "weights", "rope_prefill"],
                     help="prefill: config 3 (the default line); train: config 4 fwd+bwd; decode: config 5a; "
                          "ring: config 5b (one long sequence, K/V ring over the GPUs); key_padding: config 3 with a "
                          "key-padding mask; mha: config 2 (nn.MultiheadAttention fp32 fwd+bwd); *_strong: the fixed "
                          "config-3 / config-4 / config-5a work split over the GPUs; weights: MHA's need_weights output at "
-                         "config 3's shape")
+                         "config 3's shape; rope_prefill: config 3 with RoPE fused into the forward")
     ap.add_argument("--no-extra", action="store_true",
                     help="default line without the fwd+bwd (config 4) and decode (config 5a) measurements")
     args = ap.parse_args()
@@ -806,7 +860,7 @@ def main() -> None:
         barrier()
         runner = {"decode": run_decode, "train": run_train, "ring": run_ring, "key_padding": run_prefill_key_padding,
                   "mha": run_mha, "linear": run_linear, "prefill_strong": run_prefill_strong, "decode_strong": run_decode_strong,
-                  "train_strong": lambda *a: run_train(*a, strong=True), "weights": run_weights}[args.workload]
+                  "train_strong": lambda *a: run_train(*a, strong=True), "weights": run_weights, "rope_prefill": run_rope_prefill}[args.workload]
         res = runner(args, rank, world, dev, max_over_ranks)
         if args.workload != "decode":
             scaling = res.pop("scaling", "weak")
@@ -942,6 +996,8 @@ def main() -> None:
         line["extra"]["linear_bf16"] = run_linear(args, rank, world, dev, max_over_ranks)
         barrier()
         line["extra"]["need_weights"] = run_weights(args, rank, world, dev, max_over_ranks)
+        barrier()
+        line["extra"]["prefill_rope"] = run_rope_prefill(args, rank, world, dev, max_over_ranks)
         if world > 1:  # strong scaling: the fixed batches split over the ranks
             barrier()
             line["extra"]["prefill_strong"] = run_prefill_strong(args, rank, world, dev, max_over_ranks)

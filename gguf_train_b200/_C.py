@@ -58,6 +58,9 @@ def _configure(lib: ctypes.CDLL) -> ctypes.CDLL:
     lib.gtb_sdpa_fwd.argtypes = [P4, P4, P4, P4, c_float, c_int, P4, c_void_p, c_void_p]
     lib.gtb_sdpa_fwd_ex.argtypes = [P4, P4, P4, P4, c_float, c_int, P4, c_void_p, POPTS, c_void_p]
     lib.gtb_sdpa_fwd_ex.restype = c_int
+    lib.gtb_sdpa_fwd_rope.argtypes = [P4, P4, P4, P4, c_float, c_int, c_void_p, c_int64, c_void_p, c_int64, c_int, c_int,
+                                      c_float, c_float, c_int, P4, P4, c_void_p, c_void_p]
+    lib.gtb_sdpa_fwd_rope.restype = c_int
     lib.gtb_attn_weights.argtypes = [P4, P4, P4, c_void_p, c_float, c_int, c_int, POPTS, P4, c_void_p]
     lib.gtb_attn_weights.restype = c_int
     lib.gtb_linear.argtypes = [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_int64,

@@ -423,6 +423,96 @@ GTB_API int gtb_sdpa_fwd_ex(const gtb_tensor4* q, const gtb_tensor4* k, const gt
     return launch_fwd_simt(a, st);
 }
 
+GTB_API int gtb_sdpa_fwd_rope(const gtb_tensor4* q, const gtb_tensor4* k, const gtb_tensor4* v, const gtb_tensor4* mask,
+                              float scale, int is_causal, const int32_t* pos_q, int64_t n_pos_q, const int32_t* pos_k,
+                              int64_t n_pos_k, int n_dims, int mode, float freq_base, float freq_scale,
+                              int q_in_kernel, gtb_tensor4* k_rot, gtb_tensor4* out, void* lse, void* stream) {
+    const char* ctx = "flash_attention (rope)";
+    FwdArgs a;
+    if (!check_attn(ctx, q, k, v, mask, a.sh)) return -1;
+    if (q->dtype != F32 && q->dtype != F16 && q->dtype != BF16) {
+        set_errorf("%s: q and k must be f32, f16 or bf16", ctx);
+        return -1;
+    }
+    RopeArgs ra;
+    if (!rope_args(a.sh.D, n_dims, mode, freq_base, freq_scale, false, ra)) return -1;
+    if (!pos_q || !pos_k || n_pos_q < a.sh.L || n_pos_k < a.sh.S) {
+        set_errorf("%s: pos_q needs a position for each of the %lld queries and pos_k one for each of the %lld keys", ctx,
+                   (long long)a.sh.L, (long long)a.sh.S);
+        return -1;
+    }
+    if (!out || !k_rot) {
+        set_errorf("%s: out and k_rot are required", ctx);
+        return -1;
+    }
+    const int64_t osh[4] = {a.sh.B, a.sh.H, a.sh.L, a.sh.Dv};
+    if (!same_shape(*out, osh) || out->dtype != q->dtype) {
+        set_errorf("%s: out must be %s in q's dtype", ctx, shape_str(osh, 4).c_str());
+        return -1;
+    }
+    if (!same_shape(*k_rot, k->shape) || k_rot->dtype != k->dtype || !row_major(*k_rot) || !row_major(*k) ||
+        !row_major(*q)) {
+        set_errorf("%s: q, k and k_rot (k's shape and dtype) must be contiguous", ctx);
+        return -1;
+    }
+    if (numel4(*out) == 0) return 0;
+    if (!check_device_ptr(q->data, ctx, "q") || !check_device_ptr(out->data, ctx, "out") ||
+        !check_device_ptr(pos_q, ctx, "pos_q") || !check_device_ptr(pos_k, ctx, "pos_k"))
+        return -1;
+    if (a.sh.S > 0 && (!check_device_ptr(k->data, ctx, "k") || !check_device_ptr(v->data, ctx, "v") ||
+                       !check_device_ptr(k_rot->data, ctx, "k_rot")))
+        return -1;
+    if (mask && !check_device_ptr(mask->data, ctx, "attn_mask")) return -1;
+    if (lse && !check_device_ptr(lse, ctx, "lse")) return -1;
+    cudaStream_t st = (cudaStream_t)stream;
+    // k: rotated once in HBM (every query tile reads each key tile), into the caller's k_rot
+    if (a.sh.S > 0 && launch_rope(k->data, k->dtype, a.sh.B * a.sh.Hkv * a.sh.S, a.sh.S, a.sh.D, pos_k, ra, k_rot->data, st))
+        return -1;
+    a.q = *q; a.k = *k_rot; a.v = *v; a.o = *out;
+    a.has_mask = mask != nullptr;
+    if (mask) a.mask = broadcast_mask(*mask);
+    a.scale = resolve_scale(scale, a.sh.D);
+    a.causal = is_causal ? 1 : 0;
+    a.lse = lse;
+    int dev = 0;
+    if (cuda_failed(cudaGetDevice(&dev), ctx)) return -1;
+    retain_pool_memory(dev);
+    const size_t q_bytes = (size_t)numel4(*q) * (q->dtype == F32 ? 4 : 2);
+    if (q_in_kernel && !mask && n_dims % 16 == 0 && a.sh.L > 0 && fwd_sm100_supported(a)) {
+        // q: rotated inside the tcgen05 forward, each Q tile in shared memory once it has landed, from a
+        // (cos, sin) table of the L query positions
+        float* tab = nullptr;
+        const size_t tab_bytes = (size_t)a.sh.L * (size_t)(n_dims / 2) * 2 * sizeof(float);
+        if (cuda_failed(cudaMallocAsync((void**)&tab, tab_bytes, st), "flash_attention (rope): angle table")) return -1;
+        int rc = launch_rope_table(pos_q, a.sh.L, ra, tab, st);
+        if (rc == 0) {
+            a.rope_q_tab = tab;
+            a.rope_n_dims = n_dims;
+            a.rope_mode = mode;
+            g_last_path = "tcgen05+rope";
+            rc = launch_fwd_sm100(a, st);
+        }
+        cudaFreeAsync(tab, st);  // after the kernel on the same stream
+        return rc;
+    }
+    // otherwise q is rotated into a scratch copy first and the forward runs as gtb_sdpa_fwd would
+    void* qr = nullptr;
+    if (cuda_failed(cudaMallocAsync(&qr, q_bytes, st), "flash_attention (rope): rotated q")) return -1;
+    int rc = launch_rope(q->data, q->dtype, a.sh.B * a.sh.H * a.sh.L, a.sh.L, a.sh.D, pos_q, ra, qr, st);
+    if (rc == 0) {
+        a.q.data = qr;
+        if (fwd_sm100_supported(a)) {
+            g_last_path = "tcgen05";
+            rc = launch_fwd_sm100(a, st);
+        } else {
+            g_last_path = f32_tiled_supported(a.sh, a.q.dtype) ? "f32_tiled" : "simt";
+            rc = launch_fwd_simt(a, st);
+        }
+    }
+    cudaFreeAsync(qr, st);
+    return rc;
+}
+
 GTB_API int gtb_linear(const void* a, const void* b, const void* bias, void* c, int64_t M, int64_t N, int64_t K,
                        int64_t lda, int64_t ldb, int64_t ldc, int dtype, void* stream) {
     const char* ctx = "linear";

@@ -30,6 +30,9 @@ int launch_q8_0_append(const void* x, int x_dtype, int64_t B, int64_t Hkv, int64
 // RoPE of rows (rows = B*H*S of D values, position pos[row % S]) into out (rope.cu)
 int launch_rope(const void* x, int dtype, int64_t rows, int64_t S, int64_t D, const int32_t* pos, const RopeArgs& r,
                 void* out, cudaStream_t st);
+// (cos, sin) table of n positions (rope.cu): tab[2 (s n_dims/2 + i)] = cos, sin of pair i at pos[s],
+// as the rope kernels form the angles (the table of the tcgen05 forward's in-kernel rotation of q)
+int launch_rope_table(const int32_t* pos, int64_t n, const RopeArgs& r, float* tab, cudaStream_t st);
 int64_t decode_num_chunks(int64_t Smax);
 // Scratch of one decode call: a work area of decode_work_bytes() for the persistent kernels (item
 // counter, per-sequence item prefix [B + 1], per-sequence prefix of full-chunk items [B + 1], and at

@@ -157,4 +157,28 @@ int launch_rope(const void* x, int dtype, int64_t rows, int64_t S, int64_t D, co
     return cuda_failed(cudaGetLastError(), "rope launch") ? -1 : 0;
 }
 
+namespace {
+
+// one (position, pair) per thread: the angle as rope_theta forms it, sin times the direction's sign,
+// exactly the entries rope_rows_kernel builds in shared memory
+__global__ void rope_table_kernel(const int32_t* __restrict__ pos, int64_t n, RopeArgs r, float2* __restrict__ tab) {
+    const int np = r.n_dims / 2;
+    const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= n * np) return;
+    const int64_t s = t / np;
+    const int i = (int)(t - s * np);
+    float c, sn;
+    sincosf(rope_theta(pos[s], i, r.theta_scale, r.freq_scale), &sn, &c);
+    tab[t] = make_float2(c, sn * r.sin_sign);
+}
+
+}  // namespace
+
+int launch_rope_table(const int32_t* pos, int64_t n, const RopeArgs& r, float* tab, cudaStream_t st) {
+    const int64_t total = n * (r.n_dims / 2);
+    if (total == 0) return 0;
+    rope_table_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(pos, n, r, (float2*)tab);
+    return cuda_failed(cudaGetLastError(), "rope table launch") ? -1 : 0;
+}
+
 }  // namespace gtb

@@ -25,6 +25,11 @@ struct FwdArgs {
     float drop_p = 0.0f;         // dropout probability of the attention weights (0: none)
     uint32_t drop_thr = 0;       // keep threshold of dropout.cuh
     uint64_t drop_seed = 0;
+    // RoPE of q inside the tcgen05 forward (no mask, no dropout, n_dims % 16 == 0): (cos, sin) of query
+    // row l, pair i at rope_q_tab[2 (l n_dims/2 + i)], 16-byte aligned; null: q is used as given
+    const float* rope_q_tab = nullptr;
+    int rope_n_dims = 0;
+    int rope_mode = 0;
 };
 
 struct BwdArgs {

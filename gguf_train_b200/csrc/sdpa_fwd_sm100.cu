@@ -67,7 +67,7 @@ struct Cfg {
     static constexpr int OFF_K = 2 * TILE;
     static constexpr int OFF_V = OFF_K + KS * TILE;
     static constexpr int OFF_BAR = OFF_V + VS * TILE;
-    static constexpr int NBAR = 1 + 2 * KS + 2 * VS + 2 + 2 + 2 + 1 + 1 + 2 + 4;
+    static constexpr int NBAR = 1 + 2 * KS + 2 * VS + 2 + 2 + 2 + 1 + 1 + 2 + 4 + 1;
     static constexpr int SMEM = OFF_BAR + NBAR * 8 + 16 + 1024;  // + TMEM slot and flag, + alignment slack
 };
 
@@ -109,6 +109,98 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
     return r;
 }
 
+// RoPE of one Q tile in shared memory, in place, by the 64 threads of warps 2-3 (rt = 0..63): the
+// tile is ATOMS 128-byte-swizzled slabs of 64 columns (16-byte chunk c of row r at r * 128 +
+// 16 (c ^ (r & 7))); row r is query row0 + r, rotated with row (row0 + r) of the (cos, sin) table,
+// x0' = x0 c - x1 s, x1' = x0 s + x1 c in f32 with round-to-nearest products, rounded back to the
+// 16-bit type, as the rope kernels compute it (so the rotated tile equals rope(q) in HBM bit for bit).
+// Rows past L (zero-filled by the TMA) and dimensions past n_dims are left as they are.
+template <bool BF16>
+__device__ __forceinline__ float h16_lo(uint32_t w) {
+    if constexpr (BF16) return __uint_as_float(w << 16);
+    else return __half2float(__ushort_as_half((unsigned short)(w & 0xffffu)));
+}
+template <bool BF16>
+__device__ __forceinline__ float h16_hi(uint32_t w) {
+    if constexpr (BF16) return __uint_as_float(w & 0xffff0000u);
+    else return __half2float(__ushort_as_half((unsigned short)(w >> 16)));
+}
+__device__ __forceinline__ void rope_rot(float x0, float x1, float c, float sn, float& a, float& b) {
+    a = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn));
+    b = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, c));
+}
+__device__ __forceinline__ unsigned char* swz_chunk(unsigned char* tile, int r, int g) {
+    return tile + (g >> 3) * (BM * 128) + r * 128 + (((g & 7) ^ (r & 7)) << 4);
+}
+template <bool BF16>
+__device__ void rope_q_tile(unsigned char* tile, int row0, int64_t L, const float* __restrict__ tab, int pairs,
+                            int mode, int rt) {
+    constexpr int NB = 2;  // chunks in flight a thread: their table loads issued before any is used
+    if (mode != 2) {
+        const int cpr = pairs / 4;  // rotated 16-byte chunks per row (4 pairs each)
+        for (int u0 = rt; u0 < BM * cpr; u0 += 64 * NB) {
+            uint4 w[NB];
+            float4 t0[NB], t1[NB];
+#pragma unroll
+            for (int b = 0; b < NB; ++b) {
+                const int u = u0 + 64 * b, r = u / cpr, g = u - r * cpr;
+                if (u < BM * cpr && row0 + r < L) {
+                    const float4* tr = (const float4*)(tab + 2 * ((int64_t)(row0 + r) * pairs + 4 * g));
+                    t0[b] = __ldg(tr);      // (c, s) of pairs 4g, 4g+1
+                    t1[b] = __ldg(tr + 1);  // ... 4g+2, 4g+3
+                    w[b] = *(const uint4*)swz_chunk(tile, r, g);
+                }
+            }
+#pragma unroll
+            for (int b = 0; b < NB; ++b) {
+                const int u = u0 + 64 * b, r = u / cpr, g = u - r * cpr;
+                if (!(u < BM * cpr && row0 + r < L)) continue;
+                float a, c;
+                rope_rot(h16_lo<BF16>(w[b].x), h16_hi<BF16>(w[b].x), t0[b].x, t0[b].y, a, c); w[b].x = pack2<BF16>(a, c);
+                rope_rot(h16_lo<BF16>(w[b].y), h16_hi<BF16>(w[b].y), t0[b].z, t0[b].w, a, c); w[b].y = pack2<BF16>(a, c);
+                rope_rot(h16_lo<BF16>(w[b].z), h16_hi<BF16>(w[b].z), t1[b].x, t1[b].y, a, c); w[b].z = pack2<BF16>(a, c);
+                rope_rot(h16_lo<BF16>(w[b].w), h16_hi<BF16>(w[b].w), t1[b].z, t1[b].w, a, c); w[b].w = pack2<BF16>(a, c);
+                *(uint4*)swz_chunk(tile, r, g) = w[b];
+            }
+        }
+    } else {
+        const int cph = pairs / 8;  // chunks of the first half of a row; chunk g pairs with chunk g + cph
+        constexpr int NBX = NB / 2;
+        for (int u0 = rt; u0 < BM * cph; u0 += 64 * NBX) {
+            uint4 w0[NBX], w1[NBX];
+            float4 t[NBX][4];
+#pragma unroll
+            for (int b = 0; b < NBX; ++b) {
+                const int u = u0 + 64 * b, r = u / cph, g = u - r * cph;
+                if (u < BM * cph && row0 + r < L) {
+                    const float4* tr = (const float4*)(tab + 2 * ((int64_t)(row0 + r) * pairs + 8 * g));
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) t[b][k] = __ldg(tr + k);  // (c, s) of pairs 8g .. 8g+7
+                    w0[b] = *(const uint4*)swz_chunk(tile, r, g);
+                    w1[b] = *(const uint4*)swz_chunk(tile, r, g + cph);
+                }
+            }
+#pragma unroll
+            for (int b = 0; b < NBX; ++b) {
+                const int u = u0 + 64 * b, r = u / cph, g = u - r * cph;
+                if (!(u < BM * cph && row0 + r < L)) continue;
+                uint32_t* x0 = (uint32_t*)&w0[b];
+                uint32_t* x1 = (uint32_t*)&w1[b];
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {  // word k holds pairs 8g+2k (low halves) and 8g+2k+1 (high)
+                    float a0, b0, a1, b1;
+                    rope_rot(h16_lo<BF16>(x0[k]), h16_lo<BF16>(x1[k]), t[b][k].x, t[b][k].y, a0, b0);
+                    rope_rot(h16_hi<BF16>(x0[k]), h16_hi<BF16>(x1[k]), t[b][k].z, t[b][k].w, a1, b1);
+                    x0[k] = pack2<BF16>(a0, a1);
+                    x1[k] = pack2<BF16>(b0, b1);
+                }
+                *(uint4*)swz_chunk(tile, r, g) = w0[b];
+                *(uint4*)swz_chunk(tile, r, g + cph) = w1[b];
+            }
+        }
+    }
+}
+
 // max of three (one instruction on sm_100)
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
     float r;
@@ -139,6 +231,9 @@ struct Params {
     uint32_t drop_thr;   // dropout (DROP instances only): keep threshold, seed, 1 / (1 - p)
     uint64_t drop_seed;
     float inv_keep;
+    const float* rope_tab;  // ROPE instances: (cos, sin) of query row l, pair i at rope_tab[2 (l n_pairs + i)]
+    int rope_pairs;         // n_dims / 2
+    int rope_mode;          // 0: pairs (2i, 2i+1); 2: NeoX, pairs (i, i + n_dims / 2)
 };
 
 // keys a row of tile t may see: [0, n_kv*BN) minus causal / ragged masking
@@ -157,7 +252,7 @@ __device__ __forceinline__ void mask_chunk(float* x, int kv0, int lim) {
         if (kv0 + i > lim) x[i] = -INFINITY;
 }
 
-template <int D, bool BF16, int EMU, bool PERSIST, bool MASK, bool DROP>
+template <int D, bool BF16, int EMU, bool PERSIST, bool MASK, bool DROP, bool ROPE>
 __global__ void __launch_bounds__(NTHREADS, 1)
 fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                  const __grid_constant__ CUtensorMap tmV, const Params p) {
@@ -178,7 +273,8 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
     uint64_t* q_empty = drain + 1;           // every S MMA of an item done: its Q buffers are free
     uint64_t* o_empty = q_empty + 1;         // [2] per tile: the epilogue has read O_t (128 arrivals)
     uint64_t* item_full = o_empty + 2;       // [2] ring of claimed items: index written
-    uint64_t* item_empty = item_full + 2;    // [2] ... read by the MMA warp and the 8 softmax warps
+    uint64_t* item_empty = item_full + 2;    // [2] ... read by the MMA warp and the 8 softmax warps (+ 2 RoPE warps)
+    uint64_t* q_rot = item_empty + 2;        // ROPE: the item's Q tiles rotated in place (64 arrivals)
     uint32_t* tmem_slot = (uint32_t*)(bars + C::NBAR);
     int* abort_flag = (int*)(tmem_slot + 1);
     int* item_slot = abort_flag + 1;         // [2] claimed item index, -1: no more items
@@ -228,7 +324,8 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
             mbar_init(&s_full[t], 1); mbar_init(&p_full[t], 128); mbar_init(&o_final[t], 1); mbar_init(&o_empty[t], 128);
         }
         mbar_init(q_empty, 1);
-        for (int i = 0; i < 2; ++i) { mbar_init(&item_full[i], 1); mbar_init(&item_empty[i], 9); }
+        for (int i = 0; i < 2; ++i) { mbar_init(&item_full[i], 1); mbar_init(&item_empty[i], ROPE ? 11 : 9); }
+        mbar_init(q_rot, 64);
         mbar_init(drain, 1);
         *abort_flag = 0;
         fence_mbar_init();
@@ -376,6 +473,7 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
                     if (i < 0) break;
                     const Item it = item_of(i);
                     ok = mbar_wait(q_full, nitem & 1, p.status, 21);
+                    if (ROPE && ok) ok = mbar_wait(q_rot, nitem & 1, p.status, 28);  // and rotated by warps 2-3
                     for (int t = 0; t < 2 && ok; ++t)
                         if (it.nblk[t] > 0) ok = issue_s(t, J);
                     if (!ok) break;
@@ -407,6 +505,37 @@ fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
                     mbar_wait(drain, 0, nullptr, 0);
                 }
             }
+        } else if constexpr (ROPE) {
+            // ------------------------------------------------------------ RoPE of each item's Q tiles
+            // (warps 2-3): once both Q tiles have landed, rotate them in place, make the generic-proxy
+            // writes visible to the tensor core (async proxy), then release them to the MMA warp. The
+            // next item's Q lands while this item's last blocks are computed, so the rotation overlaps.
+            const int rt = (int)threadIdx.x - 64;
+            bool ok = true;
+            for (int nitem = 0;; ++nitem) {
+                int i;
+                if constexpr (PERSIST) {
+                    const int slot = nitem & 1;
+                    ok = warp_wait(&item_full[slot], (nitem >> 1) & 1, p.status, 17);
+                    if (!ok) break;
+                    i = item_slot[slot];
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&item_empty[slot]);
+                } else {
+                    i = nitem == 0 ? (int)blockIdx.x : -1;
+                }
+                if (i < 0) break;
+                const Item it = item_of(i);
+                ok = warp_wait(q_full, nitem & 1, p.status, 18);
+                if (!ok || __any_sync(0xffffffffu, *(volatile int*)abort_flag)) { ok = false; break; }
+                for (int t = 0; t < 2; ++t)
+                    if (it.nblk[t] > 0)
+                        rope_q_tile<BF16>(smem + C::OFF_Q + t * C::TILE, it.row0[t], p.L, p.rope_tab, p.rope_pairs,
+                                          p.rope_mode, rt);
+                fence_proxy_async_smem();
+                mbar_arrive(q_rot);
+            }
+            if (!ok) *(volatile int*)abort_flag = 1;
         }
     } else {
         setmaxnreg_inc<REG_HI>();
@@ -675,12 +804,12 @@ namespace {
 
 bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
 
-template <int D, bool BF16, int EMU, bool MASK, bool DROP>
+template <int D, bool BF16, int EMU, bool MASK, bool DROP, bool ROPE = false>
 int run(const FwdArgs& a, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const MaskView& mview,
         cudaStream_t st) {
     using C = Cfg<D>;
-    auto kern_p = fwd_sm100_kernel<D, BF16, EMU, true, MASK, DROP>;
-    auto kern_1 = fwd_sm100_kernel<D, BF16, EMU, false, MASK, DROP>;
+    auto kern_p = fwd_sm100_kernel<D, BF16, EMU, true, MASK, DROP, ROPE>;
+    auto kern_1 = fwd_sm100_kernel<D, BF16, EMU, false, MASK, DROP, ROPE>;
     static bool attr_set = false;  // benign race: setting the same attribute twice is harmless
     if (!attr_set) {
         if (cuda_failed(cudaFuncSetAttribute(kern_p, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM),
@@ -714,6 +843,9 @@ int run(const FwdArgs& a, const CUtensorMap& mq, const CUtensorMap& mk, const CU
     p.drop_thr = a.drop_thr;
     p.drop_seed = a.drop_seed;
     p.inv_keep = 1.0f / (1.0f - a.drop_p);
+    p.rope_tab = a.rope_q_tab;
+    p.rope_pairs = a.rope_n_dims / 2;
+    p.rope_mode = a.rope_mode;
     int dev = 0;
     cudaGetDevice(&dev);
     p.status = device_status_word(dev);
@@ -762,6 +894,8 @@ int emu_setting() {
 template <int D, bool BF16>
 int run_emu(const FwdArgs& a, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const MaskView& mview,
             cudaStream_t st) {
+    // RoPE of q inside the kernel: no mask, no dropout (the caller checks), MUFU exponentials
+    if (a.rope_q_tab) return run<D, BF16, 0, false, false, true>(a, mq, mk, mv, mview, st);
     // masked or dropout: MUFU exponentials only
     if (a.drop_p > 0.0f)
         return mview.data ? run<D, BF16, 0, true, true>(a, mq, mk, mv, mview, st)

@@ -122,6 +122,44 @@ def sdpa_forward(q, k, v, mask=None, scale: float | None = None, is_causal: bool
     return out, lse
 
 
+def sdpa_forward_rope(q, k, v, positions, n_dims: int | None = None, mode: int = 0, freq_base: float = 10000.0,
+                      freq_scale: float = 1.0, mask=None, scale: float | None = None, is_causal: bool = False,
+                      need_lse: bool = True, k_positions: torch.Tensor | None = None, q_in_kernel: bool = False):
+    """Prefill attention with RoPE in one call (gtb_sdpa_fwd_rope): returns (out, lse, k_rot) with
+    out = attention(rope(q), rope(k), v) and k_rot = rope(k), bit for bit what rope() on q and k followed
+    by sdpa_forward gives. `positions` (int32, one per query) are q's positions and, unless k_positions
+    is given, k's too. k is rotated once into k_rot, which a caller keeps as its K cache; q into a
+    scratch copy, or with q_in_kernel=True (tcgen05 kernel, no mask) in shared memory inside the kernel
+    (no copy of q, slower on B200)."""
+    _require_cuda("flash_attention (rope)", q, k, v, mask, positions, k_positions)
+    if q.ndim != 4 or k.ndim != 4 or v.ndim != 4:
+        raise RuntimeError("flash_attention (rope) expects 4D q, k, v tensors (B, H, L, D)")
+    B, H, L, D = q.shape
+    S, Dv = k.shape[2], v.shape[3]
+    kp = positions if k_positions is None else k_positions
+    for name, pt in (("positions", positions), ("k_positions", kp)):
+        if pt.dtype != torch.int32 or pt.ndim != 1:
+            raise RuntimeError(f"flash_attention (rope): {name} must be a 1-D int32 tensor")
+    positions, kp = positions.contiguous(), kp.contiguous()
+    q, k = q.contiguous(), k.contiguous()
+    nd = D if n_dims is None else int(n_dims)
+    sc = (1.0 / math.sqrt(D)) if scale is None else float(scale)
+    out = torch.empty((B, H, L, Dv), dtype=q.dtype, device=q.device)
+    k_rot = torch.empty_like(k)
+    lse_dt = torch.float64 if q.dtype == torch.float64 else torch.float32
+    lse = torch.empty((B, H, L), dtype=lse_dt, device=q.device) if need_lse else None
+    mt = _native_mask(mask, B, H, L, S) if mask is not None else None
+    tq, tk, tv, to, tkr = _t4(q), _t4(k), _t4(v), _t4(out), _t4(k_rot)
+    rc = _C.lib.gtb_sdpa_fwd_rope(ctypes.byref(tq), ctypes.byref(tk), ctypes.byref(tv),
+                                  ctypes.byref(mt) if mt is not None else None, sc, 1 if is_causal else 0,
+                                  positions.data_ptr() if positions.numel() else None, positions.numel(),
+                                  kp.data_ptr() if kp.numel() else None, kp.numel(), nd, int(mode), float(freq_base),
+                                  float(freq_scale), 1 if q_in_kernel else 0, ctypes.byref(tkr), ctypes.byref(to),
+                                  lse.data_ptr() if lse is not None and lse.numel() else None, _stream(q.device))
+    _C.check_rc(rc, "flash_attention (rope)")
+    return out, lse, k_rot
+
+
 def sdpa_backward(grad_out, q, k, v, mask, out, lse, scale: float, is_causal: bool,
                   deterministic: bool | None = None, grads=None, dropout_p: float = 0.0, seed: int = 0):
     """One call of the native backward: returns (dq, dk, dv). With `deterministic` (default: whether

@@ -52,6 +52,26 @@ GTB_API int gtb_sdpa_fwd(const gtb_tensor4 *q, const gtb_tensor4 *k, const gtb_t
                          const gtb_tensor4 *mask, float scale, int is_causal,
                          gtb_tensor4 *out, void *lse, void *stream);
 
+/* Prefill attention with rotary position embedding fused in: out = attention(rope(q), rope(k), v) and
+ * k_rot = rope(k), the rotation that of gtb_rope (backward = 0) with q's positions pos_q (>= L entries)
+ * and k's positions pos_k (>= S entries). New export; replaces gt_rope on q and on k (reference
+ * csrc/gt_ops_nn.cpp:2409-2421) followed by gt_flash_attention (csrc/gt_ops_nn.cpp:2423-2525).
+ *   q (B,H,L,D), k (B,Hkv,S,D) contiguous f32/f16/bf16; v, mask, scale, is_causal, out and lse as in
+ *   gtb_sdpa_fwd; k_rot: a contiguous buffer of k's shape and dtype that receives rope(k) (the rotated
+ *   keys a caller keeps as its K cache).
+ * k is rotated once in HBM (every query tile reads every key tile). q is rotated into a stream-ordered
+ * scratch copy first, or, with q_in_kernel != 0 where the tcgen05 kernel runs with no mask and
+ * n_dims % 16 == 0, inside the kernel: each Q tile in shared memory once it has landed, from a
+ * (cos, sin) table of the L query positions (gtb_last_path "tcgen05+rope"; no q copy, but slower on
+ * B200: the next item's Q lands only when the previous item's score products are issued, so the
+ * rotation is not hidden). Either way the results equal gtb_rope on q and k followed by gtb_sdpa_fwd
+ * bit for bit. */
+GTB_API int gtb_sdpa_fwd_rope(const gtb_tensor4 *q, const gtb_tensor4 *k, const gtb_tensor4 *v,
+                              const gtb_tensor4 *mask, float scale, int is_causal, const int32_t *pos_q,
+                              int64_t n_pos_q, const int32_t *pos_k, int64_t n_pos_k, int n_dims, int mode,
+                              float freq_base, float freq_scale, int q_in_kernel, gtb_tensor4 *k_rot,
+                              gtb_tensor4 *out, void *lse, void *stream);
+
 /* The forward for q, k, v and out in HOST memory (contiguous, row-major; pinned for the copies to
  * overlap, pageable works with serialised copies), no mask. New export for callers whose tensors live
  * on the host, as the reference's do (gt_flash_attention, csrc/gt_ops_nn.cpp:2423-2525, reads and
@@ -218,9 +238,10 @@ GTB_API int gtb_attn_merge(float *o_acc, float *lse_acc, const void *o_part, con
                            int part_dtype, int64_t groups, int64_t rows, int64_t D, int64_t part_gstride,
                            int64_t lse_gstride, void *stream);
 
-/* Kernel family of the calling thread's last gtb_sdpa_fwd / gtb_sdpa_bwd call: "tcgen05" (tensor
- * cores, TMA), "f32_tiled" (fp32 with head size 64, register-blocked on the CUDA cores) or "simt"
- * (one warp per row; "" before the first). Lets a caller or a test see which path a call took. */
+/* Kernel family of the calling thread's last gtb_sdpa_fwd / gtb_sdpa_fwd_rope / gtb_sdpa_bwd call:
+ * "tcgen05" (tensor cores, TMA), "tcgen05+rope" (the same with q rotated inside the kernel),
+ * "f32_tiled" (fp32 with head size 64, register-blocked on the CUDA cores) or "simt" (one warp per
+ * row; "" before the first). Lets a caller or a test see which path a call took. */
 GTB_API const char *gtb_last_path(void);
 
 /* Thread-local message of the last failure ("" if none). */
