@@ -201,3 +201,42 @@ def test_handle_rope_checks():
     x = H.Handle.from_numpy(np.zeros((1, 2, 4, 8), np.float32), device=_C.GT_DEV_CPU)
     with pytest.raises(RuntimeError, match="CUDA tensors only"):
         H.rope(x, pos, 8)
+
+
+def test_fused_rope_forward_argument_checks():
+    """gtb_sdpa_fwd_rope checks the attention shapes, the rope arguments, the positions and k_rot
+    before any device work."""
+    from gguf_train_b200 import _C
+
+    def t4(arr, dtype=None):
+        t = _C.Tensor4()
+        t.data = arr.ctypes.data
+        for i, (s, st) in enumerate(zip(arr.shape, np.array(arr.strides) // arr.itemsize)):
+            t.shape[i], t.stride[i] = s, int(st)
+        t.dtype = _C.GT_F32 if dtype is None else dtype
+        return t
+
+    q = np.zeros((1, 2, 4, 8), np.float32)
+
+    def call(qq=q, kk=q, kr=q, mode=0, n_dims=8, n_pos_q=4, n_pos_k=4, qd=None):
+        tq, tk, tkr, to = t4(qq, qd), t4(kk, qd), t4(kr, qd), t4(q.copy(), qd)
+        pos = np.arange(8, dtype=np.int32)
+        rc = _C.lib.gtb_sdpa_fwd_rope(ctypes.byref(tq), ctypes.byref(tk), ctypes.byref(tk), None, 0.0, 1,
+                                      pos.ctypes.data, n_pos_q, pos.ctypes.data, n_pos_k, n_dims, mode, 10000.0, 1.0,
+                                      1, ctypes.byref(tkr), ctypes.byref(to), None, None)
+        return rc, _C.lib.gtb_last_error().decode()
+
+    rc, msg = call(kk=np.zeros((1, 3, 4, 8), np.float32), kr=np.zeros((1, 3, 4, 8), np.float32))
+    assert rc != 0 and "num_heads must be divisible by num_kv_heads" in msg
+    rc, msg = call(mode=1)
+    assert rc != 0 and "mode must be 0 (normal) or 2 (NeoX)" in msg
+    rc, msg = call(n_dims=10)
+    assert rc != 0 and "n_dims must be an even number" in msg
+    rc, msg = call(n_pos_q=3)
+    assert rc != 0 and "a position for each of the 4 queries" in msg
+    rc, msg = call(kr=np.zeros((1, 2, 4, 4), np.float32))
+    assert rc != 0 and "k_rot" in msg
+    rc, msg = call(qd=_C.GT_F64)
+    assert rc != 0 and "f32, f16 or bf16" in msg
+    rc, msg = call()  # well-formed, but host memory: the engine has no CPU path
+    assert rc != 0 and "no CPU path" in msg
