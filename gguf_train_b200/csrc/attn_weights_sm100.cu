@@ -17,7 +17,9 @@
 //   warps 4-11   two warpgroups, one query row per thread (TMEM lane = row), warpgroup g taking keys
 //                64g..64g+63: masks as the forward applies them (the per-tile class table of
 //                mask_tiles.cuh), the exponential, dropout, and the head mean accumulated in registers
-//                (or every head's weights stored), then the output row in 16-byte stores.
+//                (or every head's weights stored), then the output rows; whole 64-key spans go
+//                through a per-warp staging area in shared memory, so that each store instruction
+//                writes 4 rows x 128 contiguous bytes.
 // Every wait is bounded as in the attention kernels: a timeout records a status code, drains the
 // CTA's own copies and MMAs, frees TMEM and returns.
 
@@ -50,7 +52,9 @@ struct WCfg {
     static constexpr int ST_BYTES = 2 * TILE;        // Q and K of one head
     static constexpr int OFF_BAR = 2 * ST_BYTES;     // two stages
     static constexpr int NBAR = 2 + 2 + 2 + 2 + 1;   // st_full, st_empty, s_full, s_empty, drain
-    static constexpr int SMEM = OFF_BAR + NBAR * 8 + 16 + 1024;
+    static constexpr int STG_ROW = 144;              // a staged output row: 64 keys x 2 B + 16 B of padding
+    static constexpr int OFF_STG = (OFF_BAR + NBAR * 8 + 16 + 127) / 128 * 128;  // [8 warps][32 rows]
+    static constexpr int SMEM = OFF_STG + 8 * 32 * STG_ROW + 1024;
 };
 
 struct WParams {
@@ -90,6 +94,32 @@ __device__ __forceinline__ void store_row(T* row, int64_t s, int64_t S, const fl
         for (int i = 0; i < N; ++i)  // unrolled with constant indices: v stays in registers
             if (s + i < S) Elem<T>::store(row + s + i, v[i]);
     }
+}
+
+// A warp's 32 rows of 64 weights (keys sk..sk+63, the thread's row = lane) written through the warp's
+// staging rows in shared memory, so that each store instruction covers 4 rows x 128 contiguous bytes
+// instead of 32 rows x 16 bytes. base: row 0 of the 32 at key sk (16-byte aligned), row_stride in
+// elements; rows_valid (warp-uniform) of the 32 exist.
+template <bool BF16, typename T>
+__device__ __forceinline__ void store_rows_staged(unsigned char* stg, const float* xa, const float* xb, T* base,
+                                                  int64_t row_stride, int rows_valid, int lane) {
+    uint4* my = (uint4*)(stg + lane * WCfg<64>::STG_ROW);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        my[q] = make_uint4(pack2w<BF16>(xa[8 * q], xa[8 * q + 1]), pack2w<BF16>(xa[8 * q + 2], xa[8 * q + 3]),
+                           pack2w<BF16>(xa[8 * q + 4], xa[8 * q + 5]), pack2w<BF16>(xa[8 * q + 6], xa[8 * q + 7]));
+        my[4 + q] = make_uint4(pack2w<BF16>(xb[8 * q], xb[8 * q + 1]), pack2w<BF16>(xb[8 * q + 2], xb[8 * q + 3]),
+                               pack2w<BF16>(xb[8 * q + 4], xb[8 * q + 5]), pack2w<BF16>(xb[8 * q + 6], xb[8 * q + 7]));
+    }
+    __syncwarp();
+    const int c = lane & 7;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const int r = (lane >> 3) + 4 * j;
+        if (r < rows_valid)
+            *(uint4*)(base + r * row_stride + 8 * c) = *(const uint4*)(stg + r * WCfg<64>::STG_ROW + 16 * c);
+    }
+    __syncwarp();  // the rows are read before the next call overwrites them
 }
 
 // one 32-key chunk of a row (keys sc..sc+31): scores in x -> weights, in place
@@ -220,6 +250,11 @@ weights_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_const
         const int lim = (int)(p.causal ? min(l, p.S - 1) : p.S - 1);  // last key the row may see
         T* const out = (T*)p.out;
         const bool vec = (p.S % 8) == 0;          // rows start 16-byte aligned
+        // whole 64-key spans of 16-byte-aligned rows go through the warp's staging rows
+        const bool staged = vec && (int64_t)sk + 64 <= p.S;
+        unsigned char* const stg = smem + C::OFF_STG + (warp - 4) * 32 * C::STG_ROW;
+        const int64_t wrow0 = l0 + quad * 32;     // the warp's first row
+        const int rows_valid = (int)max((int64_t)0, min((int64_t)32, p.L - wrow0));
         float acc[64];
 #pragma unroll
         for (int i = 0; i < 64; ++i) acc[i] = 0.0f;
@@ -253,6 +288,8 @@ weights_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_const
             if (p.average) {
 #pragma unroll
                 for (int i = 0; i < 32; ++i) { acc[i] += xa[i]; acc[32 + i] += xb[i]; }
+            } else if (staged) {
+                store_rows_staged<BF16>(stg, xa, xb, out + ((b * p.H + h) * p.L + wrow0) * p.S + sk, p.S, rows_valid, lane);
             } else if (l < p.L) {
                 T* row = out + ((b * p.H + h) * p.L + l) * p.S;
                 store_row<32, BF16>(row, sk, p.S, xa, vec);
@@ -261,6 +298,17 @@ weights_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_const
         }
         if (!ok) {
             *(volatile int*)abort_flag = 1;
+        } else if (staged) {  // warp-uniform: the whole warp stores through its staging rows
+            if (p.average) {
+                const float inv_h = 1.0f / (float)p.H;
+#pragma unroll
+                for (int i = 0; i < 64; ++i) acc[i] *= inv_h;
+                store_rows_staged<BF16>(stg, acc, acc + 32, out + (b * p.L + wrow0) * p.S + sk, p.S, rows_valid, lane);
+            } else if (nh == 0) {  // a tile wholly above the causal diagonal: zeros for every head
+                for (int64_t h = 0; h < p.H; ++h)
+                    store_rows_staged<BF16>(stg, acc, acc + 32, out + ((b * p.H + h) * p.L + wrow0) * p.S + sk, p.S,
+                                            rows_valid, lane);
+            }
         } else if (l < p.L && sk < p.S) {
             if (p.average) {
                 const float inv_h = 1.0f / (float)p.H;
